@@ -1,0 +1,359 @@
+"""Benchmark of the int8 decode step: tokens/s at B = 65536 streams per GPU, as a fraction of the HBM roofline.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c3] [--impl b200|reference]
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P \
+        bench.py --gpus N --steps K --warmup W
+
+A step is one decode step of every stream (the reference API's `step(tokens, state)` over B streams). Streams are
+independent, so N GPUs each run B streams of their own (weak scaling, no collective on the step path); the timed
+region is bracketed by a barrier and a device synchronise, and the time is the max over ranks.
+
+  value     kernel-only throughput: tokens and state resident in HBM, K launches of ygg_step on the launch stream,
+            timed with CUDA events on that stream; inputs (the 287 MB model) are larger than L2.
+  e2e       the same metric through the public API (B200Yggdrasil.step) with host tokens in pinned memory copied in
+            every step and the logits read back every step.
+  roofline  algorithmic bytes gathered per token (per-stream weights + state/logit traffic) x tokens per launch /
+            the average launch time, against the measured HBM copy bandwidth (MEASURED_PEAKS.json).
+  cpu_baseline  the reference's own int8 kernel (cpu/ygg.cpp, built under oracle/_ref) on the host cores, one
+            stream per core as the reference runs it (`ygg time`, which includes a softmax per token).
+--impl reference times that CPU path alone, on rank 0, and prints its own line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import shutil
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "int8 step tokens/s at B=65536, 1/2/4/8 B200 (% HBM roofline); batch-1 us/token"
+UNIT = "tokens/s"
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def build_model_file(workload, seed, rank, world, dist):
+    """The workload's model file, written once (rank 0) into a shared temp dir."""
+    from yggdrasil_b200 import synth
+    from yggdrasil_b200.ygg1 import write_model
+    w = synth.WORKLOADS[workload]
+    d = Path(os.environ.get("YGG_BENCH_DIR", tempfile.gettempdir())) / "ygg_bench"
+    d.mkdir(parents=True, exist_ok=True)
+    path = d / f"{workload}_s{seed}.bin"
+    if rank == 0 and not path.exists():
+        tmp = path.with_suffix(f".tmp{os.getpid()}")
+        write_model(synth.workload_layers(w, seed=seed), np.linspace(-1, 1, w.shape.vocab), tmp)
+        os.replace(tmp, path)
+    if world > 1:
+        dist.barrier()
+    return w, path
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 50 ms while running."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.proc, self.lines = index, None, []
+
+    def __enter__(self):
+        if shutil.which("nvidia-smi"):
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+            time.sleep(0.3)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            time.sleep(0.1)
+            self.proc.terminate()
+            self.proc.wait(timeout=5)
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_reference_run(model_path, workload, steps, warmup, seg=1000, cores=None):
+    """The reference's ygg.cpp (oracle/_ref/ygg) on every host core, one stream per core, pinned with taskset:
+    `ygg time model x.i32 --seg S --warm W*S` over (W + K) * S tokens per core. Returns (tokens/s, cores, median
+    ns/token over cores, kind, sample text)."""
+    from oracle import oracle as O
+    from yggdrasil_b200 import synth
+    w = synth.WORKLOADS[workload]
+    avail = sorted(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else list(range(os.cpu_count()))
+    cores = avail if cores is None else avail[:cores]
+    if not O.ref_available():
+        return None
+    tmp = Path(tempfile.mkdtemp(prefix="ygg_ref_"))
+    procs = []
+    try:
+        for i, c in enumerate(cores):
+            x = synth.workload_tokens(w, 1, (warmup + steps) * seg, seed=1000 + i)[0]
+            xf = tmp / f"x{i}.i32"
+            x.astype(np.int32).tofile(xf)
+            cmd = [str(O.REF_YGG), "time", str(model_path), str(xf), "--seg", str(seg), "--warm", str(warmup * seg)]
+            if shutil.which("taskset"):
+                cmd = ["taskset", "-c", str(c)] + cmd
+            procs.append(subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True))
+        med = []
+        for p in procs:
+            out, err = p.communicate(timeout=1800)
+            if p.returncode:
+                raise RuntimeError(f"ygg time failed: {err.strip()[:300]}")
+            tok = {k: v for k, v in (t.split("=", 1) for t in out.split() if "=" in t)}
+            med.append(float(tok["median"]))
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+    tps = float(sum(1e9 / m for m in med))
+    sample = (f"{len(cores)} processes of `ygg time --seg {seg} --warm {warmup * seg}`, {steps * seg} timed tokens "
+              f"each (one stream per core, softmax per token included), median {np.median(med):.0f} ns/token")
+    return tps, len(cores), float(np.median(med)), "reference", sample
+
+
+def cpu_model_name():
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from yggdrasil_b200 import synth
+    w, path = build_model_file(args.workload, 7, 0, 1, None)
+    res = cpu_reference_run(path, args.workload, args.steps, args.warmup, seg=args.ref_seg)
+    if res is None:
+        print(json.dumps({"impl": "reference", "unavailable": "the reference binary oracle/_ref/ygg is not built"}))
+        return 0
+    tps, cores, med, kind, sample = res
+    line = {"metric": METRIC, "value": tps, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": w.name, "streams_per_core": 1, "cpu": cpu_model_name(),
+                       "bytes_per_token": synth.gathered_bytes_per_token(w.shape)},
+            "cpu_baseline": {"value": tps, "unit": UNIT, "cores": cores, "kind": kind, "sample": sample},
+            "e2e": {"value": tps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "ns_per_token_median": med}
+    print(json.dumps(line))
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1024)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--workload", default="c3")
+    ap.add_argument("--streams", type=int, default=0, help="streams per GPU (default: the workload's, capped 65536)")
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ref-seg", type=int, default=2000, help="tokens per timed segment of the CPU reference")
+    ap.add_argument("--cpu-steps", type=int, default=100, help="timed segments per core of the CPU baseline")
+    ap.add_argument("--batch1-steps", type=int, default=512)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+
+    from yggdrasil_b200 import Yggdrasil, synth
+    w, path = build_model_file(args.workload, 7, rank, world, dist)
+    B = args.streams or min(w.streams, 65536)
+    K, W = args.steps, args.warmup
+    dev = torch.device("cuda", local)
+    model = Yggdrasil.load(path, backend="b200", device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    # ---- inputs resident in HBM: K + W steps of tokens for this rank's streams
+    x = synth.workload_tokens(w, K + W, B, seed=rank)            # (steps, B)
+    d_tok = torch.as_tensor(x).to(dev)
+    state = model.init_state(B)
+    logits = torch.empty(B, model.vocab, dtype=torch.float32, device=dev)
+
+    # realised leaf usage of the routed layers (untimed): effective number of leaves per layer
+    _, _, routes, _ = model.step_debug(d_tok[0], model.init_state(B))
+    r = routes.cpu().numpy()
+    eff = []
+    for l in range(1, model.layers):
+        h = np.bincount(r[:, l], minlength=1 << model.depth).astype(np.float64)
+        p = h[h > 0] / h.sum()
+        eff.append(round(float(np.exp(-(p * np.log(p)).sum())), 1))
+
+    for i in range(W):
+        model.step_into(d_tok[i], state, state, logits)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    try:
+        gpu_id = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:  # noqa: BLE001
+        gpu_id = str(local)
+    with ClockSampler(gpu_id) as clk:
+        e0.record(stream)
+        for i in range(K):
+            model.step_into(d_tok[W + i], state, state, logits)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    model.status()
+    tokens = B * K * world
+    value = tokens / (ms / 1e3)
+    per_launch_ms = ms / K
+
+    # ---- end to end through the public API: pinned host tokens in, logits out, every step
+    ke = min(K, 256)
+    h_tok = torch.as_tensor(x[W:W + ke]).pin_memory()
+    h_lg = torch.empty(B, model.vocab, dtype=torch.float32).pin_memory()
+    st = model.init_state(B)
+    for i in range(W):
+        lg, st = model.step(h_tok[i % ke], st)
+        h_lg.copy_(lg, non_blocking=True)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for i in range(ke):
+        lg, st = model.step(h_tok[i], st)
+        h_lg.copy_(lg, non_blocking=True)
+    a1.record(stream)
+    torch.cuda.synchronize(dev)
+    ems = a0.elapsed_time(a1)
+    if world > 1:
+        t = torch.tensor([ems], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ems = float(t.item())
+    e2e = B * ke * world / (ems / 1e3)
+
+    # ---- batch 1: us/token of one stream (the reference's published unit), rank 0 only
+    b1 = None
+    if rank == 0 and args.batch1_steps:
+        s1 = model.init_state(1)
+        t1 = d_tok[:, :1].contiguous()
+        lg1 = torch.empty(1, model.vocab, dtype=torch.float32, device=dev)
+        for i in range(W):
+            model.step_into(t1[i], s1, s1, lg1)
+        torch.cuda.synchronize(dev)
+        b0, b1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n1 = min(args.batch1_steps, K + W)
+        b0.record(stream)
+        for i in range(n1):
+            model.step_into(t1[i], s1, s1, lg1)
+        b1e.record(stream)
+        torch.cuda.synchronize(dev)
+        b1 = b0.elapsed_time(b1e) * 1e3 / n1
+
+    bpt = synth.gathered_bytes_per_token(w.shape)
+    peak, kind = peaks()
+    achieved = bpt * B / (per_launch_ms / 1e3) / 1e9
+    traffic = None
+    tf = ROOT / "profiles" / "traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get(f"{args.workload}_B{B}")
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            res = cpu_reference_run(path, args.workload, steps=args.cpu_steps, warmup=2, seg=args.ref_seg)
+        except Exception as e:  # noqa: BLE001
+            res = None
+            print(f"cpu baseline failed: {e}", file=sys.stderr)
+        if res is not None:
+            tps, cores, med, ck, sample = res
+            cpu = {"value": tps, "unit": UNIT, "cores": cores, "kind": ck, "sample": sample,
+                   "cpu": cpu_model_name()}
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic",
+            "config": {"workload": w.name, "streams_per_gpu": B, "global_streams": B * world,
+                       "model_bytes": path.stat().st_size, "bytes_per_token": bpt,
+                       "tokens": "i.i.d. DNA bases p=(0.295,0.205,0.205,0.295,0.0001)" if w.tokens == "dna"
+                       else "uniform bytes", "l2": "inputs larger than L2 (model file > 126 MB)",
+                       "parallelism": f"streams sharded, {world} replica(s)", "effective_leaves_per_layer": eff,
+                       "note": w.note},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic, "peak_kind": kind},
+            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": int(B * 4),
+                    "d2h_bytes_per_step": int(B * model.vocab * 4), "steps": ke},
+            "gpu_launches": K,
+            "batch1_us_per_token": b1,
+            "cpu_baseline": cpu,
+            "clocks": clk.summary()}
+    print(json.dumps(line))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

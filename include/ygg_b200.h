@@ -1,0 +1,109 @@
+/* ygg_b200: the int8 streaming inference step of Yggdrasil on NVIDIA B200 (sm_100a), as a C-ABI library.
+ *
+ * Plain pointers and sizes only: device pointers are raw CUDA device addresses (for example torch.Tensor.data_ptr()
+ * of a CUDA tensor), `stream` is a cudaStream_t passed as void* (NULL: the legacy default stream). Every compute
+ * call is asynchronous on that stream; the model handle is read-only after ygg_load, so calls on different streams
+ * may share it. One handle serves one device.
+ *
+ * Errors: 0 = YGG_OK, a negative YGG_E_* code otherwise (ygg_strerror). No call exits the process, unlike the
+ * reference's die() (cpu/ygg.cpp:41-43).
+ *
+ * Each entry point names the reference interface it replaces, by file:line in the reference repository.
+ */
+#ifndef YGG_B200_H
+#define YGG_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define YGG_API __attribute__((visibility("default")))
+#else
+#define YGG_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define YGG_OK 0
+#define YGG_E_ARG (-1)          /* bad argument: null pointer, negative size */
+#define YGG_E_FORMAT (-2)       /* not a YGG1 file, or its array table does not fit the file */
+#define YGG_E_UNSUPPORTED (-3)  /* header outside the format limits (cpu/export.py:47-48, cpu/ygg.cpp:141-146) */
+#define YGG_E_MISSING (-4)      /* a required array is absent or has the wrong size */
+#define YGG_E_CUDA (-5)         /* a CUDA runtime call failed */
+#define YGG_E_OOM (-6)          /* device or host allocation failed */
+#define YGG_E_TOKEN (-7)        /* a token outside [0, vocab) (cpu/ygg.cpp:493-495) */
+#define YGG_E_TIMEOUT (-8)      /* a bounded device wait gave up (reported through ygg_status) */
+#define YGG_E_DEVICE (-9)       /* no such CUDA device, or not an sm_100 device */
+
+typedef struct ygg_model ygg_model;
+
+/* Shape of a loaded model: the YGG1 header fields (cpu/export.py:41-42, cpu/ygg.cpp:79-82) plus derived sizes. */
+typedef struct {
+    int32_t n_layers, d_state, block_size, vocab, router_depth, readout_rank, layer_input_rank, router_token_dim,
+        input_rank, shift;
+    int32_t n_experts;          /* 2^router_depth */
+    int32_t vocab_pad;          /* vocab rounded up to 32 */
+    int32_t factored;           /* 1: routed layers store U_r, c_r (factored input), 0: tables T_r[x] */
+    int32_t group_scales;       /* 1: per-group state scales (r2b) are present */
+    int64_t file_array_bytes;   /* bytes of the file's array section */
+    int64_t device_bytes;       /* bytes the handle holds on the device */
+    int32_t record_bytes;       /* largest per-expert record in the device layout */
+    int32_t warps_per_block;    /* launch shape of the step kernel */
+} ygg_info_t;
+
+/* Parse a YGG1 file held in host memory, re-lay it out for the device and upload it to `device`.
+ * Replaces the reference loader: cpu/ygg.cpp:204-220 (load), :137-148 (read_header), :151-171 (read_blob),
+ * :173-202 (bind_layer); the file format is cpu/export.py:34-51,382-468. */
+YGG_API int ygg_load(const void *file_bytes, size_t nbytes, int device, ygg_model **out);
+
+/* Shape and sizes of a loaded model. */
+YGG_API int ygg_info(const ygg_model *m, ygg_info_t *out);
+
+/* One decode step of `batch` independent streams: for every layer the router descent, the leaf gather, the
+ * transition / input / layer-input update with saturation, and the readout into the logits.
+ *   d_tokens     int32 [batch]
+ *   d_state_in   int8  [batch][n_layers][d_state]   (may equal d_state_out: updated in place)
+ *   d_state_out  int8  [batch][n_layers][d_state]
+ *   d_logits     float [batch][vocab]   or NULL (logits not written)
+ * Replaces cpu/ygg.cpp:441-459 (step, one stream) and the step of yggdrasil/inference.py:175-177 /
+ * yggdrasil/inference_triton.py:187-212 (B streams per launch). */
+YGG_API int ygg_step(const ygg_model *m, int batch, const int32_t *d_tokens, const int8_t *d_state_in, int8_t *d_state_out,
+             float *d_logits, void *stream);
+
+/* ygg_step that also writes what the reference kernel keeps internal, for bit-exact checks:
+ *   d_routes  int32 [batch][n_layers]           the leaf (expert) of each layer; the token for layer 0; or NULL
+ *   d_acc     int32 [batch][n_layers][d_state]  the int32 accumulator before saturation to int8; or NULL
+ * Same arithmetic as ygg_step (cpu/ygg.cpp:271-280 route, :380-389 update). */
+YGG_API int ygg_step_debug(const ygg_model *m, int batch, const int32_t *d_tokens, const int8_t *d_state_in,
+                   int8_t *d_state_out, float *d_logits, int32_t *d_routes, int32_t *d_acc, void *stream);
+
+/* Score `batch` rows of `steps` tokens in one launch, state and logits kept on chip:
+ *   d_bits[b] = sum over t < steps-1 of -log2 softmax(logits after token t)[token t+1], in float64
+ *   d_tokens  int32 [batch][steps]
+ *   d_state   int8  [batch][n_layers][d_state] in/out (the state after the first steps-1 tokens), or NULL: zero
+ * Replaces yggdrasil/inference.py:179-188 / inference_triton.py:214-227 (score) with the float64 NLL of
+ * cpu/ygg.cpp:513-517. */
+YGG_API int ygg_score(const ygg_model *m, int batch, int steps, const int32_t *d_tokens, int8_t *d_state, double *d_bits,
+              void *stream);
+
+/* Read (and with clear != 0, reset) the model's device status word after the calls queued on `stream`:
+ * 0 when every call since the last clear ran clean, else a negative YGG_E_* code (token out of range, or a bounded
+ * wait that gave up). Synchronises `stream`. */
+YGG_API int ygg_status(const ygg_model *m, void *stream, int clear, int *status_out);
+
+/* Free the device memory of a model; NULL is a no-op. */
+YGG_API void ygg_free(ygg_model *m);
+
+/* Text of an error code. */
+YGG_API const char *ygg_strerror(int code);
+
+/* Library version string, and the sm architecture it was built for ("sm_100a"). */
+YGG_API const char *ygg_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

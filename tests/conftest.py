@@ -1,0 +1,103 @@
+"""Shared fixtures and adapters for the tests.
+
+Markers: gpu (needs a CUDA device and the built libygg_b200.so; the parity tests proper). Tests without the marker
+run on the CPU: the oracle against the reference's golden digests, the file format, the host logic, and that the
+C-ABI library loads and exports what include/ygg_b200.h declares.
+
+The adapters follow the reference's backend-conformance hooks (tests/conftest.py:165-207 of the reference):
+``ygg_step_logp`` works for any backend whose step returns (logits (1, V), state).
+"""
+import hashlib
+import json
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+sys.path.insert(0, str(ROOT))
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (sm_100) and the built libygg_b200.so")
+
+
+def has_gpu() -> bool:
+    try:
+        import torch
+        return torch.cuda.is_available()
+    except Exception:  # noqa: BLE001
+        return False
+
+
+def pytest_collection_modifyitems(config, items):
+    if has_gpu():
+        return
+    skip = pytest.mark.skip(reason="no CUDA device")
+    for item in items:
+        if "gpu" in item.keywords:
+            item.add_marker(skip)
+
+
+def golden(name):
+    return json.loads((GOLDEN / name).read_text())
+
+
+def sha(b) -> str:
+    return hashlib.sha256(bytes(b)).hexdigest()
+
+
+def shape_of(rec):
+    from yggdrasil_b200.synth import ModelShape
+    return ModelShape(**rec["shape"])
+
+
+def case_tokens(rec):
+    """The reference kernel test's tokens: default_rng(0).integers(0, V, (streams, steps)) (cpu/tests/test_kernel.py)."""
+    v = rec["shape"]["vocab"]
+    return np.random.default_rng(rec["token_seed"]).integers(0, v, (rec["streams"], rec["steps"])).astype(np.int32)
+
+
+@pytest.fixture(scope="session")
+def model_dir(tmp_path_factory):
+    return tmp_path_factory.mktemp("models")
+
+
+@pytest.fixture(scope="session")
+def case_model(model_dir):
+    """path of the random model of a kernel-test case (written once per session)."""
+    from yggdrasil_b200 import synth
+    cache = {}
+
+    def get(rec):
+        key = json.dumps(rec["shape"], sort_keys=True)
+        if key not in cache:
+            p = model_dir / f"case{len(cache)}.bin"
+            synth.write_random_model(shape_of(rec), p, seed=rec["seed"])
+            cache[key] = p
+        return cache[key]
+    return get
+
+
+def ygg_step_logp(ygg, tokens):
+    """Feed tokens (T,) one at a time through ygg.step (one stream, from ygg.init_state(1)) -> log-probabilities
+    (T, classes) of the next token."""
+    state, out = ygg.init_state(1), []
+    for t in tokens:
+        logits, state = ygg.step(np.array([t], np.int32), state)
+        out.append(_numpy(logits)[0])
+    z = np.asarray(out, np.float64)
+    return z - (np.log(np.exp(z - z.max(-1, keepdims=True)).sum(-1, keepdims=True)) + z.max(-1, keepdims=True))
+
+
+def ygg_score(ygg, tokens):
+    """score on one stream tokens (n + 1,) -> bits per token of tokens[1:]."""
+    tokens = np.asarray(tokens, np.int32)
+    return float(_numpy(ygg.score(tokens[None])).sum() / (len(tokens) - 1))
+
+
+def _numpy(a):
+    return a.detach().cpu().numpy() if hasattr(a, "detach") else np.asarray(a)

@@ -1,0 +1,106 @@
+"""Regenerate tests/golden/*.json from the reference implementation (run in a container that has the reference tree).
+
+    python tests/golden/make_golden.py [--ref /path/to/yggdrasil]
+
+The fixtures pin this repository's generator and oracle to the reference:
+  kernel_cases.json  for every shape of the reference's kernel test (cpu/tests/test_kernel.py:22-33): the sha256 of
+                     the model file the reference writes (cpu/export.py random_model + write, seed 7), and the sha256
+                     of the reference's logits (cpu/export.py:int_forward, equal to cpu/ygg.cpp's `logits` command) on
+                     the test's tokens (default_rng(0), 8 streams x 64 steps), the per-row bits derived from them in
+                     float64, and a few logits in clear for reading a failure;
+  long_cases.json    two shapes run for 512 steps (deep state dynamics, saturation);
+  workloads.json     the benchmark shapes (yggdrasil_b200.synth WORKLOADS c1-c3) written by the reference's writer, with
+                     int_forward logits on a few streams.
+The reference sources are read in place and never copied; only digests and a few numbers land here.
+"""
+from __future__ import annotations
+
+import argparse
+import hashlib
+import json
+import os
+import subprocess
+import sys
+import tempfile
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ROOT = HERE.parents[1]
+
+
+def sha(b: bytes) -> str:
+    return hashlib.sha256(b).hexdigest()
+
+
+def bits_from_logits(lg: np.ndarray, x: np.ndarray) -> np.ndarray:
+    """bits of x[:, 1:] given the logits after x[:, t], per row, float64 (the score of yggdrasil/inference.py)."""
+    z = lg[:, :-1].astype(np.float64)
+    mx = z.max(-1, keepdims=True)
+    lse = np.log(np.exp(z - mx).sum(-1)) + mx[..., 0]
+    tgt = np.take_along_axis(z, x[:, 1:, None].astype(np.int64), -1)[..., 0]
+    return (lse - tgt).sum(-1) / np.log(2.0)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default=os.environ.get("YGG_REFERENCE", "/root/reference"))
+    a = ap.parse_args()
+    ref = Path(a.ref)
+    sys.path.insert(0, str(ref / "cpu"))
+    sys.path.insert(0, str(ref))
+    sys.path.insert(0, str(ROOT))
+    import export as E  # the reference's cpu/export.py
+    from yggdrasil_b200 import synth
+    ygg = ROOT / "oracle" / "_ref" / "ygg"
+    sys.path.insert(0, str(ref / "cpu" / "tests"))
+    from test_kernel import CASES, STEPS, STREAMS
+
+    fields = [f for f in ("d_state", "block_size", "router_depth", "vocab", "n_layers", "readout_rank",
+                          "layer_input_rank", "input_rank", "group")]
+
+    def run_case(cfg, streams, steps, tmp):
+        layers = E.random_model(cfg, seed=7)
+        ob = np.linspace(-1, 1, cfg.vocab)
+        path = os.path.join(tmp, "m.bin")
+        E.write(layers, ob, path)
+        x = np.random.default_rng(0).integers(0, cfg.vocab, (streams, steps)).astype(np.int32)
+        lg = E.int_forward(layers, ob, x)
+        rec = dict(shape={k: getattr(cfg, k) for k in fields}, seed=7, streams=streams, steps=steps, token_seed=0,
+                   model_sha256=sha(Path(path).read_bytes()), model_bytes=os.path.getsize(path),
+                   logits_sha256=sha(np.ascontiguousarray(lg, np.float32).tobytes()),
+                   bits=[float(v) for v in bits_from_logits(lg, x)],
+                   logits_head=np.asarray(lg[0, :4, :8], np.float64).tolist())
+        if ygg.exists():   # the reference binary agrees with int_forward (the reference test's own assertion)
+            xf, of = os.path.join(tmp, "x.i32"), os.path.join(tmp, "o.f32")
+            x.tofile(xf)
+            subprocess.run([str(ygg), "logits", path, xf, str(streams), str(steps), of], check=True,
+                           stdout=subprocess.DEVNULL)
+            rec["ygg_equal"] = bool(np.array_equal(np.fromfile(of, np.float32).reshape(lg.shape), lg))
+        return rec
+
+    with tempfile.TemporaryDirectory() as tmp:
+        cases = [run_case(c, STREAMS, STEPS, tmp) for c in CASES]
+        (HERE / "kernel_cases.json").write_text(json.dumps(cases, indent=1) + "\n")
+        longs = [run_case(CASES[i], 4, 512, tmp) for i in (1, 12)]
+        (HERE / "long_cases.json").write_text(json.dumps(longs, indent=1) + "\n")
+        works = []
+        for key in ("c1", "c2", "c3"):
+            w = synth.WORKLOADS[key]
+            layers = synth.workload_layers(w, seed=7)
+            ob = np.linspace(-1, 1, w.shape.vocab)
+            path = os.path.join(tmp, "w.bin")
+            E.write(layers, ob, path)            # the reference's writer on this repository's layers
+            x = synth.workload_tokens(w, 4, 32, seed=0)
+            lg = E.int_forward(layers, ob, x)
+            works.append(dict(workload=key, model_sha256=sha(Path(path).read_bytes()),
+                              model_bytes=os.path.getsize(path), streams=4, steps=32, token_seed=0,
+                              logits_sha256=sha(np.ascontiguousarray(lg, np.float32).tobytes()),
+                              bits=[float(v) for v in bits_from_logits(lg, x)]))
+        (HERE / "workloads.json").write_text(json.dumps(works, indent=1) + "\n")
+    print("wrote", [p.name for p in HERE.glob("*.json")])
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,245 @@
+"""The CUDA path against the oracle and the reference's golden digests, through the C-ABI (GPU).
+
+The bar is bit-exact: routes (the leaf of every layer), the int32 accumulators before saturation, the int8 states and
+the f32 logits must equal the oracle's (the C restatement pinned to cpu/ygg.cpp / cpu/export.py:int_forward by
+tests/test_oracle.py) on every shape of the reference's kernel test, and the logits' sha256 must equal the reference's.
+Score bits are float64 sums in another order than the oracle's: rtol 1e-10 (the north-star bar is 1e-4).
+"""
+import numpy as np
+import pytest
+
+from conftest import case_tokens, golden, sha, ygg_score, ygg_step_logp
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+CASES = golden("kernel_cases.json")
+LONG = golden("long_cases.json")
+WORKLOADS = golden("workloads.json")
+BITS_RTOL = 1e-10
+
+
+def _ids(cases):
+    return ["-".join(f"{k[0]}{int(v)}" for k, v in c["shape"].items()) for c in cases]
+
+
+@pytest.fixture(scope="module")
+def torch():
+    import torch
+    return torch
+
+
+def load(path, **kw):
+    from yggdrasil_b200 import Yggdrasil
+    return Yggdrasil.load(path, backend="b200", **kw)
+
+
+def run_windows(model, om, x, torch):
+    """Step the GPU model and the oracle over windows x (S, T) from zero; compare everything at every step.
+    Returns the GPU logits (S, T, V)."""
+    s, t = x.shape
+    st = model.init_state(s)
+    ost = om.init_state(s)
+    out = np.empty((s, t, model.vocab), np.float32)
+    for i in range(t):
+        lg, nst, rt, acc = model.step_debug(x[:, i], st)
+        olg, ort = om.step(x[:, i], ost, routes=True)
+        np.testing.assert_array_equal(rt.cpu().numpy(), ort, err_msg=f"routes at step {i}")
+        np.testing.assert_array_equal(nst.cpu().numpy(), ost, err_msg=f"states at step {i}")
+        got = acc.cpu().numpy()
+        np.testing.assert_array_equal(np.clip(got, -128, 127).astype(np.int8), ost, err_msg=f"acc at step {i}")
+        np.testing.assert_array_equal(lg.cpu().numpy(), olg, err_msg=f"logits at step {i}")
+        out[:, i] = olg
+        st = nst
+    return out
+
+
+@pytest.mark.parametrize("rec", CASES, ids=_ids(CASES))
+def test_step_bit_exact(rec, case_model, torch):
+    path = case_model(rec)
+    model, om = load(path), O.OracleModel(path)
+    x = case_tokens(rec)
+    lg = run_windows(model, om, x, torch)
+    assert sha(np.ascontiguousarray(lg).tobytes()) == rec["logits_sha256"]
+    model.status()
+
+
+@pytest.mark.parametrize("rec", LONG, ids=_ids(LONG))
+def test_long_sequences_bit_exact(rec, case_model, torch):
+    path = case_model(rec)
+    model = load(path)
+    x = case_tokens(rec)
+    st = model.init_state(x.shape[0])
+    out = []
+    for i in range(x.shape[1]):
+        lg, st = model.step(x[:, i], st)
+        out.append(lg.cpu().numpy())
+    lg = np.stack(out, 1)
+    assert sha(np.ascontiguousarray(lg).tobytes()) == rec["logits_sha256"]
+
+
+@pytest.mark.parametrize("rec", CASES[::2], ids=_ids(CASES[::2]))
+def test_score_matches_reference_bits(rec, case_model, torch):
+    model = load(case_model(rec))
+    bits = model.score(case_tokens(rec))
+    np.testing.assert_allclose(bits, rec["bits"], rtol=BITS_RTOL)
+
+
+@pytest.mark.parametrize("rec", CASES[:4], ids=_ids(CASES[:4]))
+def test_score_from_state_and_state_out(rec, case_model, torch):
+    """score continues from a given state (yggdrasil/inference.py:179-188) and leaves the caller's state alone."""
+    path = case_model(rec)
+    model, om = load(path), O.OracleModel(path)
+    x = case_tokens(rec)
+    pre, rest = x[:, :16], x[:, 15:]
+    st = model.init_state(x.shape[0])
+    for i in range(15):
+        _, st = model.step(pre[:, i], st)
+    keep = st.clone()
+    bits = model.score(rest, state=st)
+    assert torch.equal(st, keep)
+    ost = om.init_state(x.shape[0])
+    for i in range(15):
+        om.step(pre[:, i], ost)
+    np.testing.assert_allclose(bits, om.score(rest, ost), rtol=BITS_RTOL)
+
+
+@pytest.mark.parametrize("batch", [1, 2, 31, 33, 257, 1000])
+def test_ragged_batches(batch, case_model, torch):
+    rec = CASES[0]
+    path = case_model(rec)
+    model, om = load(path), O.OracleModel(path)
+    rng = np.random.default_rng(batch)
+    x = rng.integers(0, model.vocab, (batch, 5)).astype(np.int32)
+    st, ost = model.init_state(batch), om.init_state(batch)
+    for i in range(x.shape[1]):
+        lg, st = model.step(x[:, i], st)
+        np.testing.assert_array_equal(lg.cpu().numpy(), om.step(x[:, i], ost))
+    np.testing.assert_array_equal(st.cpu().numpy(), ost)
+
+
+def test_empty_batch(case_model, torch):
+    model = load(case_model(CASES[0]))
+    lg, st = model.step(np.zeros(0, np.int32), model.init_state(0))
+    assert tuple(lg.shape) == (0, model.vocab) and tuple(st.shape) == (0, model.layers, model.n)
+    assert model.score(np.zeros((0, 4), np.int32)).shape == (0,)
+
+
+def test_in_place_state(case_model, torch):
+    rec = CASES[1]
+    path = case_model(rec)
+    model, om = load(path), O.OracleModel(path)
+    x = case_tokens(rec)
+    st, ost = model.init_state(x.shape[0]), om.init_state(x.shape[0])
+    logits = torch.empty(x.shape[0], model.vocab, dtype=torch.float32, device=model.device)
+    for i in range(8):
+        tok = torch.as_tensor(x[:, i], device=model.device)
+        model.step_into(tok, st, st, logits)
+        np.testing.assert_array_equal(logits.cpu().numpy(), om.step(x[:, i], ost))
+    np.testing.assert_array_equal(st.cpu().numpy(), ost)
+
+
+def test_cuda_graph_step(case_model, torch):
+    rec = CASES[2]
+    path = case_model(rec)
+    plain, graph = load(path), load(path, cuda_graph=True)
+    x = case_tokens(rec)
+    s1, s2 = plain.init_state(x.shape[0]), graph.init_state(x.shape[0])
+    for i in range(6):
+        l1, s1 = plain.step(x[:, i], s1)
+        l2, s2 = graph.step(x[:, i], s2)
+        assert torch.equal(l1, l2) and torch.equal(s1, s2)
+
+
+def test_host_token_out_of_range_raises(case_model, torch):
+    model = load(case_model(CASES[3]))
+    with pytest.raises(ValueError):
+        model.step(np.array([model.vocab], np.int32), model.init_state(1))
+    with pytest.raises(ValueError):
+        model.score(np.array([[0, 1, -1]], np.int32))
+
+
+def test_device_token_out_of_range_is_flagged(case_model, torch):
+    """A bad token on the device skips its stream (NaN logits, state unchanged) and sets the status word; the other
+    streams are exact."""
+    rec = CASES[0]
+    path = case_model(rec)
+    model, om = load(path), O.OracleModel(path)
+    x = np.array([3, model.vocab + 7, 5], np.int32)
+    st = model.init_state(3)
+    lg, nst = model.step(torch.as_tensor(x, device=model.device), st)
+    with pytest.raises(ValueError):
+        model.status()
+    model.status()   # cleared
+    ost = om.init_state(1)
+    np.testing.assert_array_equal(lg[0].cpu().numpy(), om.step(x[:1], ost)[0])
+    assert torch.isnan(lg[1]).all() and torch.equal(nst[1], st[1])
+
+
+def test_conformance_adapters(case_model, torch):
+    """The reference's backend hooks: step log-probabilities and the streamed score agree."""
+    rec = CASES[5]
+    model = load(case_model(rec))
+    x = case_tokens(rec)[0, :20]
+    logp = ygg_step_logp(model, x)
+    manual = -logp[np.arange(len(x) - 1), x[1:]].sum() / np.log(2) / (len(x) - 1)
+    np.testing.assert_allclose(ygg_score(model, x), manual, rtol=1e-9)
+
+
+def test_generate_greedy_matches_oracle(case_model, torch):
+    rec = CASES[0]
+    path = case_model(rec)
+    model, om = load(path), O.OracleModel(path)
+    prompt = np.array([1, 2, 3], np.int32)
+    out = model.generate(prompt, 5, temperature=0)
+    st, toks = om.init_state(1), list(prompt)
+    for t in prompt:
+        lg = om.step(np.array([t], np.int32), st)
+    for _ in range(5):
+        nxt = int(lg[0].argmax())
+        toks.append(nxt)
+        lg = om.step(np.array([nxt], np.int32), st)
+    np.testing.assert_array_equal(out, toks)
+    sampled = model.generate(np.array([[1, 2], [3, 4]]), 4, temperature=0.8, top_k=5, seed=1)
+    assert sampled.shape == (2, 6) and sampled.min() >= 0 and sampled.max() < model.vocab
+
+
+@pytest.mark.parametrize("rec", WORKLOADS, ids=[w["workload"] for w in WORKLOADS])
+def test_benchmark_workloads_bit_exact(rec, tmp_path, torch):
+    from yggdrasil_b200 import synth
+    from yggdrasil_b200.ygg1 import write_model
+    w = synth.WORKLOADS[rec["workload"]]
+    p = tmp_path / "w.bin"
+    write_model(synth.workload_layers(w, seed=7), np.linspace(-1, 1, w.shape.vocab), p)
+    model, om = load(p), O.OracleModel(p)
+    x = synth.workload_tokens(w, rec["streams"], rec["steps"], seed=rec["token_seed"])
+    lg = run_windows(model, om, x, torch)
+    assert sha(np.ascontiguousarray(lg).tobytes()) == rec["logits_sha256"]
+    np.testing.assert_allclose(model.score(x), rec["bits"], rtol=BITS_RTOL)
+
+
+def test_large_batch_sampled_streams(tmp_path, torch):
+    """At the benchmark batch (65536 streams of the c3 shape), a checksum over all streams' states and logits is
+    reproducible, and a sample of streams equals the oracle exactly after 3 steps."""
+    from yggdrasil_b200 import synth
+    from yggdrasil_b200.ygg1 import write_model
+    w = synth.WORKLOADS["c3"]
+    p = tmp_path / "c3.bin"
+    write_model(synth.workload_layers(w, seed=7), np.linspace(-1, 1, w.shape.vocab), p)
+    model, om = load(p), O.OracleModel(p)
+    B = 65536
+    x = synth.workload_tokens(w, B, 3, seed=0)
+    st = model.init_state(B)
+    for i in range(3):
+        lg, st = model.step(x[:, i], st)
+    st2 = model.init_state(B)
+    for i in range(3):
+        lg2, st2 = model.step(x[:, i], st2)
+    assert torch.equal(st, st2) and torch.equal(lg, lg2)
+    idx = np.random.default_rng(5).choice(B, 256, replace=False)
+    ost = om.init_state(len(idx))
+    for i in range(3):
+        olg = om.step(x[idx, i], ost)
+    np.testing.assert_array_equal(lg.cpu().numpy()[idx], olg)
+    np.testing.assert_array_equal(st.cpu().numpy()[idx], ost)

@@ -1,0 +1,161 @@
+"""Synthetic int8 models and token streams for the tests and the benchmark (no checkpoints or datasets needed).
+
+``random_layers(shape, seed)`` draws the same integers, in the same order from ``np.random.default_rng(seed)``, as the
+reference's random-model generator (``cpu/export.py:473-532``): orthogonal b x b blocks times decays U[0.6, 1] in Q14,
+int16 tables U[-24, 24], uniform int8 projections and readouts, thresholds 300 N(0, 1). Keeping the draw order lets
+a file written here equal, byte for byte, the file the reference writes for the same shape and seed, which is what
+pins this generator (and, through it, the parity fixtures) to the reference.
+
+``WORKLOADS`` are the benchmark shapes. The router rows of those are redrawn as N(0, 0.02) quantised symmetrically
+per row to int8, the scheme the benchmark configuration names; everything else is the generator above.
+"""
+from __future__ import annotations
+
+import dataclasses
+
+import numpy as np
+
+from .ygg1 import SHIFT, STATE_GROUP, FactoredInput, IntLayer, write_model
+
+f32 = np.float32
+
+
+@dataclasses.dataclass(frozen=True)
+class ModelShape:
+    """Shape of a random int8 model (the reference's KernelConfig fields, cpu/export.py:473-484)."""
+    d_state: int
+    block_size: int
+    router_depth: int
+    vocab: int
+    n_layers: int = 2
+    readout_rank: int = 8
+    layer_input_rank: int = 16
+    input_rank: int = 0          # > 0: factored input storage of this rank
+    group: bool = False          # group scales
+
+
+def random_layers(shape: ModelShape, seed: int = 1):
+    """Random IntLayers of the given shape (draw order of cpu/export.py:487-532)."""
+    rng = np.random.default_rng(seed)
+    n, b, depth, vocab = shape.d_state, shape.block_size, shape.router_depth, shape.vocab
+    r, r2 = shape.readout_rank, shape.layer_input_rank
+    blocks = np.linalg.qr(rng.standard_normal((64, b, b)))[0]   # 64 distinct orthogonal blocks
+    layers = []
+    for l in range(shape.n_layers):
+        experts = vocab if l == 0 else 2 ** depth
+        a16 = np.empty((experts, n // b, b, b), np.int64)
+        for j in range(0, experts, 4096):
+            m = min(4096, experts - j)
+            decay = rng.uniform(0.6, 1.0, (m, n // b, b, 1))
+            a16[j:j + m] = np.rint(2.0 ** SHIFT * decay * blocks[rng.integers(0, 64, (m, n // b))])
+        kw = dict(token_layer=l == 0, n=n, block=b, depth=0 if l == 0 else depth, transition=a16)
+        if l == 0:
+            kw["table"] = rng.integers(-24, 25, (vocab, 1, n), dtype=np.int16)
+        else:
+            if shape.input_rank:
+                k = shape.input_rank
+                proj = rng.integers(-127, 128, (experts, n, k), dtype=np.int8).astype(np.int64)
+                su = rng.uniform(0.5, 1.5, experts).astype(f32)
+                bias = rng.integers(-24, 25, (experts, n), dtype=np.int16)
+                code = rng.integers(-127, 128, (vocab, k))
+                ts = rng.uniform(0.0002, 0.001, n).astype(f32)
+                kw["factored"] = FactoredInput(input_proj=proj, input_scale=su, bias=bias, token_code=code,
+                                               token_scale=ts)
+            else:
+                kw["table"] = rng.integers(-24, 25, (experts, vocab, n), dtype=np.int16)
+            kw["router_weight"] = rng.integers(-127, 128, (experts - 1, n))
+            kw["router_threshold"] = (300 * rng.standard_normal((vocab, experts - 1))).astype(f32)
+            kw["rms_eps"] = f32(1e-4)
+            if r2:
+                kw["layer_input_down"] = rng.integers(-127, 128, (r2, n))
+                kw["layer_input_down_scale"] = np.full(r2, 0.05, f32)
+                kw["layer_input_proj"] = rng.integers(-127, 128, (experts, n, r2), dtype=np.int8).astype(np.int64)
+                kw["layer_input_scale"] = f32(0.002)
+        kw["readout_scale"], kw["unembed_scale"] = f32(0.002), f32(0.001)
+        if shape.group:
+            kw["readout_scale"] = rng.uniform(0.0005, 0.004, (experts, r)).astype(f32)
+            kw["unembed_scale"] = rng.uniform(0.0005, 0.002, vocab).astype(f32)
+            if l > 0:
+                kw["state_r2"] = (rng.uniform(0.05, 1.0, n // STATE_GROUP) ** 2).astype(f32)
+                if r2:
+                    kw["layer_input_scale"] = rng.uniform(0.0005, 0.004, n).astype(f32)
+        kw["readout"] = rng.integers(-127, 128, (experts, r, n))
+        kw["unembed"] = rng.integers(-127, 128, (vocab, r))
+        layers.append(IntLayer(**kw))
+    return layers
+
+
+def write_random_model(shape: ModelShape, path, seed: int = 7, output_bias=None):
+    """Random model of shape written to path; output bias linspace(-1, 1, V) by default (as the reference's kernel
+    test uses, cpu/tests/test_kernel.py:39). Returns the layers."""
+    layers = random_layers(shape, seed)
+    ob = np.linspace(-1, 1, shape.vocab) if output_bias is None else output_bias
+    write_model(layers, ob, path)
+    return layers
+
+
+def gaussian_router_rows(layers, seed: int, std: float = 0.02):
+    """Replace each routed layer's router rows by N(0, std) draws quantised symmetrically per row to int8."""
+    rng = np.random.default_rng(seed)
+    for q in layers[1:]:
+        w = rng.normal(0.0, std, q.router_weight.shape)
+        s = np.maximum(np.abs(w).max(-1, keepdims=True), 1e-12) / 127
+        q.router_weight = np.rint(w / s).astype(np.int64)
+    return layers
+
+
+# ------------------------------------------------------------------------------------------------------ workloads
+
+DNA_P = np.array([0.295, 0.205, 0.205, 0.295, 0.0001])
+DNA_P = DNA_P / DNA_P.sum()
+
+
+@dataclasses.dataclass(frozen=True)
+class Workload:
+    name: str
+    shape: ModelShape
+    streams: int
+    steps: int
+    tokens: str                  # "uniform" or "dna"
+    note: str = ""
+
+
+WORKLOADS = {
+    # V256 L2 d64 D10: batch 1, 4096 uniform bytes
+    "c1": Workload("c1-5M-enwik8", ModelShape(64, 16, 10, 256, 2, 8, 16), 1, 4096, "uniform"),
+    # V256 L4 d64 D12, factored k=16 (73.1 MB) is the file closest to the named 65 MB
+    "c2": Workload("c2-65MB-enwik8", ModelShape(64, 16, 12, 256, 4, 8, 16, input_rank=16), 4096, 1024, "uniform"),
+    # V5 L4 D13 with R = n/8, R2 = n/4 at d = 128: the YGG1 format allows d_state 64/128/256 only (not 96)
+    "c3": Workload("c3-200M-dna-d128", ModelShape(128, 16, 13, 5, 4, 16, 32), 65536, 512, "dna",
+                   "d_state 128 in place of 96 (YGG1 allows 64/128/256)"),
+    # V256 L4 d128 D13 R16 R2=32, table storage (1892 MB)
+    "c4": Workload("c4-730M-enwik8", ModelShape(128, 16, 13, 256, 4, 16, 32), 262144, 256, "uniform"),
+    # the same model with factored input storage k=32 (390 MB)
+    "c4f": Workload("c4-730M-enwik8-factored", ModelShape(128, 16, 13, 256, 4, 16, 32, input_rank=32), 262144, 256,
+                    "uniform"),
+}
+
+
+def workload_layers(w: Workload, seed: int = 7):
+    """Layers of a benchmark workload: the random generator plus N(0, 0.02) int8 router rows."""
+    return gaussian_router_rows(random_layers(w.shape, seed), seed + 1)
+
+
+def workload_tokens(w: Workload, streams: int, steps: int, seed: int = 0) -> np.ndarray:
+    """(streams, steps) int32 tokens: uniform over the vocabulary, or i.i.d. DNA bases with DNA_P."""
+    rng = np.random.default_rng(seed)
+    if w.tokens == "dna":
+        return rng.choice(len(DNA_P), size=(streams, steps), p=DNA_P).astype(np.int32)
+    return rng.integers(0, w.shape.vocab, (streams, steps)).astype(np.int32)
+
+
+def gathered_bytes_per_token(shape: ModelShape, with_io: bool = True) -> int:
+    """Algorithmic bytes gathered per token of one decode step (per-stream weights and state/logit traffic; shared
+    per-launch weights excluded): G = G_tok + (L-1) G_rt (+ IO = 2 L n + 4 V + 4)."""
+    n, b, d, v = shape.d_state, shape.block_size, shape.router_depth, shape.vocab
+    r, r2, k, L = shape.readout_rank, shape.layer_input_rank, shape.input_rank, shape.n_layers
+    g_tok = 2 * n * b + r * n + 2 * n
+    s = (n * k + 2 * n + 4) if k else 2 * n
+    g_rt = d * n + 4 * d + 2 * n * b + n * r2 + r * n + s
+    io = 2 * L * n + 4 * v + 4 if with_io else 0
+    return g_tok + (L - 1) * g_rt + io
