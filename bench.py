@@ -196,6 +196,7 @@ def main():
     ap.add_argument("--ref-seg", type=int, default=2000, help="tokens per timed segment of the CPU reference")
     ap.add_argument("--cpu-steps", type=int, default=100, help="timed segments per core of the CPU baseline")
     ap.add_argument("--batch1-steps", type=int, default=512)
+    ap.add_argument("--prime", type=int, default=64, help="untimed steps that give every stream a history first")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -229,8 +230,13 @@ def main():
     state = model.init_state(B)
     logits = torch.empty(B, model.vocab, dtype=torch.float32, device=dev)
 
-    # realised leaf usage of the routed layers (untimed): effective number of leaves per layer
-    _, _, routes, _ = model.step_debug(d_tok[0], model.init_state(B))
+    # steady state: streams carry `prime` tokens of history before anything is timed (from a zero state the first
+    # steps route on the token alone); then the realised leaf usage of the routed layers, as the effective number
+    # of leaves per layer (exp of the entropy of the leaf histogram)
+    xp = torch.as_tensor(synth.workload_tokens(w, max(args.prime, 1), B, seed=10_000 + rank)).to(dev)
+    for i in range(args.prime):
+        model.step_into(xp[i], state, state, logits)
+    _, _, routes, _ = model.step_debug(d_tok[0], state)
     r = routes.cpu().numpy()
     eff = []
     for l in range(1, model.layers):
@@ -269,7 +275,7 @@ def main():
     ke = min(K, 256)
     h_tok = torch.as_tensor(x[W:W + ke]).pin_memory()
     h_lg = torch.empty(B, model.vocab, dtype=torch.float32).pin_memory()
-    st = model.init_state(B)
+    st = state.clone()
     for i in range(W):
         lg, st = model.step(h_tok[i % ke], st)
         h_lg.copy_(lg, non_blocking=True)
@@ -291,23 +297,34 @@ def main():
         ems = float(t.item())
     e2e = B * ke * world / (ems / 1e3)
 
-    # ---- batch 1: us/token of one stream (the reference's published unit), rank 0 only
-    b1 = None
+    # ---- batch 1, rank 0 only: (a) device time per token of one stream through the fused score kernel (state on
+    # chip, the f64 softmax/NLL of every token included, as `ygg time` includes its softmax); (b) one step() launch
+    # per token through the C-ABI from Python (launch-bound)
+    b1 = b1_step = None
     if rank == 0 and args.batch1_steps:
-        s1 = model.init_state(1)
-        t1 = d_tok[:, :1].contiguous()
-        lg1 = torch.empty(1, model.vocab, dtype=torch.float32, device=dev)
+        n1 = args.batch1_steps
+        t1 = torch.as_tensor(synth.workload_tokens(w, 1, n1 + 1, seed=99)).to(dev)
+        bits1 = torch.empty(1, dtype=torch.float64, device=dev)
         for i in range(W):
-            model.step_into(t1[i], s1, s1, lg1)
+            model.score_into(t1, None, bits1)
         torch.cuda.synchronize(dev)
         b0, b1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        n1 = min(args.batch1_steps, K + W)
         b0.record(stream)
-        for i in range(n1):
-            model.step_into(t1[i], s1, s1, lg1)
+        model.score_into(t1, None, bits1)
         b1e.record(stream)
         torch.cuda.synchronize(dev)
         b1 = b0.elapsed_time(b1e) * 1e3 / n1
+        s1 = model.init_state(1)
+        lg1 = torch.empty(1, model.vocab, dtype=torch.float32, device=dev)
+        for i in range(W):
+            model.step_into(t1[0, i:i + 1], s1, s1, lg1)
+        torch.cuda.synchronize(dev)
+        b0.record(stream)
+        for i in range(n1):
+            model.step_into(t1[0, i:i + 1], s1, s1, lg1)
+        b1e.record(stream)
+        torch.cuda.synchronize(dev)
+        b1_step = b0.elapsed_time(b1e) * 1e3 / n1
 
     bpt = synth.gathered_bytes_per_token(w.shape)
     peak, kind = peaks()
@@ -341,7 +358,8 @@ def main():
                        "model_bytes": path.stat().st_size, "bytes_per_token": bpt,
                        "tokens": "i.i.d. DNA bases p=(0.295,0.205,0.205,0.295,0.0001)" if w.tokens == "dna"
                        else "uniform bytes", "l2": "inputs larger than L2 (model file > 126 MB)",
-                       "parallelism": f"streams sharded, {world} replica(s)", "effective_leaves_per_layer": eff,
+                       "parallelism": f"streams sharded, {world} replica(s)", "primed_steps": args.prime,
+                       "effective_leaves_per_layer": eff,
                        "note": w.note},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_kind": kind},
@@ -349,6 +367,7 @@ def main():
                     "d2h_bytes_per_step": int(B * model.vocab * 4), "steps": ke},
             "gpu_launches": K,
             "batch1_us_per_token": b1,
+            "batch1_step_api_us_per_token": b1_step,
             "cpu_baseline": cpu,
             "clocks": clk.summary()}
     print(json.dumps(line))

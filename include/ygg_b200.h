@@ -50,7 +50,8 @@ typedef struct {
     int64_t file_array_bytes;   /* bytes of the file's array section */
     int64_t device_bytes;       /* bytes the handle holds on the device */
     int32_t record_bytes;       /* largest per-expert record in the device layout */
-    int32_t warps_per_block;    /* launch shape of the step kernel */
+    int32_t warps_per_block;    /* launch shape of the step kernel: warps per block ... */
+    int32_t slots_per_block;    /* ... sharing this many shared-memory leaf slots */
 } ygg_info_t;
 
 /* Parse a YGG1 file held in host memory, re-lay it out for the device and upload it to `device`.

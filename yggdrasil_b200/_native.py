@@ -23,7 +23,7 @@ class YggInfo(ctypes.Structure):
         "n_layers", "d_state", "block_size", "vocab", "router_depth", "readout_rank", "layer_input_rank",
         "router_token_dim", "input_rank", "shift", "n_experts", "vocab_pad", "factored", "group_scales")] + [
         ("file_array_bytes", ctypes.c_int64), ("device_bytes", ctypes.c_int64), ("record_bytes", ctypes.c_int32),
-        ("warps_per_block", ctypes.c_int32)]
+        ("warps_per_block", ctypes.c_int32), ("slots_per_block", ctypes.c_int32)]
 
 
 class YggError(RuntimeError):

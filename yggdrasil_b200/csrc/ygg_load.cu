@@ -16,12 +16,12 @@
 #include "ygg_model.h"
 
 namespace ygg {
-cudaError_t launch_step(int n, int blk, int r, const DevModel *dm, int B, const int32_t *tok, const int8_t *sin,
+cudaError_t launch_step(int n, int blk, int r, int r2p, const DevModel &dm, int B, const int32_t *tok, const int8_t *sin,
                         int8_t *sout, float *lg, int32_t *routes, int32_t *acc, uint32_t rec_max, int warps,
-                        int grid_cap, cudaStream_t st);
-cudaError_t launch_score(int n, int blk, int r, const DevModel *dm, int B, int T, const int32_t *tok, int8_t *state,
-                         double *bits, uint32_t rec_max, int L, int warps, int grid_cap, cudaStream_t st);
-size_t step_slot_bytes(uint32_t rec_max, int n);
+                        int slots, int grid_cap, cudaStream_t st);
+cudaError_t launch_score(int n, int blk, int r, int r2p, const DevModel &dm, int B, int T, const int32_t *tok, int8_t *state,
+                         double *bits, uint32_t rec_max, int warps, int slots, int grid_cap, cudaStream_t st);
+size_t block_smem_bytes(uint32_t rec_max, int n, int slots, int warps, int state_bytes);
 }  // namespace ygg
 
 using namespace ygg;
@@ -34,7 +34,7 @@ struct ygg_model {
     size_t d_bytes;
     int *d_status;
     uint32_t rec_max;
-    int warps_step, warps_score, grid_cap;
+    int warps_step, slots_step, warps_score, slots_score, grid_cap;
     int sm_count;
     ygg_info_t info;
 };
@@ -391,20 +391,30 @@ int ygg_load(const void *file_bytes, size_t nbytes, int device, ygg_model **out)
         return YGG_E_CUDA;
     }
     m->rec_max = rec_max;
-    // launch shape: warps per block such that a block's slots fit the opt-in shared memory
-    const size_t slot = step_slot_bytes(rec_max, n);
-    const size_t smem_cap = prop.sharedMemPerBlockOptin;
-    int warps = 8;
-    while (warps > 1 && (size_t)warps * slot > smem_cap) warps--;
-    m->warps_step = warps;
-    int ws = 8;
-    while (ws > 1 && (size_t)ws * (slot + round_up((size_t)L * n, 128)) > smem_cap) ws--;
-    m->warps_score = ws;
-    m->grid_cap = 1 << 30;
-    if (const char *e = getenv("YGG_WARPS")) {
+    // launch shape: W warps per block share S leaf slots (a warp holds a slot only from its copy to its readout);
+    // S is the most slots that still let `blocks` blocks share an SM's shared memory
+    const size_t sm_smem = prop.sharedMemPerMultiprocessor, cap = prop.sharedMemPerBlockOptin;
+    auto pick_slots = [&](int W, int blocks, int state_bytes, int *S_out) {
+        int S = W;
+        while (S > 1 && (block_smem_bytes(rec_max, n, S, W, state_bytes) + 1024) * blocks > sm_smem) S--;
+        while (S > 1 && block_smem_bytes(rec_max, n, S, W, state_bytes) > cap) S--;
+        *S_out = S;
+    };
+    int W = 8, blocks = 3;
+    if (const char *e = getenv("YGG_WARPS")) { const int v = atoi(e); if (v >= 1 && v <= 8) W = v; }
+    if (const char *e = getenv("YGG_BLOCKS_PER_SM")) { const int v = atoi(e); if (v >= 1 && v <= 8) blocks = v; }
+    m->warps_step = W;
+    pick_slots(W, blocks, 0, &m->slots_step);
+    // half the warps' worth of slots is plenty (a warp holds one for a small part of a layer) and leaves more of
+    // the SM's unified L1/shared memory to the L1 cache
+    if (m->slots_step > (W + 1) / 2) m->slots_step = (W + 1) / 2;
+    if (const char *e = getenv("YGG_SLOTS")) {
         const int v = atoi(e);
-        if (v >= 1 && v <= 8 && (size_t)v * slot <= smem_cap) m->warps_step = v;
+        if (v >= 1 && v <= W && block_smem_bytes(rec_max, n, v, W, 0) <= cap) m->slots_step = v;
     }
+    m->warps_score = W;
+    pick_slots(W, blocks, (int)round_up((size_t)L * n, 128), &m->slots_score);
+    m->grid_cap = 1 << 30;
     ygg_info_t &inf = m->info;
     memset(&inf, 0, sizeof inf);
     inf.n_layers = L; inf.d_state = n; inf.block_size = b; inf.vocab = V; inf.router_depth = D; inf.readout_rank = R;
@@ -412,6 +422,7 @@ int ygg_load(const void *file_bytes, size_t nbytes, int device, ygg_model **out)
     inf.n_experts = E; inf.vocab_pad = VP; inf.factored = any_factored; inf.group_scales = any_group;
     inf.file_array_bytes = (int64_t)avail; inf.device_bytes = (int64_t)m->d_bytes; inf.record_bytes = (int32_t)rec_max;
     inf.warps_per_block = m->warps_step;
+    inf.slots_per_block = m->slots_step;
     if (prev >= 0) cudaSetDevice(prev);
     *out = m;
     return YGG_OK;
@@ -434,9 +445,9 @@ int ygg_step_debug(const ygg_model *m, int batch, const int32_t *d_tokens, const
     if (!d_tokens || !d_state_in || !d_state_out) return YGG_E_ARG;
     int prev;
     if (set_device(m, &prev)) return YGG_E_CUDA;
-    const cudaError_t e = launch_step(m->host.n, m->host.b, m->host.R, m->d_desc, batch, d_tokens, d_state_in,
-                                      d_state_out, d_logits, d_routes, d_acc, m->rec_max, m->warps_step, m->grid_cap,
-                                      (cudaStream_t)stream);
+    const cudaError_t e = launch_step(m->host.n, m->host.b, m->host.R, m->host.R2P, m->host, batch, d_tokens, d_state_in,
+                                      d_state_out, d_logits, d_routes, d_acc, m->rec_max, m->warps_step,
+                                      m->slots_step, m->grid_cap, (cudaStream_t)stream);
     restore_device(m, prev);
     return e == cudaSuccess ? YGG_OK : YGG_E_CUDA;
 }
@@ -453,8 +464,8 @@ int ygg_score(const ygg_model *m, int batch, int steps, const int32_t *d_tokens,
     if (!d_tokens || !d_bits) return YGG_E_ARG;
     int prev;
     if (set_device(m, &prev)) return YGG_E_CUDA;
-    const cudaError_t e = launch_score(m->host.n, m->host.b, m->host.R, m->d_desc, batch, steps, d_tokens, d_state,
-                                       d_bits, m->rec_max, m->host.L, m->warps_score, m->grid_cap,
+    const cudaError_t e = launch_score(m->host.n, m->host.b, m->host.R, m->host.R2P, m->host, batch, steps, d_tokens, d_state,
+                                       d_bits, m->rec_max, m->warps_score, m->slots_score, m->grid_cap,
                                        (cudaStream_t)stream);
     restore_device(m, prev);
     return e == cudaSuccess ? YGG_OK : YGG_E_CUDA;

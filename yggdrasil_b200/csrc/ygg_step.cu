@@ -3,16 +3,19 @@
 // One warp serves one stream; lane l owns the C = n/32 state coordinates [C l, C l + C) of every layer (layout in
 // ygg_model.h). Per layer the warp
 //   1. computes rho from the new state of the layer below (exact int32 sum of squares, then the reference's f32 ops),
-//   2. descends the router: D dependent levels, each one coalesced n-byte row (lane C bytes), __dp4a and a
-//      single-instruction warp reduction (redux.sync), compared in f32 with the threshold of (token, node),
-//   3. has lane 0 issue one bulk copy (cp.async.bulk, the 1-D TMA) of the chosen expert's record, and one of its
-//      table row, into the warp's shared-memory slot, completing on the warp's mbarrier,
+//   2. descends the router LOOK = 3 levels per round of loads: the 7 rows of the 3-level subtree under the current
+//      node are fetched together (16-byte lanes, n/16 lanes per row), their dots reduced within the row's lanes and
+//      compared in f32 with the thresholds of (token, node), so D dependent levels cost ceil(D / 3) L2 round trips,
+//   3. takes a leaf slot from the block's pool (a slot is held only from the copy to the readout, a small part of a
+//      layer's time, so a block runs more warps than it has slots) and has lane 0 issue one bulk copy
+//      (cp.async.bulk, the 1-D TMA, no multicast) of the chosen expert's record and one of its table row into it,
+//      completing on the slot's mbarrier,
 //   4. meanwhile computes the layer input zl (lane k: the dot of down-projection row k with the state below),
 //   5. waits on the mbarrier (bounded: it gives up after ~1 s with an error status instead of hanging),
 //   6. runs the block-diagonal int16 x int8 transition (__dp2a), the table / factored input and the layer input in
 //      int32, saturates to the new int8 state and stores it,
-//   7. reads out z = P_r q (per-row partials + redux.sync), quantises zq, and adds f32(Q zq) * s to the logits each
-//      lane holds in registers for its classes 32 m + lane.
+//   7. reads out z = P_r q (per-row partials + redux.sync), releases the slot, quantises zq, and adds f32(Q zq) * s
+//      to the logits each lane holds in registers for its classes 32 m + lane.
 // Every f32 operation is the reference's, single-rounded and in the reference's order (__fmul_rn / __fadd_rn /
 // __fsqrt_rn / __fdiv_rn; no contraction), and f32 -> int32 rounds half to even with the x86 out-of-range value, so
 // routes, int32 accumulators, states and logits equal cpu/ygg.cpp bit for bit.
@@ -26,6 +29,8 @@ namespace ygg {
 constexpr unsigned kFull = 0xFFFFFFFFu;
 constexpr int kMaxClassesPerLane = 8;   // VP <= 256
 constexpr long long kWaitCycles = 2000000000LL;
+constexpr int kLook = 3;                // router levels per round of loads
+constexpr int kLookRows = (1 << kLook) - 1;
 
 // ------------------------------------------------------------------------------------------------ PTX helpers
 
@@ -39,14 +44,16 @@ __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
+// try_wait suspends the thread until the phase completes or the hint (ns) runs out, so a waiting warp costs few
+// issue slots
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(bar), "r"(parity)
+        : "r"(bar), "r"(parity), "r"(1000000u)
         : "memory");
     return ok != 0;
 }
@@ -57,7 +64,7 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t
                  : "memory");
 }
 
-// Bounded wait for the phase `parity` of the warp's mbarrier: false after ~1 s (the caller reports a timeout).
+// Bounded wait for the phase `parity` of an mbarrier: false after ~1 s (the caller reports a timeout).
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
@@ -73,6 +80,12 @@ __device__ __forceinline__ int cvt_rne(float v) {
 }
 __device__ __forceinline__ float i2f(int v) { return __int2float_rn(v); }
 __device__ __forceinline__ int clampi(int v, int lo, int hi) { return min(max(v, lo), hi); }
+__device__ __forceinline__ int dot16(const uint4 &a, const uint4 &b, int s) {
+    s = __dp4a((int)a.x, (int)b.x, s);
+    s = __dp4a((int)a.y, (int)b.y, s);
+    s = __dp4a((int)a.z, (int)b.z, s);
+    return __dp4a((int)a.w, (int)b.w, s);
+}
 
 // --------------------------------------------------------------------------------------------- lane state words
 
@@ -97,37 +110,55 @@ template <int C> __device__ __forceinline__ int dot_q(const LaneQ<C> &a, const L
     for (int i = 0; i < (C >= 4 ? C / 4 : 1); i++) s = __dp4a((int)a.w[i], (int)b.w[i], s);
     return s;
 }
-// byte j (< C) of the lane's state, sign-extended
-template <int C> __device__ __forceinline__ int q_byte(const LaneQ<C> &q, int j) {
-    return (int)(int8_t)(q.w[j >> 2] >> (8 * (j & 3)));
-}
 
-// ------------------------------------------------------------------------------------------------ per-warp slot
+// ------------------------------------------------------------------------------------------------ shared memory
 
-struct Slot {
-    uint8_t *rec;      // the expert record (bulk copy destination)
-    int16_t *trow;     // the table row (bulk copy destination)
-    int8_t *qold;      // this layer's old state, for the transition's block reads
-    int8_t *qb;        // the new state of the layer below, for the layer-input dots
-    int8_t *zl;        // layer input codes [R2P]
-    int8_t *zq;        // readout codes [R]
-    uint32_t bar;      // mbarrier (shared address)
+// Block layout: [S slots][S mbarriers][S owners][S phases] pad 128, then [W warp scratch][W states (score only)].
+// A slot holds one expert record and one table row; the warp scratch holds the old state of the current layer, the
+// new state of the layer below, the layer-input codes and the readout codes.
+struct Pool {
+    uint8_t *slots;
+    uint32_t slot_bytes;
+    uint32_t bars;     // shared address of mbarrier 0
+    int *owner;        // -1 free, else the owning warp
+    int *phase;        // parity of the slot's mbarrier to wait for next
+    int S;
+};
+struct Scratch {
+    int8_t *qold, *qb, *zl, *zq;
 };
 
-__device__ __forceinline__ Slot make_slot(uint8_t *base, uint32_t rec_max, int n) {
-    Slot s;
-    s.rec = base;
-    s.trow = (int16_t *)(base + rec_max);
-    s.qold = (int8_t *)(base + rec_max + 2 * n);
-    s.qb = s.qold + n;
-    s.zl = s.qb + n;
-    s.zq = s.zl + 64;
-    s.bar = smem_addr(s.zq + 32);
-    return s;
+__host__ __device__ constexpr uint32_t pool_slot_bytes(uint32_t rec_max, int n) { return (rec_max + 2 * n + 127) / 128 * 128; }
+__host__ __device__ constexpr uint32_t pool_meta_bytes(int S) { return (16u * S + 127) / 128 * 128; }
+__host__ __device__ constexpr uint32_t scratch_bytes(int n) { return (2 * n + 64 + 32 + 127) / 128 * 128; }
+__host__ __device__ constexpr uint32_t block_smem(uint32_t rec_max, int n, int S, int W, int state_bytes) {
+    return S * pool_slot_bytes(rec_max, n) + pool_meta_bytes(S) + W * (scratch_bytes(n) + state_bytes);
 }
-// bytes of a slot: record, table row, qold, qb, zl, zq, mbarrier
-__host__ __device__ constexpr uint32_t slot_bytes(uint32_t rec_max, int n) {
-    return (rec_max + 2 * n + n + n + 64 + 32 + 8 + 127) / 128 * 128;
+
+// Take a free slot (lane 0 claims it with a CAS; the others learn it by shuffle). -1 after ~1 s without one.
+__device__ __forceinline__ int slot_acquire(const Pool &p, int warp, int lane) {
+    int got = -1;
+    if (lane == 0) {
+        const long long t0 = clock64();
+        int i = warp % p.S;
+        while (true) {
+            if (atomicCAS(p.owner + i, -1, warp) == -1) { got = i; break; }
+            if (++i == p.S) {
+                i = 0;
+                if (clock64() - t0 > kWaitCycles) break;
+                __nanosleep(32);
+            }
+        }
+        __threadfence_block();
+    }
+    return __shfl_sync(kFull, got, 0);
+}
+__device__ __forceinline__ void slot_release(const Pool &p, int slot, int lane) {
+    __syncwarp();
+    if (lane == 0) {
+        __threadfence_block();
+        atomicExch(p.owner + slot, -1);
+    }
 }
 
 // Lane-interleaved part: the lane's 16-byte chunk j.
@@ -140,7 +171,7 @@ __device__ __forceinline__ uint4 lane_chunk(const uint8_t *part, int j, int lane
 // rho = 1 / sqrt(f32(sum q^2) * (1/n) + eps), or with group scales the sequential f32 sum over groups of 16 of
 // r2[g] * f32(S_g) (cpu/ygg.cpp:248-266).
 template <int N>
-__device__ __forceinline__ float rms_rho(const LaneQ<N / 32> &qb, const float *r2b, float eps, int lane) {
+__device__ __forceinline__ float rms_rho(const LaneQ<N / 32> &qb, const float *r2b, float eps) {
     constexpr int C = N / 32;
     const float inv_n = 1.0f / (float)N;
     int part = dot_q<C>(qb, qb);
@@ -160,21 +191,86 @@ __device__ __forceinline__ float rms_rho(const LaneQ<N / 32> &qb, const float *r
     return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(s, inv_n), eps)));
 }
 
-// Heap-order descent from node 1: right iff f32(w_ix . qb) * rho > thr[x][ix] (cpu/ygg.cpp:271-280).
+// Heap-order descent from node 1, right iff f32(w_ix . qb) * rho > thr[x][ix] (cpu/ygg.cpp:271-280), kLook levels
+// per round of loads. Row k of a round's subtree (k = 0: ix; 1-2: 2ix + k-1; 3-6: 4ix + k-3, i.e. ix * 2^lvl(k) +
+// k + 1 - 2^lvl(k)) is read by the LPR = n/16 lanes of group k % RPI in load k / RPI, 16 bytes each; every lane of
+// the group also reads the row's threshold (one broadcast transaction), so each lane can decide its group's row and
+// one ballot per load carries every decision. qrow: the lane's 16 bytes of qb at 16 (lane % LPR). Returns the leaf
+// node index in [E, 2E).
 template <int N>
-__device__ __forceinline__ int route(const int8_t *__restrict__ w, const float *__restrict__ thr_x, int depth,
-                                     const LaneQ<N / 32> &qb, float rho, int lane) {
-    constexpr int C = N / 32;
+__device__ __forceinline__ int route_look(const int8_t *__restrict__ w, const float *__restrict__ thr_x, int depth,
+                                          const uint4 &qrow, float rho, int lane) {
+    constexpr int LPR = N / 16;                 // lanes per row
+    constexpr int RPI = 32 / LPR;               // rows per warp-wide 16-byte load
+    constexpr int NI = (kLookRows + RPI - 1) / RPI;
+    const int g = lane / LPR;
+    const int8_t *wl = w + 16 * (lane % LPR);
+    // per-lane constants of the subtree rows this lane reads: row = ix * mul + add
+    int mul[NI], add[NI], kk[NI];
+#pragma unroll
+    for (int i = 0; i < NI; i++) {
+        const int k = i * RPI + g;
+        const int lvl = k == 0 ? 0 : k < 3 ? 1 : 2;
+        kk[i] = k;
+        mul[i] = 1 << lvl;
+        add[i] = k + 1 - (1 << lvl);
+    }
     int ix = 1;
-    for (int d = 0; d < depth; d++) {
-        LaneQ<C> wr;
-        const int8_t *row = w + (size_t)ix * N + C * lane;
-        if constexpr (C == 2) wr.w[0] = __ldg((const unsigned short *)row);
-        else if constexpr (C == 4) wr.w[0] = __ldg((const unsigned int *)row);
-        else { const uint2 v = __ldg((const uint2 *)row); wr.w[0] = v.x; wr.w[1] = v.y; }
-        const float t = __ldg(thr_x + ix);
-        const int dot = __reduce_add_sync(kFull, dot_q<C>(wr, qb));
-        ix = 2 * ix + (__fmul_rn(i2f(dot), rho) > t ? 1 : 0);
+    for (int d = 0; d < depth; d += kLook) {
+        const int lv = min(kLook, depth - d);
+        const int nrows = (1 << lv) - 1;
+        uint4 v[NI];
+        float t[NI];
+#pragma unroll
+        for (int i = 0; i < NI; i++) {
+            const int row = ix * mul[i] + add[i];
+            v[i] = make_uint4(0, 0, 0, 0);
+            t[i] = 0.0f;
+            if (kk[i] < nrows) {
+                v[i] = __ldg((const uint4 *)(wl + (size_t)row * N));
+                t[i] = __ldg(thr_x + row);
+            }
+        }
+        // decisions of rows k = RPI i + g, as bit LPR (RPI i + g) of a 64-bit word (each group's LPR lanes agree)
+        uint64_t bits = 0;
+        constexpr int kFirst = LPR == 16 ? 2 : NI;      // loads whose ballots go into `bits` directly
+#pragma unroll
+        for (int i = 0; i < kFirst; i++) {
+            int dot = dot16(v[i], qrow, 0);
+#pragma unroll
+            for (int off = 1; off < LPR; off <<= 1) dot += __shfl_xor_sync(kFull, dot, off);
+            const uint32_t bal = __ballot_sync(kFull, __fmul_rn(i2f(dot), rho) > t[i]);
+            if constexpr (LPR >= 8) {
+                bits |= (uint64_t)bal << (32 * i);      // row k at bit 8 k (N = 128) or 16 k (N = 256, i < 2)
+            } else {
+                bits |= bal;                            // N = 64: one load, row k at bit 4 k
+            }
+        }
+        if constexpr (LPR == 16) {                      // N = 256: rows 4-6 sit in loads 2-3; fold them in
+            uint32_t hi = 0;
+#pragma unroll
+            for (int i = 2; i < NI; i++) {
+                int dot = dot16(v[i], qrow, 0);
+#pragma unroll
+                for (int off = 1; off < LPR; off <<= 1) dot += __shfl_xor_sync(kFull, dot, off);
+                const uint32_t bal = __ballot_sync(kFull, __fmul_rn(i2f(dot), rho) > t[i]);
+                hi |= ((bal & 1u) | ((bal >> 15) & 2u)) << (2 * (i - 2));
+            }
+            // rows 0-3 from loads 0-1 at bits 0, 16, 32, 48 -> compact to bits 0-3, then rows 4-6
+            const uint32_t lo = (uint32_t)(bits & 1u) | (uint32_t)((bits >> 15) & 2u) | (uint32_t)((bits >> 30) & 4u) |
+                                (uint32_t)((bits >> 45) & 8u);
+            bits = lo | (hi << 4);
+        }
+        constexpr int kStride = LPR == 16 ? 1 : LPR;   // bit distance between consecutive rows in `bits`
+        int k = 0;
+#pragma unroll
+        for (int j = 0; j < kLook; j++) {
+            if (j < lv) {
+                const int b = (int)((bits >> (kStride * k)) & 1u);
+                ix = 2 * ix + b;
+                k = 2 * k + 1 + b;
+            }
+        }
     }
     return ix;
 }
@@ -187,65 +283,67 @@ struct StepOut {
 
 // One token of one stream through every layer. q_in / q_out: the stream's state [L][n] (global or shared memory;
 // they may alias). lg: the logits of the lane's classes (out). Returns false if a bounded wait gave up.
-template <int N, int BLK, int R>
-__device__ __forceinline__ bool token_step(const DevModel *__restrict__ mp, const Slot &sl, uint32_t &phase, int x,
+template <int N, int BLK, int R, int R2T>
+__device__ __forceinline__ bool token_step(const DevModel &m, const Pool &pool, const Scratch &sc, int warp, int x,
                                            const int8_t *q_in, int8_t *q_out, float (&lg)[kMaxClassesPerLane],
                                            const StepOut &dbg, int lane) {
     constexpr int C = N / 32;
-    const int L = mp->L, VP = mp->VP, E = mp->E, D = mp->D, V = mp->V;
+    const int L = m.L, VP = m.VP, E = m.E, D = m.D, V = m.V;
     const int nv = VP / 32;
 #pragma unroll
-    for (int m = 0; m < kMaxClassesPerLane; m++) lg[m] = m < nv ? __ldg(mp->head_b + 32 * m + lane) : 0.0f;
+    for (int c = 0; c < kMaxClassesPerLane; c++) lg[c] = c < nv ? __ldg(m.head_b + 32 * c + lane) : 0.0f;
 
     LaneQ<C> qbelow{};
     for (int l = 0; l < L; l++) {
-        const DevLayer &y = mp->layer[l];
+        const DevLayer &y = m.layer[l];
         const LaneQ<C> qold = load_q<C>(q_in + (size_t)l * N + C * lane);
         int r = x;
         float rho = 0.0f;
+        const bool low = l > 0 && m.R2 > 0;
         if (l > 0) {
-            rho = rms_rho<N>(qbelow, y.r2b, y.rms_eps, lane);
-            r = route<N>(y.w, y.thr + (size_t)x * E, D, qbelow, rho, lane) - E;
+            rho = rms_rho<N>(qbelow, y.r2b, y.rms_eps);
+            store_q<C>(sc.qb + C * lane, qbelow);
+            __syncwarp();
+            const uint4 qrow = *(const uint4 *)(sc.qb + 16 * (lane % (N / 16)));
+            r = route_look<N>(y.w, y.thr + (size_t)x * E, D, qrow, rho, lane) - E;
         }
-        // -- the expert record and its table row into the slot (previous readers of the slot are done)
+        // -- a slot, and the expert record and its table row into it
+        const int slot = slot_acquire(pool, warp, lane);
+        if (slot < 0) return false;
+        uint8_t *rec = pool.slots + (size_t)slot * pool.slot_bytes;
+        const int16_t *trow = (const int16_t *)(rec + (pool.slot_bytes - 2 * N));
+        const uint32_t bar = pool.bars + 8u * slot;
         const uint32_t rec_bytes = y.rec_bytes;
         const bool has_table = y.table != nullptr;
-        __syncwarp();
         if (lane == 0) {
             fence_proxy_async();
-            mbar_expect_tx(sl.bar, rec_bytes + (has_table ? 2u * N : 0u));
-            bulk_g2s(smem_addr(sl.rec), y.rec + (size_t)r * rec_bytes, rec_bytes, sl.bar);
+            mbar_expect_tx(bar, rec_bytes + (has_table ? 2u * N : 0u));
+            bulk_g2s(smem_addr(rec), y.rec + (size_t)r * rec_bytes, rec_bytes, bar);
             if (has_table) {
-                const int16_t *trow = y.table + ((size_t)r * y.table_rows + (y.table_rows > 1 ? x : 0)) * N;
-                bulk_g2s(smem_addr(sl.trow), trow, 2u * N, sl.bar);
+                const int16_t *src = y.table + ((size_t)r * y.table_rows + (y.table_rows > 1 ? x : 0)) * N;
+                bulk_g2s(smem_addr(trow), src, 2u * N, bar);
             }
         }
         // -- layer input codes while the copy is in flight (cpu/ygg.cpp:285-296)
-        const bool low = l > 0 && mp->R2 > 0;
         if (low) {
-            store_q<C>(sl.qb + C * lane, qbelow);
-            __syncwarp();
-            const int R2P = mp->R2P;
+            const int R2P = R2T ? R2T : m.R2P;
             for (int k = lane; k < R2P; k += 32) {
                 int a = 0;
 #pragma unroll 4
                 for (int j = 0; j < N / 16; j++) {
                     const uint4 v = __ldg((const uint4 *)(y.vl + ((size_t)j * R2P + k) * 16));
-                    const uint4 q = *(const uint4 *)(sl.qb + 16 * j);
-                    a = __dp4a((int)v.x, (int)q.x, a);
-                    a = __dp4a((int)v.y, (int)q.y, a);
-                    a = __dp4a((int)v.z, (int)q.z, a);
-                    a = __dp4a((int)v.w, (int)q.w, a);
+                    a = dot16(v, *(const uint4 *)(sc.qb + 16 * j), a);
                 }
                 const float zf = __fmul_rn(__fmul_rn(i2f(a), __ldg(y.mv + k)), rho);
-                sl.zl[k] = (int8_t)(k < mp->R2 ? clampi(cvt_rne(zf), -127, 127) : 0);
+                sc.zl[k] = (int8_t)(k < m.R2 ? clampi(cvt_rne(zf), -127, 127) : 0);
             }
         }
-        store_q<C>(sl.qold + C * lane, qold);
+        store_q<C>(sc.qold + C * lane, qold);
         __syncwarp();
-        const bool ok = __all_sync(kFull, mbar_wait_bounded(sl.bar, phase));
-        phase ^= 1u;
+        const uint32_t parity = (uint32_t)pool.phase[slot];
+        const bool ok = __all_sync(kFull, mbar_wait_bounded(bar, parity));
         if (!ok) return false;
+        if (lane == 0) pool.phase[slot] = (int)(parity ^ 1u);
 
         // -- transition: acc_i = (sum_j A16[i][j] q[j] + 2^(shift-1)) >> shift over the row's block (cpu/ygg.cpp:312-332)
         int acc[C];
@@ -253,21 +351,21 @@ __device__ __forceinline__ bool token_step(const DevModel *__restrict__ mp, cons
             const int blk0 = ((C * lane) / BLK) * BLK;
             uint32_t qblk[BLK / 4];
             if constexpr (BLK == 8) {
-                const uint2 v = *(const uint2 *)(sl.qold + blk0);
+                const uint2 v = *(const uint2 *)(sc.qold + blk0);
                 qblk[0] = v.x; qblk[1] = v.y;
             } else {
-                const uint4 v = *(const uint4 *)(sl.qold + blk0);
+                const uint4 v = *(const uint4 *)(sc.qold + blk0);
                 qblk[0] = v.x; qblk[1] = v.y; qblk[2] = v.z; qblk[3] = v.w;
             }
             constexpr int kWords = C * BLK / 2;            // int16 pairs of the lane
             uint32_t aw[kWords];
-            const uint8_t *pa = sl.rec + y.off_a;
+            const uint8_t *pa = rec + y.off_a;
 #pragma unroll
             for (int j = 0; j < kWords / 4; j++) {
                 const uint4 v = lane_chunk(pa, j, lane);
                 aw[4 * j] = v.x; aw[4 * j + 1] = v.y; aw[4 * j + 2] = v.z; aw[4 * j + 3] = v.w;
             }
-            const int rnd = 1 << (mp->shift - 1), sh = mp->shift;
+            const int rnd = 1 << (m.shift - 1), sh = m.shift;
 #pragma unroll
             for (int ii = 0; ii < C; ii++) {
                 int s = 0;
@@ -282,43 +380,31 @@ __device__ __forceinline__ bool token_step(const DevModel *__restrict__ mp, cons
         // -- input: table row (cpu/ygg.cpp:334-337) or factored (cpu/ygg.cpp:339-358)
         if (has_table) {
 #pragma unroll
-            for (int ii = 0; ii < C; ii++) acc[ii] += sl.trow[C * lane + ii];
+            for (int ii = 0; ii < C; ii++) acc[ii] += trow[C * lane + ii];
         } else {
-            const int KP = mp->KP;
-            const uint8_t *pf = sl.rec + y.off_f;
+            const int KP = m.KP;
+            const uint8_t *pf = rec + y.off_f;
             const int8_t *v = y.vt + (size_t)x * KP;
-            const float su = *(const float *)(sl.rec + y.off_su);
-            const int16_t *cb = (const int16_t *)(sl.rec + y.off_cb);
+            const float su = *(const float *)(rec + y.off_su);
+            const int16_t *cb = (const int16_t *)(rec + y.off_cb);
 #pragma unroll
             for (int ii = 0; ii < C; ii++) {
                 int lt = 0;
-                for (int j = 0; j < KP / 16; j++) {
-                    const uint4 u = lane_chunk(pf, ii * (KP / 16) + j, lane);
-                    const uint4 t = __ldg((const uint4 *)(v + 16 * j));
-                    lt = __dp4a((int)u.x, (int)t.x, lt);
-                    lt = __dp4a((int)u.y, (int)t.y, lt);
-                    lt = __dp4a((int)u.z, (int)t.z, lt);
-                    lt = __dp4a((int)u.w, (int)t.w, lt);
-                }
+                for (int j = 0; j < KP / 16; j++)
+                    lt = dot16(lane_chunk(pf, ii * (KP / 16) + j, lane), __ldg((const uint4 *)(v + 16 * j)), lt);
                 const float mul = __fmul_rn(su, __ldg(y.mt + C * lane + ii));
                 acc[ii] += cvt_rne(__fmul_rn(i2f(lt), mul)) + cb[C * lane + ii];
             }
         }
         // -- layer input: acc_i += rint(f32(U'_r zl) m_ul) (cpu/ygg.cpp:360-377)
         if (low) {
-            const int R2P = mp->R2P;
-            const uint8_t *pu = sl.rec + y.off_u;
+            const int R2P = R2T ? R2T : m.R2P;
+            const uint8_t *pu = rec + y.off_u;
 #pragma unroll
             for (int ii = 0; ii < C; ii++) {
                 int la = 0;
-                for (int j = 0; j < R2P / 16; j++) {
-                    const uint4 u = lane_chunk(pu, ii * (R2P / 16) + j, lane);
-                    const uint4 z = *(const uint4 *)(sl.zl + 16 * j);
-                    la = __dp4a((int)u.x, (int)z.x, la);
-                    la = __dp4a((int)u.y, (int)z.y, la);
-                    la = __dp4a((int)u.z, (int)z.z, la);
-                    la = __dp4a((int)u.w, (int)z.w, la);
-                }
+                for (int j = 0; j < R2P / 16; j++)
+                    la = dot16(lane_chunk(pu, ii * (R2P / 16) + j, lane), *(const uint4 *)(sc.zl + 16 * j), la);
                 const float mu = y.mulv ? __ldg(y.mulv + C * lane + ii) : y.layer_input_scale;
                 acc[ii] += cvt_rne(__fmul_rn(i2f(la), mu));
             }
@@ -339,8 +425,9 @@ __device__ __forceinline__ bool token_step(const DevModel *__restrict__ mp, cons
 
         // -- readout z = P_r q, zq = sat(rint(f32(z) m_z)) (cpu/ygg.cpp:395-420)
         int myz = 0;
+        float mz = y.readout_scale;
         {
-            const uint8_t *pp = sl.rec + y.off_p;
+            const uint8_t *pp = rec + y.off_p;
             constexpr int kPWords = R * C / 4;
             uint32_t pw[kPWords];
 #pragma unroll
@@ -348,6 +435,7 @@ __device__ __forceinline__ bool token_step(const DevModel *__restrict__ mp, cons
                 const uint4 v = lane_chunk(pp, j, lane);
                 pw[4 * j] = v.x; pw[4 * j + 1] = v.y; pw[4 * j + 2] = v.z; pw[4 * j + 3] = v.w;
             }
+            if (y.off_mz != kNone && lane < R) mz = *(const float *)(rec + y.off_mz + 4 * lane);
 #pragma unroll
             for (int rr = 0; rr < R; rr++) {
                 int part;
@@ -363,49 +451,43 @@ __device__ __forceinline__ bool token_step(const DevModel *__restrict__ mp, cons
                 if (lane == rr) myz = z;
             }
         }
-        if (lane < R) {
-            const float mz = mp->has_mz && y.off_mz != kNone ? *(const float *)(sl.rec + y.off_mz + 4 * lane)
-                                                             : y.readout_scale;
-            sl.zq[lane] = (int8_t)clampi(cvt_rne(__fmul_rn(i2f(myz), mz)), -127, 127);
-        }
+        slot_release(pool, slot, lane);
+        if (lane < R) sc.zq[lane] = (int8_t)clampi(cvt_rne(__fmul_rn(i2f(myz), mz)), -127, 127);
         __syncwarp();
         // -- head: lg[c] += f32(Q_c . zq) * s (cpu/ygg.cpp:421-434)
         {
             uint32_t zw[R / 4];
 #pragma unroll
-            for (int j = 0; j < R / 4; j++) zw[j] = *(const uint32_t *)(sl.zq + 4 * j);
+            for (int j = 0; j < R / 4; j++) zw[j] = *(const uint32_t *)(sc.zq + 4 * j);
 #pragma unroll
-            for (int m = 0; m < kMaxClassesPerLane; m++) {
-                if (m < nv) {
-                    const int c = 32 * m + lane;
-                    const int8_t *qrow = y.unembed + (size_t)c * R;
+            for (int c = 0; c < kMaxClassesPerLane; c++) {
+                if (c < nv) {
+                    const int cls = 32 * c + lane;
+                    const int8_t *qrow = y.unembed + (size_t)cls * R;
                     int a = 0;
+                    if constexpr (R == 8) {
+                        const uint2 v = __ldg((const uint2 *)qrow);
+                        a = __dp4a((int)v.x, (int)zw[0], a);
+                        a = __dp4a((int)v.y, (int)zw[1], a);
+                    } else {
 #pragma unroll
-                    for (int j = 0; j < R / 16 + (R % 16 ? 1 : 0); j++) {
-                        if constexpr (R == 8) {
-                            const uint2 v = __ldg((const uint2 *)qrow);
-                            a = __dp4a((int)v.x, (int)zw[0], a);
-                            a = __dp4a((int)v.y, (int)zw[1], a);
-                        } else {
-                            const uint4 v = __ldg((const uint4 *)(qrow + 16 * j));
-                            a = __dp4a((int)v.x, (int)zw[4 * j], a);
-                            a = __dp4a((int)v.y, (int)zw[4 * j + 1], a);
-                            a = __dp4a((int)v.z, (int)zw[4 * j + 2], a);
-                            a = __dp4a((int)v.w, (int)zw[4 * j + 3], a);
-                        }
+                        for (int j = 0; j < R / 16; j++)
+                            a = dot16(__ldg((const uint4 *)(qrow + 16 * j)),
+                                      make_uint4(zw[4 * j], zw[4 * j + 1], zw[4 * j + 2], zw[4 * j + 3]), a);
                     }
-                    const float s = y.sqv ? __ldg(y.sqv + c) : y.unembed_scale;
-                    lg[m] = __fadd_rn(lg[m], __fmul_rn(i2f(a), s));
+                    const float s = y.sqv ? __ldg(y.sqv + cls) : y.unembed_scale;
+                    lg[c] = __fadd_rn(lg[c], __fmul_rn(i2f(a), s));
                 }
             }
         }
         qbelow = qn;
+        __syncwarp();
     }
     if (dbg.logits != nullptr) {
 #pragma unroll
-        for (int m = 0; m < kMaxClassesPerLane; m++) {
-            const int c = 32 * m + lane;
-            if (m < nv && c < V) dbg.logits[c] = lg[m];
+        for (int c = 0; c < kMaxClassesPerLane; c++) {
+            const int cls = 32 * c + lane;
+            if (c < nv && cls < V) dbg.logits[cls] = lg[c];
         }
     }
     return true;
@@ -413,30 +495,50 @@ __device__ __forceinline__ bool token_step(const DevModel *__restrict__ mp, cons
 
 // ------------------------------------------------------------------------------------------------ kernels
 
-__device__ __forceinline__ void slot_init(const Slot &sl, int lane) {
-    if (lane == 0) {
-        mbar_init(sl.bar, 1);
+// Pool and scratch of this block; the first warp initialises the slots' mbarriers and owners.
+__device__ __forceinline__ void block_init(uint8_t *smem, uint32_t rec_max, int n, int S, int state_bytes, int warp,
+                                           int lane, Pool &pool, Scratch &sc, int8_t *&state) {
+    pool.slot_bytes = pool_slot_bytes(rec_max, n);
+    pool.slots = smem;
+    uint8_t *meta = smem + (size_t)S * pool.slot_bytes;
+    pool.bars = smem_addr(meta);
+    pool.owner = (int *)(meta + 8 * S);
+    pool.phase = (int *)(meta + 12 * S);
+    pool.S = S;
+    uint8_t *ws = meta + pool_meta_bytes(S) + (size_t)warp * (scratch_bytes(n) + state_bytes);
+    sc.qold = (int8_t *)ws;
+    sc.qb = sc.qold + n;
+    sc.zl = sc.qb + n;
+    sc.zq = sc.zl + 64;
+    state = (int8_t *)(ws + scratch_bytes(n));
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; i++) {
+            mbar_init(pool.bars + 8u * i, 1);
+            pool.owner[i] = -1;
+            pool.phase[i] = 0;
+        }
         fence_mbar_init();
     }
-    __syncwarp();
+    __syncthreads();
 }
 
-template <int N, int BLK, int R>
-__global__ void __launch_bounds__(256) step_kernel(const DevModel *__restrict__ mp, int B,
+template <int N, int BLK, int R, int R2T>
+__global__ void __launch_bounds__(256, 3) step_kernel(const __grid_constant__ DevModel m, int B,
                                                    const int32_t *__restrict__ tokens, const int8_t *state_in,
                                                    int8_t *state_out, float *__restrict__ logits,
                                                    int32_t *__restrict__ routes, int32_t *__restrict__ acc_out,
-                                                   uint32_t rec_max) {
+                                                   uint32_t rec_max, int S) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = blockDim.x >> 5;
-    const Slot sl = make_slot(smem + (size_t)warp * slot_bytes(rec_max, N), rec_max, N);
-    slot_init(sl, lane);
-    uint32_t phase = 0;
-    const int L = mp->L, V = mp->V;
+    Pool pool;
+    Scratch sc;
+    int8_t *unused;
+    block_init(smem, rec_max, N, S, 0, warp, lane, pool, sc, unused);
+    const int L = m.L, V = m.V;
     for (int s = blockIdx.x * W + warp; s < B; s += gridDim.x * W) {
         const int x = tokens[s];
         if (x < 0 || x >= V) {   // cpu/ygg.cpp:493-495 rejects the whole input; here the stream is skipped
-            if (lane == 0) atomicOr(mp->status, kStatusBadToken);
+            if (lane == 0) atomicOr(m.status, kStatusBadToken);
             if (logits != nullptr)
                 for (int c = lane; c < V; c += 32) logits[(size_t)s * V + c] = __int_as_float(0x7fc00000);
             if (state_out != state_in)
@@ -447,9 +549,9 @@ __global__ void __launch_bounds__(256) step_kernel(const DevModel *__restrict__ 
         float lg[kMaxClassesPerLane];
         StepOut o{logits ? logits + (size_t)s * V : nullptr, routes ? routes + (size_t)s * L : nullptr,
                   acc_out ? acc_out + (size_t)s * L * N : nullptr};
-        if (!token_step<N, BLK, R>(mp, sl, phase, x, state_in + (size_t)s * L * N, state_out + (size_t)s * L * N,
+        if (!token_step<N, BLK, R, R2T>(m, pool, sc, warp, x, state_in + (size_t)s * L * N, state_out + (size_t)s * L * N,
                                    lg, o, lane)) {
-            if (lane == 0) atomicOr(mp->status, kStatusTimeout);
+            if (lane == 0) atomicOr(m.status, kStatusTimeout);
             return;
         }
     }
@@ -457,26 +559,24 @@ __global__ void __launch_bounds__(256) step_kernel(const DevModel *__restrict__ 
 
 // Rows of `steps` tokens; the state of a row lives in the warp's shared memory between tokens, the logits in
 // registers, and the f64 NLL of the next token is summed on chip (cpu/ygg.cpp:513-517).
-template <int N, int BLK, int R>
-__global__ void __launch_bounds__(256) score_kernel(const DevModel *__restrict__ mp, int B, int T,
+template <int N, int BLK, int R, int R2T>
+__global__ void __launch_bounds__(256, 3) score_kernel(const __grid_constant__ DevModel m, int B, int T,
                                                     const int32_t *__restrict__ tokens, int8_t *state,
-                                                    double *__restrict__ bits, uint32_t rec_max) {
+                                                    double *__restrict__ bits, uint32_t rec_max, int S) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = blockDim.x >> 5;
-    const int L = mp->L, V = mp->V, nv = mp->VP / 32;
-    const uint32_t sb = slot_bytes(rec_max, N) + (uint32_t)((L * N + 127) / 128 * 128);
-    uint8_t *base = smem + (size_t)warp * sb;
-    const Slot sl = make_slot(base, rec_max, N);
-    int8_t *qs = (int8_t *)(base + slot_bytes(rec_max, N));
-    slot_init(sl, lane);
-    uint32_t phase = 0;
+    const int L = m.L, V = m.V, nv = m.VP / 32;
+    Pool pool;
+    Scratch sc;
+    int8_t *qs;
+    block_init(smem, rec_max, N, S, (L * N + 127) / 128 * 128, warp, lane, pool, sc, qs);
     const StepOut none{nullptr, nullptr, nullptr};
     for (int s = blockIdx.x * W + warp; s < B; s += gridDim.x * W) {
         const int32_t *tok = tokens + (size_t)s * T;
         bool bad = false;
         for (int t = lane; t < T; t += 32) bad |= tok[t] < 0 || tok[t] >= V;
         if (__any_sync(kFull, bad)) {
-            if (lane == 0) { atomicOr(mp->status, kStatusBadToken); bits[s] = __longlong_as_double(0x7ff8000000000000LL); }
+            if (lane == 0) { atomicOr(m.status, kStatusBadToken); bits[s] = __longlong_as_double(0x7ff8000000000000LL); }
             continue;
         }
         for (int i = lane; i < L * N; i += 32) qs[i] = state ? state[(size_t)s * L * N + i] : 0;
@@ -484,28 +584,28 @@ __global__ void __launch_bounds__(256) score_kernel(const DevModel *__restrict__
         double nll = 0.0;
         for (int t = 0; t + 1 < T; t++) {
             float lg[kMaxClassesPerLane];
-            if (!token_step<N, BLK, R>(mp, sl, phase, tok[t], qs, qs, lg, none, lane)) {
-                if (lane == 0) atomicOr(mp->status, kStatusTimeout);
+            if (!token_step<N, BLK, R, R2T>(m, pool, sc, warp, tok[t], qs, qs, lg, none, lane)) {
+                if (lane == 0) atomicOr(m.status, kStatusTimeout);
                 return;
             }
             // -log p(next) in f64: max, sum of exp over the V classes, the target's logit
             float mx = -__int_as_float(0x7f800000);
 #pragma unroll
-            for (int m = 0; m < kMaxClassesPerLane; m++)
-                if (m < nv && 32 * m + lane < V) mx = fmaxf(mx, lg[m]);
+            for (int c = 0; c < kMaxClassesPerLane; c++)
+                if (c < nv && 32 * c + lane < V) mx = fmaxf(mx, lg[c]);
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, off));
             double se = 0.0;
 #pragma unroll
-            for (int m = 0; m < kMaxClassesPerLane; m++)
-                if (m < nv && 32 * m + lane < V) se += exp((double)lg[m] - (double)mx);
+            for (int c = 0; c < kMaxClassesPerLane; c++)
+                if (c < nv && 32 * c + lane < V) se += exp((double)lg[c] - (double)mx);
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) se += __shfl_xor_sync(kFull, se, off);
             const int y = tok[t + 1];
             float ly = 0.0f;
 #pragma unroll
-            for (int m = 0; m < kMaxClassesPerLane; m++)
-                if (m == (y >> 5)) ly = lg[m];
+            for (int c = 0; c < kMaxClassesPerLane; c++)
+                if (c == (y >> 5)) ly = lg[c];
             ly = __shfl_sync(kFull, ly, y & 31);
             nll += log(se) + (double)mx - (double)ly;
         }
@@ -519,71 +619,86 @@ __global__ void __launch_bounds__(256) score_kernel(const DevModel *__restrict__
 
 // ------------------------------------------------------------------------------------------------ launchers
 
-struct LaunchShape {
-    int grid, block;
-    size_t smem;
-};
+// The dynamic shared-memory limit of a kernel, raised once per device to the largest size asked for so far (the
+// attribute is per device; raising it on every launch would cost a driver call per step).
+constexpr int kMaxDevices = 64;
+struct SmemLimits { size_t set[kMaxDevices]; };
+template <int N, int BLK, int R, int R2T> static SmemLimits &step_limit() { static SmemLimits l{}; return l; }
+template <int N, int BLK, int R, int R2T> static SmemLimits &score_limit() { static SmemLimits l{}; return l; }
+static cudaError_t raise_smem_limit(const void *fn, size_t smem, SmemLimits &lim) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < kMaxDevices && lim.set[dev] >= smem) return cudaSuccess;
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess && dev >= 0 && dev < kMaxDevices) lim.set[dev] = smem;
+    return e;
+}
 
-template <int N, int BLK, int R>
-static cudaError_t launch_step_t(const DevModel *dm, int B, const int32_t *tok, const int8_t *sin, int8_t *sout,
-                                 float *lg, int32_t *routes, int32_t *acc, uint32_t rec_max, int warps, int grid_cap,
-                                 cudaStream_t st) {
-    const size_t smem = (size_t)warps * slot_bytes(rec_max, N);
-    cudaError_t e = cudaFuncSetAttribute(step_kernel<N, BLK, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+template <int N, int BLK, int R, int R2T>
+static cudaError_t launch_step_t(const DevModel &dm, int B, const int32_t *tok, const int8_t *sin, int8_t *sout,
+                                 float *lg, int32_t *routes, int32_t *acc, uint32_t rec_max, int warps, int slots,
+                                 int grid_cap, cudaStream_t st) {
+    const size_t smem = block_smem(rec_max, N, slots, warps, 0);
+    cudaError_t e = raise_smem_limit((const void *)step_kernel<N, BLK, R, R2T>, smem, step_limit<N, BLK, R, R2T>());
     if (e != cudaSuccess) return e;
     int grid = (B + warps - 1) / warps;
     if (grid > grid_cap) grid = grid_cap;
-    step_kernel<N, BLK, R><<<grid, 32 * warps, smem, st>>>(dm, B, tok, sin, sout, lg, routes, acc, rec_max);
+    step_kernel<N, BLK, R, R2T><<<grid, 32 * warps, smem, st>>>(dm, B, tok, sin, sout, lg, routes, acc, rec_max, slots);
     return cudaGetLastError();
 }
 
-template <int N, int BLK, int R>
-static cudaError_t launch_score_t(const DevModel *dm, int B, int T, const int32_t *tok, int8_t *state, double *bits,
-                                  uint32_t rec_max, int L, int warps, int grid_cap, cudaStream_t st) {
-    const size_t per = slot_bytes(rec_max, N) + (size_t)((L * N + 127) / 128 * 128);
-    const size_t smem = (size_t)warps * per;
-    cudaError_t e = cudaFuncSetAttribute(score_kernel<N, BLK, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+template <int N, int BLK, int R, int R2T>
+static cudaError_t launch_score_t(const DevModel &dm, int B, int T, const int32_t *tok, int8_t *state, double *bits,
+                                  uint32_t rec_max, int warps, int slots, int grid_cap, cudaStream_t st) {
+    const size_t smem = block_smem(rec_max, N, slots, warps, (dm.L * N + 127) / 128 * 128);
+    cudaError_t e = raise_smem_limit((const void *)score_kernel<N, BLK, R, R2T>, smem, score_limit<N, BLK, R, R2T>());
     if (e != cudaSuccess) return e;
     int grid = (B + warps - 1) / warps;
     if (grid > grid_cap) grid = grid_cap;
-    score_kernel<N, BLK, R><<<grid, 32 * warps, smem, st>>>(dm, B, T, tok, state, bits, rec_max);
+    score_kernel<N, BLK, R, R2T><<<grid, 32 * warps, smem, st>>>(dm, B, T, tok, state, bits, rec_max, slots);
     return cudaGetLastError();
 }
 
 #define YGG_DISPATCH(FN, ...)                                                                    \
+    /* compile-time layer-input rank for the benchmark shapes (c1/c2: n64 R8 R2=16, c3/c4: n128 R16 R2=32) */ \
+    if (n == 128 && blk == 16 && r == 16 && r2p == 32) return FN<128, 16, 16, 32>(__VA_ARGS__);               \
+    if (n == 64 && blk == 16 && r == 8 && r2p == 16) return FN<64, 16, 8, 16>(__VA_ARGS__);                   \
     switch (n * 1000 + blk * 100 + r) {                                                          \
-        case 64 * 1000 + 8 * 100 + 8: return FN<64, 8, 8>(__VA_ARGS__);                         \
-        case 64 * 1000 + 8 * 100 + 16: return FN<64, 8, 16>(__VA_ARGS__);                        \
-        case 64 * 1000 + 8 * 100 + 32: return FN<64, 8, 32>(__VA_ARGS__);                        \
-        case 64 * 1000 + 16 * 100 + 8: return FN<64, 16, 8>(__VA_ARGS__);                        \
-        case 64 * 1000 + 16 * 100 + 16: return FN<64, 16, 16>(__VA_ARGS__);                      \
-        case 64 * 1000 + 16 * 100 + 32: return FN<64, 16, 32>(__VA_ARGS__);                      \
-        case 128 * 1000 + 8 * 100 + 8: return FN<128, 8, 8>(__VA_ARGS__);                        \
-        case 128 * 1000 + 8 * 100 + 16: return FN<128, 8, 16>(__VA_ARGS__);                      \
-        case 128 * 1000 + 8 * 100 + 32: return FN<128, 8, 32>(__VA_ARGS__);                      \
-        case 128 * 1000 + 16 * 100 + 8: return FN<128, 16, 8>(__VA_ARGS__);                      \
-        case 128 * 1000 + 16 * 100 + 16: return FN<128, 16, 16>(__VA_ARGS__);                    \
-        case 128 * 1000 + 16 * 100 + 32: return FN<128, 16, 32>(__VA_ARGS__);                    \
-        case 256 * 1000 + 8 * 100 + 8: return FN<256, 8, 8>(__VA_ARGS__);                        \
-        case 256 * 1000 + 8 * 100 + 16: return FN<256, 8, 16>(__VA_ARGS__);                      \
-        case 256 * 1000 + 8 * 100 + 32: return FN<256, 8, 32>(__VA_ARGS__);                      \
-        case 256 * 1000 + 16 * 100 + 8: return FN<256, 16, 8>(__VA_ARGS__);                      \
-        case 256 * 1000 + 16 * 100 + 16: return FN<256, 16, 16>(__VA_ARGS__);                    \
-        case 256 * 1000 + 16 * 100 + 32: return FN<256, 16, 32>(__VA_ARGS__);                    \
+        case 64 * 1000 + 8 * 100 + 8: return FN<64, 8, 8, 0>(__VA_ARGS__);                     \
+        case 64 * 1000 + 8 * 100 + 16: return FN<64, 8, 16, 0>(__VA_ARGS__);                   \
+        case 64 * 1000 + 8 * 100 + 32: return FN<64, 8, 32, 0>(__VA_ARGS__);                   \
+        case 64 * 1000 + 16 * 100 + 8: return FN<64, 16, 8, 0>(__VA_ARGS__);                   \
+        case 64 * 1000 + 16 * 100 + 16: return FN<64, 16, 16, 0>(__VA_ARGS__);                 \
+        case 64 * 1000 + 16 * 100 + 32: return FN<64, 16, 32, 0>(__VA_ARGS__);                 \
+        case 128 * 1000 + 8 * 100 + 8: return FN<128, 8, 8, 0>(__VA_ARGS__);                   \
+        case 128 * 1000 + 8 * 100 + 16: return FN<128, 8, 16, 0>(__VA_ARGS__);                 \
+        case 128 * 1000 + 8 * 100 + 32: return FN<128, 8, 32, 0>(__VA_ARGS__);                 \
+        case 128 * 1000 + 16 * 100 + 8: return FN<128, 16, 8, 0>(__VA_ARGS__);                 \
+        case 128 * 1000 + 16 * 100 + 16: return FN<128, 16, 16, 0>(__VA_ARGS__);               \
+        case 128 * 1000 + 16 * 100 + 32: return FN<128, 16, 32, 0>(__VA_ARGS__);               \
+        case 256 * 1000 + 8 * 100 + 8: return FN<256, 8, 8, 0>(__VA_ARGS__);                   \
+        case 256 * 1000 + 8 * 100 + 16: return FN<256, 8, 16, 0>(__VA_ARGS__);                 \
+        case 256 * 1000 + 8 * 100 + 32: return FN<256, 8, 32, 0>(__VA_ARGS__);                 \
+        case 256 * 1000 + 16 * 100 + 8: return FN<256, 16, 8, 0>(__VA_ARGS__);                 \
+        case 256 * 1000 + 16 * 100 + 16: return FN<256, 16, 16, 0>(__VA_ARGS__);               \
+        case 256 * 1000 + 16 * 100 + 32: return FN<256, 16, 32, 0>(__VA_ARGS__);               \
         default: return cudaErrorInvalidValue;                                                   \
     }
 
-cudaError_t launch_step(int n, int blk, int r, const DevModel *dm, int B, const int32_t *tok, const int8_t *sin,
+cudaError_t launch_step(int n, int blk, int r, int r2p, const DevModel &dm, int B, const int32_t *tok, const int8_t *sin,
                         int8_t *sout, float *lg, int32_t *routes, int32_t *acc, uint32_t rec_max, int warps,
-                        int grid_cap, cudaStream_t st) {
-    YGG_DISPATCH(launch_step_t, dm, B, tok, sin, sout, lg, routes, acc, rec_max, warps, grid_cap, st)
+                        int slots, int grid_cap, cudaStream_t st) {
+    YGG_DISPATCH(launch_step_t, dm, B, tok, sin, sout, lg, routes, acc, rec_max, warps, slots, grid_cap, st)
 }
 
-cudaError_t launch_score(int n, int blk, int r, const DevModel *dm, int B, int T, const int32_t *tok, int8_t *state,
-                         double *bits, uint32_t rec_max, int L, int warps, int grid_cap, cudaStream_t st) {
-    YGG_DISPATCH(launch_score_t, dm, B, T, tok, state, bits, rec_max, L, warps, grid_cap, st)
+cudaError_t launch_score(int n, int blk, int r, int r2p, const DevModel &dm, int B, int T, const int32_t *tok, int8_t *state,
+                         double *bits, uint32_t rec_max, int warps, int slots, int grid_cap, cudaStream_t st) {
+    YGG_DISPATCH(launch_score_t, dm, B, T, tok, state, bits, rec_max, warps, slots, grid_cap, st)
 }
 
-size_t step_slot_bytes(uint32_t rec_max, int n) { return slot_bytes(rec_max, n); }
+size_t block_smem_bytes(uint32_t rec_max, int n, int slots, int warps, int state_bytes) {
+    return block_smem(rec_max, n, slots, warps, state_bytes);
+}
 
 }  // namespace ygg

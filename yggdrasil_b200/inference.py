@@ -193,6 +193,15 @@ class B200Yggdrasil:
 
     # ------------------------------------------------------------------------------------------------ score
 
+    def score_into(self, tokens, state, bits):
+        """One fused score launch into caller buffers: tokens int32 (B, T) device tensor, state int8 (B, L, n) or
+        None (zero, not written back), bits float64 (B,)."""
+        torch = _torch()
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        check(lib().ygg_score(self._h, tokens.shape[0], tokens.shape[1], ctypes.c_void_p(tokens.data_ptr()),
+                              ctypes.c_void_p(state.data_ptr()) if state is not None else None,
+                              ctypes.c_void_p(bits.data_ptr()), ctypes.c_void_p(stream)), "ygg_score")
+
     def score(self, tokens, state=None, batch=1024):
         """Bits of tokens[:, 1:] given the tokens before them, per row of tokens (B, L), as float64 (B,).
         Rows start from state, or from zero; bits per token = score(tokens).sum() / (B (L - 1)).
