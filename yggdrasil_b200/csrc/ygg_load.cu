@@ -400,7 +400,7 @@ int ygg_load(const void *file_bytes, size_t nbytes, int device, ygg_model **out)
         while (S > 1 && block_smem_bytes(rec_max, n, S, W, state_bytes) > cap) S--;
         *S_out = S;
     };
-    int W = 8, blocks = 3;
+    int W = 8, blocks = n >= 256 ? 2 : 4;   // the kernels' launch bounds (blocks_per_sm in ygg_step.cu)
     if (const char *e = getenv("YGG_WARPS")) { const int v = atoi(e); if (v >= 1 && v <= 8) W = v; }
     if (const char *e = getenv("YGG_BLOCKS_PER_SM")) { const int v = atoi(e); if (v >= 1 && v <= 8) blocks = v; }
     m->warps_step = W;

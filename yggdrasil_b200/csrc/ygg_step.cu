@@ -31,6 +31,9 @@ constexpr int kMaxClassesPerLane = 8;   // VP <= 256
 constexpr long long kWaitCycles = 2000000000LL;
 constexpr int kLook = 3;                // router levels per round of loads
 constexpr int kLookRows = (1 << kLook) - 1;
+// blocks of 8 warps per SM the register budget is sized for: 4 (64 registers a thread) for n <= 128; n = 256 needs
+// more registers per lane (8 coordinates) and runs 2 blocks
+template <int N> constexpr int blocks_per_sm() { return N >= 256 ? 2 : 4; }
 
 // ------------------------------------------------------------------------------------------------ PTX helpers
 
@@ -135,35 +138,20 @@ __host__ __device__ constexpr uint32_t block_smem(uint32_t rec_max, int n, int S
     return S * pool_slot_bytes(rec_max, n) + pool_meta_bytes(S) + W * (scratch_bytes(n) + state_bytes);
 }
 
-// Take a free slot (lane 0 claims it with a CAS; the others learn it by shuffle). -1 after ~1 s without one.
-__device__ __forceinline__ int slot_acquire(const Pool &p, int warp, int lane) {
-    int got = -1;
-    if (lane == 0) {
-        const long long t0 = clock64();
-        int i = warp % p.S;
-        while (true) {
-            if (atomicCAS(p.owner + i, -1, warp) == -1) { got = i; break; }
-            if (++i == p.S) {
-                i = 0;
-                if (clock64() - t0 > kWaitCycles) break;
-                __nanosleep(32);
-            }
+// Lane 0 claims a free slot (CAS on its owner word, starting from the warp's home slot); -1 after ~1 s without one.
+__device__ __forceinline__ int slot_claim(const Pool &p, int home, int warp) {
+    const long long t0 = clock64();
+    int i = home;
+    while (true) {
+        if (atomicCAS(p.owner + i, -1, warp) == -1) break;
+        if (++i == p.S) {
+            i = 0;
+            if (clock64() - t0 > kWaitCycles) return -1;
+            __nanosleep(32);
         }
-        __threadfence_block();
     }
-    return __shfl_sync(kFull, got, 0);
-}
-__device__ __forceinline__ void slot_release(const Pool &p, int slot, int lane) {
-    __syncwarp();
-    if (lane == 0) {
-        __threadfence_block();
-        atomicExch(p.owner + slot, -1);
-    }
-}
-
-// Lane-interleaved part: the lane's 16-byte chunk j.
-__device__ __forceinline__ uint4 lane_chunk(const uint8_t *part, int j, int lane) {
-    return *(const uint4 *)(part + ((size_t)j * 32 + lane) * 16);
+    __threadfence_block();
+    return i;
 }
 
 // ------------------------------------------------------------------------------------------------ one layer
@@ -281,207 +269,262 @@ struct StepOut {
     int32_t *acc;       // [L][n] or null
 };
 
-// One token of one stream through every layer. q_in / q_out: the stream's state [L][n] (global or shared memory;
-// they may alias). lg: the logits of the lane's classes (out). Returns false if a bounded wait gave up.
-template <int N, int BLK, int R, int R2T>
-__device__ __forceinline__ bool token_step(const DevModel &m, const Pool &pool, const Scratch &sc, int warp, int x,
-                                           const int8_t *q_in, int8_t *q_out, float (&lg)[kMaxClassesPerLane],
-                                           const StepOut &dbg, int lane) {
-    constexpr int C = N / 32;
-    const int L = m.L, VP = m.VP, E = m.E, D = m.D, V = m.V;
-    const int nv = VP / 32;
-#pragma unroll
-    for (int c = 0; c < kMaxClassesPerLane; c++) lg[c] = c < nv ? __ldg(m.head_b + 32 * c + lane) : 0.0f;
+// What a token's layers share: the block's pool and the warp's scratch, the token, the state pointers, the debug
+// outputs and the new state of the layer below (carried from one layer to the next).
+template <int C>
+struct TokenCtx {
+    const DevModel &m;
+    const Pool &pool;
+    const Scratch &sc;
+    int home, warp, lane, x;
+    const int8_t *q_in;
+    int8_t *q_out;
+    const StepOut &dbg;
+    LaneQ<C> qbelow;
+};
 
-    LaneQ<C> qbelow{};
-    for (int l = 0; l < L; l++) {
-        const DevLayer &y = m.layer[l];
-        const LaneQ<C> qold = load_q<C>(q_in + (size_t)l * N + C * lane);
-        int r = x;
-        float rho = 0.0f;
-        const bool low = l > 0 && m.R2 > 0;
-        if (l > 0) {
-            rho = rms_rho<N>(qbelow, y.r2b, y.rms_eps);
-            store_q<C>(sc.qb + C * lane, qbelow);
-            __syncwarp();
-            const uint4 qrow = *(const uint4 *)(sc.qb + 16 * (lane % (N / 16)));
-            r = route_look<N>(y.w, y.thr + (size_t)x * E, D, qrow, rho, lane) - E;
-        }
-        // -- a slot, and the expert record and its table row into it
-        const int slot = slot_acquire(pool, warp, lane);
-        if (slot < 0) return false;
-        uint8_t *rec = pool.slots + (size_t)slot * pool.slot_bytes;
-        const int16_t *trow = (const int16_t *)(rec + (pool.slot_bytes - 2 * N));
-        const uint32_t bar = pool.bars + 8u * slot;
-        const uint32_t rec_bytes = y.rec_bytes;
-        const bool has_table = y.table != nullptr;
-        if (lane == 0) {
+// Layer l of a token (cpu/ygg.cpp:443-458). Returns false if a bounded wait gave up. Always inlined: the warp
+// collectives in it (shuffles, ballots, redux) rely on the caller's converged warp.
+template <int N, int BLK, int R, int R2T, int NVT>
+__device__ __forceinline__ bool layer_step(TokenCtx<N / 32> &t, const int l, float (&lg)[kMaxClassesPerLane]) {
+    constexpr int C = N / 32;
+    const DevModel &m = t.m;
+    const Pool &pool = t.pool;
+    const Scratch &sc = t.sc;
+    const int lane = t.lane, x = t.x, home = t.home, warp = t.warp;
+    const int E = m.E, D = m.D;
+    const int nv = NVT ? NVT : m.VP / 32;
+    const int8_t *q_in = t.q_in;
+    int8_t *q_out = t.q_out;
+    const StepOut &dbg = t.dbg;
+    LaneQ<C> &qbelow = t.qbelow;
+    const DevLayer &y = m.layer[l];
+    const LaneQ<C> qold = load_q<C>(q_in + (size_t)l * N + C * lane);
+    int r = x;
+    float rho = 0.0f;
+    const bool low = l > 0 && (R2T > 0 || m.R2 > 0);
+    if (l > 0) {
+        rho = rms_rho<N>(qbelow, y.r2b, y.rms_eps);
+        store_q<C>(sc.qb + C * lane, qbelow);
+        __syncwarp();
+        const uint4 qrow = *(const uint4 *)(sc.qb + 16 * (lane % (N / 16)));
+        r = route_look<N>(y.w, y.thr + (size_t)x * E, D, qrow, rho, lane) - E;
+    }
+    // -- lane 0 claims a slot and issues the bulk copies of the expert record and its table row into it; the
+    // slot index and the parity to wait for reach the other lanes in one shuffle
+    const uint32_t rec_bytes = y.rec_bytes;
+    const bool has_table = y.table != nullptr;
+    int tag = -1;
+    if (lane == 0) {
+        const int slot = slot_claim(pool, home, warp);
+        if (slot >= 0) {
+            uint8_t *rec = pool.slots + (size_t)slot * pool.slot_bytes;
+            const uint32_t bar = pool.bars + 8u * slot;
             fence_proxy_async();
             mbar_expect_tx(bar, rec_bytes + (has_table ? 2u * N : 0u));
             bulk_g2s(smem_addr(rec), y.rec + (size_t)r * rec_bytes, rec_bytes, bar);
             if (has_table) {
                 const int16_t *src = y.table + ((size_t)r * y.table_rows + (y.table_rows > 1 ? x : 0)) * N;
-                bulk_g2s(smem_addr(trow), src, 2u * N, bar);
+                bulk_g2s(smem_addr(rec + pool.slot_bytes - 2 * N), src, 2u * N, bar);
             }
+            tag = 2 * slot + pool.phase[slot];
         }
-        // -- layer input codes while the copy is in flight (cpu/ygg.cpp:285-296)
-        if (low) {
-            const int R2P = R2T ? R2T : m.R2P;
-            for (int k = lane; k < R2P; k += 32) {
-                int a = 0;
-#pragma unroll 4
-                for (int j = 0; j < N / 16; j++) {
-                    const uint4 v = __ldg((const uint4 *)(y.vl + ((size_t)j * R2P + k) * 16));
-                    a = dot16(v, *(const uint4 *)(sc.qb + 16 * j), a);
-                }
-                const float zf = __fmul_rn(__fmul_rn(i2f(a), __ldg(y.mv + k)), rho);
-                sc.zl[k] = (int8_t)(k < m.R2 ? clampi(cvt_rne(zf), -127, 127) : 0);
-            }
+    }
+    tag = __shfl_sync(kFull, tag, 0);
+    if (tag < 0) return false;
+    const int slot = tag >> 1;
+    const uint32_t parity = (uint32_t)(tag & 1);
+    const uint8_t *rec = pool.slots + (size_t)slot * pool.slot_bytes;
+    const int16_t *trow = (const int16_t *)(rec + (pool.slot_bytes - 2 * N));
+    const uint32_t bar = pool.bars + 8u * slot;
+    // -- layer input codes while the copy is in flight (cpu/ygg.cpp:285-296)
+    if (low) {
+        const int R2P = R2T ? R2T : m.R2P;
+        for (int k = lane; k < R2P; k += 32) {
+            const int8_t *vk = y.vl + (size_t)k * 16;
+            int a = 0;
+#pragma unroll
+            for (int j = 0; j < N / 16; j++)
+                a = dot16(__ldg((const uint4 *)(vk + (size_t)j * R2P * 16)), *(const uint4 *)(sc.qb + 16 * j), a);
+            const float zf = __fmul_rn(__fmul_rn(i2f(a), __ldg(y.mv + k)), rho);
+            sc.zl[k] = (int8_t)(k < m.R2 ? clampi(cvt_rne(zf), -127, 127) : 0);
         }
-        store_q<C>(sc.qold + C * lane, qold);
-        __syncwarp();
-        const uint32_t parity = (uint32_t)pool.phase[slot];
-        const bool ok = __all_sync(kFull, mbar_wait_bounded(bar, parity));
-        if (!ok) return false;
-        if (lane == 0) pool.phase[slot] = (int)(parity ^ 1u);
+    }
+    store_q<C>(sc.qold + C * lane, qold);
+    __syncwarp();
+    if (!__all_sync(kFull, mbar_wait_bounded(bar, parity))) return false;
 
-        // -- transition: acc_i = (sum_j A16[i][j] q[j] + 2^(shift-1)) >> shift over the row's block (cpu/ygg.cpp:312-332)
-        int acc[C];
-        {
-            const int blk0 = ((C * lane) / BLK) * BLK;
-            uint32_t qblk[BLK / 4];
-            if constexpr (BLK == 8) {
-                const uint2 v = *(const uint2 *)(sc.qold + blk0);
-                qblk[0] = v.x; qblk[1] = v.y;
-            } else {
-                const uint4 v = *(const uint4 *)(sc.qold + blk0);
-                qblk[0] = v.x; qblk[1] = v.y; qblk[2] = v.z; qblk[3] = v.w;
-            }
-            constexpr int kWords = C * BLK / 2;            // int16 pairs of the lane
-            uint32_t aw[kWords];
-            const uint8_t *pa = rec + y.off_a;
-#pragma unroll
-            for (int j = 0; j < kWords / 4; j++) {
-                const uint4 v = lane_chunk(pa, j, lane);
-                aw[4 * j] = v.x; aw[4 * j + 1] = v.y; aw[4 * j + 2] = v.z; aw[4 * j + 3] = v.w;
-            }
-            const int rnd = 1 << (m.shift - 1), sh = m.shift;
-#pragma unroll
-            for (int ii = 0; ii < C; ii++) {
-                int s = 0;
-#pragma unroll
-                for (int p = 0; p < BLK / 2; p++) {
-                    const uint32_t a = aw[ii * (BLK / 2) + p];
-                    s = (p & 1) ? __dp2a_hi((int)a, (int)qblk[p >> 1], s) : __dp2a_lo((int)a, (int)qblk[p >> 1], s);
-                }
-                acc[ii] = (s + rnd) >> sh;
-            }
-        }
-        // -- input: table row (cpu/ygg.cpp:334-337) or factored (cpu/ygg.cpp:339-358)
-        if (has_table) {
-#pragma unroll
-            for (int ii = 0; ii < C; ii++) acc[ii] += trow[C * lane + ii];
+    // -- transition: acc_i = (sum_j A16[i][j] q[j] + 2^(shift-1)) >> shift over the row's block (cpu/ygg.cpp:312-332)
+    int acc[C];
+    {
+        const int blk0 = ((C * lane) / BLK) * BLK;
+        uint32_t qblk[BLK / 4];
+        if constexpr (BLK == 8) {
+            const uint2 v = *(const uint2 *)(sc.qold + blk0);
+            qblk[0] = v.x; qblk[1] = v.y;
         } else {
-            const int KP = m.KP;
-            const uint8_t *pf = rec + y.off_f;
-            const int8_t *v = y.vt + (size_t)x * KP;
-            const float su = *(const float *)(rec + y.off_su);
-            const int16_t *cb = (const int16_t *)(rec + y.off_cb);
-#pragma unroll
-            for (int ii = 0; ii < C; ii++) {
-                int lt = 0;
-                for (int j = 0; j < KP / 16; j++)
-                    lt = dot16(lane_chunk(pf, ii * (KP / 16) + j, lane), __ldg((const uint4 *)(v + 16 * j)), lt);
-                const float mul = __fmul_rn(su, __ldg(y.mt + C * lane + ii));
-                acc[ii] += cvt_rne(__fmul_rn(i2f(lt), mul)) + cb[C * lane + ii];
-            }
+            const uint4 v = *(const uint4 *)(sc.qold + blk0);
+            qblk[0] = v.x; qblk[1] = v.y; qblk[2] = v.z; qblk[3] = v.w;
         }
-        // -- layer input: acc_i += rint(f32(U'_r zl) m_ul) (cpu/ygg.cpp:360-377)
-        if (low) {
-            const int R2P = R2T ? R2T : m.R2P;
-            const uint8_t *pu = rec + y.off_u;
+        constexpr int kWords = C * BLK / 2;            // int16 pairs of the lane
+        uint32_t aw[kWords];
+        const uint8_t *pa = rec + y.off_a + 16 * lane;
 #pragma unroll
-            for (int ii = 0; ii < C; ii++) {
-                int la = 0;
-                for (int j = 0; j < R2P / 16; j++)
-                    la = dot16(lane_chunk(pu, ii * (R2P / 16) + j, lane), *(const uint4 *)(sc.zl + 16 * j), la);
-                const float mu = y.mulv ? __ldg(y.mulv + C * lane + ii) : y.layer_input_scale;
-                acc[ii] += cvt_rne(__fmul_rn(i2f(la), mu));
-            }
+        for (int j = 0; j < kWords / 4; j++) {
+            const uint4 v = *(const uint4 *)(pa + 512 * j);
+            aw[4 * j] = v.x; aw[4 * j + 1] = v.y; aw[4 * j + 2] = v.z; aw[4 * j + 3] = v.w;
         }
-        // -- saturate to the new int8 state (cpu/ygg.cpp:388)
-        LaneQ<C> qn{};
+        const int rnd = 1 << (m.shift - 1), sh = m.shift;
 #pragma unroll
         for (int ii = 0; ii < C; ii++) {
-            const uint32_t b = (uint32_t)(uint8_t)(int8_t)clampi(acc[ii], -128, 127);
-            qn.w[ii >> 2] |= b << (8 * (ii & 3));
-        }
-        store_q<C>(q_out + (size_t)l * N + C * lane, qn);
-        if (dbg.routes != nullptr && lane == 0) dbg.routes[l] = r;
-        if (dbg.acc != nullptr) {
+            int s = 0;
 #pragma unroll
-            for (int ii = 0; ii < C; ii++) dbg.acc[(size_t)l * N + C * lane + ii] = acc[ii];
+            for (int p = 0; p < BLK / 2; p++) {
+                const uint32_t a = aw[ii * (BLK / 2) + p];
+                s = (p & 1) ? __dp2a_hi((int)a, (int)qblk[p >> 1], s) : __dp2a_lo((int)a, (int)qblk[p >> 1], s);
+            }
+            acc[ii] = (s + rnd) >> sh;
         }
+    }
+    // -- input: table row (cpu/ygg.cpp:334-337) or factored (cpu/ygg.cpp:339-358)
+    if (has_table) {
+#pragma unroll
+        for (int ii = 0; ii < C; ii++) acc[ii] += trow[C * lane + ii];
+    } else {
+        const int KP = m.KP;
+        const uint8_t *pf = rec + y.off_f + 16 * lane;
+        const int8_t *v = y.vt + (size_t)x * KP;
+        const float su = *(const float *)(rec + y.off_su);
+        const int16_t *cb = (const int16_t *)(rec + y.off_cb);
+#pragma unroll
+        for (int ii = 0; ii < C; ii++) {
+            int lt = 0;
+            for (int j = 0; j < KP / 16; j++)
+                lt = dot16(*(const uint4 *)(pf + 512 * (ii * (KP / 16) + j)), __ldg((const uint4 *)(v + 16 * j)), lt);
+            const float mul = __fmul_rn(su, __ldg(y.mt + C * lane + ii));
+            acc[ii] += cvt_rne(__fmul_rn(i2f(lt), mul)) + cb[C * lane + ii];
+        }
+    }
+    // -- layer input: acc_i += rint(f32(U'_r zl) m_ul) (cpu/ygg.cpp:360-377)
+    if (low) {
+        const int R2P = R2T ? R2T : m.R2P;
+        const uint8_t *pu = rec + y.off_u + 16 * lane;
+#pragma unroll
+        for (int ii = 0; ii < C; ii++) {
+            int la = 0;
+#pragma unroll
+            for (int j = 0; j < (R2T ? R2T / 16 : 4); j++)
+                if (R2T || j < R2P / 16)
+                    la = dot16(*(const uint4 *)(pu + 512 * (ii * (R2P / 16) + j)), *(const uint4 *)(sc.zl + 16 * j), la);
+            const float mu = y.mulv ? __ldg(y.mulv + C * lane + ii) : y.layer_input_scale;
+            acc[ii] += cvt_rne(__fmul_rn(i2f(la), mu));
+        }
+    }
+    // -- saturate to the new int8 state (cpu/ygg.cpp:388)
+    LaneQ<C> qn{};
+#pragma unroll
+    for (int ii = 0; ii < C; ii++) {
+        const uint32_t b = (uint32_t)(uint8_t)(int8_t)clampi(acc[ii], -128, 127);
+        qn.w[ii >> 2] |= b << (8 * (ii & 3));
+    }
+    store_q<C>(q_out + (size_t)l * N + C * lane, qn);
+    if (dbg.routes != nullptr && lane == 0) dbg.routes[l] = r;
+    if (dbg.acc != nullptr) {
+#pragma unroll
+        for (int ii = 0; ii < C; ii++) dbg.acc[(size_t)l * N + C * lane + ii] = acc[ii];
+    }
 
-        // -- readout z = P_r q, zq = sat(rint(f32(z) m_z)) (cpu/ygg.cpp:395-420)
-        int myz = 0;
-        float mz = y.readout_scale;
-        {
-            const uint8_t *pp = rec + y.off_p;
-            constexpr int kPWords = R * C / 4;
-            uint32_t pw[kPWords];
+    // -- readout z = P_r q, zq = sat(rint(f32(z) m_z)) (cpu/ygg.cpp:395-420)
+    int myz = 0;
+    float mz = y.readout_scale;
+    {
+        const uint8_t *pp = rec + y.off_p + 16 * lane;
+        constexpr int kPWords = R * C / 4;
+        uint32_t pw[kPWords];
 #pragma unroll
-            for (int j = 0; j < kPWords / 4; j++) {
-                const uint4 v = lane_chunk(pp, j, lane);
-                pw[4 * j] = v.x; pw[4 * j + 1] = v.y; pw[4 * j + 2] = v.z; pw[4 * j + 3] = v.w;
+        for (int j = 0; j < kPWords / 4; j++) {
+            const uint4 v = *(const uint4 *)(pp + 512 * j);
+            pw[4 * j] = v.x; pw[4 * j + 1] = v.y; pw[4 * j + 2] = v.z; pw[4 * j + 3] = v.w;
+        }
+        if (y.off_mz != kNone && lane < R) mz = *(const float *)(rec + y.off_mz + 4 * lane);
+        // the slot is free once its bytes are in registers: flip its parity and hand it back
+        __syncwarp();
+        if (lane == 0) {
+            pool.phase[slot] = (int)(parity ^ 1u);
+            __threadfence_block();
+            atomicExch(pool.owner + slot, -1);
+        }
+#pragma unroll
+        for (int rr = 0; rr < R; rr++) {
+            int part;
+            if constexpr (C == 2) {
+                const uint32_t word = pw[rr >> 1];
+                part = __dp4a((int)((rr & 1) ? (word >> 16) : (word & 0xFFFFu)), (int)qn.w[0], 0);
+            } else {
+                part = 0;
+#pragma unroll
+                for (int w = 0; w < C / 4; w++) part = __dp4a((int)pw[rr * (C / 4) + w], (int)qn.w[w], part);
             }
-            if (y.off_mz != kNone && lane < R) mz = *(const float *)(rec + y.off_mz + 4 * lane);
+            const int z = __reduce_add_sync(kFull, part);
+            if (lane == rr) myz = z;
+        }
+    }
+    if (lane < R) sc.zq[lane] = (int8_t)clampi(cvt_rne(__fmul_rn(i2f(myz), mz)), -127, 127);
+    __syncwarp();
+    // -- head: lg[c] += f32(Q_c . zq) * s (cpu/ygg.cpp:421-434)
+    {
+        uint32_t zw[R / 4];
 #pragma unroll
-            for (int rr = 0; rr < R; rr++) {
-                int part;
-                if constexpr (C == 2) {
-                    const uint32_t word = pw[rr >> 1];
-                    part = __dp4a((int)((rr & 1) ? (word >> 16) : (word & 0xFFFFu)), (int)qn.w[0], 0);
+        for (int j = 0; j < R / 4; j++) zw[j] = *(const uint32_t *)(sc.zq + 4 * j);
+#pragma unroll
+        for (int c = 0; c < (NVT ? NVT : kMaxClassesPerLane); c++) {
+            if (NVT || c < nv) {
+                const int cls = 32 * c + lane;
+                const int8_t *qrow = y.unembed + (size_t)cls * R;
+                int a = 0;
+                if constexpr (R == 8) {
+                    const uint2 v = __ldg((const uint2 *)qrow);
+                    a = __dp4a((int)v.x, (int)zw[0], a);
+                    a = __dp4a((int)v.y, (int)zw[1], a);
                 } else {
-                    part = 0;
 #pragma unroll
-                    for (int w = 0; w < C / 4; w++) part = __dp4a((int)pw[rr * (C / 4) + w], (int)qn.w[w], part);
+                    for (int j = 0; j < R / 16; j++)
+                        a = dot16(__ldg((const uint4 *)(qrow + 16 * j)),
+                                  make_uint4(zw[4 * j], zw[4 * j + 1], zw[4 * j + 2], zw[4 * j + 3]), a);
                 }
-                const int z = __reduce_add_sync(kFull, part);
-                if (lane == rr) myz = z;
+                const float s = y.sqv ? __ldg(y.sqv + cls) : y.unembed_scale;
+                lg[c] = __fadd_rn(lg[c], __fmul_rn(i2f(a), s));
             }
         }
-        slot_release(pool, slot, lane);
-        if (lane < R) sc.zq[lane] = (int8_t)clampi(cvt_rne(__fmul_rn(i2f(myz), mz)), -127, 127);
-        __syncwarp();
-        // -- head: lg[c] += f32(Q_c . zq) * s (cpu/ygg.cpp:421-434)
-        {
-            uint32_t zw[R / 4];
+    }
+    qbelow = qn;
+    __syncwarp();
+    return true;
+}
+
+// One token of one stream through every layer. q_in / q_out: the stream's state [L][n] (global or shared memory;
+// they may alias). lg: the logits of the lane's classes (out). Returns false if a bounded wait gave up.
+// Compile-time shape where a fast instance fixes it (0: read from the model at run time): R2T the padded layer-input
+// rank, LT the number of layers, NVT the classes per lane (VP / 32).
+template <int N, int BLK, int R, int R2T, int LT, int NVT>
+__device__ __forceinline__ bool token_step(const DevModel &m, const Pool &pool, const Scratch &sc, int home, int warp,
+                                           int x, const int8_t *q_in, int8_t *q_out,
+                                           float (&lg)[kMaxClassesPerLane], const StepOut &dbg, int lane) {
+    const int V = m.V;
+    const int nv = NVT ? NVT : m.VP / 32;
 #pragma unroll
-            for (int j = 0; j < R / 4; j++) zw[j] = *(const uint32_t *)(sc.zq + 4 * j);
-#pragma unroll
-            for (int c = 0; c < kMaxClassesPerLane; c++) {
-                if (c < nv) {
-                    const int cls = 32 * c + lane;
-                    const int8_t *qrow = y.unembed + (size_t)cls * R;
-                    int a = 0;
-                    if constexpr (R == 8) {
-                        const uint2 v = __ldg((const uint2 *)qrow);
-                        a = __dp4a((int)v.x, (int)zw[0], a);
-                        a = __dp4a((int)v.y, (int)zw[1], a);
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < R / 16; j++)
-                            a = dot16(__ldg((const uint4 *)(qrow + 16 * j)),
-                                      make_uint4(zw[4 * j], zw[4 * j + 1], zw[4 * j + 2], zw[4 * j + 3]), a);
-                    }
-                    const float s = y.sqv ? __ldg(y.sqv + cls) : y.unembed_scale;
-                    lg[c] = __fadd_rn(lg[c], __fmul_rn(i2f(a), s));
-                }
-            }
-        }
-        qbelow = qn;
-        __syncwarp();
+    for (int c = 0; c < kMaxClassesPerLane; c++) lg[c] = c < nv ? __ldg(m.head_b + 32 * c + lane) : 0.0f;
+    TokenCtx<N / 32> t{m, pool, sc, home, warp, lane, x, q_in, q_out, dbg, {}};
+    if constexpr (LT > 0) {
+        // not unrolled: an unrolled layer loop with its early exits defeats the compiler's proof that the warp is
+        // converged at the collectives, and each shuffle / ballot / redux then pays a re-convergence loop
+#pragma unroll 1
+        for (int l = 0; l < LT; l++)
+            if (!layer_step<N, BLK, R, R2T, NVT>(t, l, lg)) return false;
+    } else {
+#pragma unroll 1
+        for (int l = 0; l < m.L; l++)
+            if (!layer_step<N, BLK, R, R2T, NVT>(t, l, lg)) return false;
     }
     if (dbg.logits != nullptr) {
 #pragma unroll
@@ -522,8 +565,8 @@ __device__ __forceinline__ void block_init(uint8_t *smem, uint32_t rec_max, int 
     __syncthreads();
 }
 
-template <int N, int BLK, int R, int R2T>
-__global__ void __launch_bounds__(256, 3) step_kernel(const __grid_constant__ DevModel m, int B,
+template <int N, int BLK, int R, int R2T, int LT, int NVT>
+__global__ void __launch_bounds__(256, blocks_per_sm<N>()) step_kernel(const __grid_constant__ DevModel m, int B,
                                                    const int32_t *__restrict__ tokens, const int8_t *state_in,
                                                    int8_t *state_out, float *__restrict__ logits,
                                                    int32_t *__restrict__ routes, int32_t *__restrict__ acc_out,
@@ -534,6 +577,7 @@ __global__ void __launch_bounds__(256, 3) step_kernel(const __grid_constant__ De
     Scratch sc;
     int8_t *unused;
     block_init(smem, rec_max, N, S, 0, warp, lane, pool, sc, unused);
+    const int home = warp % S;
     const int L = m.L, V = m.V;
     for (int s = blockIdx.x * W + warp; s < B; s += gridDim.x * W) {
         const int x = tokens[s];
@@ -549,7 +593,7 @@ __global__ void __launch_bounds__(256, 3) step_kernel(const __grid_constant__ De
         float lg[kMaxClassesPerLane];
         StepOut o{logits ? logits + (size_t)s * V : nullptr, routes ? routes + (size_t)s * L : nullptr,
                   acc_out ? acc_out + (size_t)s * L * N : nullptr};
-        if (!token_step<N, BLK, R, R2T>(m, pool, sc, warp, x, state_in + (size_t)s * L * N, state_out + (size_t)s * L * N,
+        if (!token_step<N, BLK, R, R2T, LT, NVT>(m, pool, sc, home, warp, x, state_in + (size_t)s * L * N, state_out + (size_t)s * L * N,
                                    lg, o, lane)) {
             if (lane == 0) atomicOr(m.status, kStatusTimeout);
             return;
@@ -559,8 +603,8 @@ __global__ void __launch_bounds__(256, 3) step_kernel(const __grid_constant__ De
 
 // Rows of `steps` tokens; the state of a row lives in the warp's shared memory between tokens, the logits in
 // registers, and the f64 NLL of the next token is summed on chip (cpu/ygg.cpp:513-517).
-template <int N, int BLK, int R, int R2T>
-__global__ void __launch_bounds__(256, 3) score_kernel(const __grid_constant__ DevModel m, int B, int T,
+template <int N, int BLK, int R, int R2T, int LT, int NVT>
+__global__ void __launch_bounds__(256, blocks_per_sm<N>()) score_kernel(const __grid_constant__ DevModel m, int B, int T,
                                                     const int32_t *__restrict__ tokens, int8_t *state,
                                                     double *__restrict__ bits, uint32_t rec_max, int S) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -570,6 +614,7 @@ __global__ void __launch_bounds__(256, 3) score_kernel(const __grid_constant__ D
     Scratch sc;
     int8_t *qs;
     block_init(smem, rec_max, N, S, (L * N + 127) / 128 * 128, warp, lane, pool, sc, qs);
+    const int home = warp % S;
     const StepOut none{nullptr, nullptr, nullptr};
     for (int s = blockIdx.x * W + warp; s < B; s += gridDim.x * W) {
         const int32_t *tok = tokens + (size_t)s * T;
@@ -584,7 +629,7 @@ __global__ void __launch_bounds__(256, 3) score_kernel(const __grid_constant__ D
         double nll = 0.0;
         for (int t = 0; t + 1 < T; t++) {
             float lg[kMaxClassesPerLane];
-            if (!token_step<N, BLK, R, R2T>(m, pool, sc, warp, tok[t], qs, qs, lg, none, lane)) {
+            if (!token_step<N, BLK, R, R2T, LT, NVT>(m, pool, sc, home, warp, tok[t], qs, qs, lg, none, lane)) {
                 if (lane == 0) atomicOr(m.status, kStatusTimeout);
                 return;
             }
@@ -623,8 +668,8 @@ __global__ void __launch_bounds__(256, 3) score_kernel(const __grid_constant__ D
 // attribute is per device; raising it on every launch would cost a driver call per step).
 constexpr int kMaxDevices = 64;
 struct SmemLimits { size_t set[kMaxDevices]; };
-template <int N, int BLK, int R, int R2T> static SmemLimits &step_limit() { static SmemLimits l{}; return l; }
-template <int N, int BLK, int R, int R2T> static SmemLimits &score_limit() { static SmemLimits l{}; return l; }
+template <int N, int BLK, int R, int R2T, int LT, int NVT> static SmemLimits &step_limit() { static SmemLimits l{}; return l; }
+template <int N, int BLK, int R, int R2T, int LT, int NVT> static SmemLimits &score_limit() { static SmemLimits l{}; return l; }
 static cudaError_t raise_smem_limit(const void *fn, size_t smem, SmemLimits &lim) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -635,65 +680,70 @@ static cudaError_t raise_smem_limit(const void *fn, size_t smem, SmemLimits &lim
     return e;
 }
 
-template <int N, int BLK, int R, int R2T>
+template <int N, int BLK, int R, int R2T, int LT, int NVT>
 static cudaError_t launch_step_t(const DevModel &dm, int B, const int32_t *tok, const int8_t *sin, int8_t *sout,
                                  float *lg, int32_t *routes, int32_t *acc, uint32_t rec_max, int warps, int slots,
                                  int grid_cap, cudaStream_t st) {
     const size_t smem = block_smem(rec_max, N, slots, warps, 0);
-    cudaError_t e = raise_smem_limit((const void *)step_kernel<N, BLK, R, R2T>, smem, step_limit<N, BLK, R, R2T>());
+    cudaError_t e = raise_smem_limit((const void *)step_kernel<N, BLK, R, R2T, LT, NVT>, smem, step_limit<N, BLK, R, R2T, LT, NVT>());
     if (e != cudaSuccess) return e;
     int grid = (B + warps - 1) / warps;
     if (grid > grid_cap) grid = grid_cap;
-    step_kernel<N, BLK, R, R2T><<<grid, 32 * warps, smem, st>>>(dm, B, tok, sin, sout, lg, routes, acc, rec_max, slots);
+    step_kernel<N, BLK, R, R2T, LT, NVT><<<grid, 32 * warps, smem, st>>>(dm, B, tok, sin, sout, lg, routes, acc, rec_max, slots);
     return cudaGetLastError();
 }
 
-template <int N, int BLK, int R, int R2T>
+template <int N, int BLK, int R, int R2T, int LT, int NVT>
 static cudaError_t launch_score_t(const DevModel &dm, int B, int T, const int32_t *tok, int8_t *state, double *bits,
                                   uint32_t rec_max, int warps, int slots, int grid_cap, cudaStream_t st) {
     const size_t smem = block_smem(rec_max, N, slots, warps, (dm.L * N + 127) / 128 * 128);
-    cudaError_t e = raise_smem_limit((const void *)score_kernel<N, BLK, R, R2T>, smem, score_limit<N, BLK, R, R2T>());
+    cudaError_t e = raise_smem_limit((const void *)score_kernel<N, BLK, R, R2T, LT, NVT>, smem, score_limit<N, BLK, R, R2T, LT, NVT>());
     if (e != cudaSuccess) return e;
     int grid = (B + warps - 1) / warps;
     if (grid > grid_cap) grid = grid_cap;
-    score_kernel<N, BLK, R, R2T><<<grid, 32 * warps, smem, st>>>(dm, B, T, tok, state, bits, rec_max, slots);
+    score_kernel<N, BLK, R, R2T, LT, NVT><<<grid, 32 * warps, smem, st>>>(dm, B, T, tok, state, bits, rec_max, slots);
     return cudaGetLastError();
 }
 
-#define YGG_DISPATCH(FN, ...)                                                                    \
-    /* compile-time layer-input rank for the benchmark shapes (c1/c2: n64 R8 R2=16, c3/c4: n128 R16 R2=32) */ \
-    if (n == 128 && blk == 16 && r == 16 && r2p == 32) return FN<128, 16, 16, 32>(__VA_ARGS__);               \
-    if (n == 64 && blk == 16 && r == 8 && r2p == 16) return FN<64, 16, 8, 16>(__VA_ARGS__);                   \
-    switch (n * 1000 + blk * 100 + r) {                                                          \
-        case 64 * 1000 + 8 * 100 + 8: return FN<64, 8, 8, 0>(__VA_ARGS__);                     \
-        case 64 * 1000 + 8 * 100 + 16: return FN<64, 8, 16, 0>(__VA_ARGS__);                   \
-        case 64 * 1000 + 8 * 100 + 32: return FN<64, 8, 32, 0>(__VA_ARGS__);                   \
-        case 64 * 1000 + 16 * 100 + 8: return FN<64, 16, 8, 0>(__VA_ARGS__);                   \
-        case 64 * 1000 + 16 * 100 + 16: return FN<64, 16, 16, 0>(__VA_ARGS__);                 \
-        case 64 * 1000 + 16 * 100 + 32: return FN<64, 16, 32, 0>(__VA_ARGS__);                 \
-        case 128 * 1000 + 8 * 100 + 8: return FN<128, 8, 8, 0>(__VA_ARGS__);                   \
-        case 128 * 1000 + 8 * 100 + 16: return FN<128, 8, 16, 0>(__VA_ARGS__);                 \
-        case 128 * 1000 + 8 * 100 + 32: return FN<128, 8, 32, 0>(__VA_ARGS__);                 \
-        case 128 * 1000 + 16 * 100 + 8: return FN<128, 16, 8, 0>(__VA_ARGS__);                 \
-        case 128 * 1000 + 16 * 100 + 16: return FN<128, 16, 16, 0>(__VA_ARGS__);               \
-        case 128 * 1000 + 16 * 100 + 32: return FN<128, 16, 32, 0>(__VA_ARGS__);               \
-        case 256 * 1000 + 8 * 100 + 8: return FN<256, 8, 8, 0>(__VA_ARGS__);                   \
-        case 256 * 1000 + 8 * 100 + 16: return FN<256, 8, 16, 0>(__VA_ARGS__);                 \
-        case 256 * 1000 + 8 * 100 + 32: return FN<256, 8, 32, 0>(__VA_ARGS__);                 \
-        case 256 * 1000 + 16 * 100 + 8: return FN<256, 16, 8, 0>(__VA_ARGS__);                 \
-        case 256 * 1000 + 16 * 100 + 16: return FN<256, 16, 16, 0>(__VA_ARGS__);               \
-        case 256 * 1000 + 16 * 100 + 32: return FN<256, 16, 32, 0>(__VA_ARGS__);               \
-        default: return cudaErrorInvalidValue;                                                   \
+#define YGG_DISPATCH(FN, ...)                                                                          \
+    /* fast instances with the benchmark shapes fixed at compile time: c3 (n128 R16 R2=32, 4 layers, V <= 32), */ \
+    /* c4 (same, V = 256), c1 / c2 (n64 R8 R2=16, 2 / 4 layers, V = 256) */                                    \
+    if (n == 128 && blk == 16 && r == 16 && r2p == 32 && L == 4 && nv == 1) return FN<128, 16, 16, 32, 4, 1>(__VA_ARGS__); \
+    if (n == 128 && blk == 16 && r == 16 && r2p == 32 && L == 4 && nv == 8) return FN<128, 16, 16, 32, 4, 8>(__VA_ARGS__); \
+    if (n == 64 && blk == 16 && r == 8 && r2p == 16 && L == 2 && nv == 8) return FN<64, 16, 8, 16, 2, 8>(__VA_ARGS__);     \
+    if (n == 64 && blk == 16 && r == 8 && r2p == 16 && L == 4 && nv == 8) return FN<64, 16, 8, 16, 4, 8>(__VA_ARGS__);     \
+    switch (n * 1000 + blk * 100 + r) {                                                                \
+        case 64 * 1000 + 8 * 100 + 8: return FN<64, 8, 8, 0, 0, 0>(__VA_ARGS__);                     \
+        case 64 * 1000 + 8 * 100 + 16: return FN<64, 8, 16, 0, 0, 0>(__VA_ARGS__);                   \
+        case 64 * 1000 + 8 * 100 + 32: return FN<64, 8, 32, 0, 0, 0>(__VA_ARGS__);                   \
+        case 64 * 1000 + 16 * 100 + 8: return FN<64, 16, 8, 0, 0, 0>(__VA_ARGS__);                   \
+        case 64 * 1000 + 16 * 100 + 16: return FN<64, 16, 16, 0, 0, 0>(__VA_ARGS__);                 \
+        case 64 * 1000 + 16 * 100 + 32: return FN<64, 16, 32, 0, 0, 0>(__VA_ARGS__);                 \
+        case 128 * 1000 + 8 * 100 + 8: return FN<128, 8, 8, 0, 0, 0>(__VA_ARGS__);                   \
+        case 128 * 1000 + 8 * 100 + 16: return FN<128, 8, 16, 0, 0, 0>(__VA_ARGS__);                 \
+        case 128 * 1000 + 8 * 100 + 32: return FN<128, 8, 32, 0, 0, 0>(__VA_ARGS__);                 \
+        case 128 * 1000 + 16 * 100 + 8: return FN<128, 16, 8, 0, 0, 0>(__VA_ARGS__);                 \
+        case 128 * 1000 + 16 * 100 + 16: return FN<128, 16, 16, 0, 0, 0>(__VA_ARGS__);               \
+        case 128 * 1000 + 16 * 100 + 32: return FN<128, 16, 32, 0, 0, 0>(__VA_ARGS__);               \
+        case 256 * 1000 + 8 * 100 + 8: return FN<256, 8, 8, 0, 0, 0>(__VA_ARGS__);                   \
+        case 256 * 1000 + 8 * 100 + 16: return FN<256, 8, 16, 0, 0, 0>(__VA_ARGS__);                 \
+        case 256 * 1000 + 8 * 100 + 32: return FN<256, 8, 32, 0, 0, 0>(__VA_ARGS__);                 \
+        case 256 * 1000 + 16 * 100 + 8: return FN<256, 16, 8, 0, 0, 0>(__VA_ARGS__);                 \
+        case 256 * 1000 + 16 * 100 + 16: return FN<256, 16, 16, 0, 0, 0>(__VA_ARGS__);               \
+        case 256 * 1000 + 16 * 100 + 32: return FN<256, 16, 32, 0, 0, 0>(__VA_ARGS__);               \
+        default: return cudaErrorInvalidValue;                                                         \
     }
 
 cudaError_t launch_step(int n, int blk, int r, int r2p, const DevModel &dm, int B, const int32_t *tok, const int8_t *sin,
                         int8_t *sout, float *lg, int32_t *routes, int32_t *acc, uint32_t rec_max, int warps,
                         int slots, int grid_cap, cudaStream_t st) {
+    const int L = dm.L, nv = dm.VP / 32;
     YGG_DISPATCH(launch_step_t, dm, B, tok, sin, sout, lg, routes, acc, rec_max, warps, slots, grid_cap, st)
 }
 
 cudaError_t launch_score(int n, int blk, int r, int r2p, const DevModel &dm, int B, int T, const int32_t *tok, int8_t *state,
                          double *bits, uint32_t rec_max, int warps, int slots, int grid_cap, cudaStream_t st) {
+    const int L = dm.L, nv = dm.VP / 32;
     YGG_DISPATCH(launch_score_t, dm, B, T, tok, state, bits, rec_max, warps, slots, grid_cap, st)
 }
 
