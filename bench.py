@@ -58,11 +58,46 @@ def build_model_file(workload, seed, rank, world, dist):
     path = d / f"{workload}_s{seed}.bin"
     if rank == 0 and not path.exists():
         tmp = path.with_suffix(f".tmp{os.getpid()}")
-        write_model(synth.workload_layers(w, seed=seed), np.linspace(-1, 1, w.shape.vocab), tmp)
+        layers = synth.workload_layers(w, seed=seed)
+        ob = np.linspace(-1, 1, w.shape.vocab)
+        if w.leaves == "zipf":
+            calibrate_zipf(w, layers, ob, tmp, seed)
+        write_model(layers, ob, tmp)
         os.replace(tmp, path)
     if world > 1:
         dist.barrier()
     return w, path
+
+
+def calibrate_zipf(w, layers, ob, tmp, seed, streams=65536, prime=48, snapshots=(48, 56, 64), s=1.1):
+    """Set each routed layer's thresholds (the same for every token) so that its leaf usage follows Zipf(s) over a
+    seeded random leaf order: layer by layer, run the model on the GPU (this library's step) to sample the new state
+    of the layer below in steady state, then place each node's threshold at the score quantile that sends the Zipf
+    share of its subtree mass to the right (synth.zipf_thresholds). Untimed set-up of the benchmark model."""
+    import torch
+
+    from yggdrasil_b200 import Yggdrasil, synth
+    from yggdrasil_b200.ygg1 import write_model
+    E = 2 ** w.shape.router_depth
+    for l in range(1, len(layers)):
+        write_model(layers, ob, tmp)
+        model = Yggdrasil.load(tmp, backend="b200")
+        dev = model.device
+        x = torch.as_tensor(synth.workload_tokens(w, max(snapshots), streams, seed=77)).to(dev)
+        st = model.init_state(streams)
+        lg = torch.empty(streams, model.vocab, dtype=torch.float32, device=dev)
+        qb = []
+        for t in range(max(snapshots)):
+            model.step_into(x[t], st, st, lg)
+            if t + 1 in snapshots:
+                qb.append(st[:, l - 1].cpu().numpy())
+        del model
+        torch.cuda.empty_cache()
+        qb = np.concatenate(qb)
+        q = layers[l]
+        rho = synth.rho_f32(qb, q.rms_eps, q.state_r2)
+        thr = synth.zipf_thresholds(q.router_weight, qb, rho, synth.zipf_leaf_probs(E, s, seed + 100 + l))
+        q.router_threshold = np.ascontiguousarray(np.broadcast_to(thr, (w.shape.vocab, E - 1)), dtype=np.float32)
 
 
 class ClockSampler:
@@ -272,13 +307,24 @@ def main():
     per_launch_ms = ms / K
 
     # ---- end to end through the public API: pinned host tokens in, logits out, every step
+    # (a serving loop: step t+1 runs while the logits of step t travel to the host on a copy stream; the token
+    # upload happens on the compute stream inside step())
     ke = min(K, 256)
     h_tok = torch.as_tensor(x[W:W + ke]).pin_memory()
-    h_lg = torch.empty(B, model.vocab, dtype=torch.float32).pin_memory()
+    h_lg = [torch.empty(B, model.vocab, dtype=torch.float32).pin_memory() for _ in range(2)]
+    copy_stream = torch.cuda.Stream(dev)
+
+    def e2e_step(i, st):
+        lg, st = model.step(h_tok[i % ke], st)
+        copy_stream.wait_stream(stream)
+        with torch.cuda.stream(copy_stream):
+            h_lg[i % 2].copy_(lg, non_blocking=True)
+        lg.record_stream(copy_stream)
+        return st
+
     st = state.clone()
     for i in range(W):
-        lg, st = model.step(h_tok[i % ke], st)
-        h_lg.copy_(lg, non_blocking=True)
+        st = e2e_step(i, st)
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
@@ -286,8 +332,8 @@ def main():
     a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a0.record(stream)
     for i in range(ke):
-        lg, st = model.step(h_tok[i], st)
-        h_lg.copy_(lg, non_blocking=True)
+        st = e2e_step(i, st)
+    stream.wait_stream(copy_stream)
     a1.record(stream)
     torch.cuda.synchronize(dev)
     ems = a0.elapsed_time(a1)
@@ -360,6 +406,8 @@ def main():
                        else "uniform bytes", "l2": "inputs larger than L2 (model file > 126 MB)",
                        "parallelism": f"streams sharded, {world} replica(s)", "primed_steps": args.prime,
                        "effective_leaves_per_layer": eff,
+                       "leaf_usage": w.leaves if w.leaves != "zipf" else
+                       f"Zipf(1.1) over a seeded leaf order (target {synth.effective_leaves(synth.zipf_leaf_probs(1 << model.depth, 1.1, 0)):.0f} effective leaves)",
                        "note": w.note},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_kind": kind},

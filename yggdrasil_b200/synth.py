@@ -118,6 +118,7 @@ class Workload:
     steps: int
     tokens: str                  # "uniform" or "dna"
     note: str = ""
+    leaves: str = "random"       # "random": the generator's thresholds; "zipf": calibrated to Zipf(1.1) leaf usage
 
 
 WORKLOADS = {
@@ -129,10 +130,11 @@ WORKLOADS = {
     "c3": Workload("c3-200M-dna-d128", ModelShape(128, 16, 13, 5, 4, 16, 32), 65536, 512, "dna",
                    "d_state 128 in place of 96 (YGG1 allows 64/128/256)"),
     # V256 L4 d128 D13 R16 R2=32, table storage (1892 MB)
-    "c4": Workload("c4-730M-enwik8", ModelShape(128, 16, 13, 256, 4, 16, 32), 262144, 256, "uniform"),
+    "c4": Workload("c4-730M-enwik8", ModelShape(128, 16, 13, 256, 4, 16, 32), 262144, 256, "uniform",
+                   "table storage, 1892 MB; thresholds calibrated to Zipf(1.1) leaf usage", leaves="zipf"),
     # the same model with factored input storage k=32 (390 MB)
     "c4f": Workload("c4-730M-enwik8-factored", ModelShape(128, 16, 13, 256, 4, 16, 32, input_rank=32), 262144, 256,
-                    "uniform"),
+                    "uniform", "factored storage k=32, 390 MB; Zipf(1.1) leaf usage", leaves="zipf"),
 }
 
 
@@ -147,6 +149,69 @@ def workload_tokens(w: Workload, streams: int, steps: int, seed: int = 0) -> np.
     if w.tokens == "dna":
         return rng.choice(len(DNA_P), size=(streams, steps), p=DNA_P).astype(np.int32)
     return rng.integers(0, w.shape.vocab, (streams, steps)).astype(np.int32)
+
+
+def zipf_leaf_probs(n_leaves: int, s: float, seed: int) -> np.ndarray:
+    """Zipf(s) probabilities over the leaves in a seeded random order: leaf perm[i] gets rank i + 1."""
+    p = 1.0 / np.arange(1, n_leaves + 1, dtype=np.float64) ** s
+    out = np.empty(n_leaves)
+    out[np.random.default_rng(seed).permutation(n_leaves)] = p / p.sum()
+    return out
+
+
+def effective_leaves(p: np.ndarray) -> float:
+    """exp of the entropy of a leaf distribution (the number of equally used leaves with the same entropy)."""
+    p = p[p > 0] / p.sum()
+    return float(np.exp(-(p * np.log(p)).sum()))
+
+
+def rho_f32(qb: np.ndarray, eps, r2b=None) -> np.ndarray:
+    """The router's f32 rho of int8 states qb (S, n), as the reference computes it (cpu/ygg.cpp:248-266)."""
+    n = qb.shape[1]
+    q = qb.astype(np.int64)
+    if r2b is None:
+        ss = (q * q).sum(1).astype(f32)
+    else:
+        g = (q * q).reshape(len(q), -1, STATE_GROUP).sum(-1)
+        ss = np.zeros(len(q), f32)
+        for j in range(g.shape[1]):
+            ss = (ss + f32(r2b[j]) * g[:, j].astype(f32)).astype(f32)
+    return (f32(1) / np.sqrt(ss * f32(1.0 / n) + f32(eps))).astype(f32)
+
+
+def zipf_thresholds(router_weight: np.ndarray, qb: np.ndarray, rho: np.ndarray, leaf_p: np.ndarray) -> np.ndarray:
+    """Per-node thresholds (2^D - 1,) that route the sample states qb (S, n) with rho (S,) to leaf frequencies leaf_p
+    (2^D,): top-down, node ix sends the share mass(right subtree) / mass(subtree) of the samples reaching it to the
+    right, the threshold being that quantile of their f32 scores f32(w_ix . qb) * rho. Nodes no sample reaches get 0."""
+    E = len(leaf_p)
+    depth = E.bit_length() - 1
+    mass = np.zeros(2 * E)
+    mass[E:] = leaf_p
+    for ix in range(E - 1, 0, -1):
+        mass[ix] = mass[2 * ix] + mass[2 * ix + 1]
+    thr = np.zeros(E, f32)                                   # heap slots 1 .. E-1
+    w = np.zeros((E, router_weight.shape[1]), np.int64)
+    w[1:] = router_weight
+    node = np.ones(len(qb), np.int64)
+    q = qb.astype(np.int64)
+    for _ in range(depth):
+        score = (np.einsum("sn,sn->s", w[node], q).astype(f32) * rho).astype(f32)
+        order = np.lexsort((score, node))
+        ns, sc = node[order], score[order]
+        starts = np.flatnonzero(np.r_[True, ns[1:] != ns[:-1]])
+        ends = np.r_[starts[1:], len(ns)]
+        for a, b in zip(starts, ends):
+            ix = ns[a]
+            p_right = mass[2 * ix + 1] / mass[ix] if mass[ix] > 0 else 0.5
+            k = int(np.clip(round((b - a) * (1.0 - p_right)), 0, b - a))  # k samples stay left
+            if k <= 0:
+                thr[ix] = np.nextafter(sc[a], f32(-np.inf))
+            elif k >= b - a:
+                thr[ix] = sc[b - 1]
+            else:
+                thr[ix] = sc[a + k - 1]                      # right iff score > thr: the top (b - a - k) go right
+        node = 2 * node + (score > thr[node])
+    return thr[1:]
 
 
 def gathered_bytes_per_token(shape: ModelShape, with_io: bool = True) -> int:
