@@ -89,6 +89,17 @@ YGG_API int ygg_step_debug(const ygg_model *m, int batch, const int32_t *d_token
 YGG_API int ygg_score(const ygg_model *m, int batch, int steps, const int32_t *d_tokens, int8_t *d_state, double *d_bits,
               void *stream);
 
+/* Bytes of device workspace ygg_score_grouped needs for `batch` rows. */
+YGG_API size_t ygg_score_grouped_workspace(const ygg_model *m, int batch);
+
+/* ygg_score computed step by step with the streams of each layer bucketed by leaf: a leaf that at least `min_group`
+ * streams share runs its update as int8 tensor-core GEMMs (tcgen05, n <= 128), the others the per-stream update.
+ * Same arguments and bit-identical results as ygg_score; d_workspace: ygg_score_grouped_workspace(m, batch) bytes of
+ * device memory owned by the caller (256-byte aligned). The grouping is new: the reference has no counterpart; its
+ * result is defined by yggdrasil/inference.py:179-188 and cpu/ygg.cpp:441-459,513-517 as for ygg_score. */
+YGG_API int ygg_score_grouped(const ygg_model *m, int batch, int steps, const int32_t *d_tokens, int8_t *d_state,
+                              double *d_bits, int min_group, void *d_workspace, size_t workspace_bytes, void *stream);
+
 /* Read (and with clear != 0, reset) the model's device status word after the calls queued on `stream`:
  * 0 when every call since the last clear ran clean, else a negative YGG_E_* code (token out of range, or a bounded
  * wait that gave up). Synchronises `stream`. */

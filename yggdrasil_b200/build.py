@@ -15,8 +15,8 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libygg_b200.so"
-SOURCES = [CSRC / "ygg_load.cu", CSRC / "ygg_step.cu"]
-HEADERS = [CSRC / "ygg_model.h", ROOT / "include" / "ygg_b200.h"]
+SOURCES = [CSRC / "ygg_load.cu", CSRC / "ygg_step.cu", CSRC / "ygg_grouped.cu"]
+HEADERS = [CSRC / "ygg_model.h", CSRC / "ygg_device.cuh", ROOT / "include" / "ygg_b200.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 # no --use_fast_math and no FMA contraction: every f32 op of the step is single-rounded as in the reference
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "--fmad=false", "-Xcompiler", "-fPIC", "-cudart", "static",
@@ -41,20 +41,22 @@ def build(verbose: bool = False, force: bool = False) -> Path:
     """Compile the library if a source is newer than it; returns its path."""
     if not force and not stale():
         return LIB
-    objs = []
+    objs, procs = [], []
     tmp = PKG / "_build"
     tmp.mkdir(exist_ok=True)
-    for src in SOURCES:
+    for src in SOURCES:   # the translation units compile in parallel
         obj = tmp / (src.stem + ".o")
         cmd = [nvcc(), *ARCH, *FLAGS, "-I", str(ROOT / "include"), "-c", str(src), "-o", str(obj)]
         if verbose:
             cmd += ["-Xptxas", "-v"]
-        r = subprocess.run(cmd, capture_output=True, text=True)
-        if r.returncode:
-            raise RuntimeError(f"nvcc failed on {src.name}:\n{r.stdout}\n{r.stderr}")
-        if verbose:
-            print(r.stderr, file=sys.stderr)
+        procs.append((src, subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)))
         objs.append(str(obj))
+    for src, p in procs:
+        out, err = p.communicate()
+        if p.returncode:
+            raise RuntimeError(f"nvcc failed on {src.name}:\n{out}\n{err}")
+        if verbose:
+            print(err, file=sys.stderr)
     cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", str(LIB), *objs]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode:

@@ -22,6 +22,9 @@ cudaError_t launch_step(int n, int blk, int r, int r2p, const DevModel &dm, int 
 cudaError_t launch_score(int n, int blk, int r, int r2p, const DevModel &dm, int B, int T, const int32_t *tok, int8_t *state,
                          double *bits, uint32_t rec_max, int warps, int slots, int grid_cap, cudaStream_t st);
 size_t block_smem_bytes(uint32_t rec_max, int n, int slots, int warps, int state_bytes);
+size_t grouped_ws_bytes(const DevModel &m, int B);
+cudaError_t run_grouped(int n, int blk, int r, int r2p, const DevModel &m, int B, int T, const int32_t *tok,
+                        int8_t *state, double *bits, void *workspace, int G, int sm_count, cudaStream_t st);
 }  // namespace ygg
 
 using namespace ygg;
@@ -467,6 +470,26 @@ int ygg_score(const ygg_model *m, int batch, int steps, const int32_t *d_tokens,
     const cudaError_t e = launch_score(m->host.n, m->host.b, m->host.R, m->host.R2P, m->host, batch, steps, d_tokens, d_state,
                                        d_bits, m->rec_max, m->warps_score, m->slots_score, m->grid_cap,
                                        (cudaStream_t)stream);
+    restore_device(m, prev);
+    return e == cudaSuccess ? YGG_OK : YGG_E_CUDA;
+}
+
+size_t ygg_score_grouped_workspace(const ygg_model *m, int batch) {
+    if (!m || batch < 0) return 0;
+    return grouped_ws_bytes(m->host, batch);
+}
+
+int ygg_score_grouped(const ygg_model *m, int batch, int steps, const int32_t *d_tokens, int8_t *d_state,
+                      double *d_bits, int min_group, void *d_workspace, size_t workspace_bytes, void *stream) {
+    if (!m || batch < 0 || steps < 0) return YGG_E_ARG;
+    if (batch == 0) return YGG_OK;
+    if (!d_tokens || !d_bits || !d_workspace || ((uintptr_t)d_workspace & 255) ||
+        workspace_bytes < grouped_ws_bytes(m->host, batch))
+        return YGG_E_ARG;
+    int prev;
+    if (set_device(m, &prev)) return YGG_E_CUDA;
+    const cudaError_t e = run_grouped(m->host.n, m->host.b, m->host.R, m->host.R2P, m->host, batch, steps, d_tokens,
+                                      d_state, d_bits, d_workspace, min_group, m->sm_count, (cudaStream_t)stream);
     restore_device(m, prev);
     return e == cudaSuccess ? YGG_OK : YGG_E_CUDA;
 }

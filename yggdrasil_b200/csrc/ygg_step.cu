@@ -22,97 +22,13 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "ygg_model.h"
+#include "ygg_device.cuh"
 
 namespace ygg {
 
-constexpr unsigned kFull = 0xFFFFFFFFu;
-constexpr int kMaxClassesPerLane = 8;   // VP <= 256
-constexpr long long kWaitCycles = 2000000000LL;
-constexpr int kLook = 3;                // router levels per round of loads
-constexpr int kLookRows = (1 << kLook) - 1;
 // blocks of 8 warps per SM the register budget is sized for: 4 (64 registers a thread) for n <= 128; n = 256 needs
 // more registers per lane (8 coordinates) and runs 2 blocks
 template <int N> constexpr int blocks_per_sm() { return N >= 256 ? 2 : 4; }
-
-// ------------------------------------------------------------------------------------------------ PTX helpers
-
-__device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-// try_wait suspends the thread until the phase completes or the hint (ns) runs out, so a waiting warp costs few
-// issue slots
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity), "r"(1000000u)
-        : "memory");
-    return ok != 0;
-}
-// 1-D bulk copy global -> this CTA's shared memory (no multicast), completion counted on the mbarrier.
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-                 "l"(src), "r"(bytes), "r"(bar)
-                 : "memory");
-}
-
-// Bounded wait for the phase `parity` of an mbarrier: false after ~1 s (the caller reports a timeout).
-__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const long long t0 = clock64();
-    while (!mbar_try_wait(bar, parity))
-        if (clock64() - t0 > kWaitCycles) return false;
-    return true;
-}
-
-// f32 -> int32 rounded half to even; NaN and values outside int32 give INT_MIN, as x86 cvtps2dq (the reference's
-// _mm512_cvtps_epi32), which the callers then clamp.
-__device__ __forceinline__ int cvt_rne(float v) {
-    return (v >= -2147483648.0f && v < 2147483648.0f) ? __float2int_rn(v) : (int)0x80000000;
-}
-__device__ __forceinline__ float i2f(int v) { return __int2float_rn(v); }
-__device__ __forceinline__ int clampi(int v, int lo, int hi) { return min(max(v, lo), hi); }
-__device__ __forceinline__ int dot16(const uint4 &a, const uint4 &b, int s) {
-    s = __dp4a((int)a.x, (int)b.x, s);
-    s = __dp4a((int)a.y, (int)b.y, s);
-    s = __dp4a((int)a.z, (int)b.z, s);
-    return __dp4a((int)a.w, (int)b.w, s);
-}
-
-// --------------------------------------------------------------------------------------------- lane state words
-
-// The C state bytes of one lane as int32 words: C = 2 uses the low half of one word (high half zero).
-template <int C> struct LaneQ { uint32_t w[C >= 4 ? C / 4 : 1]; };
-
-template <int C> __device__ __forceinline__ LaneQ<C> load_q(const int8_t *p) {
-    LaneQ<C> q;
-    if constexpr (C == 2) q.w[0] = *(const uint16_t *)p;
-    else if constexpr (C == 4) q.w[0] = *(const uint32_t *)p;
-    else { const uint2 v = *(const uint2 *)p; q.w[0] = v.x; q.w[1] = v.y; }
-    return q;
-}
-template <int C> __device__ __forceinline__ void store_q(int8_t *p, const LaneQ<C> &q) {
-    if constexpr (C == 2) *(uint16_t *)p = (uint16_t)q.w[0];
-    else if constexpr (C == 4) *(uint32_t *)p = q.w[0];
-    else *(uint2 *)p = make_uint2(q.w[0], q.w[1]);
-}
-template <int C> __device__ __forceinline__ int dot_q(const LaneQ<C> &a, const LaneQ<C> &b) {
-    int s = 0;
-#pragma unroll
-    for (int i = 0; i < (C >= 4 ? C / 4 : 1); i++) s = __dp4a((int)a.w[i], (int)b.w[i], s);
-    return s;
-}
 
 // ------------------------------------------------------------------------------------------------ shared memory
 
@@ -152,115 +68,6 @@ __device__ __forceinline__ int slot_claim(const Pool &p, int home, int warp) {
     }
     __threadfence_block();
     return i;
-}
-
-// ------------------------------------------------------------------------------------------------ one layer
-
-// rho = 1 / sqrt(f32(sum q^2) * (1/n) + eps), or with group scales the sequential f32 sum over groups of 16 of
-// r2[g] * f32(S_g) (cpu/ygg.cpp:248-266).
-template <int N>
-__device__ __forceinline__ float rms_rho(const LaneQ<N / 32> &qb, const float *r2b, float eps) {
-    constexpr int C = N / 32;
-    const float inv_n = 1.0f / (float)N;
-    int part = dot_q<C>(qb, qb);
-    if (r2b == nullptr) {
-        const int S = __reduce_add_sync(kFull, part);
-        return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(i2f(S), inv_n), eps)));
-    }
-    constexpr int kLanesPerGroup = 16 / C;
-#pragma unroll
-    for (int off = 1; off < kLanesPerGroup; off <<= 1) part += __shfl_xor_sync(kFull, part, off);
-    float s = 0.0f;
-#pragma unroll
-    for (int g = 0; g < N / 16; g++) {
-        const int sg = __shfl_sync(kFull, part, g * kLanesPerGroup);
-        s = __fadd_rn(s, __fmul_rn(__ldg(r2b + g), i2f(sg)));
-    }
-    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(s, inv_n), eps)));
-}
-
-// Heap-order descent from node 1, right iff f32(w_ix . qb) * rho > thr[x][ix] (cpu/ygg.cpp:271-280), kLook levels
-// per round of loads. Row k of a round's subtree (k = 0: ix; 1-2: 2ix + k-1; 3-6: 4ix + k-3, i.e. ix * 2^lvl(k) +
-// k + 1 - 2^lvl(k)) is read by the LPR = n/16 lanes of group k % RPI in load k / RPI, 16 bytes each; every lane of
-// the group also reads the row's threshold (one broadcast transaction), so each lane can decide its group's row and
-// one ballot per load carries every decision. qrow: the lane's 16 bytes of qb at 16 (lane % LPR). Returns the leaf
-// node index in [E, 2E).
-template <int N>
-__device__ __forceinline__ int route_look(const int8_t *__restrict__ w, const float *__restrict__ thr_x, int depth,
-                                          const uint4 &qrow, float rho, int lane) {
-    constexpr int LPR = N / 16;                 // lanes per row
-    constexpr int RPI = 32 / LPR;               // rows per warp-wide 16-byte load
-    constexpr int NI = (kLookRows + RPI - 1) / RPI;
-    const int g = lane / LPR;
-    const int8_t *wl = w + 16 * (lane % LPR);
-    // per-lane constants of the subtree rows this lane reads: row = ix * mul + add
-    int mul[NI], add[NI], kk[NI];
-#pragma unroll
-    for (int i = 0; i < NI; i++) {
-        const int k = i * RPI + g;
-        const int lvl = k == 0 ? 0 : k < 3 ? 1 : 2;
-        kk[i] = k;
-        mul[i] = 1 << lvl;
-        add[i] = k + 1 - (1 << lvl);
-    }
-    int ix = 1;
-    for (int d = 0; d < depth; d += kLook) {
-        const int lv = min(kLook, depth - d);
-        const int nrows = (1 << lv) - 1;
-        uint4 v[NI];
-        float t[NI];
-#pragma unroll
-        for (int i = 0; i < NI; i++) {
-            const int row = ix * mul[i] + add[i];
-            v[i] = make_uint4(0, 0, 0, 0);
-            t[i] = 0.0f;
-            if (kk[i] < nrows) {
-                v[i] = __ldg((const uint4 *)(wl + (size_t)row * N));
-                t[i] = __ldg(thr_x + row);
-            }
-        }
-        // decisions of rows k = RPI i + g, as bit LPR (RPI i + g) of a 64-bit word (each group's LPR lanes agree)
-        uint64_t bits = 0;
-        constexpr int kFirst = LPR == 16 ? 2 : NI;      // loads whose ballots go into `bits` directly
-#pragma unroll
-        for (int i = 0; i < kFirst; i++) {
-            int dot = dot16(v[i], qrow, 0);
-#pragma unroll
-            for (int off = 1; off < LPR; off <<= 1) dot += __shfl_xor_sync(kFull, dot, off);
-            const uint32_t bal = __ballot_sync(kFull, __fmul_rn(i2f(dot), rho) > t[i]);
-            if constexpr (LPR >= 8) {
-                bits |= (uint64_t)bal << (32 * i);      // row k at bit 8 k (N = 128) or 16 k (N = 256, i < 2)
-            } else {
-                bits |= bal;                            // N = 64: one load, row k at bit 4 k
-            }
-        }
-        if constexpr (LPR == 16) {                      // N = 256: rows 4-6 sit in loads 2-3; fold them in
-            uint32_t hi = 0;
-#pragma unroll
-            for (int i = 2; i < NI; i++) {
-                int dot = dot16(v[i], qrow, 0);
-#pragma unroll
-                for (int off = 1; off < LPR; off <<= 1) dot += __shfl_xor_sync(kFull, dot, off);
-                const uint32_t bal = __ballot_sync(kFull, __fmul_rn(i2f(dot), rho) > t[i]);
-                hi |= ((bal & 1u) | ((bal >> 15) & 2u)) << (2 * (i - 2));
-            }
-            // rows 0-3 from loads 0-1 at bits 0, 16, 32, 48 -> compact to bits 0-3, then rows 4-6
-            const uint32_t lo = (uint32_t)(bits & 1u) | (uint32_t)((bits >> 15) & 2u) | (uint32_t)((bits >> 30) & 4u) |
-                                (uint32_t)((bits >> 45) & 8u);
-            bits = lo | (hi << 4);
-        }
-        constexpr int kStride = LPR == 16 ? 1 : LPR;   // bit distance between consecutive rows in `bits`
-        int k = 0;
-#pragma unroll
-        for (int j = 0; j < kLook; j++) {
-            if (j < lv) {
-                const int b = (int)((bits >> (kStride * k)) & 1u);
-                ix = 2 * ix + b;
-                k = 2 * k + 1 + b;
-            }
-        }
-    }
-    return ix;
 }
 
 struct StepOut {
@@ -338,165 +145,32 @@ __device__ __forceinline__ bool layer_step(TokenCtx<N / 32> &t, const int l, flo
     const int16_t *trow = (const int16_t *)(rec + (pool.slot_bytes - 2 * N));
     const uint32_t bar = pool.bars + 8u * slot;
     // -- layer input codes while the copy is in flight (cpu/ygg.cpp:285-296)
-    if (low) {
-        const int R2P = R2T ? R2T : m.R2P;
-        for (int k = lane; k < R2P; k += 32) {
-            const int8_t *vk = y.vl + (size_t)k * 16;
-            int a = 0;
-#pragma unroll
-            for (int j = 0; j < N / 16; j++)
-                a = dot16(__ldg((const uint4 *)(vk + (size_t)j * R2P * 16)), *(const uint4 *)(sc.qb + 16 * j), a);
-            const float zf = __fmul_rn(__fmul_rn(i2f(a), __ldg(y.mv + k)), rho);
-            sc.zl[k] = (int8_t)(k < m.R2 ? clampi(cvt_rne(zf), -127, 127) : 0);
-        }
-    }
+    if (low) layer_input_codes<N, R2T>(m, y, sc.qb, rho, sc.zl, lane);
     store_q<C>(sc.qold + C * lane, qold);
     __syncwarp();
     if (!__all_sync(kFull, mbar_wait_bounded(bar, parity))) return false;
 
-    // -- transition: acc_i = (sum_j A16[i][j] q[j] + 2^(shift-1)) >> shift over the row's block (cpu/ygg.cpp:312-332)
     int acc[C];
-    {
-        const int blk0 = ((C * lane) / BLK) * BLK;
-        uint32_t qblk[BLK / 4];
-        if constexpr (BLK == 8) {
-            const uint2 v = *(const uint2 *)(sc.qold + blk0);
-            qblk[0] = v.x; qblk[1] = v.y;
-        } else {
-            const uint4 v = *(const uint4 *)(sc.qold + blk0);
-            qblk[0] = v.x; qblk[1] = v.y; qblk[2] = v.z; qblk[3] = v.w;
-        }
-        constexpr int kWords = C * BLK / 2;            // int16 pairs of the lane
-        uint32_t aw[kWords];
-        const uint8_t *pa = rec + y.off_a + 16 * lane;
-#pragma unroll
-        for (int j = 0; j < kWords / 4; j++) {
-            const uint4 v = *(const uint4 *)(pa + 512 * j);
-            aw[4 * j] = v.x; aw[4 * j + 1] = v.y; aw[4 * j + 2] = v.z; aw[4 * j + 3] = v.w;
-        }
-        const int rnd = 1 << (m.shift - 1), sh = m.shift;
-#pragma unroll
-        for (int ii = 0; ii < C; ii++) {
-            int s = 0;
-#pragma unroll
-            for (int p = 0; p < BLK / 2; p++) {
-                const uint32_t a = aw[ii * (BLK / 2) + p];
-                s = (p & 1) ? __dp2a_hi((int)a, (int)qblk[p >> 1], s) : __dp2a_lo((int)a, (int)qblk[p >> 1], s);
-            }
-            acc[ii] = (s + rnd) >> sh;
-        }
-    }
-    // -- input: table row (cpu/ygg.cpp:334-337) or factored (cpu/ygg.cpp:339-358)
-    if (has_table) {
-#pragma unroll
-        for (int ii = 0; ii < C; ii++) acc[ii] += trow[C * lane + ii];
-    } else {
-        const int KP = m.KP;
-        const uint8_t *pf = rec + y.off_f + 16 * lane;
-        const int8_t *v = y.vt + (size_t)x * KP;
-        const float su = *(const float *)(rec + y.off_su);
-        const int16_t *cb = (const int16_t *)(rec + y.off_cb);
-#pragma unroll
-        for (int ii = 0; ii < C; ii++) {
-            int lt = 0;
-            for (int j = 0; j < KP / 16; j++)
-                lt = dot16(*(const uint4 *)(pf + 512 * (ii * (KP / 16) + j)), __ldg((const uint4 *)(v + 16 * j)), lt);
-            const float mul = __fmul_rn(su, __ldg(y.mt + C * lane + ii));
-            acc[ii] += cvt_rne(__fmul_rn(i2f(lt), mul)) + cb[C * lane + ii];
-        }
-    }
-    // -- layer input: acc_i += rint(f32(U'_r zl) m_ul) (cpu/ygg.cpp:360-377)
-    if (low) {
-        const int R2P = R2T ? R2T : m.R2P;
-        const uint8_t *pu = rec + y.off_u + 16 * lane;
-#pragma unroll
-        for (int ii = 0; ii < C; ii++) {
-            int la = 0;
-#pragma unroll
-            for (int j = 0; j < (R2T ? R2T / 16 : 4); j++)
-                if (R2T || j < R2P / 16)
-                    la = dot16(*(const uint4 *)(pu + 512 * (ii * (R2P / 16) + j)), *(const uint4 *)(sc.zl + 16 * j), la);
-            const float mu = y.mulv ? __ldg(y.mulv + C * lane + ii) : y.layer_input_scale;
-            acc[ii] += cvt_rne(__fmul_rn(i2f(la), mu));
-        }
-    }
-    // -- saturate to the new int8 state (cpu/ygg.cpp:388)
-    LaneQ<C> qn{};
-#pragma unroll
-    for (int ii = 0; ii < C; ii++) {
-        const uint32_t b = (uint32_t)(uint8_t)(int8_t)clampi(acc[ii], -128, 127);
-        qn.w[ii >> 2] |= b << (8 * (ii & 3));
-    }
+    LaneQ<C> qn;
+    leaf_update<N, BLK, R2T>(m, y, rec, has_table ? trow : nullptr, x, sc.qold, sc.zl, low, lane, acc, qn);
     store_q<C>(q_out + (size_t)l * N + C * lane, qn);
     if (dbg.routes != nullptr && lane == 0) dbg.routes[l] = r;
     if (dbg.acc != nullptr) {
 #pragma unroll
         for (int ii = 0; ii < C; ii++) dbg.acc[(size_t)l * N + C * lane + ii] = acc[ii];
     }
-
-    // -- readout z = P_r q, zq = sat(rint(f32(z) m_z)) (cpu/ygg.cpp:395-420)
-    int myz = 0;
-    float mz = y.readout_scale;
-    {
-        const uint8_t *pp = rec + y.off_p + 16 * lane;
-        constexpr int kPWords = R * C / 4;
-        uint32_t pw[kPWords];
-#pragma unroll
-        for (int j = 0; j < kPWords / 4; j++) {
-            const uint4 v = *(const uint4 *)(pp + 512 * j);
-            pw[4 * j] = v.x; pw[4 * j + 1] = v.y; pw[4 * j + 2] = v.z; pw[4 * j + 3] = v.w;
-        }
-        if (y.off_mz != kNone && lane < R) mz = *(const float *)(rec + y.off_mz + 4 * lane);
-        // the slot is free once its bytes are in registers: flip its parity and hand it back
-        __syncwarp();
-        if (lane == 0) {
-            pool.phase[slot] = (int)(parity ^ 1u);
-            __threadfence_block();
-            atomicExch(pool.owner + slot, -1);
-        }
-#pragma unroll
-        for (int rr = 0; rr < R; rr++) {
-            int part;
-            if constexpr (C == 2) {
-                const uint32_t word = pw[rr >> 1];
-                part = __dp4a((int)((rr & 1) ? (word >> 16) : (word & 0xFFFFu)), (int)qn.w[0], 0);
-            } else {
-                part = 0;
-#pragma unroll
-                for (int w = 0; w < C / 4; w++) part = __dp4a((int)pw[rr * (C / 4) + w], (int)qn.w[w], part);
-            }
-            const int z = __reduce_add_sync(kFull, part);
-            if (lane == rr) myz = z;
-        }
-    }
-    if (lane < R) sc.zq[lane] = (int8_t)clampi(cvt_rne(__fmul_rn(i2f(myz), mz)), -127, 127);
+    const ReadoutWords<N, R> ro = load_readout<N, R>(y, rec, lane);
+    // the slot is free once its bytes are in registers: flip its parity and hand it back
     __syncwarp();
-    // -- head: lg[c] += f32(Q_c . zq) * s (cpu/ygg.cpp:421-434)
-    {
-        uint32_t zw[R / 4];
-#pragma unroll
-        for (int j = 0; j < R / 4; j++) zw[j] = *(const uint32_t *)(sc.zq + 4 * j);
-#pragma unroll
-        for (int c = 0; c < (NVT ? NVT : kMaxClassesPerLane); c++) {
-            if (NVT || c < nv) {
-                const int cls = 32 * c + lane;
-                const int8_t *qrow = y.unembed + (size_t)cls * R;
-                int a = 0;
-                if constexpr (R == 8) {
-                    const uint2 v = __ldg((const uint2 *)qrow);
-                    a = __dp4a((int)v.x, (int)zw[0], a);
-                    a = __dp4a((int)v.y, (int)zw[1], a);
-                } else {
-#pragma unroll
-                    for (int j = 0; j < R / 16; j++)
-                        a = dot16(__ldg((const uint4 *)(qrow + 16 * j)),
-                                  make_uint4(zw[4 * j], zw[4 * j + 1], zw[4 * j + 2], zw[4 * j + 3]), a);
-                }
-                const float s = y.sqv ? __ldg(y.sqv + cls) : y.unembed_scale;
-                lg[c] = __fadd_rn(lg[c], __fmul_rn(i2f(a), s));
-            }
-        }
+    if (lane == 0) {
+        pool.phase[slot] = (int)(parity ^ 1u);
+        __threadfence_block();
+        atomicExch(pool.owner + slot, -1);
     }
+    const int zq = readout_code<N, R>(ro, qn, lane);
+    if (lane < R) sc.zq[lane] = (int8_t)zq;
+    __syncwarp();
+    head_accumulate<R, NVT>(m, y, sc.zq, lg, lane);
     qbelow = qn;
     __syncwarp();
     return true;
@@ -633,26 +307,7 @@ __global__ void __launch_bounds__(256, blocks_per_sm<N>()) score_kernel(const __
                 if (lane == 0) atomicOr(m.status, kStatusTimeout);
                 return;
             }
-            // -log p(next) in f64: max, sum of exp over the V classes, the target's logit
-            float mx = -__int_as_float(0x7f800000);
-#pragma unroll
-            for (int c = 0; c < kMaxClassesPerLane; c++)
-                if (c < nv && 32 * c + lane < V) mx = fmaxf(mx, lg[c]);
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, off));
-            double se = 0.0;
-#pragma unroll
-            for (int c = 0; c < kMaxClassesPerLane; c++)
-                if (c < nv && 32 * c + lane < V) se += exp((double)lg[c] - (double)mx);
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) se += __shfl_xor_sync(kFull, se, off);
-            const int y = tok[t + 1];
-            float ly = 0.0f;
-#pragma unroll
-            for (int c = 0; c < kMaxClassesPerLane; c++)
-                if (c == (y >> 5)) ly = lg[c];
-            ly = __shfl_sync(kFull, ly, y & 31);
-            nll += log(se) + (double)mx - (double)ly;
+            nll += nll_of(lg, nv, V, tok[t + 1], lane);
         }
         if (lane == 0) bits[s] = nll / 0.69314718055994530942;
         __syncwarp();

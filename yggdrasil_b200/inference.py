@@ -202,10 +202,27 @@ class B200Yggdrasil:
                               ctypes.c_void_p(state.data_ptr()) if state is not None else None,
                               ctypes.c_void_p(bits.data_ptr()), ctypes.c_void_p(stream)), "ygg_score")
 
-    def score(self, tokens, state=None, batch=1024):
+    def score_grouped_into(self, tokens, state, bits, min_group=32):
+        """score_into through the grouped path: per step and layer the streams are bucketed by leaf and leaves with
+        at least min_group streams run as int8 tensor-core GEMMs. Allocates the workspace with torch."""
+        torch = _torch()
+        b = tokens.shape[0]
+        nbytes = lib().ygg_score_grouped_workspace(self._h, b)
+        ws = torch.empty(nbytes + 256, dtype=torch.uint8, device=self.device)
+        base = ws.data_ptr()
+        base += (-base) % 256
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        check(lib().ygg_score_grouped(self._h, b, tokens.shape[1], ctypes.c_void_p(tokens.data_ptr()),
+                                      ctypes.c_void_p(state.data_ptr()) if state is not None else None,
+                                      ctypes.c_void_p(bits.data_ptr()), int(min_group), ctypes.c_void_p(base),
+                                      nbytes, ctypes.c_void_p(stream)), "ygg_score_grouped")
+
+    def score(self, tokens, state=None, batch=1024, grouped=False, min_group=32):
         """Bits of tokens[:, 1:] given the tokens before them, per row of tokens (B, L), as float64 (B,).
         Rows start from state, or from zero; bits per token = score(tokens).sum() / (B (L - 1)).
-        One fused launch per batch of rows: the state and the logits stay on chip across the whole row."""
+        One fused launch per batch of rows: the state and the logits stay on chip across the whole row.
+        grouped=True: the leaf-grouped path instead (tensor-core GEMMs for leaves shared by >= min_group streams);
+        same bits."""
         torch = _torch()
         with torch.cuda.device(self.device):
             if isinstance(tokens, torch.Tensor) and tokens.is_cuda:
@@ -222,9 +239,12 @@ class B200Yggdrasil:
                 x = tok[i:i + batch].contiguous()
                 st = None if state is None else self._check_state(state[i:i + batch], x.shape[0]).clone()
                 bits = torch.empty(x.shape[0], dtype=torch.float64, device=self.device)
-                check(lib().ygg_score(self._h, x.shape[0], steps, ctypes.c_void_p(x.data_ptr()),
-                                      ctypes.c_void_p(st.data_ptr()) if st is not None else None,
-                                      ctypes.c_void_p(bits.data_ptr()), ctypes.c_void_p(stream)), "ygg_score")
+                if grouped:
+                    self.score_grouped_into(x, st, bits, min_group)
+                else:
+                    check(lib().ygg_score(self._h, x.shape[0], steps, ctypes.c_void_p(x.data_ptr()),
+                                          ctypes.c_void_p(st.data_ptr()) if st is not None else None,
+                                          ctypes.c_void_p(bits.data_ptr()), ctypes.c_void_p(stream)), "ygg_score")
                 out.append(bits)
             res = torch.cat(out).cpu().numpy() if out else np.zeros(0, np.float64)
             self.status()
