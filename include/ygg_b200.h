@@ -36,6 +36,7 @@ extern "C" {
 #define YGG_E_TOKEN (-7)        /* a token outside [0, vocab) (cpu/ygg.cpp:493-495) */
 #define YGG_E_TIMEOUT (-8)      /* a bounded device wait gave up (reported through ygg_status) */
 #define YGG_E_DEVICE (-9)       /* no such CUDA device, or not an sm_100 device */
+#define YGG_E_CAPACITY (-10)    /* the batch needs more scratch than ygg_score_grouped_noalloc's fixed scratch holds */
 
 typedef struct ygg_model ygg_model;
 
@@ -99,6 +100,18 @@ YGG_API size_t ygg_score_grouped_workspace(const ygg_model *m, int batch);
  * result is defined by yggdrasil/inference.py:179-188 and cpu/ygg.cpp:441-459,513-517 as for ygg_score. */
 YGG_API int ygg_score_grouped(const ygg_model *m, int batch, int steps, const int32_t *d_tokens, int8_t *d_state,
                               double *d_bits, int min_group, void *d_workspace, size_t workspace_bytes, void *stream);
+
+/* ygg_score_grouped for callers that cannot allocate device memory while they run: a host whose own pool owns the
+ * GPU's memory, a serving loop that forbids allocation on its hot path, or a binding with no CUDA allocator. It
+ * takes no workspace: its scratch is one fixed 16 MiB array in device memory that every GPU loading this library holds
+ * until the process exits, so it calls no allocator at all. A batch whose scratch (ygg_score_grouped_workspace)
+ * exceeds 16 MiB is refused with YGG_E_CAPACITY (22 784 rows at n = 128, L = 4, 8192 leaves). The first call on a device
+ * looks up the array's device address (once per device); make that first call before any stream capture. Every call
+ * shares the array and clears what must start at zero; calls whose work overlaps on the GPU (other streams, other
+ * threads) race on it, so run them one after another. Same arguments (less the workspace) and the same results as
+ * ygg_score_grouped. No counterpart in the reference: it is an addition of this library. */
+YGG_API int ygg_score_grouped_noalloc(const ygg_model *m, int batch, int steps, const int32_t *d_tokens,
+                                      int8_t *d_state, double *d_bits, int min_group, void *stream);
 
 /* Read (and with clear != 0, reset) the model's device status word after the calls queued on `stream`:
  * 0 when every call since the last clear ran clean, else a negative YGG_E_* code (token out of range, or a bounded

@@ -28,7 +28,7 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_strerror_covers_every_code():
-    for code in range(0, -10, -1):
+    for code in range(0, -11, -1):
         assert _native.strerror(code) != "unknown error"
     assert _native.strerror(-99) == "unknown error"
 

@@ -11,11 +11,11 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "libygg_b200.so"
 
 EXPORTS = ("ygg_load", "ygg_info", "ygg_step", "ygg_step_debug", "ygg_score", "ygg_score_grouped_workspace",
-           "ygg_score_grouped", "ygg_status", "ygg_free", "ygg_strerror", "ygg_version")
+           "ygg_score_grouped", "ygg_score_grouped_noalloc", "ygg_status", "ygg_free", "ygg_strerror", "ygg_version")
 
 YGG_OK = 0
 YGG_E_ARG, YGG_E_FORMAT, YGG_E_UNSUPPORTED, YGG_E_MISSING, YGG_E_CUDA, YGG_E_OOM, YGG_E_TOKEN, YGG_E_TIMEOUT, \
-    YGG_E_DEVICE = range(-1, -10, -1)
+    YGG_E_DEVICE, YGG_E_CAPACITY = range(-1, -11, -1)
 
 
 class YggInfo(ctypes.Structure):
@@ -51,6 +51,7 @@ def lib() -> ctypes.CDLL:
         l.ygg_score_grouped_workspace.argtypes = [vp, i32]
         l.ygg_score_grouped_workspace.restype = sz
         l.ygg_score_grouped.argtypes = [vp, i32, i32, vp, vp, vp, i32, vp, sz, vp]
+        l.ygg_score_grouped_noalloc.argtypes = [vp, i32, i32, vp, vp, vp, i32, vp]
         l.ygg_status.argtypes = [vp, vp, i32, ctypes.POINTER(ctypes.c_int)]
         l.ygg_free.argtypes = [vp]
         l.ygg_free.restype = None
@@ -58,7 +59,8 @@ def lib() -> ctypes.CDLL:
         l.ygg_strerror.restype = ctypes.c_char_p
         l.ygg_version.argtypes = []
         l.ygg_version.restype = ctypes.c_char_p
-        for f in (l.ygg_load, l.ygg_info, l.ygg_step, l.ygg_step_debug, l.ygg_score, l.ygg_score_grouped, l.ygg_status):
+        for f in (l.ygg_load, l.ygg_info, l.ygg_step, l.ygg_step_debug, l.ygg_score, l.ygg_score_grouped,
+                  l.ygg_score_grouped_noalloc, l.ygg_status):
             f.restype = ctypes.c_int
         _lib = l
     return _lib

@@ -553,3 +553,42 @@ cudaError_t run_grouped(int n, int blk, int r, int r2p, const DevModel &m, int B
 }
 
 }  // namespace ygg
+
+// ------------------------------------------------------------------------------------------------ fixed scratch
+//
+// Scratch for callers that cannot allocate device memory while they run: a host that has handed every byte of the
+// GPU to its own pool, a real-time serving loop that forbids allocation on its hot path, or a foreign-language
+// binding with no CUDA allocator of its own. ygg_score_grouped_noalloc uses this array instead of a caller
+// workspace. It is a fixed, modest size (kNoAllocScratchBytes), and every GPU that loads this library holds it until
+// the process exits. All calls share it and it keeps the last call's contents, so each call clears what must start
+// at zero, and calls whose work overlaps on the GPU (several streams, several host threads) race on it.
+#include <mutex>
+
+namespace ygg {
+constexpr size_t kNoAllocScratchBytes = (size_t)16 << 20;   // 16 MiB
+}
+
+static __device__ __align__(256) uint8_t g_noalloc_scratch[ygg::kNoAllocScratchBytes];
+
+namespace ygg {
+
+// The device address of the fixed scratch on `device`, which must be the current device. Resolved once per device
+// (the array's name is only a host-side handle); later calls return the cached address.
+cudaError_t noalloc_scratch(int device, void **ptr, size_t *bytes) {
+    constexpr int kMaxDev = 64;
+    static std::mutex mu;
+    static void *addr[kMaxDev] = {};
+    if (device < 0 || device >= kMaxDev) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(mu);
+    if (addr[device] == nullptr) {
+        void *p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return e;
+        addr[device] = p;
+    }
+    *ptr = addr[device];
+    *bytes = kNoAllocScratchBytes;
+    return cudaSuccess;
+}
+
+}  // namespace ygg

@@ -25,6 +25,7 @@ size_t block_smem_bytes(uint32_t rec_max, int n, int slots, int warps, int state
 size_t grouped_ws_bytes(const DevModel &m, int B);
 cudaError_t run_grouped(int n, int blk, int r, int r2p, const DevModel &m, int B, int T, const int32_t *tok,
                         int8_t *state, double *bits, void *workspace, int G, int sm_count, cudaStream_t st);
+cudaError_t noalloc_scratch(int device, void **ptr, size_t *bytes);
 }  // namespace ygg
 
 using namespace ygg;
@@ -106,6 +107,7 @@ const char *ygg_strerror(int code) {
         case YGG_E_TOKEN: return "token out of range";
         case YGG_E_TIMEOUT: return "a bounded device wait gave up";
         case YGG_E_DEVICE: return "no usable sm_100 CUDA device";
+        case YGG_E_CAPACITY: return "the batch needs more scratch than the fixed scratch of the allocation-free call holds";
         default: return "unknown error";
     }
 }
@@ -490,6 +492,30 @@ int ygg_score_grouped(const ygg_model *m, int batch, int steps, const int32_t *d
     if (set_device(m, &prev)) return YGG_E_CUDA;
     const cudaError_t e = run_grouped(m->host.n, m->host.b, m->host.R, m->host.R2P, m->host, batch, steps, d_tokens,
                                       d_state, d_bits, d_workspace, min_group, m->sm_count, (cudaStream_t)stream);
+    restore_device(m, prev);
+    return e == cudaSuccess ? YGG_OK : YGG_E_CUDA;
+}
+
+int ygg_score_grouped_noalloc(const ygg_model *m, int batch, int steps, const int32_t *d_tokens, int8_t *d_state,
+                              double *d_bits, int min_group, void *stream) {
+    if (!m || batch < 0 || steps < 0) return YGG_E_ARG;
+    if (batch == 0) return YGG_OK;
+    if (!d_tokens || !d_bits) return YGG_E_ARG;
+    const size_t need = grouped_ws_bytes(m->host, batch);
+    int prev;
+    if (set_device(m, &prev)) return YGG_E_CUDA;
+    void *scratch = nullptr;
+    size_t cap = 0;
+    if (noalloc_scratch(m->device, &scratch, &cap) != cudaSuccess) {
+        restore_device(m, prev);
+        return YGG_E_CUDA;
+    }
+    if (need > cap) {
+        restore_device(m, prev);
+        return YGG_E_CAPACITY;
+    }
+    const cudaError_t e = run_grouped(m->host.n, m->host.b, m->host.R, m->host.R2P, m->host, batch, steps, d_tokens,
+                                      d_state, d_bits, scratch, min_group, m->sm_count, (cudaStream_t)stream);
     restore_device(m, prev);
     return e == cudaSuccess ? YGG_OK : YGG_E_CUDA;
 }
