@@ -55,7 +55,7 @@ def build_model_file(workload, seed, rank, world, dist):
     w = synth.WORKLOADS[workload]
     d = Path(os.environ.get("YGG_BENCH_DIR", tempfile.gettempdir())) / "ygg_bench"
     d.mkdir(parents=True, exist_ok=True)
-    path = d / f"{workload}_s{seed}.bin"
+    path = d / f"{w.model or workload}_s{seed}.bin"
     if rank == 0 and not path.exists():
         tmp = path.with_suffix(f".tmp{os.getpid()}")
         layers = synth.workload_layers(w, seed=seed)
@@ -219,6 +219,84 @@ def run_reference(args):
     return 0
 
 
+def run_score(args, w, path, world, rank, local, dist):
+    """Whole rows scored on the GPU (bits of tokens[:, 1:], the reference's score): B rows of T tokens per GPU, the
+    fused score kernel (state and logits on chip for the whole row) and, with --grouped, the leaf-grouped path whose
+    heavy leaves run as int8 tensor-core GEMMs. Tokens scored per second = B (T - 1) / time, summed over the GPUs."""
+    import torch
+
+    from yggdrasil_b200 import Yggdrasil, synth
+    dev = torch.device("cuda", local)
+    model = Yggdrasil.load(path, backend="b200", device=dev)
+    stream = torch.cuda.current_stream(dev)
+    B = args.streams or w.streams
+    T = args.score_steps or w.steps
+    K, W = args.steps, args.warmup
+    x = torch.as_tensor(synth.workload_tokens(w, B, T, seed=rank)).to(dev)
+    bits = torch.empty(B, dtype=torch.float64, device=dev)
+
+    def timed(fn, reps):
+        for _ in range(W):
+            fn()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / reps
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    reps = max(1, K)
+    ms_fused = timed(lambda: model.score_into(x, None, bits), reps)
+    fused_bits = bits.clone()
+    ms_grouped = None
+    if args.grouped:
+        ms_grouped = timed(lambda: model.score_grouped_into(x, None, bits, min_group=args.min_group), reps)
+        if not torch.equal(bits, fused_bits):
+            raise RuntimeError("grouped and fused scores differ")
+    model.status()
+    tok = B * (T - 1) * world
+    # end to end through the public API: host tokens in, bits (float64 per row) out
+    h = synth.workload_tokens(w, B, T, seed=rank)
+    a0 = time.perf_counter()
+    model.score(h, batch=B, grouped=args.grouped, min_group=args.min_group)
+    e2e_s = time.perf_counter() - a0
+    ms = ms_grouped if args.grouped else ms_fused
+    bpt = synth.gathered_bytes_per_token(w.shape, with_io=False) + 4
+    peak, kind = peaks()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    L = model.layers
+    line = {"metric": "tokens scored/s (bits of whole rows)", "value": tok / (ms / 1e3), "unit": "tokens/s",
+            "n_gpus": world, "steps": reps, "warmup": W, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": w.name, "rows_per_gpu": B, "tokens_per_row": T, "mode": "score",
+                       "path": f"grouped (min_group {args.min_group})" if args.grouped else "fused",
+                       "fused_tokens_per_s": tok / (ms_fused / 1e3),
+                       "grouped_tokens_per_s": tok / (ms_grouped / 1e3) if ms_grouped else None,
+                       "bytes_per_token": bpt},
+            "roofline": {"bound": "hbm", "achieved": bpt * B * (T - 1) / (ms / 1e3) / 1e9, "peak": peak,
+                         "unit": "GB/s", "frac": bpt * B * (T - 1) / (ms / 1e3) / 1e9 / peak, "traffic": None,
+                         "peak_kind": kind},
+            "e2e": {"value": B * (T - 1) / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": int(B * T * 4),
+                    "d2h_bytes_per_step": int(B * 8)},
+            "gpu_launches": reps * ((T - 1) * (5 * L + 1) + 2 if args.grouped else 1)}
+    print(json.dumps(line))
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -232,6 +310,11 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=100, help="timed segments per core of the CPU baseline")
     ap.add_argument("--batch1-steps", type=int, default=512)
     ap.add_argument("--prime", type=int, default=64, help="untimed steps that give every stream a history first")
+    ap.add_argument("--mode", default="step", choices=["step", "score"],
+                    help="step: the decode step (the headline metric); score: whole rows scored on the GPU")
+    ap.add_argument("--score-steps", type=int, default=0, help="tokens per row in score mode (default: the workload's)")
+    ap.add_argument("--grouped", action="store_true", help="score mode: also time the leaf-grouped tensor-core path")
+    ap.add_argument("--min-group", type=int, default=64, help="streams a leaf needs for the tensor-core path")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -253,6 +336,8 @@ def main():
 
     from yggdrasil_b200 import Yggdrasil, synth
     w, path = build_model_file(args.workload, 7, rank, world, dist)
+    if args.mode == "score":
+        return run_score(args, w, path, world, rank, local, dist)
     B = args.streams or min(w.streams, 65536)
     K, W = args.steps, args.warmup
     dev = torch.device("cuda", local)

@@ -119,6 +119,7 @@ class Workload:
     tokens: str                  # "uniform" or "dna"
     note: str = ""
     leaves: str = "random"       # "random": the generator's thresholds; "zipf": calibrated to Zipf(1.1) leaf usage
+    model: str = ""              # the workload whose model file this one shares ("": its own)
 
 
 WORKLOADS = {
@@ -135,6 +136,9 @@ WORKLOADS = {
     # the same model with factored input storage k=32 (390 MB)
     "c4f": Workload("c4-730M-enwik8-factored", ModelShape(128, 16, 13, 256, 4, 16, 32, input_rank=32), 262144, 256,
                     "uniform", "factored storage k=32, 390 MB; Zipf(1.1) leaf usage", leaves="zipf"),
+    # the scoring configuration: 512 rows of 8192 uniform bytes on the c4 model
+    "c5": Workload("c5-score-730M", ModelShape(128, 16, 13, 256, 4, 16, 32), 512, 8192, "uniform",
+                   "whole rows scored on the c4 model", leaves="zipf", model="c4"),
 }
 
 
