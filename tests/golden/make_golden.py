@@ -99,6 +99,45 @@ def main():
                               logits_sha256=sha(np.ascontiguousarray(lg, np.float32).tobytes()),
                               bits=[float(v) for v in bits_from_logits(lg, x)]))
         (HERE / "workloads.json").write_text(json.dumps(works, indent=1) + "\n")
+
+        # checkpoints: the reference's read (yggdrasil/inference.py:129-139), FloatLayer, quantize and write
+        # (cpu/export.py:68-96,216-265,461-468) on seeded synthetic checkpoints and export records; the float64
+        # transitions come from torch.linalg.matrix_exp (the reference's exporter uses JAX, absent here), checked
+        # against the reference Triton backend's own transitions (yggdrasil/inference_triton.py:109-114)
+        sys.path.insert(0, str(HERE.parent))
+        import checkpoints as C
+        from yggdrasil import inference as I
+        from yggdrasil import inference_triton as IT
+        from yggdrasil_b200.checkpoint import transitions64
+        ckpts = []
+        for seed, old in ((0, False), (1, True)):
+            npz = os.path.join(tmp, f"ck{seed}.npz")
+            C.synthetic_checkpoint(npz, seed=seed, old_keys=old)
+            raw, ob = I.read(npz)
+            raw = [{k: v.astype(np.float64) for k, v in p.items()} for p in raw]
+            tr_ok = all(np.array_equal(transitions64(p["rotation"], p["decay"]).astype(np.float32),
+                                       IT._transitions(p).numpy()) for p in raw)
+            depth = I.router_depth(raw[1])
+            fl = []
+            for i, p in enumerate(raw):
+                table = np.einsum("lkr,vr->lvk", p["input_proj"], p["token_embed"]) + p["bias"][:, None]
+                kw = {k: p[k] for k in ("router_embed", "router_weight", "router_bias", "layer_input_down",
+                                        "layer_input_proj") if k in p}
+                fl.append(E.FloatLayer(token_layer=i == 0, depth=depth if i else 0,
+                                       transition=transitions64(p["rotation"], p["decay"]), table=table,
+                                       input_proj=p["input_proj"], token_embed=p["token_embed"], bias=p["bias"],
+                                       readout=p["readout"], unembed=p["unembed"], **kw))
+            for rs, (hm, group, fac) in enumerate(((0.85, False, False), (1.0, True, True))):
+                rec = C.synthetic_record(seed=rs, hmargin=hm, group=group, factored=fac)
+                stats = [E.LayerStats(**{k: (np.asarray(v) if isinstance(v, list) else v) for k, v in s.items()})
+                         for s in rec["stats"]]
+                q = E.quantize(fl, stats, **rec["quantize"])
+                out = os.path.join(tmp, "ck.bin")
+                E.write(q, ob, out, router_token_dim=fl[-1].router_token_dim, input_rank=fl[0].token_embed.shape[1])
+                ckpts.append(dict(seed=seed, old_keys=old, record_seed=rs, quantize=rec["quantize"],
+                                  model_sha256=sha(Path(out).read_bytes()), model_bytes=os.path.getsize(out),
+                                  transitions_match_reference_triton_backend=bool(tr_ok)))
+        (HERE / "checkpoints.json").write_text(json.dumps(ckpts, indent=1) + "\n")
     print("wrote", [p.name for p in HERE.glob("*.json")])
 
 

@@ -48,17 +48,23 @@ class Yggdrasil:
 
 
 class B200Yggdrasil:
-    def __init__(self, model, device="cuda", cuda_graph=False):
-        """model: path of a YGG1 file, or its bytes. device: a CUDA device. cuda_graph: replay one captured step per
-        batch size (as the reference's Triton backend, inference_triton.py:196-212)."""
+    def __init__(self, model, device="cuda", cuda_graph=False, record=None):
+        """model: path of a YGG1 file, or its bytes, or a float checkpoint (.npz) with `record`, the export record
+        (model.bin.json, or its dict) whose calibration stats and quantize arguments rebuild the int8 model
+        (yggdrasil_b200.checkpoint). device: a CUDA device. cuda_graph: replay one captured step per batch size (as
+        the reference's Triton backend, inference_triton.py:196-212)."""
         torch = _torch()
         if isinstance(model, (str, Path)):
             p = Path(model)
             if p.suffix == ".npz":
-                raise NotImplementedError(
-                    f"{p}: a float checkpoint needs calibration before it runs in int8; export it to a YGG1 file "
-                    "first (the reference's cpu/export.py --npz ... --out model.bin)")
-            data = p.read_bytes()
+                if record is None:
+                    raise NotImplementedError(
+                        f"{p}: a float checkpoint needs its calibration before it runs in int8: pass record= (the "
+                        "model.bin.json the reference's cpu/export.py writes), or export a YGG1 file first")
+                from .checkpoint import export_bytes
+                data = export_bytes(p, record)
+            else:
+                data = p.read_bytes()
         else:
             data = bytes(model)
         dev = torch.device(device)
