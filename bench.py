@@ -15,7 +15,9 @@ region is bracketed by a barrier and a device synchronise, and the time is the m
   roofline  algorithmic bytes gathered per token (per-stream weights + state/logit traffic) x tokens per launch /
             the average launch time, against the measured HBM copy bandwidth (MEASURED_PEAKS.json).
   cpu_baseline  the reference's own int8 kernel (cpu/ygg.cpp, built under oracle/_ref) on the host cores, one
-            stream per core as the reference runs it (`ygg time`, which includes a softmax per token).
+            stream per core as the reference runs it (`ygg time`, which includes a softmax per token). A workload of
+            the d_state 96 format extension (c3n96), whose file the reference's ygg refuses, is timed on the C oracle
+            (the scalar port, one core) instead.
 --impl reference times that CPU path alone, on rank 0, and prints its own line.
 """
 from __future__ import annotations
@@ -62,7 +64,7 @@ def build_model_file(workload, seed, rank, world, dist):
         ob = np.linspace(-1, 1, w.shape.vocab)
         if w.leaves == "zipf":
             calibrate_zipf(w, layers, ob, tmp, seed)
-        write_model(layers, ob, tmp)
+        write_model(layers, ob, tmp, extended=w.extended)
         os.replace(tmp, path)
     if world > 1:
         dist.barrier()
@@ -80,7 +82,7 @@ def calibrate_zipf(w, layers, ob, tmp, seed, streams=65536, prime=48, snapshots=
     from yggdrasil_b200.ygg1 import write_model
     E = 2 ** w.shape.router_depth
     for l in range(1, len(layers)):
-        write_model(layers, ob, tmp)
+        write_model(layers, ob, tmp, extended=w.extended)
         model = Yggdrasil.load(tmp, backend="b200")
         dev = model.device
         x = torch.as_tensor(synth.workload_tokens(w, max(snapshots), streams, seed=77)).to(dev)
@@ -186,6 +188,29 @@ def cpu_reference_run(model_path, workload, steps, warmup, seg=1000, cores=None)
     return tps, len(cores), float(np.median(med)), "reference", sample
 
 
+def cpu_port_run(model_path, workload, seconds=10.0):
+    """The C oracle (the scalar restatement of cpu/ygg.cpp) on one core and one stream, for a file the reference's
+    ygg refuses (the d_state 96 extension): tokens/s over about `seconds` of stepping, no softmax. Returns the tuple
+    of cpu_reference_run."""
+    from oracle import oracle as O
+    from yggdrasil_b200 import synth
+    w = synth.WORKLOADS[workload]
+    om = O.OracleModel(model_path)
+    x = synth.workload_tokens(w, 1, 1 << 20, seed=1000)[0]
+    st = om.init_state(1)
+    for t in range(64):
+        om.step(x[t:t + 1], st)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        for t in range(256):
+            om.step(x[64 + n + t:65 + n + t], st)
+        n += 256
+    dt = time.perf_counter() - t0
+    sample = (f"the C oracle (scalar port of cpu/ygg.cpp), one stream on one core, {n} steps after 64 warm-up "
+              f"steps (no softmax); the reference's ygg refuses d_state 96 files (cpu/ygg.cpp:141-146)")
+    return n / dt, 1, dt / n * 1e9, "port", sample
+
+
 def cpu_model_name():
     try:
         for line in Path("/proc/cpuinfo").read_text().splitlines():
@@ -202,7 +227,10 @@ def run_reference(args):
         return 0
     from yggdrasil_b200 import synth
     w, path = build_model_file(args.workload, 7, 0, 1, None)
-    res = cpu_reference_run(path, args.workload, args.steps, args.warmup, seg=args.ref_seg)
+    if w.extended:
+        res = cpu_port_run(path, args.workload)
+    else:
+        res = cpu_reference_run(path, args.workload, args.steps, args.warmup, seg=args.ref_seg)
     if res is None:
         print(json.dumps({"impl": "reference", "unavailable": "the reference binary oracle/_ref/ygg is not built"}))
         return 0
@@ -468,7 +496,10 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
-            res = cpu_reference_run(path, args.workload, steps=args.cpu_steps, warmup=2, seg=args.ref_seg)
+            if w.extended:
+                res = cpu_port_run(path, args.workload)
+            else:
+                res = cpu_reference_run(path, args.workload, steps=args.cpu_steps, warmup=2, seg=args.ref_seg)
         except Exception as e:  # noqa: BLE001
             res = None
             print(f"cpu baseline failed: {e}", file=sys.stderr)

@@ -46,13 +46,16 @@ static const uint8_t *find(const Entry *tab, int na, const uint8_t *base, const 
     return NULL;
 }
 
-/* YGG1 parse: header and limits as cpu/ygg.cpp:137-148, array binding as cpu/ygg.cpp:173-220. */
+/* YGG1 parse: header and limits as cpu/ygg.cpp:137-148, array binding as cpu/ygg.cpp:173-220. Beyond the reference's
+ * limits it admits this repository's one format extension, d_state 96 with readout rank 12 (stored in the rank-16
+ * readout layout with zero rows 12-15), which int_forward (cpu/export.py:268-316) computes at any shape. */
 orc_model *orc_load(const uint8_t *bytes, size_t nbytes, char *err, int errlen) {
     int32_t h[12];
     if (nbytes < 52 || memcmp(bytes, "YGG1", 4)) { snprintf(err, errlen, "not a model file"); return NULL; }
     memcpy(h, bytes + 4, 48);
     const int L = h[0], n = h[1], b = h[2], V = h[3], D = h[4], R = h[5], R2 = h[6], na = h[11];
-    const int ok = (n == 64 || n == 128 || n == 256) && (b == 8 || b == 16) && (R == 8 || R == 16 || R == 32) &&
+    const int ok = (n == 64 || n == 96 || n == 128 || n == 256) && (b == 8 || b == 16) &&
+                   (R == 8 || R == 12 || R == 16 || R == 32) &&
                    R2 <= 64 && R2 % 4 == 0 && L >= 1 && L <= MAX_LAYERS && V <= 256 && D <= 16 &&
                    (L == 1 || D >= 1) && h[7] == 0;
     if (!ok) { snprintf(err, errlen, "unsupported model"); return NULL; }

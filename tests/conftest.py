@@ -76,7 +76,8 @@ def case_model(model_dir):
         key = json.dumps(rec["shape"], sort_keys=True)
         if key not in cache:
             p = model_dir / f"case{len(cache)}.bin"
-            synth.write_random_model(shape_of(rec), p, seed=rec["seed"])
+            shape = shape_of(rec)
+            synth.write_random_model(shape, p, seed=rec["seed"], extended=shape.extended)
             cache[key] = p
         return cache[key]
     return get

@@ -10,7 +10,11 @@ The fixtures pin this repository's generator and oracle to the reference:
                      float64, and a few logits in clear for reading a failure;
   long_cases.json    two shapes run for 512 steps (deep state dynamics, saturation);
   workloads.json     the benchmark shapes (yggdrasil_b200.synth WORKLOADS c1-c3) written by the reference's writer, with
-                     int_forward logits on a few streams.
+                     int_forward logits on a few streams;
+  extended_cases.json  shapes of this repository's d_state 96 format extension, which the reference's writer and ygg
+                     refuse: the reference's random_model (seed 7) and int_forward logits on the kernel test's tokens,
+                     and the c3n96 benchmark shape's int_forward logits on a few streams. The model digests here are
+                     this repository's writer's (a regression check, not a pin); the logits are the pin.
 The reference sources are read in place and never copied; only digests and a few numbers land here.
 """
 from __future__ import annotations
@@ -99,6 +103,40 @@ def main():
                               logits_sha256=sha(np.ascontiguousarray(lg, np.float32).tobytes()),
                               bits=[float(v) for v in bits_from_logits(lg, x)]))
         (HERE / "workloads.json").write_text(json.dumps(works, indent=1) + "\n")
+
+        # the d_state 96 extension: int_forward works at any shape; the file is this repository's writer's
+        from yggdrasil_b200.synth import ModelShape, write_random_model
+        from yggdrasil_b200.ygg1 import write_model
+        ext_cfgs = [E.KernelConfig(96, 16, 8, 256, 2, 12, 24), E.KernelConfig(96, 8, 6, 5, 3, 12, 24, group=True),
+                    E.KernelConfig(96, 16, 7, 27, 3, 12, 24, input_rank=24, group=True),
+                    E.KernelConfig(96, 16, 6, 256, 2, 16, 32), E.KernelConfig(96, 8, 5, 5, 2, 8, 0)]
+        ext = []
+        for cfg in ext_cfgs:
+            layers = E.random_model(cfg, seed=7)
+            ob = np.linspace(-1, 1, cfg.vocab)
+            path = os.path.join(tmp, "x.bin")
+            shape = ModelShape(**{k: getattr(cfg, k) for k in fields})
+            write_random_model(shape, path, seed=7, extended=True)
+            x = np.random.default_rng(0).integers(0, cfg.vocab, (STREAMS, STEPS)).astype(np.int32)
+            lg = E.int_forward(layers, ob, x)
+            ext.append(dict(shape={k: getattr(cfg, k) for k in fields}, seed=7, streams=STREAMS, steps=STEPS,
+                            token_seed=0, extended=True, model_sha256=sha(Path(path).read_bytes()),
+                            model_bytes=os.path.getsize(path),
+                            logits_sha256=sha(np.ascontiguousarray(lg, np.float32).tobytes()),
+                            bits=[float(v) for v in bits_from_logits(lg, x)],
+                            logits_head=np.asarray(lg[0, :4, :8], np.float64).tolist()))
+        w = synth.WORKLOADS["c3n96"]
+        layers = synth.workload_layers(w, seed=7)
+        ob = np.linspace(-1, 1, w.shape.vocab)
+        path = os.path.join(tmp, "w.bin")
+        write_model(layers, ob, path, extended=True)
+        x = synth.workload_tokens(w, 4, 32, seed=0)
+        lg = E.int_forward(layers, ob, x)
+        ext.append(dict(workload="c3n96", extended=True, model_sha256=sha(Path(path).read_bytes()),
+                        model_bytes=os.path.getsize(path), streams=4, steps=32, token_seed=0,
+                        logits_sha256=sha(np.ascontiguousarray(lg, np.float32).tobytes()),
+                        bits=[float(v) for v in bits_from_logits(lg, x)]))
+        (HERE / "extended_cases.json").write_text(json.dumps(ext, indent=1) + "\n")
 
         # checkpoints: the reference's read (yggdrasil/inference.py:129-139), FloatLayer, quantize and write
         # (cpu/export.py:68-96,216-265,461-468) on seeded synthetic checkpoints and export records; the float64

@@ -14,6 +14,7 @@ from oracle import oracle as O
 pytestmark = pytest.mark.gpu
 
 CASES = golden("kernel_cases.json")
+EXT_CASES = [r for r in golden("extended_cases.json") if "shape" in r]   # d_state 96 (device layout padded to 128)
 BITS_RTOL = 1e-10
 
 
@@ -45,7 +46,7 @@ def torch():
 
 
 @pytest.mark.parametrize("min_group", [1, 3, 1 << 30])
-@pytest.mark.parametrize("rec", CASES, ids=_ids(CASES))
+@pytest.mark.parametrize("rec", CASES + EXT_CASES, ids=_ids(CASES) + [f"ext-{i}" for i in _ids(EXT_CASES)])
 def test_grouped_equals_fused(rec, min_group, case_model, torch):
     """min_group 1: every leaf through the tensor cores; 3: mixed; 2^30: every stream on the per-stream path."""
     path = case_model(rec)
@@ -68,8 +69,8 @@ def test_grouped_matches_oracle(rec, case_model, torch):
     np.testing.assert_allclose(bits, om.score(x), rtol=BITS_RTOL)
 
 
-def test_grouped_from_state(case_model, torch):
-    rec = CASES[0]
+@pytest.mark.parametrize("rec", [CASES[0], EXT_CASES[0]], ids=["n128", "ext-n96"])
+def test_grouped_from_state(rec, case_model, torch):
     model = load(case_model(rec))
     x = np.random.default_rng(3).integers(0, rec["shape"]["vocab"], (200, 10)).astype(np.int32)
     st = model.init_state(200)
@@ -80,14 +81,15 @@ def test_grouped_from_state(case_model, torch):
     assert torch.equal(s1, s2)
 
 
-def test_grouped_benchmark_shape(tmp_path, torch):
-    """The c3 shape (n128 b16 R16 R2=32, 4 layers, V = 5) at 4096 streams: DNA tokens make the token layer's five
-    leaves and the hot routed leaves heavy."""
+@pytest.mark.parametrize("key", ["c3", "c3n96"])
+def test_grouped_benchmark_shape(key, tmp_path, torch):
+    """The c3 shape (n128 b16 R16 R2=32, 4 layers, V = 5; and the d 96 extension, padded to n 128 on the device) at
+    4096 streams: DNA tokens make the token layer's five leaves and the hot routed leaves heavy."""
     from yggdrasil_b200 import synth
     from yggdrasil_b200.ygg1 import write_model
-    w = synth.WORKLOADS["c3"]
+    w = synth.WORKLOADS[key]
     p = tmp_path / "c3.bin"
-    write_model(synth.workload_layers(w, seed=7), np.linspace(-1, 1, w.shape.vocab), p)
+    write_model(synth.workload_layers(w, seed=7), np.linspace(-1, 1, w.shape.vocab), p, extended=w.extended)
     model = load(p)
     x = synth.workload_tokens(w, 4096, 16, seed=2)
     for g in (1, 32):

@@ -48,8 +48,13 @@ def test_load_rejects_unsupported_header(tmp_path):
     p = tmp_path / "m.bin"
     synth.write_random_model(synth.ModelShape(64, 8, 3, 5, 2, 8, 0), p, seed=1)
     data = bytearray(p.read_bytes())
-    data[8:12] = np.int32(96).tobytes()            # d_state 96: outside the YGG1 limits
+    data[8:12] = np.int32(80).tobytes()            # d_state 80: outside the YGG1 limits and the extension
     assert _load(data)[0] == _native.YGG_E_UNSUPPORTED
+    data[8:12] = np.int32(96).tobytes()            # the extension's d_state, but arrays sized for 64
+    assert _load(data)[0] == _native.YGG_E_MISSING
+    data[8:12] = np.int32(64).tobytes()
+    data[20:24] = np.int32(12).tobytes()           # readout rank 12 with arrays of rank 8
+    assert _load(data)[0] == _native.YGG_E_MISSING
 
 
 def test_load_rejects_truncated_arrays(tmp_path):

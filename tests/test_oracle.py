@@ -15,6 +15,9 @@ from oracle import oracle as O
 CASES = golden("kernel_cases.json")
 LONG = golden("long_cases.json")
 WORKLOADS = golden("workloads.json")
+EXTENDED = golden("extended_cases.json")
+EXT_CASES = [r for r in EXTENDED if "shape" in r]
+EXT_WORKLOADS = [r for r in EXTENDED if "workload" in r]
 
 
 def _ids(cases):
@@ -87,3 +90,28 @@ def test_workload_models_match_reference_writer(rec, tmp_path):
     x = synth.workload_tokens(w, rec["streams"], rec["steps"], seed=rec["token_seed"])
     lg = O.OracleModel(p).logits(x)
     assert sha(np.ascontiguousarray(lg).tobytes()) == rec["logits_sha256"]
+
+
+@pytest.mark.parametrize("rec", EXT_CASES, ids=_ids(EXT_CASES))
+def test_extension_oracle_matches_reference_int_forward(rec, case_model):
+    """The d_state 96 extension, which the reference's writer and ygg refuse: the oracle over this repository's file
+    equals the reference's int_forward on the same random model, bit for bit."""
+    p = case_model(rec)
+    assert sha(p.read_bytes()) == rec["model_sha256"] and p.stat().st_size == rec["model_bytes"]
+    lg = O.OracleModel(p).logits(case_tokens(rec))
+    if sha(np.ascontiguousarray(lg).tobytes()) != rec["logits_sha256"]:
+        np.testing.assert_array_equal(lg[0, :4, :8], np.asarray(rec["logits_head"], np.float32))
+        pytest.fail("oracle logits differ from the reference's int_forward")
+    np.testing.assert_allclose(O.OracleModel(p).score(case_tokens(rec)), rec["bits"], rtol=1e-12)
+
+
+@pytest.mark.parametrize("rec", EXT_WORKLOADS, ids=[w["workload"] for w in EXT_WORKLOADS])
+def test_extension_workload_matches_reference_int_forward(rec, tmp_path):
+    from yggdrasil_b200 import synth
+    from yggdrasil_b200.ygg1 import write_model
+    w = synth.WORKLOADS[rec["workload"]]
+    p = tmp_path / "w.bin"
+    write_model(synth.workload_layers(w, seed=7), np.linspace(-1, 1, w.shape.vocab), p, extended=w.extended)
+    assert sha(p.read_bytes()) == rec["model_sha256"]
+    x = synth.workload_tokens(w, rec["streams"], rec["steps"], seed=rec["token_seed"])
+    assert sha(np.ascontiguousarray(O.OracleModel(p).logits(x)).tobytes()) == rec["logits_sha256"]

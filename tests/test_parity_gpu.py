@@ -17,6 +17,9 @@ pytestmark = pytest.mark.gpu
 CASES = golden("kernel_cases.json")
 LONG = golden("long_cases.json")
 WORKLOADS = golden("workloads.json")
+EXTENDED = golden("extended_cases.json")      # the d_state 96 extension, pinned to the reference's int_forward
+EXT_CASES = [r for r in EXTENDED if "shape" in r]
+EXT_WORKLOADS = [r for r in EXTENDED if "workload" in r]
 BITS_RTOL = 1e-10
 
 
@@ -55,7 +58,7 @@ def run_windows(model, om, x, torch):
     return out
 
 
-@pytest.mark.parametrize("rec", CASES, ids=_ids(CASES))
+@pytest.mark.parametrize("rec", CASES + EXT_CASES, ids=_ids(CASES) + [f"ext-{i}" for i in _ids(EXT_CASES)])
 def test_step_bit_exact(rec, case_model, torch):
     path = case_model(rec)
     model, om = load(path), O.OracleModel(path)
@@ -79,7 +82,8 @@ def test_long_sequences_bit_exact(rec, case_model, torch):
     assert sha(np.ascontiguousarray(lg).tobytes()) == rec["logits_sha256"]
 
 
-@pytest.mark.parametrize("rec", CASES[::2], ids=_ids(CASES[::2]))
+@pytest.mark.parametrize("rec", CASES[::2] + EXT_CASES,
+                         ids=_ids(CASES[::2]) + [f"ext-{i}" for i in _ids(EXT_CASES)])
 def test_score_matches_reference_bits(rec, case_model, torch):
     model = load(case_model(rec))
     bits = model.score(case_tokens(rec))
@@ -205,13 +209,13 @@ def test_generate_greedy_matches_oracle(case_model, torch):
     assert sampled.shape == (2, 6) and sampled.min() >= 0 and sampled.max() < model.vocab
 
 
-@pytest.mark.parametrize("rec", WORKLOADS, ids=[w["workload"] for w in WORKLOADS])
+@pytest.mark.parametrize("rec", WORKLOADS + EXT_WORKLOADS, ids=[w["workload"] for w in WORKLOADS + EXT_WORKLOADS])
 def test_benchmark_workloads_bit_exact(rec, tmp_path, torch):
     from yggdrasil_b200 import synth
     from yggdrasil_b200.ygg1 import write_model
     w = synth.WORKLOADS[rec["workload"]]
     p = tmp_path / "w.bin"
-    write_model(synth.workload_layers(w, seed=7), np.linspace(-1, 1, w.shape.vocab), p)
+    write_model(synth.workload_layers(w, seed=7), np.linspace(-1, 1, w.shape.vocab), p, extended=w.extended)
     model, om = load(p), O.OracleModel(p)
     x = synth.workload_tokens(w, rec["streams"], rec["steps"], seed=rec["token_seed"])
     lg = run_windows(model, om, x, torch)
@@ -219,14 +223,15 @@ def test_benchmark_workloads_bit_exact(rec, tmp_path, torch):
     np.testing.assert_allclose(model.score(x), rec["bits"], rtol=BITS_RTOL)
 
 
-def test_large_batch_sampled_streams(tmp_path, torch):
-    """At the benchmark batch (65536 streams of the c3 shape), a checksum over all streams' states and logits is
-    reproducible, and a sample of streams equals the oracle exactly after 3 steps."""
+@pytest.mark.parametrize("key", ["c3", "c3n96"])
+def test_large_batch_sampled_streams(key, tmp_path, torch):
+    """At the benchmark batch (65536 streams of the c3 shape, at d 128 and d 96), a checksum over all streams' states
+    and logits is reproducible, and a sample of streams equals the oracle exactly after 3 steps."""
     from yggdrasil_b200 import synth
     from yggdrasil_b200.ygg1 import write_model
-    w = synth.WORKLOADS["c3"]
+    w = synth.WORKLOADS[key]
     p = tmp_path / "c3.bin"
-    write_model(synth.workload_layers(w, seed=7), np.linspace(-1, 1, w.shape.vocab), p)
+    write_model(synth.workload_layers(w, seed=7), np.linspace(-1, 1, w.shape.vocab), p, extended=w.extended)
     model, om = load(p), O.OracleModel(p)
     B = 65536
     x = synth.workload_tokens(w, B, 3, seed=0)
@@ -243,3 +248,22 @@ def test_large_batch_sampled_streams(tmp_path, torch):
         olg = om.step(x[idx, i], ost)
     np.testing.assert_array_equal(lg.cpu().numpy()[idx], olg)
     np.testing.assert_array_equal(st.cpu().numpy()[idx], ost)
+
+
+@pytest.mark.parametrize("rec", EXT_CASES[:3], ids=_ids(EXT_CASES[:3]))
+def test_extension_state_layout(rec, case_model, torch):
+    """A d_state 96 model keeps the caller's (B, L, 96) state: in-place steps, score from a state and the state it
+    leaves equal the oracle's."""
+    path = case_model(rec)
+    model, om = load(path), O.OracleModel(path)
+    assert model.n == 96
+    x = case_tokens(rec)
+    st, ost = model.init_state(x.shape[0]), om.init_state(x.shape[0])
+    assert tuple(st.shape) == (x.shape[0], model.layers, 96)
+    logits = torch.empty(x.shape[0], model.vocab, dtype=torch.float32, device=model.device)
+    for i in range(10):
+        model.step_into(torch.as_tensor(x[:, i], device=model.device), st, st, logits)
+        np.testing.assert_array_equal(logits.cpu().numpy(), om.step(x[:, i], ost))
+    np.testing.assert_array_equal(st.cpu().numpy(), ost)
+    bits = model.score(x[:, 9:], state=st)
+    np.testing.assert_allclose(bits, om.score(x[:, 9:], ost), rtol=BITS_RTOL)

@@ -98,11 +98,11 @@ template <int C> __device__ __forceinline__ int dot_q(const LaneQ<C> &a, const L
 // ------------------------------------------------------------------------------------------------ one layer
 
 // rho = 1 / sqrt(f32(sum q^2) * (1/n) + eps), or with group scales the sequential f32 sum over groups of 16 of
-// r2[g] * f32(S_g) (cpu/ygg.cpp:248-266).
+// r2[g] * f32(S_g) (cpu/ygg.cpp:248-266). inv_n = f32(1 / n) of the model's own n (the device layout may be padded:
+// padded coordinates are 0 and padded groups have r2 = 0, so they add exactly nothing).
 template <int N>
-__device__ __forceinline__ float rms_rho(const LaneQ<N / 32> &qb, const float *r2b, float eps) {
+__device__ __forceinline__ float rms_rho(const LaneQ<N / 32> &qb, const float *r2b, float eps, float inv_n) {
     constexpr int C = N / 32;
-    const float inv_n = 1.0f / (float)N;
     int part = dot_q<C>(qb, qb);
     if (r2b == nullptr) {
         const int S = __reduce_add_sync(kFull, part);

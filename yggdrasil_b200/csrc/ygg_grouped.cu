@@ -135,7 +135,7 @@ __global__ void __launch_bounds__(256) g_route(const __grid_constant__ DevModel 
     int leaf = x;
     if (l > 0) {
         const LaneQ<C> qbelow = load_q<C>(state + ((size_t)s * m.L + (l - 1)) * N + C * lane);
-        const float rho = rms_rho<N>(qbelow, y.r2b, y.rms_eps);
+        const float rho = rms_rho<N>(qbelow, y.r2b, y.rms_eps, m.inv_n);
         store_q<C>(qb_s[warp] + C * lane, qbelow);
         __syncwarp();
         const uint4 qrow = *(const uint4 *)(qb_s[warp] + 16 * (lane % (N / 16)));
@@ -466,6 +466,21 @@ __global__ void g_check(int B, int T, int V, const int32_t *__restrict__ tokens,
     }
 }
 
+// The caller's state [B][L][ns] to and from the device layout [B][L][N] of a model whose n is padded (ns < N): the
+// grouped kernels then work on the padded copy, whose extra coordinates start and stay 0.
+__global__ void g_state_pad(int B, int L, int ns, int N, const int8_t *__restrict__ src, int8_t *__restrict__ dst) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)B * L * N) return;
+    const size_t row = i / N;
+    const int c = (int)(i % N);
+    dst[i] = (src != nullptr && c < ns) ? src[row * ns + c] : (int8_t)0;
+}
+__global__ void g_state_unpad(int B, int L, int ns, int N, const int8_t *__restrict__ src, int8_t *__restrict__ dst) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)B * L * ns) return;
+    dst[i] = src[(i / ns) * N + i % ns];
+}
+
 // ------------------------------------------------------------------------------------------------ host side
 
 size_t grouped_ws_bytes(const DevModel &m, int B) {
@@ -501,13 +516,17 @@ template <int N, int BLK, int R, int R2T, int NVT>
 static cudaError_t run_grouped_t(const DevModel &m, int B, int T, const int32_t *tok, int8_t *state, double *bits,
                                  void *workspace, int G, int sm_count, cudaStream_t st) {
     GroupWs ws = grouped_layout(m, B, (uint8_t *)workspace);
-    int8_t *q = state ? state : ws.state;
+    // the caller's state in place, unless there is none (zero start) or its layout is narrower than the device's
+    const bool padded = m.ns != N;
+    int8_t *q = (state && !padded) ? state : ws.state;
     const size_t Emax = (size_t)(m.E > m.V ? m.E : m.V);
     cudaError_t e = cudaMemsetAsync(ws.cnt, 0, 4 * Emax, st);
     if (e == cudaSuccess) e = cudaMemsetAsync(ws.nll, 0, 8 * (size_t)B, st);
     if (e == cudaSuccess) e = cudaMemsetAsync(bits, 0, 8 * (size_t)B, st);
-    if (e == cudaSuccess && !state) e = cudaMemsetAsync(ws.state, 0, (size_t)B * m.L * N, st);
+    if (e == cudaSuccess && !state && !padded) e = cudaMemsetAsync(ws.state, 0, (size_t)B * m.L * N, st);
     if (e != cudaSuccess) return e;
+    const size_t cells = (size_t)B * m.L * N;
+    if (padded) g_state_pad<<<(unsigned)((cells + 255) / 256), 256, 0, st>>>(B, m.L, m.ns, N, state, ws.state);
     g_check<<<(B + 255) / 256, 256, 0, st>>>(B, T, m.V, tok, m.status, bits, ws.bad);
     if (T < 2) return cudaGetLastError();   // no next token to score
     // N = 256 has no tensor-core path (its operands do not fit a block's shared memory): every stream is light
@@ -531,6 +550,8 @@ static cudaError_t run_grouped_t(const DevModel &m, int B, int T, const int32_t 
         }
         g_head_nll<R, NVT><<<rb, 256, 0, st>>>(m, B, T, t, tok, ws, bits);
     }
+    if (padded && state)
+        g_state_unpad<<<(unsigned)(((size_t)B * m.L * m.ns + 255) / 256), 256, 0, st>>>(B, m.L, m.ns, N, ws.state, state);
     return cudaGetLastError();
 }
 

@@ -2,7 +2,9 @@
 // layout of ygg_model.h, one device allocation per model, and the launch entry points.
 //
 // File format (the reference's, cpu/export.py:34-51,382-468, read by cpu/ygg.cpp:137-220): "YGG1", 11 int32 header
-// fields, the array count, a table of (name[32], offset int64, bytes int64), zero padding to 64, the arrays.
+// fields, the array count, a table of (name[32], offset int64, bytes int64), zero padding to 64, the arrays. Beyond
+// the reference's limits the loader admits one extension, d_state 96 with readout rank 12 (the readout stored in the
+// rank-16 layout with zero rows 12-15); it is laid out on the device as n = 128, R = 16 with zero padding.
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <stdlib.h>
@@ -138,9 +140,12 @@ int ygg_load(const void *file_bytes, size_t nbytes, int device, ygg_model **out)
     if (nbytes < 4 + sizeof(FileHeader) || memcmp(f, "YGG1", 4)) return YGG_E_FORMAT;
     FileHeader h;
     memcpy(&h, f + 4, sizeof h);
-    const int L = h.n_layers, n = h.d_state, b = h.block_size, V = h.vocab, D = h.router_depth, R = h.readout_rank,
+    const int L = h.n_layers, nf = h.d_state, b = h.block_size, V = h.vocab, D = h.router_depth, Rf = h.readout_rank,
               R2 = h.layer_input_rank, K = h.input_rank;
-    const bool ok = (n == 64 || n == 128 || n == 256) && (b == 8 || b == 16) && (R == 8 || R == 16 || R == 32) &&
+    // nf, Rf: the file's state size and readout rank; n, R: the device layout's (the extension pads 96 -> 128 and
+    // 12 -> 16); Rs: readout rows as stored in the file (rank 12 takes the rank-16 layout)
+    const bool ok = (nf == 64 || nf == 96 || nf == 128 || nf == 256) && (b == 8 || b == 16) &&
+                    (Rf == 8 || Rf == 12 || Rf == 16 || Rf == 32) &&
                     R2 >= 0 && R2 <= 64 && R2 % 4 == 0 && L >= 1 && L <= kMaxLayers && V >= 1 && V <= 256 &&
                     D >= 0 && D <= 16 && (L == 1 || D >= 1) && h.reserved == 0 && h.shift >= 1 && h.shift <= 30 &&
                     K >= 0 && K <= 64 && K % 4 == 0;
@@ -158,8 +163,9 @@ int ygg_load(const void *file_bytes, size_t nbytes, int device, ygg_model **out)
             return YGG_E_FORMAT;
         arr[std::string(e.name, strnlen(e.name, 32))] = Arr{f + pos + e.offset, e.bytes};
     }
+    const int n = nf == 96 ? 128 : nf, R = Rf == 12 ? 16 : Rf, Rs = Rf == 12 ? 16 : Rf;
     const int E = 1 << D, VP = (V + kClassPad - 1) / kClassPad * kClassPad, C = n / 32;
-    const int R2P = (int)round_up(R2, 16), KP = (int)round_up(K, 16), NG = n / 16;
+    const int R2P = (int)round_up(R2, 16), KP = (int)round_up(K, 16), NG = n / 16, NGf = nf / 16;
     auto get = [&](int l, const char *tag, int64_t want, Arr &a) -> int {  // 1 found, 0 absent, <0 bad size
         const auto it = arr.find("l" + std::to_string(l) + "_" + tag);
         if (it == arr.end()) return 0;
@@ -182,7 +188,7 @@ int ygg_load(const void *file_bytes, size_t nbytes, int device, ygg_model **out)
         LayerPlan &P = plan[l];
         const int Ee = l == 0 ? V : E;   // experts of the layer: the token layer has one per token
         Arr meta, rec, Q, scal;
-        if (get(l, "meta", -1, meta) != 1 || get(l, "rec", -1, rec) != 1 || get(l, "Q", (int64_t)R * VP, Q) != 1 ||
+        if (get(l, "meta", -1, meta) != 1 || get(l, "rec", -1, rec) != 1 || get(l, "Q", (int64_t)Rf * VP, Q) != 1 ||
             get(l, "scal", 16, scal) != 1)
             return YGG_E_MISSING;
         if (meta.bytes != 20 && meta.bytes != 32) return YGG_E_MISSING;
@@ -195,19 +201,19 @@ int ygg_load(const void *file_bytes, size_t nbytes, int device, ygg_model **out)
         const int hv = get(l, "vt", (int64_t)V * K, vt);
         if (hv < 0) return YGG_E_MISSING;
         const bool fact = hv == 1;
-        if (fact && (K < 4 || meta.bytes != 32 || get(l, "mT", 4 * (int64_t)n, mT) != 1)) return YGG_E_MISSING;
+        if (fact && (K < 4 || meta.bytes != 32 || get(l, "mT", 4 * (int64_t)nf, mT) != 1)) return YGG_E_MISSING;
         const bool low = l > 0 && R2 > 0;
         auto part_ok = [&](int off, int64_t size) { return off >= 0 && (int64_t)off + size <= rb; };
-        if (!part_ok(mt[1], 2LL * n * b) || !part_ok(mt[3], (int64_t)R * n)) return YGG_E_MISSING;
-        if (low && !part_ok(mt[2], (int64_t)n * R2)) return YGG_E_MISSING;
+        if (!part_ok(mt[1], 2LL * nf * b) || !part_ok(mt[3], (int64_t)Rs * nf)) return YGG_E_MISSING;
+        if (low && !part_ok(mt[2], (int64_t)nf * R2)) return YGG_E_MISSING;
         if (fact) {
-            if (!part_ok(mt[5], (int64_t)n * K) || !part_ok(mt[6], 2LL * n) || !part_ok(mt[7], 4)) return YGG_E_MISSING;
+            if (!part_ok(mt[5], (int64_t)nf * K) || !part_ok(mt[6], 2LL * nf) || !part_ok(mt[7], 4)) return YGG_E_MISSING;
         } else {
             // table rows: V per routed expert, the own row for the token layer (cpu/ygg.cpp:188)
-            if (!part_ok(mt[4], (l == 0 ? 2LL : 2LL * V) * n)) return YGG_E_MISSING;
+            if (!part_ok(mt[4], (l == 0 ? 2LL : 2LL * V) * nf)) return YGG_E_MISSING;
         }
         Arr mzl, sqv;
-        const int hmz = get(l, "mzl", (int64_t)Ee * (R == 8 ? 16 : R) * 4, mzl);
+        const int hmz = get(l, "mzl", (int64_t)Ee * (Rf == 8 ? 16 : Rf) * 4, mzl);
         const int hsq = get(l, "sqv", 4LL * VP, sqv);
         if (hmz < 0 || hsq < 0) return YGG_E_MISSING;
 
@@ -234,6 +240,7 @@ int ygg_load(const void *file_bytes, size_t nbytes, int device, ygg_model **out)
             for (int ln = 0; ln < 32; ln++)
                 for (int ii = 0; ii < C; ii++) {
                     const int i = C * ln + ii;
+                    if (i >= nf) continue;   // padded coordinates: zero rows
                     for (int jj = 0; jj < b; jj++) {
                         const int16_t v = A[(((i / 16) * (b / 2) + jj / 2) * 16 + i % 16) * 2 + jj % 2];
                         const size_t lb = (size_t)(ii * (b / 2) + jj / 2) * 4 + (jj % 2) * 2;
@@ -245,9 +252,10 @@ int ygg_load(const void *file_bytes, size_t nbytes, int device, ygg_model **out)
                 for (int ln = 0; ln < 32; ln++)
                     for (int ii = 0; ii < C; ii++) {
                         const int i = C * ln + ii;
+                        if (i >= nf) continue;
                         for (int k = 0; k < rank; k++)
                             pd[lane_byte(ln, (size_t)ii * rankp + k)] =
-                                (uint8_t)(u[((size_t)(k / 4) * n + i) * 4 + k % 4] - 128);
+                                (uint8_t)(u[((size_t)(k / 4) * nf + i) * 4 + k % 4] - 128);
                     }
             };
             if (low) proj(src + mt[2], R2, R2P, dst + P.off_u);
@@ -255,30 +263,32 @@ int ygg_load(const void *file_bytes, size_t nbytes, int device, ygg_model **out)
             uint8_t *pp = dst + P.off_p;
             const uint8_t *ps = src + mt[3];
             for (int ln = 0; ln < 32; ln++)
-                for (int rr = 0; rr < R; rr++)
+                for (int rr = 0; rr < Rf; rr++)
                     for (int cc = 0; cc < C; cc++) {
                         const int i = C * ln + cc;
-                        const size_t idx = R == 8 ? ((size_t)(i / 8) * 16 + 2 * rr + (i % 8) / 4) * 4 + i % 4
-                                                  : ((size_t)((rr / 16) * (n / 4) + i / 4) * 16 + rr % 16) * 4 + i % 4;
+                        if (i >= nf) continue;
+                        const size_t idx = Rf == 8 ? ((size_t)(i / 8) * 16 + 2 * rr + (i % 8) / 4) * 4 + i % 4
+                                                   : ((size_t)((rr / 16) * (nf / 4) + i / 4) * 16 + rr % 16) * 4 + i % 4;
                         pp[lane_byte(ln, (size_t)rr * C + cc)] = (uint8_t)(ps[idx] - 128);
                     }
             if (fact) {
                 proj(src + mt[5], K, KP, dst + P.off_f);
-                memcpy(dst + P.off_cb, src + mt[6], 2 * (size_t)n);
+                memcpy(dst + P.off_cb, src + mt[6], 2 * (size_t)nf);
                 memcpy(dst + P.off_su, src + mt[7], 4);
             }
             if (hmz == 1) {   // R = 8: the file holds each row's scale twice (lanes 2r, 2r+1)
-                const float *mz = (const float *)mzl.p + (size_t)r * (R == 8 ? 16 : R);
-                for (int rr = 0; rr < R; rr++) memcpy(dst + P.off_mz + 4 * rr, mz + (R == 8 ? 2 * rr : rr), 4);
+                const float *mz = (const float *)mzl.p + (size_t)r * (Rf == 8 ? 16 : Rf);
+                for (int rr = 0; rr < Rf; rr++) memcpy(dst + P.off_mz + 4 * rr, mz + (Rf == 8 ? 2 * rr : rr), 4);
             }
         }
         P.rec = blob.add(std::move(dr));
         if (!fact) {   // table rows int16, contiguous per expert
             P.table_rows = l == 0 ? 1 : (uint32_t)V;
-            std::vector<uint8_t> t((size_t)Ee * P.table_rows * 2 * n);
+            std::vector<uint8_t> t((size_t)Ee * P.table_rows * 2 * n, 0);
             for (int r = 0; r < Ee; r++)
-                memcpy(t.data() + (size_t)r * P.table_rows * 2 * n, rec.p + (size_t)r * rb + mt[4],
-                       (size_t)P.table_rows * 2 * n);
+                for (uint32_t row = 0; row < P.table_rows; row++)
+                    memcpy(t.data() + ((size_t)r * P.table_rows + row) * 2 * n,
+                           rec.p + (size_t)r * rb + mt[4] + (size_t)row * 2 * nf, 2 * (size_t)nf);
             P.table = blob.add(std::move(t));
             P.has_table = true;
         } else {
@@ -286,46 +296,54 @@ int ygg_load(const void *file_bytes, size_t nbytes, int device, ygg_model **out)
             for (int x = 0; x < V; x++) memcpy(c.data() + (size_t)x * KP, vt.p + (size_t)x * K, K);
             P.vt = blob.add(std::move(c));
             P.has_vt = true;
-            P.mt = blob.add(std::vector<uint8_t>(mT.p, mT.p + 4 * n));
+            std::vector<uint8_t> ts(4 * (size_t)n, 0);
+            memcpy(ts.data(), mT.p, 4 * (size_t)nf);
+            P.mt = blob.add(std::move(ts));
             any_factored = true;
         }
         // ---- shared per-layer arrays
         {   // unembedding u8 (q + 128) [R/4][VP][4] (cpu/export.py:345-350) -> s8 [VP][R] (class c = 32 m + lane)
-            std::vector<uint8_t> q((size_t)VP * R);
+            std::vector<uint8_t> q((size_t)VP * R, 0);
             for (int c = 0; c < VP; c++)
-                for (int k = 0; k < R; k++) q[(size_t)c * R + k] = (uint8_t)(Q.p[((size_t)(k / 4) * VP + c) * 4 + k % 4] - 128);
+                for (int k = 0; k < Rf; k++) q[(size_t)c * R + k] = (uint8_t)(Q.p[((size_t)(k / 4) * VP + c) * 4 + k % 4] - 128);
             P.unembed = blob.add(std::move(q));
         }
         if (hsq == 1) { P.sqv = blob.add(std::vector<uint8_t>(sqv.p, sqv.p + 4 * VP)); P.has_sqv = true; }
         if (hmz == 1) any_mz = true;
         if (l > 0) {
             Arr w, thr;
-            if (get(l, "w", (int64_t)E * n, w) != 1 || get(l, "thr", 4LL * V * E, thr) != 1) return YGG_E_MISSING;
-            std::vector<uint8_t> ws(w.p, w.p + (size_t)E * n);
-            for (auto &v : ws) v = (uint8_t)(v - 128);   // u8 (w + 128) -> s8 w
+            if (get(l, "w", (int64_t)E * nf, w) != 1 || get(l, "thr", 4LL * V * E, thr) != 1) return YGG_E_MISSING;
+            std::vector<uint8_t> ws((size_t)E * n, 0);
+            for (int e = 0; e < E; e++)   // u8 (w + 128) -> s8 w
+                for (int j = 0; j < nf; j++) ws[(size_t)e * n + j] = (uint8_t)(w.p[(size_t)e * nf + j] - 128);
             P.w = blob.add(std::move(ws));
             P.thr = blob.add(std::vector<uint8_t>(thr.p, thr.p + 4 * (size_t)V * E));
             P.has_w = true;
             if (R2) {
                 const int RG = R2P / 16;
                 Arr vl, mv;
-                if (get(l, "vl", (int64_t)RG * 16 * n, vl) != 1 || get(l, "mv", 4LL * 16 * RG, mv) != 1)
+                if (get(l, "vl", (int64_t)RG * 16 * nf, vl) != 1 || get(l, "mv", 4LL * 16 * RG, mv) != 1)
                     return YGG_E_MISSING;
                 // u8 (v + 128) [RG][n/4][16][4] (cpu/export.py:402-409) -> s8 [n/16][R2P][16]: lane k's chunk j
-                std::vector<uint8_t> d((size_t)NG * R2P * 16);
+                std::vector<uint8_t> d((size_t)NG * R2P * 16, 0);
                 for (int k = 0; k < R2P; k++)
-                    for (int col = 0; col < n; col++)
+                    for (int col = 0; col < nf; col++)
                         d[((size_t)(col / 16) * R2P + k) * 16 + col % 16] =
-                            (uint8_t)(vl.p[(((size_t)(k / 16) * (n / 4) + col / 4) * 16 + k % 16) * 4 + col % 4] - 128);
+                            (uint8_t)(vl.p[(((size_t)(k / 16) * (nf / 4) + col / 4) * 16 + k % 16) * 4 + col % 4] - 128);
                 P.vl = blob.add(std::move(d));
                 P.mv = blob.add(std::vector<uint8_t>(mv.p, mv.p + 4 * R2P));
                 P.has_vl = true;
             }
             Arr mulv, r2b;
-            const int hm = get(l, "mulv", 4LL * n, mulv), hr = get(l, "r2b", 4LL * NG, r2b);
+            const int hm = get(l, "mulv", 4LL * nf, mulv), hr = get(l, "r2b", 4LL * NGf, r2b);
             if (hm < 0 || hr < 0) return YGG_E_MISSING;
-            if (hm == 1) { P.mulv = blob.add(std::vector<uint8_t>(mulv.p, mulv.p + 4 * n)); P.has_mulv = true; }
-            if (hr == 1) { P.r2b = blob.add(std::vector<uint8_t>(r2b.p, r2b.p + 4 * NG)); P.has_r2b = true; any_group = true; }
+            auto padded = [](const Arr &a, size_t bytes) {   // a's bytes, zero padded to `bytes`
+                std::vector<uint8_t> v(bytes, 0);
+                memcpy(v.data(), a.p, (size_t)a.bytes);
+                return v;
+            };
+            if (hm == 1) { P.mulv = blob.add(padded(mulv, 4 * (size_t)n)); P.has_mulv = true; }
+            if (hr == 1) { P.r2b = blob.add(padded(r2b, 4 * (size_t)NG)); P.has_r2b = true; any_group = true; }
         }
     }
 
@@ -363,6 +381,8 @@ int ygg_load(const void *file_bytes, size_t nbytes, int device, ygg_model **out)
     memset(&dm, 0, sizeof dm);
     dm.L = L; dm.n = n; dm.b = b; dm.V = V; dm.VP = VP; dm.D = D; dm.E = E; dm.R = R; dm.R2 = R2; dm.R2P = R2P;
     dm.K = K; dm.KP = KP; dm.shift = h.shift; dm.factored = any_factored; dm.has_mz = any_mz;
+    dm.ns = nf;
+    dm.inv_n = 1.0f / (float)nf;   // the reference's (1.0f / N) (cpu/ygg.cpp:253), f32(1.0 / n) in int_forward
     dm.head_b = (const float *)d;
     dm.status = (int *)(d + status_off);
     m->d_status = dm.status;
@@ -422,7 +442,7 @@ int ygg_load(const void *file_bytes, size_t nbytes, int device, ygg_model **out)
     m->grid_cap = 1 << 30;
     ygg_info_t &inf = m->info;
     memset(&inf, 0, sizeof inf);
-    inf.n_layers = L; inf.d_state = n; inf.block_size = b; inf.vocab = V; inf.router_depth = D; inf.readout_rank = R;
+    inf.n_layers = L; inf.d_state = nf; inf.block_size = b; inf.vocab = V; inf.router_depth = D; inf.readout_rank = Rf;
     inf.layer_input_rank = R2; inf.router_token_dim = h.router_token_dim; inf.input_rank = K; inf.shift = h.shift;
     inf.n_experts = E; inf.vocab_pad = VP; inf.factored = any_factored; inf.group_scales = any_group;
     inf.file_array_bytes = (int64_t)avail; inf.device_bytes = (int64_t)m->d_bytes; inf.record_bytes = (int32_t)rec_max;

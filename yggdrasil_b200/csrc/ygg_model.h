@@ -17,6 +17,11 @@
 // Shared per layer: router rows s8 [E][n] (heap order, row 0 unused), thresholds f32 [V][E], the layer-input down
 // projection s8 [n/16][R2P][16] (lane k reads its row k as 16-byte chunks), mv f32 [R2P], tables int16 rows of n,
 // token codes s8 [V][KP], the unembedding s8 [VP/32][32][R] (class 32 m + lane), optional group scales.
+//
+// A file of the d_state 96 extension (readout rank 12) is laid out as n = 128 and R = 16 with zero rows and columns:
+// the padded coordinates see zero weights everywhere, so they stay 0 and add nothing to any dot, and the kernels run
+// the n = 128 code. Only two things keep the file's n: the caller's state layout (ns coordinates per layer) and rho's
+// f32(1 / ns).
 #pragma once
 #include <stdint.h>
 
@@ -53,7 +58,9 @@ struct DevLayer {
 };
 
 struct DevModel {
-    int L, n, b, V, VP, D, E, R, R2, R2P, K, KP, shift;
+    int L, n, b, V, VP, D, E, R, R2, R2P, K, KP, shift;   // n, R: the device layout's (padded) sizes
+    int ns;                      // state coordinates per layer in the caller's layout: the file's d_state (<= n)
+    float inv_n;                 // f32(1 / ns), rho's mean factor
     int factored, has_mz;
     const float *head_b;         // [VP]
     int *status;                 // device status word (bit flags of Status)

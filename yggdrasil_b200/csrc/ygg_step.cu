@@ -76,8 +76,9 @@ struct StepOut {
     int32_t *acc;       // [L][n] or null
 };
 
-// What a token's layers share: the block's pool and the warp's scratch, the token, the state pointers, the debug
-// outputs and the new state of the layer below (carried from one layer to the next).
+// What a token's layers share: the block's pool and the warp's scratch, the token, the state pointers (qstride
+// coordinates per layer; qlane: this lane's coordinates exist there), the debug outputs and the new state of the
+// layer below (carried from one layer to the next).
 template <int C>
 struct TokenCtx {
     const DevModel &m;
@@ -86,6 +87,8 @@ struct TokenCtx {
     int home, warp, lane, x;
     const int8_t *q_in;
     int8_t *q_out;
+    int qstride;
+    bool qlane;
     const StepOut &dbg;
     LaneQ<C> qbelow;
 };
@@ -103,15 +106,18 @@ __device__ __forceinline__ bool layer_step(TokenCtx<N / 32> &t, const int l, flo
     const int nv = NVT ? NVT : m.VP / 32;
     const int8_t *q_in = t.q_in;
     int8_t *q_out = t.q_out;
+    const int qstride = t.qstride;
+    const bool qlane = t.qlane;
     const StepOut &dbg = t.dbg;
     LaneQ<C> &qbelow = t.qbelow;
     const DevLayer &y = m.layer[l];
-    const LaneQ<C> qold = load_q<C>(q_in + (size_t)l * N + C * lane);
+    LaneQ<C> qold = {};
+    if (qlane) qold = load_q<C>(q_in + (size_t)l * qstride + C * lane);
     int r = x;
     float rho = 0.0f;
     const bool low = l > 0 && (R2T > 0 || m.R2 > 0);
     if (l > 0) {
-        rho = rms_rho<N>(qbelow, y.r2b, y.rms_eps);
+        rho = rms_rho<N>(qbelow, y.r2b, y.rms_eps, m.inv_n);
         store_q<C>(sc.qb + C * lane, qbelow);
         __syncwarp();
         const uint4 qrow = *(const uint4 *)(sc.qb + 16 * (lane % (N / 16)));
@@ -153,11 +159,17 @@ __device__ __forceinline__ bool layer_step(TokenCtx<N / 32> &t, const int l, flo
     int acc[C];
     LaneQ<C> qn;
     leaf_update<N, BLK, R2T>(m, y, rec, has_table ? trow : nullptr, x, sc.qold, sc.zl, low, lane, acc, qn);
-    store_q<C>(q_out + (size_t)l * N + C * lane, qn);
-    if (dbg.routes != nullptr && lane == 0) dbg.routes[l] = r;
-    if (dbg.acc != nullptr) {
+    if (m.ns < N && C * lane >= m.ns) {   // padding of a narrower model: held at exactly 0
 #pragma unroll
-        for (int ii = 0; ii < C; ii++) dbg.acc[(size_t)l * N + C * lane + ii] = acc[ii];
+        for (int i = 0; i < (C >= 4 ? C / 4 : 1); i++) qn.w[i] = 0;
+#pragma unroll
+        for (int ii = 0; ii < C; ii++) acc[ii] = 0;
+    }
+    if (qlane) store_q<C>(q_out + (size_t)l * qstride + C * lane, qn);
+    if (dbg.routes != nullptr && lane == 0) dbg.routes[l] = r;
+    if (dbg.acc != nullptr && qlane) {
+#pragma unroll
+        for (int ii = 0; ii < C; ii++) dbg.acc[(size_t)l * qstride + C * lane + ii] = acc[ii];
     }
     const ReadoutWords<N, R> ro = load_readout<N, R>(y, rec, lane);
     // the slot is free once its bytes are in registers: flip its parity and hand it back
@@ -176,19 +188,20 @@ __device__ __forceinline__ bool layer_step(TokenCtx<N / 32> &t, const int l, flo
     return true;
 }
 
-// One token of one stream through every layer. q_in / q_out: the stream's state [L][n] (global or shared memory;
-// they may alias). lg: the logits of the lane's classes (out). Returns false if a bounded wait gave up.
+// One token of one stream through every layer. q_in / q_out: the stream's state [L][qstride] (global memory in the
+// caller's layout, qstride = the model's ns, or shared memory in the device layout, qstride = n; they may alias).
+// lg: the logits of the lane's classes (out). Returns false if a bounded wait gave up.
 // Compile-time shape where a fast instance fixes it (0: read from the model at run time): R2T the padded layer-input
 // rank, LT the number of layers, NVT the classes per lane (VP / 32).
 template <int N, int BLK, int R, int R2T, int LT, int NVT>
 __device__ __forceinline__ bool token_step(const DevModel &m, const Pool &pool, const Scratch &sc, int home, int warp,
-                                           int x, const int8_t *q_in, int8_t *q_out,
+                                           int x, const int8_t *q_in, int8_t *q_out, int qstride,
                                            float (&lg)[kMaxClassesPerLane], const StepOut &dbg, int lane) {
     const int V = m.V;
     const int nv = NVT ? NVT : m.VP / 32;
 #pragma unroll
     for (int c = 0; c < kMaxClassesPerLane; c++) lg[c] = c < nv ? __ldg(m.head_b + 32 * c + lane) : 0.0f;
-    TokenCtx<N / 32> t{m, pool, sc, home, warp, lane, x, q_in, q_out, dbg, {}};
+    TokenCtx<N / 32> t{m, pool, sc, home, warp, lane, x, q_in, q_out, qstride, (N / 32) * lane < qstride, dbg, {}};
     if constexpr (LT > 0) {
         // not unrolled: an unrolled layer loop with its early exits defeats the compiler's proof that the warp is
         // converged at the collectives, and each shuffle / ballot / redux then pays a re-convergence loop
@@ -252,7 +265,7 @@ __global__ void __launch_bounds__(256, blocks_per_sm<N>()) step_kernel(const __g
     int8_t *unused;
     block_init(smem, rec_max, N, S, 0, warp, lane, pool, sc, unused);
     const int home = warp % S;
-    const int L = m.L, V = m.V;
+    const int L = m.L, V = m.V, ns = m.ns;
     for (int s = blockIdx.x * W + warp; s < B; s += gridDim.x * W) {
         const int x = tokens[s];
         if (x < 0 || x >= V) {   // cpu/ygg.cpp:493-495 rejects the whole input; here the stream is skipped
@@ -260,15 +273,15 @@ __global__ void __launch_bounds__(256, blocks_per_sm<N>()) step_kernel(const __g
             if (logits != nullptr)
                 for (int c = lane; c < V; c += 32) logits[(size_t)s * V + c] = __int_as_float(0x7fc00000);
             if (state_out != state_in)
-                for (int i = lane; i < L * N; i += 32) state_out[(size_t)s * L * N + i] = state_in[(size_t)s * L * N + i];
+                for (int i = lane; i < L * ns; i += 32) state_out[(size_t)s * L * ns + i] = state_in[(size_t)s * L * ns + i];
             if (routes != nullptr && lane < L) routes[(size_t)s * L + lane] = -1;
             continue;
         }
         float lg[kMaxClassesPerLane];
         StepOut o{logits ? logits + (size_t)s * V : nullptr, routes ? routes + (size_t)s * L : nullptr,
-                  acc_out ? acc_out + (size_t)s * L * N : nullptr};
-        if (!token_step<N, BLK, R, R2T, LT, NVT>(m, pool, sc, home, warp, x, state_in + (size_t)s * L * N, state_out + (size_t)s * L * N,
-                                   lg, o, lane)) {
+                  acc_out ? acc_out + (size_t)s * L * ns : nullptr};
+        if (!token_step<N, BLK, R, R2T, LT, NVT>(m, pool, sc, home, warp, x, state_in + (size_t)s * L * ns,
+                                                 state_out + (size_t)s * L * ns, ns, lg, o, lane)) {
             if (lane == 0) atomicOr(m.status, kStatusTimeout);
             return;
         }
@@ -283,7 +296,7 @@ __global__ void __launch_bounds__(256, blocks_per_sm<N>()) score_kernel(const __
                                                     double *__restrict__ bits, uint32_t rec_max, int S) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = blockDim.x >> 5;
-    const int L = m.L, V = m.V, nv = m.VP / 32;
+    const int L = m.L, V = m.V, nv = m.VP / 32, ns = m.ns;
     Pool pool;
     Scratch sc;
     int8_t *qs;
@@ -298,12 +311,16 @@ __global__ void __launch_bounds__(256, blocks_per_sm<N>()) score_kernel(const __
             if (lane == 0) { atomicOr(m.status, kStatusBadToken); bits[s] = __longlong_as_double(0x7ff8000000000000LL); }
             continue;
         }
-        for (int i = lane; i < L * N; i += 32) qs[i] = state ? state[(size_t)s * L * N + i] : 0;
+        // the row's state into the device layout (n per layer; coordinates past the model's ns are 0)
+        for (int i = lane; i < L * N; i += 32) {
+            const int li = i / N, c = i % N;
+            qs[i] = (state != nullptr && c < ns) ? state[((size_t)s * L + li) * ns + c] : (int8_t)0;
+        }
         __syncwarp();
         double nll = 0.0;
         for (int t = 0; t + 1 < T; t++) {
             float lg[kMaxClassesPerLane];
-            if (!token_step<N, BLK, R, R2T, LT, NVT>(m, pool, sc, home, warp, tok[t], qs, qs, lg, none, lane)) {
+            if (!token_step<N, BLK, R, R2T, LT, NVT>(m, pool, sc, home, warp, tok[t], qs, qs, N, lg, none, lane)) {
                 if (lane == 0) atomicOr(m.status, kStatusTimeout);
                 return;
             }
@@ -312,7 +329,10 @@ __global__ void __launch_bounds__(256, blocks_per_sm<N>()) score_kernel(const __
         if (lane == 0) bits[s] = nll / 0.69314718055994530942;
         __syncwarp();
         if (state)
-            for (int i = lane; i < L * N; i += 32) state[(size_t)s * L * N + i] = qs[i];
+            for (int i = lane; i < L * N; i += 32) {
+                const int li = i / N, c = i % N;
+                if (c < ns) state[((size_t)s * L + li) * ns + c] = qs[i];
+            }
         __syncwarp();
     }
 }

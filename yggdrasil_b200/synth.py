@@ -15,7 +15,7 @@ import dataclasses
 
 import numpy as np
 
-from .ygg1 import SHIFT, STATE_GROUP, FactoredInput, IntLayer, write_model
+from .ygg1 import LIMITS, SHIFT, STATE_GROUP, FactoredInput, IntLayer, write_model
 
 f32 = np.float32
 
@@ -32,6 +32,11 @@ class ModelShape:
     layer_input_rank: int = 16
     input_rank: int = 0          # > 0: factored input storage of this rank
     group: bool = False          # group scales
+
+    @property
+    def extended(self) -> bool:
+        """Outside the reference's YGG1 limits: a file of this shape needs the d_state 96 extension (ygg1 module)."""
+        return self.d_state not in LIMITS["d_state"] or self.readout_rank not in LIMITS["readout_rank"]
 
 
 def random_layers(shape: ModelShape, seed: int = 1):
@@ -85,12 +90,12 @@ def random_layers(shape: ModelShape, seed: int = 1):
     return layers
 
 
-def write_random_model(shape: ModelShape, path, seed: int = 7, output_bias=None):
+def write_random_model(shape: ModelShape, path, seed: int = 7, output_bias=None, extended: bool = False):
     """Random model of shape written to path; output bias linspace(-1, 1, V) by default (as the reference's kernel
-    test uses, cpu/tests/test_kernel.py:39). Returns the layers."""
+    test uses, cpu/tests/test_kernel.py:39). extended: admit the d_state 96 extension. Returns the layers."""
     layers = random_layers(shape, seed)
     ob = np.linspace(-1, 1, shape.vocab) if output_bias is None else output_bias
-    write_model(layers, ob, path)
+    write_model(layers, ob, path, extended=extended)
     return layers
 
 
@@ -121,15 +126,24 @@ class Workload:
     leaves: str = "random"       # "random": the generator's thresholds; "zipf": calibrated to Zipf(1.1) leaf usage
     model: str = ""              # the workload whose model file this one shares ("": its own)
 
+    @property
+    def extended(self) -> bool:
+        return self.shape.extended
+
 
 WORKLOADS = {
     # V256 L2 d64 D10: batch 1, 4096 uniform bytes
     "c1": Workload("c1-5M-enwik8", ModelShape(64, 16, 10, 256, 2, 8, 16), 1, 4096, "uniform"),
     # V256 L4 d64 D12, factored k=16 (73.1 MB) is the file closest to the named 65 MB
     "c2": Workload("c2-65MB-enwik8", ModelShape(64, 16, 12, 256, 4, 8, 16, input_rank=16), 4096, 1024, "uniform"),
-    # V5 L4 D13 with R = n/8, R2 = n/4 at d = 128: the YGG1 format allows d_state 64/128/256 only (not 96)
+    # V5 L4 D13 with R = n/8, R2 = n/4 at d = 128 (287 MB): the nearest shape inside the reference's YGG1 limits
+    # (d_state 64/128/256, readout rank 8/16/32), so that the reference's ygg runs the same file as the CPU baseline
     "c3": Workload("c3-200M-dna-d128", ModelShape(128, 16, 13, 5, 4, 16, 32), 65536, 512, "dna",
-                   "d_state 128 in place of 96 (YGG1 allows 64/128/256)"),
+                   "d_state 128 in place of 96 (the reference's YGG1 allows 64/128/256)"),
+    # the named d = 96 (186.9 MB, R = 12, R2 = 24) through this repository's d_state 96 extension, which the
+    # reference's ygg refuses; its oracle is the reference's int_forward
+    "c3n96": Workload("c3-200M-dna-d96", ModelShape(96, 16, 13, 5, 4, 12, 24), 65536, 512, "dna",
+                      "d_state 96 through the format extension (the reference's ygg refuses the file)"),
     # V256 L4 d128 D13 R16 R2=32, table storage (1892 MB)
     "c4": Workload("c4-730M-enwik8", ModelShape(128, 16, 13, 256, 4, 16, 32), 262144, 256, "uniform",
                    "table storage, 1892 MB; thresholds calibrated to Zipf(1.1) leaf usage", leaves="zipf"),

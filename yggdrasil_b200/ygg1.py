@@ -1,6 +1,6 @@
 """The YGG1 int8 model container: header, array table and per-expert records (host side, NumPy).
 
-The product's loader is native (``ygg_load`` in ``csrc/ygg_load.cpp`` parses the same bytes); this module writes files
+The product's loader is native (``ygg_load`` in ``csrc/ygg_load.cu`` parses the same bytes); this module writes files
 (synthetic models for the tests and the benchmark) and reads headers for the Python API. The byte layout has to be the
 reference's, so that files written by either side load in both:
 
@@ -13,6 +13,12 @@ reference's, so that files written by either side load in both:
 * expert records (``cpu/export.py:321-350,410-430``): transition int16 ``[n/16][b/2][16][2]``, projections u8
   ``[rank/4][n][4]`` (stored +128), readout u8 (R = 8: ``[n/8][16][4]``, R >= 16: ``[R/16][n/4][16][4]``),
   table int16 rows, each record padded to 64 bytes.
+
+One extension, written only when asked (``write_model(..., extended=True)``) and read only by this repository's
+loader and oracle: ``d_state = 96`` (the 200M DNA benchmark shape) with its readout rank ``n/8 = 12``. Every packing
+above holds at n = 96 (n/16, n/8 and n/4 are whole). A readout of rank 12 is stored in the R >= 16 layout as one group
+of 16 rows whose rows 12-15 are zero weights; its group scales (``mzl``) stay 12 per expert. The reference's writer
+and ``ygg`` refuse such files (``cpu/export.py:47``, ``cpu/ygg.cpp:141-146``).
 """
 from __future__ import annotations
 
@@ -35,6 +41,7 @@ ALIGN = 64
 RANK_MULTIPLE = 4
 LIMITS = dict(d_state=(64, 128, 256), block_size=(8, 16), readout_rank=(8, 16, 32), max_layer_input_rank=64,
               max_input_rank=64, max_vocab=256, max_layers=8, max_router_depth=16)
+EXTENDED_LIMITS = dict(LIMITS, d_state=(64, 96, 128, 256), readout_rank=(8, 12, 16, 32))
 f32 = np.float32
 
 
@@ -96,8 +103,12 @@ def _pack_projection(u: np.ndarray) -> np.ndarray:
 
 
 def _pack_readout(p: np.ndarray) -> np.ndarray:
-    """(E, R, n) -> per expert u8 (p + 128): R = 8 as [n/8][16 lanes][4], R >= 16 as [R/16][n/4][16][4]."""
+    """(E, R, n) -> per expert u8 (p + 128): R = 8 as [n/8][16 lanes][4], R >= 16 as [R/16][n/4][16][4]; the
+    extension's R = 12 as the R = 16 layout with zero rows 12-15."""
     e, r, n = p.shape
+    if r == 12:
+        p = np.concatenate([p, np.zeros((e, 4, n), p.dtype)], axis=1)
+        r = 16
     if r >= 16:
         t = p.reshape(e, r // 16, 16, n // 4, 4).transpose(0, 1, 3, 2, 4)
     else:
@@ -113,8 +124,10 @@ def _pack_unembed(q: np.ndarray, vp: int) -> np.ndarray:
     return np.ascontiguousarray((full + 128).reshape(vp, r // 4, 4).transpose(1, 0, 2).astype(np.uint8))
 
 
-def header_of(layers, vocab: int, router_token_dim: int = 0, input_rank: int = 0) -> dict:
-    """Header values of layers, checked against LIMITS; ValueError names the failing field."""
+def header_of(layers, vocab: int, router_token_dim: int = 0, input_rank: int = 0, extended: bool = False) -> dict:
+    """Header values of layers, checked against LIMITS (EXTENDED_LIMITS if extended); ValueError names the failing
+    field."""
+    limits = EXTENDED_LIMITS if extended else LIMITS
     first, routed = layers[0], layers[1:]
     r2 = routed[0].layer_input_proj.shape[2] if routed and routed[0].layer_input_proj is not None else 0
     fac = [q.factored for q in layers if q.factored is not None]
@@ -125,15 +138,15 @@ def header_of(layers, vocab: int, router_token_dim: int = 0, input_rank: int = 0
 
     def need(ok, field):
         if not ok:
-            raise ValueError(f"YGG1 cannot hold {field} = {hdr.get(field)} (limits {LIMITS})")
+            raise ValueError(f"YGG1 cannot hold {field} = {hdr.get(field)} (limits {limits})")
     for k in ("d_state", "block_size", "readout_rank"):
-        need(hdr[k] in LIMITS[k], k)
-    need(r2 % RANK_MULTIPLE == 0 and r2 <= LIMITS["max_layer_input_rank"], "layer_input_rank")
-    need(vocab <= LIMITS["max_vocab"], "vocab")
-    need(1 <= len(layers) <= LIMITS["max_layers"], "n_layers")
-    need(not routed or 1 <= hdr["router_depth"] <= LIMITS["max_router_depth"], "router_depth")
+        need(hdr[k] in limits[k], k)
+    need(r2 % RANK_MULTIPLE == 0 and r2 <= limits["max_layer_input_rank"], "layer_input_rank")
+    need(vocab <= limits["max_vocab"], "vocab")
+    need(1 <= len(layers) <= limits["max_layers"], "n_layers")
+    need(not routed or 1 <= hdr["router_depth"] <= limits["max_router_depth"], "router_depth")
     need(not fac or (hdr["input_rank"] % RANK_MULTIPLE == 0
-                     and RANK_MULTIPLE <= hdr["input_rank"] <= LIMITS["max_input_rank"]), "input_rank")
+                     and RANK_MULTIPLE <= hdr["input_rank"] <= limits["max_input_rank"]), "input_rank")
     for q in routed:
         need(q.depth == hdr["router_depth"], "router_depth")
         need(q.readout.shape[1] == hdr["readout_rank"], "readout_rank")
@@ -207,10 +220,11 @@ def _layer_arrays(l: int, q: IntLayer, hdr: dict):
     return out
 
 
-def write_model(layers, output_bias, path, router_token_dim: int = 0, input_rank: int = 0):
-    """IntLayers -> a YGG1 file at path; returns (header dict, array bytes)."""
+def write_model(layers, output_bias, path, router_token_dim: int = 0, input_rank: int = 0, extended: bool = False):
+    """IntLayers -> a YGG1 file at path; returns (header dict, array bytes). extended: admit the d_state = 96
+    extension (module docstring)."""
     v = len(output_bias)
-    hdr = header_of(layers, v, router_token_dim, input_rank)
+    hdr = header_of(layers, v, router_token_dim, input_rank, extended)
     ob = np.zeros(round_up(v, CLASS_PAD), f32)
     ob[:v] = output_bias
     arrays = [(OUTPUT_BIAS, ob)] + [a for l, q in enumerate(layers) for a in _layer_arrays(l, q, hdr)]
