@@ -29,7 +29,8 @@ extern "C" {
 #define YGG_OK 0
 #define YGG_E_ARG (-1)          /* bad argument: null pointer, negative size */
 #define YGG_E_FORMAT (-2)       /* not a YGG1 file, or its array table does not fit the file */
-#define YGG_E_UNSUPPORTED (-3)  /* header outside the format limits (cpu/export.py:47-48, cpu/ygg.cpp:141-146) */
+#define YGG_E_UNSUPPORTED (-3)  /* header outside the format limits (cpu/export.py:47-48, cpu/ygg.cpp:141-146) and
+                                   the d_state 96 extension (ygg_load) */
 #define YGG_E_MISSING (-4)      /* a required array is absent or has the wrong size */
 #define YGG_E_CUDA (-5)         /* a CUDA runtime call failed */
 #define YGG_E_OOM (-6)          /* device or host allocation failed */
@@ -57,7 +58,9 @@ typedef struct {
 
 /* Parse a YGG1 file held in host memory, re-lay it out for the device and upload it to `device`.
  * Replaces the reference loader: cpu/ygg.cpp:204-220 (load), :137-148 (read_header), :151-171 (read_blob),
- * :173-202 (bind_layer); the file format is cpu/export.py:34-51,382-468. */
+ * :173-202 (bind_layer); the file format is cpu/export.py:34-51,382-468. Beyond the reference's limits it also
+ * admits d_state 96 with readout rank 12 (that readout stored in the rank-16 layout with zero rows 12-15), a format
+ * extension of this library; ygg_info then reports d_state 96, and every state buffer is [..][n_layers][96]. */
 YGG_API int ygg_load(const void *file_bytes, size_t nbytes, int device, ygg_model **out);
 
 /* Shape and sizes of a loaded model. */
