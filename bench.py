@@ -19,6 +19,8 @@ region is bracketed by a barrier and a device synchronise, and the time is the m
             the d_state 96 format extension (c3n96), whose file the reference's ygg refuses, is timed on the C oracle
             (the scalar port, one core) instead.
 --impl reference times that CPU path alone, on rank 0, and prints its own line.
+--sweep B1,B2,... measures a batch sweep instead (one JSON line per batch size, kernel time only): decode steps, or
+whole rows scored with --mode score.
 """
 from __future__ import annotations
 
@@ -325,6 +327,90 @@ def run_score(args, w, path, world, rank, local, dist):
     return 0
 
 
+def run_sweep(args, w, path, world, rank, local, dist):
+    """Kernel-only throughput over a batch sweep (streams per GPU; weak scaling under torchrun, time = max over
+    ranks). step: 16 untimed steps, W warm-up steps, then K steps with K ~ 2^22 / B (64 to 2048), tokens resident in
+    HBM, launched as replays of a CUDA graph of 32 steps (so that a small batch measures the device, not the rate at
+    which Python launches). score: rows of T tokens with T ~ 2^24 / B (64 to the workload's row length), the fused
+    score kernel."""
+    import torch
+
+    from yggdrasil_b200 import Yggdrasil, synth
+    dev = torch.device("cuda", local)
+    model = Yggdrasil.load(path, backend="b200", device=dev)
+    stream = torch.cuda.current_stream(dev)
+    peak, kind = peaks()
+
+    def max_ms(ms):
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    for B in (int(v) for v in args.sweep.split(",")):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if args.mode == "step":
+            G = 32
+            K, W, P = min(2048, max(2 * G, (1 << 22) // B)) // G * G, args.warmup, 16
+            x = torch.as_tensor(synth.workload_tokens(w, P + W + G, B, seed=rank)).to(dev)
+            state = model.init_state(B)
+            logits = torch.empty(B, model.vocab, dtype=torch.float32, device=dev)
+            for i in range(P + W):
+                model.step_into(x[i], state, state, logits)
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(stream)
+            with torch.cuda.stream(side):   # one eager pass on the capture stream first
+                for i in range(G):
+                    model.step_into(x[P + W + i], state, state, logits)
+            stream.wait_stream(side)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for i in range(G):
+                    model.step_into(x[P + W + i], state, state, logits)
+            graph.replay()
+            torch.cuda.synchronize(dev)
+            if world > 1:
+                dist.barrier()
+            e0.record(stream)
+            for _ in range(K // G):
+                graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            ms = max_ms(e0.elapsed_time(e1)) / K
+            tokens, bpt = B * world, synth.gathered_bytes_per_token(w.shape)
+            rec = {"steps": K, "us_per_step": ms * 1e3, "launch": "CUDA graph of 32 steps"}
+            del graph, x, state, logits
+        else:
+            T = min(w.steps, max(64, (1 << 24) // B))
+            x = torch.as_tensor(synth.workload_tokens(w, B, T, seed=rank)).to(dev)
+            bits = torch.empty(B, dtype=torch.float64, device=dev)
+            for _ in range(max(1, args.warmup // 3)):
+                model.score_into(x, None, bits)
+            torch.cuda.synchronize(dev)
+            if world > 1:
+                dist.barrier()
+            e0.record(stream)
+            model.score_into(x, None, bits)
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            ms = max_ms(e0.elapsed_time(e1))
+            tokens, bpt = B * (T - 1) * world, synth.gathered_bytes_per_token(w.shape, with_io=False) + 4
+            rec = {"tokens_per_row": T, "ms": ms}
+            del x, bits
+        torch.cuda.empty_cache()
+        model.status()
+        if rank == 0:
+            tps = tokens / (ms / 1e3)
+            print(json.dumps({"sweep": args.mode, "workload": w.name, "n_gpus": world, "streams_per_gpu": B, **rec,
+                              "tokens_per_s": tps, "roofline_frac": tps / world * bpt / 1e9 / peak,
+                              "peak_kind": kind}), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -343,6 +429,7 @@ def main():
     ap.add_argument("--score-steps", type=int, default=0, help="tokens per row in score mode (default: the workload's)")
     ap.add_argument("--grouped", action="store_true", help="score mode: also time the leaf-grouped tensor-core path")
     ap.add_argument("--min-group", type=int, default=64, help="streams a leaf needs for the tensor-core path")
+    ap.add_argument("--sweep", default="", help="comma-separated streams per GPU: a batch sweep, one line per size")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -364,6 +451,8 @@ def main():
 
     from yggdrasil_b200 import Yggdrasil, synth
     w, path = build_model_file(args.workload, 7, rank, world, dist)
+    if args.sweep:
+        return run_sweep(args, w, path, world, rank, local, dist)
     if args.mode == "score":
         return run_score(args, w, path, world, rank, local, dist)
     B = args.streams or min(w.streams, 65536)

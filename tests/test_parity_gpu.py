@@ -267,3 +267,42 @@ def test_extension_state_layout(rec, case_model, torch):
     np.testing.assert_array_equal(st.cpu().numpy(), ost)
     bits = model.score(x[:, 9:], state=st)
     np.testing.assert_allclose(bits, om.score(x[:, 9:], ost), rtol=BITS_RTOL)
+
+
+@pytest.mark.parametrize("direct", ["0", "1"])
+@pytest.mark.parametrize("lanes", ["16", "32"])
+@pytest.mark.parametrize("rec", CASES[:6] + CASES[11:14] + EXT_CASES[:2],
+                         ids=_ids(CASES[:6] + CASES[11:14]) + [f"ext-{i}" for i in _ids(EXT_CASES[:2])])
+def test_both_lane_layouts_bit_exact(lanes, direct, rec, case_model, torch, monkeypatch):
+    """Every launch configuration: YGG_LANES=16 runs two streams per warp (16 lanes per stream; shapes that allow it,
+    else a warp per stream), 32 a warp per stream; YGG_DIRECT=1 has the fast kernels read records from global memory,
+    0 stages them in shared memory. Each gives the oracle's routes, states and logits, with ragged batches (an odd
+    count leaves a warp's second stream unseen) and the score path."""
+    monkeypatch.setenv("YGG_LANES", lanes)
+    monkeypatch.setenv("YGG_DIRECT", direct)
+    path = case_model(rec)
+    model, om = load(path), O.OracleModel(path)
+    x = case_tokens(rec)[:7, :12]
+    run_windows(model, om, x, torch)
+    np.testing.assert_allclose(model.score(x), om.score(x), rtol=BITS_RTOL)
+
+
+@pytest.mark.parametrize("direct", ["0", "1"])
+@pytest.mark.parametrize("lanes", ["16", "32"])
+@pytest.mark.parametrize("rec", WORKLOADS + EXT_WORKLOADS, ids=[w["workload"] for w in WORKLOADS + EXT_WORKLOADS])
+def test_fast_instances_bit_exact(lanes, direct, rec, tmp_path, torch, monkeypatch):
+    """The benchmark shapes run the fast instances (shape fixed at compile time): every lane layout and record path
+    against the oracle and the reference's digest, with 7 streams (ragged) in the score path."""
+    from yggdrasil_b200 import synth
+    from yggdrasil_b200.ygg1 import write_model
+    monkeypatch.setenv("YGG_LANES", lanes)
+    monkeypatch.setenv("YGG_DIRECT", direct)
+    w = synth.WORKLOADS[rec["workload"]]
+    p = tmp_path / "w.bin"
+    write_model(synth.workload_layers(w, seed=7), np.linspace(-1, 1, w.shape.vocab), p, extended=w.extended)
+    model, om = load(p), O.OracleModel(p)
+    x = synth.workload_tokens(w, rec["streams"], rec["steps"], seed=rec["token_seed"])
+    lg = run_windows(model, om, x, torch)
+    assert sha(np.ascontiguousarray(lg).tobytes()) == rec["logits_sha256"]
+    x7 = synth.workload_tokens(w, 7, 20, seed=3)
+    np.testing.assert_allclose(model.score(x7), om.score(x7), rtol=BITS_RTOL)

@@ -3,8 +3,9 @@
 // the 5th-generation tensor cores (tcgen05.mma kind::i8, accumulators in TMEM), the other streams take the per-stream
 // path of the fused kernels. The results equal the fused score kernel bit for bit.
 //
-// One step is, for every layer l:
-//   g_route    warp per stream: rho, router descent, layer-input codes; leaf id and its rank in the leaf's bucket
+// One step is, for every layer l (the per-stream kernels serve a stream with G lanes, the model's lw: a warp, or half
+// a warp with two streams per warp):
+//   g_route    G lanes per stream: rho, router descent, layer-input codes; leaf id and its rank in the leaf's bucket
 //   g_scan     one block: prefix sum of the per-leaf counts, the list of heavy leaves (count >= G), counts zeroed
 //   g_scatter  thread per stream: heavy streams into their leaf's bucket, the others into the light list
 //   g_heavy    block per heavy leaf (persistent): the leaf's weights once into shared memory as K-major operands,
@@ -13,8 +14,10 @@
 //                D_u  = ZL . U'^T,  D_f = V(x) . U^T (factored input)
 //              an epilogue per stream (thread = TMEM lane = stream) forms the int32 accumulators as the reference does,
 //              saturates the new state into shared memory, and D_p = Q_new . P^T gives the readout codes
-//   g_light    warp per stream on a light leaf: the per-stream update (leaf_update / readout_code)
-// then g_head_nll: warp per stream, logits of all layers in order and the f64 NLL of the next token.
+//   g_light    G lanes per stream on a light leaf: the per-stream update (leaf_update / readout_code)
+// then g_head_nll: G lanes per stream, logits of all layers in order and the f64 NLL of the next token.
+// A warp whose second stream is past the end runs a copy of its first unseen (nothing written), so that its
+// collectives stay full-warp.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -122,27 +125,34 @@ struct HeavyPlan {
 
 // ------------------------------------------------------------------------------------------------ kernels
 
-template <int N, int R2T>
+template <int N, int R2T, int G>
 __global__ void __launch_bounds__(256) g_route(const __grid_constant__ DevModel m, int l, int B, int T, int t,
                                                const int32_t *__restrict__ tokens, const int8_t *state, GroupWs ws) {
-    constexpr int C = N / 32;
-    __shared__ __align__(16) int8_t qb_s[8][N];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int s = blockIdx.x * 8 + warp;
-    if (s >= B) return;
-    const int x = tok_at(tokens, ws, s, T, t);
+    constexpr int C = N / G, P = 32 / G;
+    __shared__ __align__(16) int8_t qb_s[8 * P][N];
+    __shared__ __align__(16) int8_t zl_unseen[8 * P][kZlStride];   // where a stream that runs unseen writes
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gh = lane / G, gl = lane & (G - 1);
+    const int base = (blockIdx.x * 8 + warp) * P;
+    if (base >= B) return;
+    const int s = base + gh;
+    const bool real = s < B;
+    const int se = real ? s : base;
+    const int sidx = warp * P + gh;
+    const int x = tok_at(tokens, ws, se, T, t);
     const DevLayer &y = m.layer[l];
     int leaf = x;
     if (l > 0) {
-        const LaneQ<C> qbelow = load_q<C>(state + ((size_t)s * m.L + (l - 1)) * N + C * lane);
-        const float rho = rms_rho<N>(qbelow, y.r2b, y.rms_eps, m.inv_n);
-        store_q<C>(qb_s[warp] + C * lane, qbelow);
+        const LaneQ<C> qbelow = load_q<C>(state + ((size_t)se * m.L + (l - 1)) * N + C * gl);
+        const float rho = rms_rho<N, G>(qbelow, y.r2b, y.rms_eps, m.inv_n, lane);
+        store_q<C>(qb_s[sidx] + C * gl, qbelow);
         __syncwarp();
-        const uint4 qrow = *(const uint4 *)(qb_s[warp] + 16 * (lane % (N / 16)));
-        leaf = route_look<N>(y.w, y.thr + (size_t)x * m.E, m.D, qrow, rho, lane) - m.E;
-        if (R2T > 0 || m.R2 > 0) layer_input_codes<N, R2T>(m, y, qb_s[warp], rho, ws.zl + (size_t)s * kZlStride, lane);
+        const uint4 qrow = *(const uint4 *)(qb_s[sidx] + 16 * (gl % (N / 16)));
+        leaf = route_look<N, G>(y.w, y.thr + (size_t)x * m.E, m.D, qrow, rho, lane) - m.E;
+        if (R2T > 0 || m.R2 > 0)
+            layer_input_codes<N, R2T, G>(m, y, qb_s[sidx], rho, real ? ws.zl + (size_t)s * kZlStride : zl_unseen[sidx],
+                                         lane);
     }
-    if (lane == 0) {
+    if (real && gl == 0) {
         ws.leaf[s] = leaf;
         ws.pos[s] = atomicAdd(ws.cnt + leaf, 1);
     }
@@ -196,16 +206,18 @@ __global__ void g_scatter(GroupWs ws, int B, int G) {
     else ws.light[atomicAdd(ws.counts + 1, 1)] = s;
 }
 
-template <int N, int BLK, int R, int R2T>
+template <int N, int BLK, int R, int R2T, int G>
 __global__ void __launch_bounds__(256) g_light(const __grid_constant__ DevModel m, int l, int T, int t,
                                                const int32_t *__restrict__ tokens, int8_t *state, GroupWs ws) {
-    constexpr int C = N / 32;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = blockDim.x >> 5;
+    constexpr int C = N / G, P = 32 / G;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = blockDim.x >> 5, gh = lane / G,
+              gl = lane & (G - 1);
     const int nlight = ws.counts[1];
     const DevLayer &y = m.layer[l];
     const bool low = l > 0 && (R2T > 0 || m.R2 > 0);
-    for (int i = blockIdx.x * W + warp; i < nlight; i += gridDim.x * W) {
-        const int s = ws.light[i];
+    for (int base = (blockIdx.x * W + warp) * P; base < nlight; base += gridDim.x * W * P) {
+        const bool real = base + gh < nlight;
+        const int s = ws.light[real ? base + gh : base];
         const int x = tok_at(tokens, ws, s, T, t);
         const int r = ws.leaf[s];
         const uint8_t *rec = y.rec + (size_t)r * y.rec_bytes;
@@ -214,23 +226,25 @@ __global__ void __launch_bounds__(256) g_light(const __grid_constant__ DevModel 
         int8_t *q = state + ((size_t)s * m.L + l) * N;
         int acc[C];
         LaneQ<C> qn;
-        leaf_update<N, BLK, R2T>(m, y, rec, trow, x, q, ws.zl + (size_t)s * kZlStride, low, lane, acc, qn);
+        leaf_update<N, BLK, R2T, G>(m, y, rec, trow, x, q, ws.zl + (size_t)s * kZlStride, low, lane, acc, qn);
         __syncwarp();                              // every lane has read the old state before it is overwritten
-        store_q<C>(q + C * lane, qn);
-        const ReadoutWords<N, R> ro = load_readout<N, R>(y, rec, lane);
-        const int zq = readout_code<N, R>(ro, qn, lane);
-        if (lane < R) ws.zq[((size_t)s * m.L + l) * kZqStride + lane] = (int8_t)zq;
+        if (real) store_q<C>(q + C * gl, qn);
+        const ReadoutPart<N, R, G> ro = readout_partials<N, R, G>(y, rec, qn, lane);
+        const int zq = readout_code<N, R, G>(ro, lane);
+        const int row = readout_row<R, G>(gl);
+        if (real && row >= 0 && (G == 32 || R == 16 || (gl & 1) == 0))
+            ws.zq[((size_t)s * m.L + l) * kZqStride + row] = (int8_t)zq;
     }
 }
 
 // Block per heavy leaf (persistent over the heavy list), 128 threads; one tile of up to 128 of the leaf's streams at
 // a time. Thread i is TMEM lane i: stream i of the tile in the epilogue, output row i of the leaf when the weights
 // are staged.
-template <int N, int BLK, int R, int R2T>
+template <int N, int BLK, int R, int R2T, int G>
 __global__ void __launch_bounds__(kHeavyThreads, 1) g_heavy(const __grid_constant__ DevModel m, int l, int T, int t,
                                                              const int32_t *__restrict__ tokens, int8_t *state,
                                                              GroupWs ws) {
-    constexpr int C = N / 32;
+    constexpr int C = N / G;                   // the record layout: coordinates per lane, interleaved over G lanes
     extern __shared__ __align__(1024) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5;
     const DevLayer &y = m.layer[l];
@@ -283,7 +297,7 @@ __global__ void __launch_bounds__(kHeavyThreads, 1) g_heavy(const __grid_constan
             const uint8_t *pa = rec + y.off_a;
             for (int p = 0; p < BLK / 2; p++) {
                 const int lb = (ii * (BLK / 2) + p) * 4;                   // the lane's byte of the int16 pair
-                const uint32_t wv = *(const uint32_t *)(pa + ((lb / 16) * 32 + ln) * 16 + lb % 16);
+                const uint32_t wv = *(const uint32_t *)(pa + ((lb / 16) * G + ln) * 16 + lb % 16);
                 const int a0 = (int)(int16_t)(wv & 0xFFFFu), a1 = (int)(int16_t)(wv >> 16);
                 bhi[core_off(i, c0 + 2 * p, N)] = (uint8_t)(a0 >> 8);
                 blo[core_off(i, c0 + 2 * p, N)] = (uint8_t)(a0 & 0xFF);
@@ -294,14 +308,14 @@ __global__ void __launch_bounds__(kHeavyThreads, 1) g_heavy(const __grid_constan
                 const uint8_t *pu = rec + y.off_u;
                 for (int k = 0; k < hp.ku; k++) {
                     const int lb = ii * R2P + k;
-                    bu[core_off(i, k, hp.ku)] = k < R2P ? pu[((lb / 16) * 32 + ln) * 16 + lb % 16] : 0;
+                    bu[core_off(i, k, hp.ku)] = k < R2P ? pu[((lb / 16) * G + ln) * 16 + lb % 16] : 0;
                 }
             }
             if (fact) {
                 const uint8_t *pf = rec + y.off_f;
                 for (int k = 0; k < hp.kf; k++) {
                     const int lb = ii * KP + k;
-                    bf[core_off(i, k, hp.kf)] = k < KP ? pf[((lb / 16) * 32 + ln) * 16 + lb % 16] : 0;
+                    bf[core_off(i, k, hp.kf)] = k < KP ? pf[((lb / 16) * G + ln) * 16 + lb % 16] : 0;
                 }
             }
         }
@@ -309,7 +323,7 @@ __global__ void __launch_bounds__(kHeavyThreads, 1) g_heavy(const __grid_constan
             const uint8_t *pp = rec + y.off_p;
             for (int i = 0; i < N; i++) {
                 const int lb = tid * C + i % C, ln = i / C;
-                bp[core_off(tid, i, N)] = pp[((lb / 16) * 32 + ln) * 16 + lb % 16];
+                bp[core_off(tid, i, N)] = pp[((lb / 16) * G + ln) * 16 + lb % 16];
             }
         }
         if (tid < R) mzs[tid] = y.off_mz != kNone ? *(const float *)(rec + y.off_mz + 4 * tid) : y.readout_scale;
@@ -431,21 +445,23 @@ __global__ void __launch_bounds__(kHeavyThreads, 1) g_heavy(const __grid_constan
     if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols));
 }
 
-template <int R, int NVT>
+template <int R, int NVT, int G>
 __global__ void __launch_bounds__(256) g_head_nll(const __grid_constant__ DevModel m, int B, int T, int t,
                                                   const int32_t *__restrict__ tokens, GroupWs ws, double *bits) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int s = blockIdx.x * 8 + warp;
-    if (s >= B) return;
-    const int nv = NVT ? NVT : m.VP / 32;
-    float lg[kMaxClassesPerLane];
+    constexpr int P = 32 / G;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, gh = lane / G, gl = lane & (G - 1);
+    const int base = (blockIdx.x * 8 + warp) * P;
+    if (base >= B) return;
+    const int s = base + gh < B ? base + gh : base;
+    const bool live = base + gh < B && !ws.bad[s];
+    const int nv = NVT ? NVT : m.VP / G;
+    float lg[kMaxClasses<G>];
 #pragma unroll
-    for (int c = 0; c < kMaxClassesPerLane; c++) lg[c] = c < nv ? __ldg(m.head_b + 32 * c + lane) : 0.0f;
+    for (int c = 0; c < kMaxClasses<G>; c++) lg[c] = c < nv ? __ldg(m.head_b + G * c + gl) : 0.0f;
     for (int l = 0; l < m.L; l++)
-        head_accumulate<R, NVT>(m, m.layer[l], ws.zq + ((size_t)s * m.L + l) * kZqStride, lg, lane);
-    if (ws.bad[s]) return;
-    const double nll = ws.nll[s] + nll_of(lg, nv, m.V, tokens[(size_t)s * T + t + 1], lane);
-    if (lane == 0) {
+        head_accumulate<R, NVT, G>(m, m.layer[l], ws.zq + ((size_t)s * m.L + l) * kZqStride, lg, lane);
+    const double nll = ws.nll[s] + nll_of<G>(lg, nv, m.V, live ? tokens[(size_t)s * T + t + 1] : 0, lane);
+    if (live && gl == 0) {
         ws.nll[s] = nll;
         if (t + 2 == T) bits[s] = nll / 0.69314718055994530942;
     }
@@ -512,7 +528,8 @@ static GroupWs grouped_layout(const DevModel &m, int B, uint8_t *base) {
     return ws;
 }
 
-template <int N, int BLK, int R, int R2T, int NVT>
+// LG: lanes per stream of the per-stream kernels (the model's lw); G: streams a leaf needs for the tensor-core path.
+template <int N, int BLK, int R, int R2T, int NVT, int LG>
 static cudaError_t run_grouped_t(const DevModel &m, int B, int T, const int32_t *tok, int8_t *state, double *bits,
                                  void *workspace, int G, int sm_count, cudaStream_t st) {
     GroupWs ws = grouped_layout(m, B, (uint8_t *)workspace);
@@ -534,21 +551,23 @@ static cudaError_t run_grouped_t(const DevModel &m, int B, int T, const int32_t 
     const int Geff = tc ? (G < 1 ? 1 : G) : (1 << 30);
     const HeavyPlan hp(N, m.R2P, m.factored ? m.KP : 0, R);
     if constexpr (tc) {
-        e = cudaFuncSetAttribute(g_heavy<N, BLK, R, R2T>, cudaFuncAttributeMaxDynamicSharedMemorySize, hp.bytes);
+        e = cudaFuncSetAttribute(g_heavy<N, BLK, R, R2T, LG>, cudaFuncAttributeMaxDynamicSharedMemorySize, hp.bytes);
         if (e != cudaSuccess) return e;
     }
-    const int rb = (B + 7) / 8;
+    constexpr int P = 32 / LG;   // streams per warp
+    const int rb = (B + 8 * P - 1) / (8 * P);
+    const int lb = rb < 4 * sm_count ? rb : 4 * sm_count;
     for (int t = 0; t + 1 < T; t++) {
         for (int l = 0; l < m.L; l++) {
             const int n_leaves = l == 0 ? m.V : m.E;
-            g_route<N, R2T><<<rb, 256, 0, st>>>(m, l, B, T, t, tok, q, ws);
+            g_route<N, R2T, LG><<<rb, 256, 0, st>>>(m, l, B, T, t, tok, q, ws);
             g_scan<<<1, 1024, 0, st>>>(ws, n_leaves, Geff);
             g_scatter<<<(B + 255) / 256, 256, 0, st>>>(ws, B, Geff);
-            if constexpr (tc) g_heavy<N, BLK, R, R2T><<<sm_count, kHeavyThreads, hp.bytes, st>>>(m, l, T, t, tok, q, ws);
-            g_light<N, BLK, R, R2T><<<(B + 7) / 8 < 4 * sm_count ? (B + 7) / 8 : 4 * sm_count, 256, 0, st>>>(
-                m, l, T, t, tok, q, ws);
+            if constexpr (tc)
+                g_heavy<N, BLK, R, R2T, LG><<<sm_count, kHeavyThreads, hp.bytes, st>>>(m, l, T, t, tok, q, ws);
+            g_light<N, BLK, R, R2T, LG><<<lb, 256, 0, st>>>(m, l, T, t, tok, q, ws);
         }
-        g_head_nll<R, NVT><<<rb, 256, 0, st>>>(m, B, T, t, tok, ws, bits);
+        g_head_nll<R, NVT, LG><<<rb, 256, 0, st>>>(m, B, T, t, tok, ws, bits);
     }
     if (padded && state)
         g_state_unpad<<<(unsigned)(((size_t)B * m.L * m.ns + 255) / 256), 256, 0, st>>>(B, m.L, m.ns, N, ws.state, state);
@@ -557,14 +576,28 @@ static cudaError_t run_grouped_t(const DevModel &m, int B, int T, const int32_t 
 
 cudaError_t run_grouped(int n, int blk, int r, int r2p, const DevModel &m, int B, int T, const int32_t *tok,
                         int8_t *state, double *bits, void *workspace, int G, int sm_count, cudaStream_t st) {
-    const int nv = m.VP / 32;
-    if (n == 128 && blk == 16 && r == 16 && r2p == 32 && nv == 1)
-        return run_grouped_t<128, 16, 16, 32, 1>(m, B, T, tok, state, bits, workspace, G, sm_count, st);
-    if (n == 128 && blk == 16 && r == 16 && r2p == 32 && nv == 8)
-        return run_grouped_t<128, 16, 16, 32, 8>(m, B, T, tok, state, bits, workspace, G, sm_count, st);
+    const int VP = m.VP;
+    if (m.lw == 16) {
+        if (n == 128 && blk == 16 && r == 16 && r2p == 32 && VP == 32)
+            return run_grouped_t<128, 16, 16, 32, 2, 16>(m, B, T, tok, state, bits, workspace, G, sm_count, st);
+        if (n == 128 && blk == 16 && r == 16 && r2p == 32 && VP == 256)
+            return run_grouped_t<128, 16, 16, 32, 16, 16>(m, B, T, tok, state, bits, workspace, G, sm_count, st);
+        switch (n * 1000 + blk * 100 + r) {
+#define YGG_G(N_, B_, R_) \
+    case N_ * 1000 + B_ * 100 + R_: return run_grouped_t<N_, B_, R_, 0, 0, 16>(m, B, T, tok, state, bits, workspace, G, sm_count, st);
+            YGG_G(64, 8, 8) YGG_G(64, 8, 16) YGG_G(64, 16, 8) YGG_G(64, 16, 16)
+            YGG_G(128, 8, 8) YGG_G(128, 8, 16) YGG_G(128, 16, 8) YGG_G(128, 16, 16)
+#undef YGG_G
+            default: return cudaErrorInvalidValue;
+        }
+    }
+    if (n == 128 && blk == 16 && r == 16 && r2p == 32 && VP == 32)
+        return run_grouped_t<128, 16, 16, 32, 1, 32>(m, B, T, tok, state, bits, workspace, G, sm_count, st);
+    if (n == 128 && blk == 16 && r == 16 && r2p == 32 && VP == 256)
+        return run_grouped_t<128, 16, 16, 32, 8, 32>(m, B, T, tok, state, bits, workspace, G, sm_count, st);
     switch (n * 1000 + blk * 100 + r) {
 #define YGG_G(N_, B_, R_) \
-    case N_ * 1000 + B_ * 100 + R_: return run_grouped_t<N_, B_, R_, 0, 0>(m, B, T, tok, state, bits, workspace, G, sm_count, st);
+    case N_ * 1000 + B_ * 100 + R_: return run_grouped_t<N_, B_, R_, 0, 0, 32>(m, B, T, tok, state, bits, workspace, G, sm_count, st);
         YGG_G(64, 8, 8) YGG_G(64, 8, 16) YGG_G(64, 8, 32) YGG_G(64, 16, 8) YGG_G(64, 16, 16) YGG_G(64, 16, 32)
         YGG_G(128, 8, 8) YGG_G(128, 8, 16) YGG_G(128, 8, 32) YGG_G(128, 16, 8) YGG_G(128, 16, 16) YGG_G(128, 16, 32)
         YGG_G(256, 8, 8) YGG_G(256, 8, 16) YGG_G(256, 8, 32) YGG_G(256, 16, 8) YGG_G(256, 16, 16) YGG_G(256, 16, 32)

@@ -10,6 +10,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <algorithm>
 #include <map>
 #include <string>
 #include <vector>
@@ -32,15 +33,28 @@ cudaError_t noalloc_scratch(int device, void **ptr, size_t *bytes);
 
 using namespace ygg;
 
+// A launch configuration: the descriptor (device pointers resolved; its records interleaved over lw lanes) and the
+// staging slots per block of its step and score kernels.
+struct LaunchCfg {
+    DevModel dm;
+    int slots_step, slots_score;
+};
+
 struct ygg_model {
     int device;
-    DevModel host;            // the descriptor, device pointers already resolved
-    DevModel *d_desc;         // the same descriptor in device memory (kernel argument)
+    LaunchCfg warp;           // a warp per stream (records over 32 lanes): every shape
+    LaunchCfg half;           // two streams per warp (records over 16 lanes), when has_half
+    bool has_half;
+    // launch policy (ygg_step / ygg_score / grouped, by the batch B): B <= small_max stages records in shared memory
+    // (a warp per stream: the shortest per-token latency); B >= big_min runs two streams per warp (fewest
+    // instructions per token); in between a warp per stream reads records from global memory. YGG_LANES (16 / 32)
+    // and YGG_DIRECT (0 / 1) fix the choice instead.
+    int small_max, big_min, force_lanes, force_direct;
     uint8_t *d_blob;          // every device array
     size_t d_bytes;
     int *d_status;
     uint32_t rec_max;
-    int warps_step, slots_step, warps_score, slots_score, grid_cap;
+    int warps, grid_cap;
     int sm_count;
     ygg_info_t info;
 };
@@ -79,12 +93,12 @@ struct Blob {
     }
 };
 
-// the 16-byte chunk layout: byte `b` of lane `l`'s data in a lane-interleaved part
-inline size_t lane_byte(int l, size_t b) { return ((b / 16) * 32 + (size_t)l) * 16 + b % 16; }
+// the 16-byte chunk layout: byte `b` of lane `l`'s data in a part interleaved over `lw` lanes
+inline size_t lane_byte(int lw, int l, size_t b) { return ((b / 16) * lw + (size_t)l) * 16 + b % 16; }
 
 struct LayerPlan {
     // offsets into the device blob
-    size_t rec = 0, table = 0, w = 0, thr = 0, vl = 0, mv = 0, mulv = 0, r2b = 0, vt = 0, mt = 0, unembed = 0, sqv = 0;
+    size_t rec = 0, rec16 = 0, table = 0, w = 0, thr = 0, vl = 0, mv = 0, mulv = 0, r2b = 0, vt = 0, mt = 0, unembed = 0, sqv = 0;
     bool has_table = false, has_w = false, has_vl = false, has_mulv = false, has_r2b = false, has_vt = false,
          has_sqv = false;
     uint32_t rec_bytes = 0, table_rows = 0;
@@ -164,7 +178,12 @@ int ygg_load(const void *file_bytes, size_t nbytes, int device, ygg_model **out)
         arr[std::string(e.name, strnlen(e.name, 32))] = Arr{f + pos + e.offset, e.bytes};
     }
     const int n = nf == 96 ? 128 : nf, R = Rf == 12 ? 16 : Rf, Rs = Rf == 12 ? 16 : Rf;
-    const int E = 1 << D, VP = (V + kClassPad - 1) / kClassPad * kClassPad, C = n / 32;
+    // record layouts: interleaved over 32 lanes (a warp per stream) always, and over 16 lanes (two streams per warp)
+    // where a half-warp's share of the work fits its registers (n <= 128 and readout rank <= 16), unless
+    // YGG_LANES=32 asks for the warp per stream only
+    bool lay16 = n <= 128 && R <= 16;
+    if (const char *e = getenv("YGG_LANES")) { if (atoi(e) == 32) lay16 = false; }
+    const int E = 1 << D, VP = (V + kClassPad - 1) / kClassPad * kClassPad;
     const int R2P = (int)round_up(R2, 16), KP = (int)round_up(K, 16), NG = n / 16, NGf = nf / 16;
     auto get = [&](int l, const char *tag, int64_t want, Arr &a) -> int {  // 1 found, 0 absent, <0 bad size
         const auto it = arr.find("l" + std::to_string(l) + "_" + tag);
@@ -229,59 +248,65 @@ int ygg_load(const void *file_bytes, size_t nbytes, int device, ygg_model **out)
         }
         if (hmz == 1) { P.off_mz = off; off += (uint32_t)round_up(4 * R, 16); }
         P.rec_bytes = (uint32_t)round_up(off, 128);
-        std::vector<uint8_t> dr((size_t)Ee * P.rec_bytes, 0);
-        for (int r = 0; r < Ee; r++) {
-            const uint8_t *src = rec.p + (size_t)r * rb;
-            uint8_t *dst = dr.data() + (size_t)r * P.rec_bytes;
-            const int16_t *A = (const int16_t *)(src + mt[1]);
-            // transition: lane data word ii * b/2 + p = (A[i][c0 + 2p], A[i][c0 + 2p + 1]); file element (i, jj) of the
-            // row's block at ((i/16) * b/2 + jj/2) * 16 + i%16) * 2 + jj%2 (cpu/export.py:321-326)
-            uint8_t *pa = dst + P.off_a;
-            for (int ln = 0; ln < 32; ln++)
-                for (int ii = 0; ii < C; ii++) {
-                    const int i = C * ln + ii;
-                    if (i >= nf) continue;   // padded coordinates: zero rows
-                    for (int jj = 0; jj < b; jj++) {
-                        const int16_t v = A[(((i / 16) * (b / 2) + jj / 2) * 16 + i % 16) * 2 + jj % 2];
-                        const size_t lb = (size_t)(ii * (b / 2) + jj / 2) * 4 + (jj % 2) * 2;
-                        memcpy(pa + lane_byte(ln, lb), &v, 2);   // lb even: both bytes in one chunk
-                    }
-                }
-            // projections u8 (u + 128) [rank/4][n][4] (cpu/export.py:329-332) -> lane bytes ii * rankP + k, signed
-            auto proj = [&](const uint8_t *u, int rank, int rankp, uint8_t *pd) {
-                for (int ln = 0; ln < 32; ln++)
+        // the records interleaved over lw lanes (C = n / lw coordinates per lane)
+        auto records = [&](const int lw) {
+            const int C = n / lw;
+            std::vector<uint8_t> dr((size_t)Ee * P.rec_bytes, 0);
+            for (int r = 0; r < Ee; r++) {
+                const uint8_t *src = rec.p + (size_t)r * rb;
+                uint8_t *dst = dr.data() + (size_t)r * P.rec_bytes;
+                const int16_t *A = (const int16_t *)(src + mt[1]);
+                // transition: lane data word ii * b/2 + p = (A[i][c0 + 2p], A[i][c0 + 2p + 1]); file element (i, jj) of the
+                // row's block at ((i/16) * b/2 + jj/2) * 16 + i%16) * 2 + jj%2 (cpu/export.py:321-326)
+                uint8_t *pa = dst + P.off_a;
+                for (int ln = 0; ln < lw; ln++)
                     for (int ii = 0; ii < C; ii++) {
                         const int i = C * ln + ii;
-                        if (i >= nf) continue;
-                        for (int k = 0; k < rank; k++)
-                            pd[lane_byte(ln, (size_t)ii * rankp + k)] =
-                                (uint8_t)(u[((size_t)(k / 4) * nf + i) * 4 + k % 4] - 128);
+                        if (i >= nf) continue;   // padded coordinates: zero rows
+                        for (int jj = 0; jj < b; jj++) {
+                            const int16_t v = A[(((i / 16) * (b / 2) + jj / 2) * 16 + i % 16) * 2 + jj % 2];
+                            const size_t lb = (size_t)(ii * (b / 2) + jj / 2) * 4 + (jj % 2) * 2;
+                            memcpy(pa + lane_byte(lw, ln, lb), &v, 2);   // lb even: both bytes in one chunk
+                        }
                     }
-            };
-            if (low) proj(src + mt[2], R2, R2P, dst + P.off_u);
-            // readout u8 (p + 128) (cpu/export.py:335-342) -> lane bytes r * C + cc = P[r][C l + cc], signed
-            uint8_t *pp = dst + P.off_p;
-            const uint8_t *ps = src + mt[3];
-            for (int ln = 0; ln < 32; ln++)
-                for (int rr = 0; rr < Rf; rr++)
-                    for (int cc = 0; cc < C; cc++) {
-                        const int i = C * ln + cc;
-                        if (i >= nf) continue;
-                        const size_t idx = Rf == 8 ? ((size_t)(i / 8) * 16 + 2 * rr + (i % 8) / 4) * 4 + i % 4
-                                                   : ((size_t)((rr / 16) * (nf / 4) + i / 4) * 16 + rr % 16) * 4 + i % 4;
-                        pp[lane_byte(ln, (size_t)rr * C + cc)] = (uint8_t)(ps[idx] - 128);
-                    }
-            if (fact) {
-                proj(src + mt[5], K, KP, dst + P.off_f);
-                memcpy(dst + P.off_cb, src + mt[6], 2 * (size_t)nf);
-                memcpy(dst + P.off_su, src + mt[7], 4);
+                // projections u8 (u + 128) [rank/4][n][4] (cpu/export.py:329-332) -> lane bytes ii * rankP + k, signed
+                auto proj = [&](const uint8_t *u, int rank, int rankp, uint8_t *pd) {
+                    for (int ln = 0; ln < lw; ln++)
+                        for (int ii = 0; ii < C; ii++) {
+                            const int i = C * ln + ii;
+                            if (i >= nf) continue;
+                            for (int k = 0; k < rank; k++)
+                                pd[lane_byte(lw, ln, (size_t)ii * rankp + k)] =
+                                    (uint8_t)(u[((size_t)(k / 4) * nf + i) * 4 + k % 4] - 128);
+                        }
+                };
+                if (low) proj(src + mt[2], R2, R2P, dst + P.off_u);
+                // readout u8 (p + 128) (cpu/export.py:335-342) -> lane bytes r * C + cc = P[r][C l + cc], signed
+                uint8_t *pp = dst + P.off_p;
+                const uint8_t *ps = src + mt[3];
+                for (int ln = 0; ln < lw; ln++)
+                    for (int rr = 0; rr < Rf; rr++)
+                        for (int cc = 0; cc < C; cc++) {
+                            const int i = C * ln + cc;
+                            if (i >= nf) continue;
+                            const size_t idx = Rf == 8 ? ((size_t)(i / 8) * 16 + 2 * rr + (i % 8) / 4) * 4 + i % 4
+                                                       : ((size_t)((rr / 16) * (nf / 4) + i / 4) * 16 + rr % 16) * 4 + i % 4;
+                            pp[lane_byte(lw, ln, (size_t)rr * C + cc)] = (uint8_t)(ps[idx] - 128);
+                        }
+                if (fact) {
+                    proj(src + mt[5], K, KP, dst + P.off_f);
+                    memcpy(dst + P.off_cb, src + mt[6], 2 * (size_t)nf);
+                    memcpy(dst + P.off_su, src + mt[7], 4);
+                }
+                if (hmz == 1) {   // R = 8: the file holds each row's scale twice (lanes 2r, 2r+1)
+                    const float *mz = (const float *)mzl.p + (size_t)r * (Rf == 8 ? 16 : Rf);
+                    for (int rr = 0; rr < Rf; rr++) memcpy(dst + P.off_mz + 4 * rr, mz + (Rf == 8 ? 2 * rr : rr), 4);
+                }
             }
-            if (hmz == 1) {   // R = 8: the file holds each row's scale twice (lanes 2r, 2r+1)
-                const float *mz = (const float *)mzl.p + (size_t)r * (Rf == 8 ? 16 : Rf);
-                for (int rr = 0; rr < Rf; rr++) memcpy(dst + P.off_mz + 4 * rr, mz + (Rf == 8 ? 2 * rr : rr), 4);
-            }
-        }
-        P.rec = blob.add(std::move(dr));
+            return dr;
+        };
+        P.rec = blob.add(records(32));
+        if (lay16) P.rec16 = blob.add(records(16));
         if (!fact) {   // table rows int16, contiguous per expert
             P.table_rows = l == 0 ? 1 : (uint32_t)V;
             std::vector<uint8_t> t((size_t)Ee * P.table_rows * 2 * n, 0);
@@ -358,8 +383,7 @@ int ygg_load(const void *file_bytes, size_t nbytes, int device, ygg_model **out)
     ygg_model *m = new ygg_model();
     m->device = device;
     m->sm_count = prop.multiProcessorCount;
-    const size_t desc_off = blob.size;
-    const size_t status_off = round_up(desc_off + sizeof(DevModel), 256);
+    const size_t status_off = blob.size;
     m->d_bytes = status_off + 256;
     int rc = YGG_OK;
     if (cudaMalloc((void **)&m->d_blob, m->d_bytes) != cudaSuccess) {
@@ -377,11 +401,13 @@ int ygg_load(const void *file_bytes, size_t nbytes, int device, ygg_model **out)
         return rc;
     }
     uint8_t *d = m->d_blob;
-    DevModel &dm = m->host;
+    DevModel &dm = m->warp.dm;
     memset(&dm, 0, sizeof dm);
     dm.L = L; dm.n = n; dm.b = b; dm.V = V; dm.VP = VP; dm.D = D; dm.E = E; dm.R = R; dm.R2 = R2; dm.R2P = R2P;
     dm.K = K; dm.KP = KP; dm.shift = h.shift; dm.factored = any_factored; dm.has_mz = any_mz;
     dm.ns = nf;
+    dm.lw = 32;
+    dm.direct = 0;                 // set per launch
     dm.inv_n = 1.0f / (float)nf;   // the reference's (1.0f / N) (cpu/ygg.cpp:253), f32(1.0 / n) in int_forward
     dm.head_b = (const float *)d;
     dm.status = (int *)(d + status_off);
@@ -408,37 +434,48 @@ int ygg_load(const void *file_bytes, size_t nbytes, int device, ygg_model **out)
         y.readout_scale = P.scal[0]; y.unembed_scale = P.scal[1]; y.rms_eps = P.scal[2]; y.layer_input_scale = P.scal[3];
         if (P.rec_bytes > rec_max) rec_max = P.rec_bytes;
     }
-    m->d_desc = (DevModel *)(d + desc_off);
-    if (cudaMemcpy(m->d_desc, &dm, sizeof dm, cudaMemcpyHostToDevice) != cudaSuccess) {
-        cudaFree(m->d_blob);
-        delete m;
-        if (prev >= 0) cudaSetDevice(prev);
-        return YGG_E_CUDA;
-    }
+    // the same model with its records interleaved over 16 lanes
+    m->has_half = lay16;
+    m->half.dm = dm;
+    m->half.dm.lw = 16;
+    if (lay16)
+        for (int l = 0; l < L; l++) m->half.dm.layer[l].rec = d + plan[l].rec16;
     m->rec_max = rec_max;
-    // launch shape: W warps per block share S leaf slots (a warp holds a slot only from its copy to its readout);
-    // S is the most slots that still let `blocks` blocks share an SM's shared memory
+    // launch shape: W warps per block, each serving 32 / lw streams, share S leaf slots (a stream holds a slot only
+    // from its copy to its readout); S is the most slots that still let `blocks` blocks share an SM's shared memory
     const size_t sm_smem = prop.sharedMemPerMultiprocessor, cap = prop.sharedMemPerBlockOptin;
-    auto pick_slots = [&](int W, int blocks, int state_bytes, int *S_out) {
-        int S = W;
-        while (S > 1 && (block_smem_bytes(rec_max, n, S, W, state_bytes) + 1024) * blocks > sm_smem) S--;
-        while (S > 1 && block_smem_bytes(rec_max, n, S, W, state_bytes) > cap) S--;
-        *S_out = S;
-    };
     int W = 8, blocks = n >= 256 ? 2 : 4;   // the kernels' launch bounds (blocks_per_sm in ygg_step.cu)
     if (const char *e = getenv("YGG_WARPS")) { const int v = atoi(e); if (v >= 1 && v <= 8) W = v; }
     if (const char *e = getenv("YGG_BLOCKS_PER_SM")) { const int v = atoi(e); if (v >= 1 && v <= 8) blocks = v; }
-    m->warps_step = W;
-    pick_slots(W, blocks, 0, &m->slots_step);
-    // half the warps' worth of slots is plenty (a warp holds one for a small part of a layer) and leaves more of
-    // the SM's unified L1/shared memory to the L1 cache
-    if (m->slots_step > (W + 1) / 2) m->slots_step = (W + 1) / 2;
-    if (const char *e = getenv("YGG_SLOTS")) {
-        const int v = atoi(e);
-        if (v >= 1 && v <= W && block_smem_bytes(rec_max, n, v, W, 0) <= cap) m->slots_step = v;
-    }
-    m->warps_score = W;
-    pick_slots(W, blocks, (int)round_up((size_t)L * n, 128), &m->slots_score);
+    m->warps = W;
+    // slots come in units of P = 32 / lw (a warp claims one slot per stream it serves, all at once)
+    auto pick_slots = [&](LaunchCfg &c) {
+        const int P = 32 / c.dm.lw, streams = W * P;
+        auto fit = [&](int state_bytes) {
+            int S = streams;
+            while (S > P && (block_smem_bytes(rec_max, n, S, streams, state_bytes) + 1024) * blocks > sm_smem) S -= P;
+            while (S > P && block_smem_bytes(rec_max, n, S, streams, state_bytes) > cap) S -= P;
+            return S;
+        };
+        // half the streams' worth of slots is plenty (a stream holds one for a small part of a layer) and leaves
+        // more of the SM's unified L1/shared memory to the L1 cache
+        c.slots_step = std::min(fit(0), (streams / 2 + P - 1) / P * P);
+        if (const char *e = getenv("YGG_SLOTS")) {
+            const int v = atoi(e) / P * P;
+            if (v >= P && v <= streams && block_smem_bytes(rec_max, n, v, streams, 0) <= cap) c.slots_step = v;
+        }
+        c.slots_score = fit((int)round_up((size_t)L * n, 128));
+    };
+    pick_slots(m->warp);
+    if (lay16) pick_slots(m->half);
+    m->small_max = 4;
+    m->big_min = 32768;
+    m->force_lanes = 0;
+    m->force_direct = -1;
+    if (const char *e = getenv("YGG_SMALL_BATCH")) m->small_max = atoi(e);
+    if (const char *e = getenv("YGG_BIG_BATCH")) m->big_min = atoi(e);
+    if (const char *e = getenv("YGG_LANES")) m->force_lanes = atoi(e) == 16 ? 16 : atoi(e) == 32 ? 32 : 0;
+    if (const char *e = getenv("YGG_DIRECT")) m->force_direct = atoi(e) != 0;
     m->grid_cap = 1 << 30;
     ygg_info_t &inf = m->info;
     memset(&inf, 0, sizeof inf);
@@ -446,11 +483,20 @@ int ygg_load(const void *file_bytes, size_t nbytes, int device, ygg_model **out)
     inf.layer_input_rank = R2; inf.router_token_dim = h.router_token_dim; inf.input_rank = K; inf.shift = h.shift;
     inf.n_experts = E; inf.vocab_pad = VP; inf.factored = any_factored; inf.group_scales = any_group;
     inf.file_array_bytes = (int64_t)avail; inf.device_bytes = (int64_t)m->d_bytes; inf.record_bytes = (int32_t)rec_max;
-    inf.warps_per_block = m->warps_step;
-    inf.slots_per_block = m->slots_step;
+    inf.warps_per_block = m->warps;
+    inf.slots_per_block = m->warp.slots_step;
     if (prev >= 0) cudaSetDevice(prev);
     *out = m;
     return YGG_OK;
+}
+
+// The configuration a launch over `batch` streams (or rows) runs with, its record path set (the launch policy of
+// ygg_model).
+static LaunchCfg choose(const ygg_model *m, int batch) {
+    const bool half = m->has_half && (m->force_lanes == 16 || (m->force_lanes == 0 && batch >= m->big_min));
+    LaunchCfg c = half ? m->half : m->warp;
+    c.dm.direct = m->force_direct >= 0 ? m->force_direct : (batch > m->small_max ? 1 : 0);
+    return c;
 }
 
 static int set_device(const ygg_model *m, int *prev) {
@@ -470,9 +516,11 @@ int ygg_step_debug(const ygg_model *m, int batch, const int32_t *d_tokens, const
     if (!d_tokens || !d_state_in || !d_state_out) return YGG_E_ARG;
     int prev;
     if (set_device(m, &prev)) return YGG_E_CUDA;
-    const cudaError_t e = launch_step(m->host.n, m->host.b, m->host.R, m->host.R2P, m->host, batch, d_tokens, d_state_in,
-                                      d_state_out, d_logits, d_routes, d_acc, m->rec_max, m->warps_step,
-                                      m->slots_step, m->grid_cap, (cudaStream_t)stream);
+    const LaunchCfg c = choose(m, batch);
+    const DevModel &dm = c.dm;
+    const cudaError_t e = launch_step(dm.n, dm.b, dm.R, dm.R2P, dm, batch, d_tokens, d_state_in, d_state_out, d_logits,
+                                      d_routes, d_acc, m->rec_max, m->warps, c.slots_step, m->grid_cap,
+                                      (cudaStream_t)stream);
     restore_device(m, prev);
     return e == cudaSuccess ? YGG_OK : YGG_E_CUDA;
 }
@@ -489,16 +537,17 @@ int ygg_score(const ygg_model *m, int batch, int steps, const int32_t *d_tokens,
     if (!d_tokens || !d_bits) return YGG_E_ARG;
     int prev;
     if (set_device(m, &prev)) return YGG_E_CUDA;
-    const cudaError_t e = launch_score(m->host.n, m->host.b, m->host.R, m->host.R2P, m->host, batch, steps, d_tokens, d_state,
-                                       d_bits, m->rec_max, m->warps_score, m->slots_score, m->grid_cap,
-                                       (cudaStream_t)stream);
+    const LaunchCfg c = choose(m, batch);
+    const DevModel &dm = c.dm;
+    const cudaError_t e = launch_score(dm.n, dm.b, dm.R, dm.R2P, dm, batch, steps, d_tokens, d_state, d_bits,
+                                       m->rec_max, m->warps, c.slots_score, m->grid_cap, (cudaStream_t)stream);
     restore_device(m, prev);
     return e == cudaSuccess ? YGG_OK : YGG_E_CUDA;
 }
 
 size_t ygg_score_grouped_workspace(const ygg_model *m, int batch) {
     if (!m || batch < 0) return 0;
-    return grouped_ws_bytes(m->host, batch);
+    return grouped_ws_bytes(m->warp.dm, batch);
 }
 
 int ygg_score_grouped(const ygg_model *m, int batch, int steps, const int32_t *d_tokens, int8_t *d_state,
@@ -506,11 +555,13 @@ int ygg_score_grouped(const ygg_model *m, int batch, int steps, const int32_t *d
     if (!m || batch < 0 || steps < 0) return YGG_E_ARG;
     if (batch == 0) return YGG_OK;
     if (!d_tokens || !d_bits || !d_workspace || ((uintptr_t)d_workspace & 255) ||
-        workspace_bytes < grouped_ws_bytes(m->host, batch))
+        workspace_bytes < grouped_ws_bytes(m->warp.dm, batch))
         return YGG_E_ARG;
     int prev;
     if (set_device(m, &prev)) return YGG_E_CUDA;
-    const cudaError_t e = run_grouped(m->host.n, m->host.b, m->host.R, m->host.R2P, m->host, batch, steps, d_tokens,
+    const LaunchCfg c = choose(m, batch);
+    const DevModel &dm = c.dm;
+    const cudaError_t e = run_grouped(dm.n, dm.b, dm.R, dm.R2P, dm, batch, steps, d_tokens,
                                       d_state, d_bits, d_workspace, min_group, m->sm_count, (cudaStream_t)stream);
     restore_device(m, prev);
     return e == cudaSuccess ? YGG_OK : YGG_E_CUDA;
@@ -521,7 +572,7 @@ int ygg_score_grouped_noalloc(const ygg_model *m, int batch, int steps, const in
     if (!m || batch < 0 || steps < 0) return YGG_E_ARG;
     if (batch == 0) return YGG_OK;
     if (!d_tokens || !d_bits) return YGG_E_ARG;
-    const size_t need = grouped_ws_bytes(m->host, batch);
+    const size_t need = grouped_ws_bytes(m->warp.dm, batch);
     int prev;
     if (set_device(m, &prev)) return YGG_E_CUDA;
     void *scratch = nullptr;
@@ -534,7 +585,9 @@ int ygg_score_grouped_noalloc(const ygg_model *m, int batch, int steps, const in
         restore_device(m, prev);
         return YGG_E_CAPACITY;
     }
-    const cudaError_t e = run_grouped(m->host.n, m->host.b, m->host.R, m->host.R2P, m->host, batch, steps, d_tokens,
+    const LaunchCfg c = choose(m, batch);
+    const DevModel &dm = c.dm;
+    const cudaError_t e = run_grouped(dm.n, dm.b, dm.R, dm.R2P, dm, batch, steps, d_tokens,
                                       d_state, d_bits, scratch, min_group, m->sm_count, (cudaStream_t)stream);
     restore_device(m, prev);
     return e == cudaSuccess ? YGG_OK : YGG_E_CUDA;

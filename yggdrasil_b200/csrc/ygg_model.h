@@ -1,10 +1,11 @@
 // Device layout of a loaded model, shared by the loader (ygg_load.cu) and the kernels (ygg_step.cu).
 //
-// A stream is served by one warp. Lane l owns the C = n/32 state coordinates [C l, C l + C) of every layer, and
+// A stream is served by LW lanes (lw: 32, a warp, or 16, half a warp; the loader picks 16 for n = 64 / 128 with
+// readout rank <= 16). Lane l of the group owns the C = n/LW state coordinates [C l, C l + C) of every layer, and
 // every per-expert array is re-laid out at load time so that the bytes lane l needs sit in the lane's own 16-byte
-// chunks: chunk j of lane l is at byte (32 j + l) * 16 of the part. One warp-wide 16-byte load therefore reads 512
-// contiguous bytes (conflict-free in shared memory, fully coalesced in global memory), and a whole expert record is
-// one contiguous block that a single bulk copy (cp.async.bulk) brings into the warp's shared-memory slot.
+// chunks: chunk j of lane l is at byte (LW j + l) * 16 of the part. One 16-byte load of the group therefore reads
+// 16 LW contiguous bytes (conflict-free in shared memory, fully coalesced in global memory), and a whole expert
+// record is one contiguous block that a single bulk copy (cp.async.bulk) brings into the stream's shared-memory slot.
 //
 // Per-expert record (rec_bytes each, a multiple of 128):
 //   A   transition int16, lane data = C rows x BLK columns of the row's own diagonal block, as (C * BLK / 2) words
@@ -59,6 +60,8 @@ struct DevLayer {
 
 struct DevModel {
     int L, n, b, V, VP, D, E, R, R2, R2P, K, KP, shift;   // n, R: the device layout's (padded) sizes
+    int lw;                      // lanes per stream of the record layout and the kernels: 32 or 16
+    int direct;                  // 1: the fast step / score kernels read records from global memory (no staging)
     int ns;                      // state coordinates per layer in the caller's layout: the file's d_state (<= n)
     float inv_n;                 // f32(1 / ns), rho's mean factor
     int factored, has_mz;

@@ -1,21 +1,25 @@
 // The int8 decode step and the fused scoring loop of Yggdrasil on sm_100a.
 //
-// One warp serves one stream; lane l owns the C = n/32 state coordinates [C l, C l + C) of every layer (layout in
-// ygg_model.h). Per layer the warp
+// G lanes serve one stream: a warp per stream (G = 32), or two streams per warp (G = 16, the layout the loader picks
+// for n = 64 / 128 with readout rank <= 16), which shares every per-stream step a lane does not own (the router's
+// decisions, rho, the slot and copy handshakes, the descriptor loads, the loop control) between two streams. Lane gl of
+// a group owns the C = n/G state coordinates [C gl, C gl + C) of every layer (layout in ygg_model.h). Per layer the
+// group
 //   1. computes rho from the new state of the layer below (exact int32 sum of squares, then the reference's f32 ops),
 //   2. descends the router LOOK = 3 levels per round of loads: the 7 rows of the 3-level subtree under the current
 //      node are fetched together (16-byte lanes, n/16 lanes per row), their dots reduced within the row's lanes and
 //      compared in f32 with the thresholds of (token, node), so D dependent levels cost ceil(D / 3) L2 round trips,
 //   3. takes a leaf slot from the block's pool (a slot is held only from the copy to the readout, a small part of a
-//      layer's time, so a block runs more warps than it has slots) and has lane 0 issue one bulk copy
+//      layer's time, so a block runs more streams than it has slots) and has its first lane issue one bulk copy
 //      (cp.async.bulk, the 1-D TMA, no multicast) of the chosen expert's record and one of its table row into it,
 //      completing on the slot's mbarrier,
-//   4. meanwhile computes the layer input zl (lane k: the dot of down-projection row k with the state below),
+//   4. meanwhile computes the layer input zl (lane gl: the dots of down-projection rows gl, gl + G, ... with the state
+//      below),
 //   5. waits on the mbarrier (bounded: it gives up after ~1 s with an error status instead of hanging),
 //   6. runs the block-diagonal int16 x int8 transition (__dp2a), the table / factored input and the layer input in
 //      int32, saturates to the new int8 state and stores it,
-//   7. reads out z = P_r q (per-row partials + redux.sync), releases the slot, quantises zq, and adds f32(Q zq) * s
-//      to the logits each lane holds in registers for its classes 32 m + lane.
+//   7. reads out z = P_r q (per-row partials, the slot released, then redux.sync or a butterfly over the group),
+//      quantises zq, and adds f32(Q zq) * s to the logits each lane holds in registers for its classes G m + gl.
 // Every f32 operation is the reference's, single-rounded and in the reference's order (__fmul_rn / __fadd_rn /
 // __fsqrt_rn / __fdiv_rn; no contraction), and f32 -> int32 rounds half to even with the x86 out-of-range value, so
 // routes, int32 accumulators, states and logits equal cpu/ygg.cpp bit for bit.
@@ -32,16 +36,16 @@ template <int N> constexpr int blocks_per_sm() { return N >= 256 ? 2 : 4; }
 
 // ------------------------------------------------------------------------------------------------ shared memory
 
-// Block layout: [S slots][S mbarriers][S owners][S phases] pad 128, then [W warp scratch][W states (score only)].
-// A slot holds one expert record and one table row; the warp scratch holds the old state of the current layer, the
-// new state of the layer below, the layer-input codes and the readout codes.
+// Block layout: [S slots][S mbarriers][S owners][S phases] pad 128, then per stream of the block (W warps x P) its
+// scratch and, for the score kernel, its state. A slot holds one expert record and one table row; the scratch holds
+// the old state of the current layer, the new state of the layer below, the layer-input codes and the readout codes.
 struct Pool {
     uint8_t *slots;
     uint32_t slot_bytes;
-    uint32_t bars;     // shared address of mbarrier 0
-    int *owner;        // -1 free, else the owning warp
-    int *phase;        // parity of the slot's mbarrier to wait for next
-    int S;
+    uint32_t bars;     // shared address of mbarrier 0 (one per slot)
+    int *owner;        // per unit of P slots: -1 free, else the owning warp
+    int *phase;        // per slot: parity of the slot's mbarrier to wait for next
+    int S, units;      // slots, and units of P = 32 / G slots (S is a multiple of P)
 };
 struct Scratch {
     int8_t *qold, *qb, *zl, *zq;
@@ -50,17 +54,20 @@ struct Scratch {
 __host__ __device__ constexpr uint32_t pool_slot_bytes(uint32_t rec_max, int n) { return (rec_max + 2 * n + 127) / 128 * 128; }
 __host__ __device__ constexpr uint32_t pool_meta_bytes(int S) { return (16u * S + 127) / 128 * 128; }
 __host__ __device__ constexpr uint32_t scratch_bytes(int n) { return (2 * n + 64 + 32 + 127) / 128 * 128; }
-__host__ __device__ constexpr uint32_t block_smem(uint32_t rec_max, int n, int S, int W, int state_bytes) {
-    return S * pool_slot_bytes(rec_max, n) + pool_meta_bytes(S) + W * (scratch_bytes(n) + state_bytes);
+__host__ __device__ constexpr uint32_t block_smem(uint32_t rec_max, int n, int S, int streams, int state_bytes) {
+    return S * pool_slot_bytes(rec_max, n) + pool_meta_bytes(S) + streams * (scratch_bytes(n) + state_bytes);
 }
 
-// Lane 0 claims a free slot (CAS on its owner word, starting from the warp's home slot); -1 after ~1 s without one.
-__device__ __forceinline__ int slot_claim(const Pool &p, int home, int warp) {
+// Lane 0 claims a free unit of P slots for its warp, one slot per stream of the warp (CAS of the warp's id into the
+// unit's owner word, starting from the warp's home unit); -1 after ~1 s without one. A warp claims all its slots in
+// one step and releases them together, so a warp that holds slots never waits for more: no two warps can each hold
+// part of what the other needs.
+__device__ __forceinline__ int unit_claim(const Pool &p, int home, int owner) {
     const long long t0 = clock64();
     int i = home;
     while (true) {
-        if (atomicCAS(p.owner + i, -1, warp) == -1) break;
-        if (++i == p.S) {
+        if (atomicCAS(p.owner + i, -1, owner) == -1) break;
+        if (++i == p.units) {
             i = 0;
             if (clock64() - t0 > kWaitCycles) return -1;
             __nanosleep(32);
@@ -73,12 +80,12 @@ __device__ __forceinline__ int slot_claim(const Pool &p, int home, int warp) {
 struct StepOut {
     float *logits;      // [V] of this stream, or null
     int32_t *routes;    // [L] or null
-    int32_t *acc;       // [L][n] or null
+    int32_t *acc;       // [L][ns] or null
 };
 
-// What a token's layers share: the block's pool and the warp's scratch, the token, the state pointers (qstride
-// coordinates per layer; qlane: this lane's coordinates exist there), the debug outputs and the new state of the
-// layer below (carried from one layer to the next).
+// What a token's layers share: the block's pool and the stream's scratch, the token, the state pointers (qstride
+// coordinates per layer; qlane: this lane's coordinates exist there and are read and written), the debug outputs and
+// the new state of the layer below (carried from one layer to the next).
 template <int C>
 struct TokenCtx {
     const DevModel &m;
@@ -93,44 +100,89 @@ struct TokenCtx {
     LaneQ<C> qbelow;
 };
 
-// Layer l of a token (cpu/ygg.cpp:443-458). Returns false if a bounded wait gave up. Always inlined: the warp
-// collectives in it (shuffles, ballots, redux) rely on the caller's converged warp.
-template <int N, int BLK, int R, int R2T, int NVT>
-__device__ __forceinline__ bool layer_step(TokenCtx<N / 32> &t, const int l, float (&lg)[kMaxClassesPerLane]) {
-    constexpr int C = N / 32;
+// The new state of layer l (padding of a narrower model held at exactly 0) into the stream's state, and the debug
+// outputs.
+template <int N, int G>
+__device__ __forceinline__ void finish_state(const DevModel &m, TokenCtx<N / G> &t, int l, int r, int (&acc)[N / G],
+                                             LaneQ<N / G> &qn) {
+    constexpr int C = N / G;
+    const int gl = t.lane & (G - 1);
+    if (m.ns < N && C * gl >= m.ns) {
+#pragma unroll
+        for (int i = 0; i < (C >= 4 ? C / 4 : 1); i++) qn.w[i] = 0;
+#pragma unroll
+        for (int ii = 0; ii < C; ii++) acc[ii] = 0;
+    }
+    if (t.qlane) store_q<C>(t.q_out + (size_t)l * t.qstride + C * gl, qn);
+    if (t.dbg.routes != nullptr && gl == 0) t.dbg.routes[l] = r;
+    if (t.dbg.acc != nullptr && t.qlane) {
+#pragma unroll
+        for (int ii = 0; ii < C; ii++) t.dbg.acc[(size_t)l * t.qstride + C * gl + ii] = acc[ii];
+    }
+}
+
+// Layer l of a token (cpu/ygg.cpp:443-458) for the stream of the caller's lane group (G lanes). DIRECT: the expert
+// record is read from global memory after an L2 prefetch; else it is staged in a shared-memory slot by a bulk copy. Returns false if a
+// bounded wait gave up (for every stream of the warp). Always inlined: the warp collectives in it (shuffles, ballots,
+// redux) rely on the caller's converged warp, and both stream groups of a warp run it together.
+template <int N, int BLK, int R, int R2T, int NVT, int G, bool DIRECT>
+__device__ __forceinline__ bool layer_step(TokenCtx<N / G> &t, const int l, float (&lg)[kMaxClasses<G>]) {
+    constexpr int C = N / G;
     const DevModel &m = t.m;
     const Pool &pool = t.pool;
     const Scratch &sc = t.sc;
-    const int lane = t.lane, x = t.x, home = t.home, warp = t.warp;
+    const int lane = t.lane, x = t.x;
+    const int gl = lane & (G - 1);
     const int E = m.E, D = m.D;
-    const int nv = NVT ? NVT : m.VP / 32;
-    const int8_t *q_in = t.q_in;
-    int8_t *q_out = t.q_out;
-    const int qstride = t.qstride;
-    const bool qlane = t.qlane;
-    const StepOut &dbg = t.dbg;
     LaneQ<C> &qbelow = t.qbelow;
     const DevLayer &y = m.layer[l];
     LaneQ<C> qold = {};
-    if (qlane) qold = load_q<C>(q_in + (size_t)l * qstride + C * lane);
+    if (t.qlane) qold = load_q<C>(t.q_in + (size_t)l * t.qstride + C * gl);
     int r = x;
     float rho = 0.0f;
     const bool low = l > 0 && (R2T > 0 || m.R2 > 0);
     if (l > 0) {
-        rho = rms_rho<N>(qbelow, y.r2b, y.rms_eps, m.inv_n);
-        store_q<C>(sc.qb + C * lane, qbelow);
+        rho = rms_rho<N, G>(qbelow, y.r2b, y.rms_eps, m.inv_n, lane);
+        store_q<C>(sc.qb + C * gl, qbelow);
         __syncwarp();
-        const uint4 qrow = *(const uint4 *)(sc.qb + 16 * (lane % (N / 16)));
-        r = route_look<N>(y.w, y.thr + (size_t)x * E, D, qrow, rho, lane) - E;
+        const uint4 qrow = *(const uint4 *)(sc.qb + 16 * (gl % (N / 16)));
+        r = route_look<N, G>(y.w, y.thr + (size_t)x * E, D, qrow, rho, lane) - E;
     }
-    // -- lane 0 claims a slot and issues the bulk copies of the expert record and its table row into it; the
-    // slot index and the parity to wait for reach the other lanes in one shuffle
     const uint32_t rec_bytes = y.rec_bytes;
     const bool has_table = y.table != nullptr;
-    int tag = -1;
-    if (lane == 0) {
-        const int slot = slot_claim(pool, home, warp);
-        if (slot >= 0) {
+    int acc[C];
+    LaneQ<C> qn;
+    ReadoutPart<N, R, G> ro;
+    if constexpr (DIRECT) {
+        // -- the record and its table row are read straight from global memory: the group's first lane asks L2 for
+        // them now, and the layer-input codes run while they arrive
+        const uint8_t *rec = y.rec + (size_t)r * rec_bytes;
+        const int16_t *trow =
+            has_table ? y.table + ((size_t)r * y.table_rows + (y.table_rows > 1 ? x : 0)) * N : nullptr;
+        if (gl == 0) {
+            prefetch_l2(rec, rec_bytes);
+            if (has_table) prefetch_l2(trow, 2u * N);
+        }
+        if (low) layer_input_codes<N, R2T, G>(m, y, sc.qb, rho, sc.zl, lane);
+        store_q<C>(sc.qold + C * gl, qold);
+        __syncwarp();
+        leaf_update<N, BLK, R2T, G, true>(m, y, rec, trow, x, sc.qold, sc.zl, low, lane, acc, qn);
+        finish_state<N, G>(m, t, l, r, acc, qn);
+        ro = readout_partials<N, R, G, true>(y, rec, qn, lane);
+    } else {
+        // -- lane 0 claims a unit of slots for the warp (slot unit * P + group for each stream group); each group's
+        // first lane issues the bulk copies of its expert record and table row into its slot; the slot index and the
+        // parity to wait for reach the group's lanes in one shuffle
+        constexpr int P = 32 / G;
+        const int leader = lane & (32 - G);
+        int unit = 0;
+        if (lane == 0) unit = unit_claim(pool, t.home, t.warp);
+        unit = __shfl_sync(kFull, unit, 0);
+        if (unit < 0) return false;
+        __syncwarp();   // the phases the unit's last holder flipped are visible to every group leader
+        int tag = 0;
+        if (gl == 0) {
+            const int slot = unit * P + lane / G;
             uint8_t *rec = pool.slots + (size_t)slot * pool.slot_bytes;
             const uint32_t bar = pool.bars + 8u * slot;
             fence_proxy_async();
@@ -142,81 +194,71 @@ __device__ __forceinline__ bool layer_step(TokenCtx<N / 32> &t, const int l, flo
             }
             tag = 2 * slot + pool.phase[slot];
         }
+        tag = __shfl_sync(kFull, tag, leader);
+        const int slot = tag >> 1;
+        const uint32_t parity = (uint32_t)(tag & 1);
+        const uint8_t *rec = pool.slots + (size_t)slot * pool.slot_bytes;
+        const int16_t *trow = (const int16_t *)(rec + (pool.slot_bytes - 2 * N));
+        const uint32_t bar = pool.bars + 8u * slot;
+        // -- layer input codes while the copy is in flight (cpu/ygg.cpp:285-296)
+        if (low) layer_input_codes<N, R2T, G>(m, y, sc.qb, rho, sc.zl, lane);
+        store_q<C>(sc.qold + C * gl, qold);
+        __syncwarp();
+        if (!__all_sync(kFull, mbar_wait_bounded(bar, parity))) return false;
+        leaf_update<N, BLK, R2T, G>(m, y, rec, has_table ? trow : nullptr, x, sc.qold, sc.zl, low, lane, acc, qn);
+        finish_state<N, G>(m, t, l, r, acc, qn);
+        ro = readout_partials<N, R, G>(y, rec, qn, lane);
+        // the slots are free once their bytes are used: flip their parities and hand the unit back
+        __syncwarp();
+        if (gl == 0) pool.phase[slot] = (int)(parity ^ 1u);
+        __syncwarp();
+        if (lane == 0) {
+            __threadfence_block();
+            atomicExch(pool.owner + unit, -1);
+        }
     }
-    tag = __shfl_sync(kFull, tag, 0);
-    if (tag < 0) return false;
-    const int slot = tag >> 1;
-    const uint32_t parity = (uint32_t)(tag & 1);
-    const uint8_t *rec = pool.slots + (size_t)slot * pool.slot_bytes;
-    const int16_t *trow = (const int16_t *)(rec + (pool.slot_bytes - 2 * N));
-    const uint32_t bar = pool.bars + 8u * slot;
-    // -- layer input codes while the copy is in flight (cpu/ygg.cpp:285-296)
-    if (low) layer_input_codes<N, R2T>(m, y, sc.qb, rho, sc.zl, lane);
-    store_q<C>(sc.qold + C * lane, qold);
+    const int zq = readout_code<N, R, G>(ro, lane);
+    const int row = readout_row<R, G>(gl);
+    if (row >= 0 && (G == 32 || R == 16 || (gl & 1) == 0)) sc.zq[row] = (int8_t)zq;
     __syncwarp();
-    if (!__all_sync(kFull, mbar_wait_bounded(bar, parity))) return false;
-
-    int acc[C];
-    LaneQ<C> qn;
-    leaf_update<N, BLK, R2T>(m, y, rec, has_table ? trow : nullptr, x, sc.qold, sc.zl, low, lane, acc, qn);
-    if (m.ns < N && C * lane >= m.ns) {   // padding of a narrower model: held at exactly 0
-#pragma unroll
-        for (int i = 0; i < (C >= 4 ? C / 4 : 1); i++) qn.w[i] = 0;
-#pragma unroll
-        for (int ii = 0; ii < C; ii++) acc[ii] = 0;
-    }
-    if (qlane) store_q<C>(q_out + (size_t)l * qstride + C * lane, qn);
-    if (dbg.routes != nullptr && lane == 0) dbg.routes[l] = r;
-    if (dbg.acc != nullptr && qlane) {
-#pragma unroll
-        for (int ii = 0; ii < C; ii++) dbg.acc[(size_t)l * qstride + C * lane + ii] = acc[ii];
-    }
-    const ReadoutWords<N, R> ro = load_readout<N, R>(y, rec, lane);
-    // the slot is free once its bytes are in registers: flip its parity and hand it back
-    __syncwarp();
-    if (lane == 0) {
-        pool.phase[slot] = (int)(parity ^ 1u);
-        __threadfence_block();
-        atomicExch(pool.owner + slot, -1);
-    }
-    const int zq = readout_code<N, R>(ro, qn, lane);
-    if (lane < R) sc.zq[lane] = (int8_t)zq;
-    __syncwarp();
-    head_accumulate<R, NVT>(m, y, sc.zq, lg, lane);
+    head_accumulate<R, NVT, G>(m, y, sc.zq, lg, lane);
     qbelow = qn;
     __syncwarp();
     return true;
 }
 
-// One token of one stream through every layer. q_in / q_out: the stream's state [L][qstride] (global memory in the
-// caller's layout, qstride = the model's ns, or shared memory in the device layout, qstride = n; they may alias).
-// lg: the logits of the lane's classes (out). Returns false if a bounded wait gave up.
-// Compile-time shape where a fast instance fixes it (0: read from the model at run time): R2T the padded layer-input
-// rank, LT the number of layers, NVT the classes per lane (VP / 32).
-template <int N, int BLK, int R, int R2T, int LT, int NVT>
+// One token of the stream of the caller's lane group through every layer. q_in / q_out: the stream's state
+// [L][qstride] (global memory in the caller's layout, qstride = the model's ns, or shared memory in the device layout,
+// qstride = n; they may alias); qlane false: the state is neither read (zeros) nor written (a stream that only keeps
+// its warp's collectives company). lg: the logits of the lane's classes (out). Returns false if a bounded wait gave
+// up. Compile-time shape where a fast instance fixes it (0: read from the model at run time): R2T the padded
+// layer-input rank, LT the number of layers, NVT the classes per lane (VP / G).
+template <int N, int BLK, int R, int R2T, int LT, int NVT, int G, bool DIRECT>
 __device__ __forceinline__ bool token_step(const DevModel &m, const Pool &pool, const Scratch &sc, int home, int warp,
-                                           int x, const int8_t *q_in, int8_t *q_out, int qstride,
-                                           float (&lg)[kMaxClassesPerLane], const StepOut &dbg, int lane) {
+                                           int x, const int8_t *q_in, int8_t *q_out, int qstride, bool qlane,
+                                           float (&lg)[kMaxClasses<G>], const StepOut &dbg, int lane) {
     const int V = m.V;
-    const int nv = NVT ? NVT : m.VP / 32;
+    const int nv = NVT ? NVT : m.VP / G;
+    const int gl = lane & (G - 1);
 #pragma unroll
-    for (int c = 0; c < kMaxClassesPerLane; c++) lg[c] = c < nv ? __ldg(m.head_b + 32 * c + lane) : 0.0f;
-    TokenCtx<N / 32> t{m, pool, sc, home, warp, lane, x, q_in, q_out, qstride, (N / 32) * lane < qstride, dbg, {}};
+    for (int c = 0; c < kMaxClasses<G>; c++) lg[c] = c < nv ? __ldg(m.head_b + G * c + gl) : 0.0f;
+    TokenCtx<N / G> t{m, pool, sc, home, warp, lane, x, q_in, q_out, qstride, qlane && (N / G) * gl < qstride,
+                      dbg, {}};
     if constexpr (LT > 0) {
         // not unrolled: an unrolled layer loop with its early exits defeats the compiler's proof that the warp is
         // converged at the collectives, and each shuffle / ballot / redux then pays a re-convergence loop
 #pragma unroll 1
         for (int l = 0; l < LT; l++)
-            if (!layer_step<N, BLK, R, R2T, NVT>(t, l, lg)) return false;
+            if (!layer_step<N, BLK, R, R2T, NVT, G, DIRECT>(t, l, lg)) return false;
     } else {
 #pragma unroll 1
         for (int l = 0; l < m.L; l++)
-            if (!layer_step<N, BLK, R, R2T, NVT>(t, l, lg)) return false;
+            if (!layer_step<N, BLK, R, R2T, NVT, G, DIRECT>(t, l, lg)) return false;
     }
     if (dbg.logits != nullptr) {
 #pragma unroll
-        for (int c = 0; c < kMaxClassesPerLane; c++) {
-            const int cls = 32 * c + lane;
+        for (int c = 0; c < kMaxClasses<G>; c++) {
+            const int cls = G * c + gl;
             if (c < nv && cls < V) dbg.logits[cls] = lg[c];
         }
     }
@@ -225,9 +267,10 @@ __device__ __forceinline__ bool token_step(const DevModel &m, const Pool &pool, 
 
 // ------------------------------------------------------------------------------------------------ kernels
 
-// Pool and scratch of this block; the first warp initialises the slots' mbarriers and owners.
-__device__ __forceinline__ void block_init(uint8_t *smem, uint32_t rec_max, int n, int S, int state_bytes, int warp,
-                                           int lane, Pool &pool, Scratch &sc, int8_t *&state) {
+// Pool and the scratch of this block's stream `sidx` (warp * P + group); the first thread initialises the slots'
+// mbarriers and phases and the units' owners.
+__device__ __forceinline__ void block_init(uint8_t *smem, uint32_t rec_max, int n, int S, int P, int state_bytes,
+                                           int sidx, Pool &pool, Scratch &sc, int8_t *&state) {
     pool.slot_bytes = pool_slot_bytes(rec_max, n);
     pool.slots = smem;
     uint8_t *meta = smem + (size_t)S * pool.slot_bytes;
@@ -235,7 +278,8 @@ __device__ __forceinline__ void block_init(uint8_t *smem, uint32_t rec_max, int 
     pool.owner = (int *)(meta + 8 * S);
     pool.phase = (int *)(meta + 12 * S);
     pool.S = S;
-    uint8_t *ws = meta + pool_meta_bytes(S) + (size_t)warp * (scratch_bytes(n) + state_bytes);
+    pool.units = S / P;   // 0: no slots (records read from global memory)
+    uint8_t *ws = meta + pool_meta_bytes(S) + (size_t)sidx * (scratch_bytes(n) + state_bytes);
     sc.qold = (int8_t *)ws;
     sc.qb = sc.qold + n;
     sc.zl = sc.qb + n;
@@ -244,7 +288,7 @@ __device__ __forceinline__ void block_init(uint8_t *smem, uint32_t rec_max, int 
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; i++) {
             mbar_init(pool.bars + 8u * i, 1);
-            pool.owner[i] = -1;
+            pool.owner[i] = -1;   // units < S: owner words of the units, the rest unused
             pool.phase[i] = 0;
         }
         fence_mbar_init();
@@ -252,84 +296,106 @@ __device__ __forceinline__ void block_init(uint8_t *smem, uint32_t rec_max, int 
     __syncthreads();
 }
 
-template <int N, int BLK, int R, int R2T, int LT, int NVT>
+// Each warp serves P = 32 / G streams at a time, stream base + (lane / G); a warp whose second stream is past B runs
+// it on a copy of its first (nothing of it is read or written) so that its collectives stay full-warp.
+template <int N, int BLK, int R, int R2T, int LT, int NVT, int G, bool DIRECT>
 __global__ void __launch_bounds__(256, blocks_per_sm<N>()) step_kernel(const __grid_constant__ DevModel m, int B,
                                                    const int32_t *__restrict__ tokens, const int8_t *state_in,
                                                    int8_t *state_out, float *__restrict__ logits,
                                                    int32_t *__restrict__ routes, int32_t *__restrict__ acc_out,
                                                    uint32_t rec_max, int S) {
+    constexpr int P = 32 / G;
     extern __shared__ __align__(128) uint8_t smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = blockDim.x >> 5;
+    const int gh = lane / G, gl = lane & (G - 1);
+    const int sidx = warp * P + gh;
     Pool pool;
     Scratch sc;
     int8_t *unused;
-    block_init(smem, rec_max, N, S, 0, warp, lane, pool, sc, unused);
-    const int home = warp % S;
+    block_init(smem, rec_max, N, S, P, 0, sidx, pool, sc, unused);
+    const int home = pool.units ? warp % pool.units : 0;
     const int L = m.L, V = m.V, ns = m.ns;
-    for (int s = blockIdx.x * W + warp; s < B; s += gridDim.x * W) {
-        const int x = tokens[s];
-        if (x < 0 || x >= V) {   // cpu/ygg.cpp:493-495 rejects the whole input; here the stream is skipped
-            if (lane == 0) atomicOr(m.status, kStatusBadToken);
-            if (logits != nullptr)
-                for (int c = lane; c < V; c += 32) logits[(size_t)s * V + c] = __int_as_float(0x7fc00000);
-            if (state_out != state_in)
-                for (int i = lane; i < L * ns; i += 32) state_out[(size_t)s * L * ns + i] = state_in[(size_t)s * L * ns + i];
-            if (routes != nullptr && lane < L) routes[(size_t)s * L + lane] = -1;
-            continue;
-        }
-        float lg[kMaxClassesPerLane];
-        StepOut o{logits ? logits + (size_t)s * V : nullptr, routes ? routes + (size_t)s * L : nullptr,
-                  acc_out ? acc_out + (size_t)s * L * ns : nullptr};
-        if (!token_step<N, BLK, R, R2T, LT, NVT>(m, pool, sc, home, warp, x, state_in + (size_t)s * L * ns,
-                                                 state_out + (size_t)s * L * ns, ns, lg, o, lane)) {
+    for (int base = (blockIdx.x * W + warp) * P; base < B; base += gridDim.x * W * P) {
+        const int s = base + gh;
+        const bool real = s < B;
+        const int se = real ? s : base;
+        const int x = tokens[se];
+        // a token out of range (cpu/ygg.cpp:493-495 rejects the whole input): the stream is skipped, NaN logits and
+        // its state unchanged; it runs token 0 unseen so that its warp's collectives stay full
+        const bool bad = x < 0 || x >= V;
+        const bool live = real && !bad;
+        if (real && bad && gl == 0) atomicOr(m.status, kStatusBadToken);
+        float lg[kMaxClasses<G>];
+        StepOut o{(live && logits) ? logits + (size_t)s * V : nullptr, (live && routes) ? routes + (size_t)s * L : nullptr,
+                  (live && acc_out) ? acc_out + (size_t)se * L * ns : nullptr};
+        if (!token_step<N, BLK, R, R2T, LT, NVT, G, DIRECT>(m, pool, sc, home, warp, bad ? 0 : x, state_in + (size_t)se * L * ns,
+                                                    state_out + (size_t)se * L * ns, ns, live, lg, o, lane)) {
             if (lane == 0) atomicOr(m.status, kStatusTimeout);
             return;
+        }
+        if (real && bad) {
+            if (logits != nullptr)
+                for (int c = gl; c < V; c += G) logits[(size_t)s * V + c] = __int_as_float(0x7fc00000);
+            if (state_out != state_in)
+                for (int i = gl; i < L * ns; i += G) state_out[(size_t)s * L * ns + i] = state_in[(size_t)s * L * ns + i];
+            if (routes != nullptr && gl < L) routes[(size_t)s * L + gl] = -1;
         }
     }
 }
 
-// Rows of `steps` tokens; the state of a row lives in the warp's shared memory between tokens, the logits in
-// registers, and the f64 NLL of the next token is summed on chip (cpu/ygg.cpp:513-517).
-template <int N, int BLK, int R, int R2T, int LT, int NVT>
+// Rows of `steps` tokens; the state of a row lives in its group's shared memory between tokens, the logits in
+// registers, and the f64 NLL of the next token is summed on chip (cpu/ygg.cpp:513-517). Each warp scores P = 32 / G
+// rows at a time; a row past B, or with a token out of range, runs unseen (token 0, nothing written; the bad row
+// scores NaN).
+template <int N, int BLK, int R, int R2T, int LT, int NVT, int G, bool DIRECT>
 __global__ void __launch_bounds__(256, blocks_per_sm<N>()) score_kernel(const __grid_constant__ DevModel m, int B, int T,
                                                     const int32_t *__restrict__ tokens, int8_t *state,
                                                     double *__restrict__ bits, uint32_t rec_max, int S) {
+    constexpr int P = 32 / G;
     extern __shared__ __align__(128) uint8_t smem[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = blockDim.x >> 5;
-    const int L = m.L, V = m.V, nv = m.VP / 32, ns = m.ns;
+    const int gh = lane / G, gl = lane & (G - 1);
+    const int sidx = warp * P + gh;
+    const int L = m.L, V = m.V, nv = m.VP / G, ns = m.ns;
     Pool pool;
     Scratch sc;
     int8_t *qs;
-    block_init(smem, rec_max, N, S, (L * N + 127) / 128 * 128, warp, lane, pool, sc, qs);
-    const int home = warp % S;
+    block_init(smem, rec_max, N, S, P, (L * N + 127) / 128 * 128, sidx, pool, sc, qs);
+    const int home = pool.units ? warp % pool.units : 0;
     const StepOut none{nullptr, nullptr, nullptr};
-    for (int s = blockIdx.x * W + warp; s < B; s += gridDim.x * W) {
-        const int32_t *tok = tokens + (size_t)s * T;
+    for (int base = (blockIdx.x * W + warp) * P; base < B; base += gridDim.x * W * P) {
+        const int s = base + gh;
+        const bool real = s < B;
+        const int32_t *tok = tokens + (size_t)(real ? s : base) * T;
         bool bad = false;
-        for (int t = lane; t < T; t += 32) bad |= tok[t] < 0 || tok[t] >= V;
-        if (__any_sync(kFull, bad)) {
-            if (lane == 0) { atomicOr(m.status, kStatusBadToken); bits[s] = __longlong_as_double(0x7ff8000000000000LL); }
-            continue;
+        for (int t = gl; t < T; t += G) bad |= tok[t] < 0 || tok[t] >= V;
+        const uint32_t bb = __ballot_sync(kFull, bad);
+        bad = ((bb >> (lane & (32 - G))) & (G == 32 ? kFull : 0xFFFFu)) != 0;
+        const bool live = real && !bad;
+        if (real && bad && gl == 0) {
+            atomicOr(m.status, kStatusBadToken);
+            bits[s] = __longlong_as_double(0x7ff8000000000000LL);
         }
         // the row's state into the device layout (n per layer; coordinates past the model's ns are 0)
-        for (int i = lane; i < L * N; i += 32) {
+        for (int i = gl; i < L * N; i += G) {
             const int li = i / N, c = i % N;
-            qs[i] = (state != nullptr && c < ns) ? state[((size_t)s * L + li) * ns + c] : (int8_t)0;
+            qs[i] = (live && state != nullptr && c < ns) ? state[((size_t)s * L + li) * ns + c] : (int8_t)0;
         }
         __syncwarp();
         double nll = 0.0;
         for (int t = 0; t + 1 < T; t++) {
-            float lg[kMaxClassesPerLane];
-            if (!token_step<N, BLK, R, R2T, LT, NVT>(m, pool, sc, home, warp, tok[t], qs, qs, N, lg, none, lane)) {
+            float lg[kMaxClasses<G>];
+            const int xt = live ? tok[t] : 0;
+            if (!token_step<N, BLK, R, R2T, LT, NVT, G, DIRECT>(m, pool, sc, home, warp, xt, qs, qs, N, true, lg, none, lane)) {
                 if (lane == 0) atomicOr(m.status, kStatusTimeout);
                 return;
             }
-            nll += nll_of(lg, nv, V, tok[t + 1], lane);
+            nll += nll_of<G>(lg, nv, V, live ? tok[t + 1] : 0, lane);
         }
-        if (lane == 0) bits[s] = nll / 0.69314718055994530942;
+        if (live && gl == 0) bits[s] = nll / 0.69314718055994530942;
         __syncwarp();
-        if (state)
-            for (int i = lane; i < L * N; i += 32) {
+        if (live && state)
+            for (int i = gl; i < L * N; i += G) {
                 const int li = i / N, c = i % N;
                 if (c < ns) state[((size_t)s * L + li) * ns + c] = qs[i];
             }
@@ -343,8 +409,8 @@ __global__ void __launch_bounds__(256, blocks_per_sm<N>()) score_kernel(const __
 // attribute is per device; raising it on every launch would cost a driver call per step).
 constexpr int kMaxDevices = 64;
 struct SmemLimits { size_t set[kMaxDevices]; };
-template <int N, int BLK, int R, int R2T, int LT, int NVT> static SmemLimits &step_limit() { static SmemLimits l{}; return l; }
-template <int N, int BLK, int R, int R2T, int LT, int NVT> static SmemLimits &score_limit() { static SmemLimits l{}; return l; }
+template <int N, int BLK, int R, int R2T, int LT, int NVT, int G, bool D> static SmemLimits &step_limit() { static SmemLimits l{}; return l; }
+template <int N, int BLK, int R, int R2T, int LT, int NVT, int G, bool D> static SmemLimits &score_limit() { static SmemLimits l{}; return l; }
 static cudaError_t raise_smem_limit(const void *fn, size_t smem, SmemLimits &lim) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -355,70 +421,98 @@ static cudaError_t raise_smem_limit(const void *fn, size_t smem, SmemLimits &lim
     return e;
 }
 
-template <int N, int BLK, int R, int R2T, int LT, int NVT>
+// blocks for B streams: W warps of P = 32 / G streams each, at most grid_cap blocks
+template <int G> static int grid_for(int B, int warps, int grid_cap) {
+    const int per = warps * (32 / G);
+    const int grid = (B + per - 1) / per;
+    return grid > grid_cap ? grid_cap : grid;
+}
+
+// D (direct): records read from global memory, no slots; else `slots` staging slots per block.
+template <int N, int BLK, int R, int R2T, int LT, int NVT, int G, bool D>
 static cudaError_t launch_step_t(const DevModel &dm, int B, const int32_t *tok, const int8_t *sin, int8_t *sout,
                                  float *lg, int32_t *routes, int32_t *acc, uint32_t rec_max, int warps, int slots,
                                  int grid_cap, cudaStream_t st) {
-    const size_t smem = block_smem(rec_max, N, slots, warps, 0);
-    cudaError_t e = raise_smem_limit((const void *)step_kernel<N, BLK, R, R2T, LT, NVT>, smem, step_limit<N, BLK, R, R2T, LT, NVT>());
+    const int S = D ? 0 : slots;
+    const size_t smem = block_smem(rec_max, N, S, warps * (32 / G), 0);
+    cudaError_t e = raise_smem_limit((const void *)step_kernel<N, BLK, R, R2T, LT, NVT, G, D>, smem,
+                                     step_limit<N, BLK, R, R2T, LT, NVT, G, D>());
     if (e != cudaSuccess) return e;
-    int grid = (B + warps - 1) / warps;
-    if (grid > grid_cap) grid = grid_cap;
-    step_kernel<N, BLK, R, R2T, LT, NVT><<<grid, 32 * warps, smem, st>>>(dm, B, tok, sin, sout, lg, routes, acc, rec_max, slots);
+    step_kernel<N, BLK, R, R2T, LT, NVT, G, D><<<grid_for<G>(B, warps, grid_cap), 32 * warps, smem, st>>>(
+        dm, B, tok, sin, sout, lg, routes, acc, rec_max, S);
     return cudaGetLastError();
 }
 
-template <int N, int BLK, int R, int R2T, int LT, int NVT>
+template <int N, int BLK, int R, int R2T, int LT, int NVT, int G, bool D>
 static cudaError_t launch_score_t(const DevModel &dm, int B, int T, const int32_t *tok, int8_t *state, double *bits,
                                   uint32_t rec_max, int warps, int slots, int grid_cap, cudaStream_t st) {
-    const size_t smem = block_smem(rec_max, N, slots, warps, (dm.L * N + 127) / 128 * 128);
-    cudaError_t e = raise_smem_limit((const void *)score_kernel<N, BLK, R, R2T, LT, NVT>, smem, score_limit<N, BLK, R, R2T, LT, NVT>());
+    const int S = D ? 0 : slots;
+    const size_t smem = block_smem(rec_max, N, S, warps * (32 / G), (dm.L * N + 127) / 128 * 128);
+    cudaError_t e = raise_smem_limit((const void *)score_kernel<N, BLK, R, R2T, LT, NVT, G, D>, smem,
+                                     score_limit<N, BLK, R, R2T, LT, NVT, G, D>());
     if (e != cudaSuccess) return e;
-    int grid = (B + warps - 1) / warps;
-    if (grid > grid_cap) grid = grid_cap;
-    score_kernel<N, BLK, R, R2T, LT, NVT><<<grid, 32 * warps, smem, st>>>(dm, B, T, tok, state, bits, rec_max, slots);
+    score_kernel<N, BLK, R, R2T, LT, NVT, G, D><<<grid_for<G>(B, warps, grid_cap), 32 * warps, smem, st>>>(
+        dm, B, T, tok, state, bits, rec_max, S);
     return cudaGetLastError();
 }
 
-#define YGG_DISPATCH(FN, ...)                                                                          \
-    /* fast instances with the benchmark shapes fixed at compile time: c3 (n128 R16 R2=32, 4 layers, V <= 32), */ \
-    /* c4 (same, V = 256), c1 / c2 (n64 R8 R2=16, 2 / 4 layers, V = 256) */                                    \
-    if (n == 128 && blk == 16 && r == 16 && r2p == 32 && L == 4 && nv == 1) return FN<128, 16, 16, 32, 4, 1>(__VA_ARGS__); \
-    if (n == 128 && blk == 16 && r == 16 && r2p == 32 && L == 4 && nv == 8) return FN<128, 16, 16, 32, 4, 8>(__VA_ARGS__); \
-    if (n == 64 && blk == 16 && r == 8 && r2p == 16 && L == 2 && nv == 8) return FN<64, 16, 8, 16, 2, 8>(__VA_ARGS__);     \
-    if (n == 64 && blk == 16 && r == 8 && r2p == 16 && L == 4 && nv == 8) return FN<64, 16, 8, 16, 4, 8>(__VA_ARGS__);     \
-    switch (n * 1000 + blk * 100 + r) {                                                                \
-        case 64 * 1000 + 8 * 100 + 8: return FN<64, 8, 8, 0, 0, 0>(__VA_ARGS__);                     \
-        case 64 * 1000 + 8 * 100 + 16: return FN<64, 8, 16, 0, 0, 0>(__VA_ARGS__);                   \
-        case 64 * 1000 + 8 * 100 + 32: return FN<64, 8, 32, 0, 0, 0>(__VA_ARGS__);                   \
-        case 64 * 1000 + 16 * 100 + 8: return FN<64, 16, 8, 0, 0, 0>(__VA_ARGS__);                   \
-        case 64 * 1000 + 16 * 100 + 16: return FN<64, 16, 16, 0, 0, 0>(__VA_ARGS__);                 \
-        case 64 * 1000 + 16 * 100 + 32: return FN<64, 16, 32, 0, 0, 0>(__VA_ARGS__);                 \
-        case 128 * 1000 + 8 * 100 + 8: return FN<128, 8, 8, 0, 0, 0>(__VA_ARGS__);                   \
-        case 128 * 1000 + 8 * 100 + 16: return FN<128, 8, 16, 0, 0, 0>(__VA_ARGS__);                 \
-        case 128 * 1000 + 8 * 100 + 32: return FN<128, 8, 32, 0, 0, 0>(__VA_ARGS__);                 \
-        case 128 * 1000 + 16 * 100 + 8: return FN<128, 16, 8, 0, 0, 0>(__VA_ARGS__);                 \
-        case 128 * 1000 + 16 * 100 + 16: return FN<128, 16, 16, 0, 0, 0>(__VA_ARGS__);               \
-        case 128 * 1000 + 16 * 100 + 32: return FN<128, 16, 32, 0, 0, 0>(__VA_ARGS__);               \
-        case 256 * 1000 + 8 * 100 + 8: return FN<256, 8, 8, 0, 0, 0>(__VA_ARGS__);                   \
-        case 256 * 1000 + 8 * 100 + 16: return FN<256, 8, 16, 0, 0, 0>(__VA_ARGS__);                 \
-        case 256 * 1000 + 8 * 100 + 32: return FN<256, 8, 32, 0, 0, 0>(__VA_ARGS__);                 \
-        case 256 * 1000 + 16 * 100 + 8: return FN<256, 16, 8, 0, 0, 0>(__VA_ARGS__);                 \
-        case 256 * 1000 + 16 * 100 + 16: return FN<256, 16, 16, 0, 0, 0>(__VA_ARGS__);               \
-        case 256 * 1000 + 16 * 100 + 32: return FN<256, 16, 32, 0, 0, 0>(__VA_ARGS__);               \
-        default: return cudaErrorInvalidValue;                                                         \
+// Instances: lw = 16 (two streams per warp; the layout the loader picks for n 64 / 128 with readout rank <= 16) or
+// lw = 32 (a warp per stream: every shape). Fast instances fix the benchmark shapes at compile time: c3 (n128 R16
+// R2=32, 4 layers, V <= 32), c4 (the same, V = 256), c1 / c2 (n64 R8 R2=16, 2 / 4 layers, V = 256).
+#define YGG_DISPATCH(FN, ...)                                                                                          \
+    if (lw == 16) {                                                                                                    \
+        if (n == 128 && blk == 16 && r == 16 && r2p == 32 && L == 4 && VP == 32) return dm.direct ? FN<128, 16, 16, 32, 4, 2, 16, true>(__VA_ARGS__) : FN<128, 16, 16, 32, 4, 2, 16, false>(__VA_ARGS__); \
+        if (n == 128 && blk == 16 && r == 16 && r2p == 32 && L == 4 && VP == 256) return dm.direct ? FN<128, 16, 16, 32, 4, 16, 16, true>(__VA_ARGS__) : FN<128, 16, 16, 32, 4, 16, 16, false>(__VA_ARGS__); \
+        if (n == 64 && blk == 16 && r == 8 && r2p == 16 && L == 2 && VP == 256) return dm.direct ? FN<64, 16, 8, 16, 2, 16, 16, true>(__VA_ARGS__) : FN<64, 16, 8, 16, 2, 16, 16, false>(__VA_ARGS__);     \
+        if (n == 64 && blk == 16 && r == 8 && r2p == 16 && L == 4 && VP == 256) return dm.direct ? FN<64, 16, 8, 16, 4, 16, 16, true>(__VA_ARGS__) : FN<64, 16, 8, 16, 4, 16, 16, false>(__VA_ARGS__);     \
+        switch (n * 1000 + blk * 100 + r) {                                                                            \
+            case 64 * 1000 + 8 * 100 + 8: return FN<64, 8, 8, 0, 0, 0, 16, false>(__VA_ARGS__);                              \
+            case 64 * 1000 + 8 * 100 + 16: return FN<64, 8, 16, 0, 0, 0, 16, false>(__VA_ARGS__);                            \
+            case 64 * 1000 + 16 * 100 + 8: return FN<64, 16, 8, 0, 0, 0, 16, false>(__VA_ARGS__);                            \
+            case 64 * 1000 + 16 * 100 + 16: return FN<64, 16, 16, 0, 0, 0, 16, false>(__VA_ARGS__);                          \
+            case 128 * 1000 + 8 * 100 + 8: return FN<128, 8, 8, 0, 0, 0, 16, false>(__VA_ARGS__);                            \
+            case 128 * 1000 + 8 * 100 + 16: return FN<128, 8, 16, 0, 0, 0, 16, false>(__VA_ARGS__);                          \
+            case 128 * 1000 + 16 * 100 + 8: return FN<128, 16, 8, 0, 0, 0, 16, false>(__VA_ARGS__);                          \
+            case 128 * 1000 + 16 * 100 + 16: return FN<128, 16, 16, 0, 0, 0, 16, false>(__VA_ARGS__);                        \
+            default: return cudaErrorInvalidValue;                                                                     \
+        }                                                                                                              \
+    }                                                                                                                  \
+    if (n == 128 && blk == 16 && r == 16 && r2p == 32 && L == 4 && VP == 32) return dm.direct ? FN<128, 16, 16, 32, 4, 1, 32, true>(__VA_ARGS__) : FN<128, 16, 16, 32, 4, 1, 32, false>(__VA_ARGS__); \
+    if (n == 128 && blk == 16 && r == 16 && r2p == 32 && L == 4 && VP == 256) return dm.direct ? FN<128, 16, 16, 32, 4, 8, 32, true>(__VA_ARGS__) : FN<128, 16, 16, 32, 4, 8, 32, false>(__VA_ARGS__); \
+    if (n == 64 && blk == 16 && r == 8 && r2p == 16 && L == 2 && VP == 256) return dm.direct ? FN<64, 16, 8, 16, 2, 8, 32, true>(__VA_ARGS__) : FN<64, 16, 8, 16, 2, 8, 32, false>(__VA_ARGS__);     \
+    if (n == 64 && blk == 16 && r == 8 && r2p == 16 && L == 4 && VP == 256) return dm.direct ? FN<64, 16, 8, 16, 4, 8, 32, true>(__VA_ARGS__) : FN<64, 16, 8, 16, 4, 8, 32, false>(__VA_ARGS__);     \
+    switch (n * 1000 + blk * 100 + r) {                                                                                \
+        case 64 * 1000 + 8 * 100 + 8: return FN<64, 8, 8, 0, 0, 0, 32, false>(__VA_ARGS__);                                  \
+        case 64 * 1000 + 8 * 100 + 16: return FN<64, 8, 16, 0, 0, 0, 32, false>(__VA_ARGS__);                                \
+        case 64 * 1000 + 8 * 100 + 32: return FN<64, 8, 32, 0, 0, 0, 32, false>(__VA_ARGS__);                                \
+        case 64 * 1000 + 16 * 100 + 8: return FN<64, 16, 8, 0, 0, 0, 32, false>(__VA_ARGS__);                                \
+        case 64 * 1000 + 16 * 100 + 16: return FN<64, 16, 16, 0, 0, 0, 32, false>(__VA_ARGS__);                              \
+        case 64 * 1000 + 16 * 100 + 32: return FN<64, 16, 32, 0, 0, 0, 32, false>(__VA_ARGS__);                              \
+        case 128 * 1000 + 8 * 100 + 8: return FN<128, 8, 8, 0, 0, 0, 32, false>(__VA_ARGS__);                                \
+        case 128 * 1000 + 8 * 100 + 16: return FN<128, 8, 16, 0, 0, 0, 32, false>(__VA_ARGS__);                              \
+        case 128 * 1000 + 8 * 100 + 32: return FN<128, 8, 32, 0, 0, 0, 32, false>(__VA_ARGS__);                              \
+        case 128 * 1000 + 16 * 100 + 8: return FN<128, 16, 8, 0, 0, 0, 32, false>(__VA_ARGS__);                              \
+        case 128 * 1000 + 16 * 100 + 16: return FN<128, 16, 16, 0, 0, 0, 32, false>(__VA_ARGS__);                            \
+        case 128 * 1000 + 16 * 100 + 32: return FN<128, 16, 32, 0, 0, 0, 32, false>(__VA_ARGS__);                            \
+        case 256 * 1000 + 8 * 100 + 8: return FN<256, 8, 8, 0, 0, 0, 32, false>(__VA_ARGS__);                                \
+        case 256 * 1000 + 8 * 100 + 16: return FN<256, 8, 16, 0, 0, 0, 32, false>(__VA_ARGS__);                              \
+        case 256 * 1000 + 8 * 100 + 32: return FN<256, 8, 32, 0, 0, 0, 32, false>(__VA_ARGS__);                              \
+        case 256 * 1000 + 16 * 100 + 8: return FN<256, 16, 8, 0, 0, 0, 32, false>(__VA_ARGS__);                              \
+        case 256 * 1000 + 16 * 100 + 16: return FN<256, 16, 16, 0, 0, 0, 32, false>(__VA_ARGS__);                            \
+        case 256 * 1000 + 16 * 100 + 32: return FN<256, 16, 32, 0, 0, 0, 32, false>(__VA_ARGS__);                            \
+        default: return cudaErrorInvalidValue;                                                                         \
     }
 
 cudaError_t launch_step(int n, int blk, int r, int r2p, const DevModel &dm, int B, const int32_t *tok, const int8_t *sin,
                         int8_t *sout, float *lg, int32_t *routes, int32_t *acc, uint32_t rec_max, int warps,
                         int slots, int grid_cap, cudaStream_t st) {
-    const int L = dm.L, nv = dm.VP / 32;
+    const int L = dm.L, VP = dm.VP, lw = dm.lw;
     YGG_DISPATCH(launch_step_t, dm, B, tok, sin, sout, lg, routes, acc, rec_max, warps, slots, grid_cap, st)
 }
 
 cudaError_t launch_score(int n, int blk, int r, int r2p, const DevModel &dm, int B, int T, const int32_t *tok, int8_t *state,
                          double *bits, uint32_t rec_max, int warps, int slots, int grid_cap, cudaStream_t st) {
-    const int L = dm.L, nv = dm.VP / 32;
+    const int L = dm.L, VP = dm.VP, lw = dm.lw;
     YGG_DISPATCH(launch_score_t, dm, B, T, tok, state, bits, rec_max, warps, slots, grid_cap, st)
 }
 
