@@ -46,9 +46,9 @@ struct ygg_model {
     LaunchCfg half;           // two streams per warp (records over 16 lanes), when has_half
     bool has_half;
     // launch policy (ygg_step / ygg_score / grouped, by the batch B): B <= small_max stages records in shared memory
-    // (a warp per stream: the shortest per-token latency); B >= big_min runs two streams per warp (fewest
-    // instructions per token); in between a warp per stream reads records from global memory. YGG_LANES (16 / 32)
-    // and YGG_DIRECT (0 / 1) fix the choice instead.
+    // (a warp per stream: the shortest per-token latency at small batches); B >= big_min runs two streams per warp
+    // (fewest instructions per token); in between a warp per stream reads records from global memory. YGG_LANES
+    // (16 / 32) and YGG_DIRECT (0 / 1) fix the choice instead.
     int small_max, big_min, force_lanes, force_direct;
     uint8_t *d_blob;          // every device array
     size_t d_bytes;
@@ -468,7 +468,9 @@ int ygg_load(const void *file_bytes, size_t nbytes, int device, ygg_model **out)
     };
     pick_slots(m->warp);
     if (lay16) pick_slots(m->half);
-    m->small_max = 4;
+    // staging pays below ~2 K streams for n >= 128 (a 10 KB record lands with one bulk copy instead of ~40 loads per
+    // lane with few in flight); the smaller records of n = 64 read as fast directly at every batch
+    m->small_max = n >= 128 ? 2048 : 0;
     m->big_min = 32768;
     m->force_lanes = 0;
     m->force_direct = -1;
