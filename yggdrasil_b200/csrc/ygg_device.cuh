@@ -297,19 +297,27 @@ __device__ __forceinline__ void leaf_update(const DevModel &m, const DevLayer &y
         constexpr int kRowWords = BLK / 2;             // int16 pairs of one row
         const uint8_t *pa = rec + y.off_a + 16 * gl;
         const int rnd = 1 << (m.shift - 1), sh = m.shift;
+        // G = 32 (C <= 4 rows): every word of the lane first, so that the loads overlap; G = 16 (8 rows): row by row,
+        // which keeps the registers of one row live
+        constexpr int kPre = G == 32 ? C : 1;
+        uint32_t aw[kPre * kRowWords];
 #pragma unroll
-        for (int ii = 0; ii < C; ii++) {
-            uint32_t aw[kRowWords];
+        for (int ii0 = 0; ii0 < C; ii0 += kPre) {
 #pragma unroll
-            for (int j = 0; j < kRowWords / 4; j++) {
-                const uint4 v = ld16<GL>(pa + kChunk * (ii * (kRowWords / 4) + j));
+            for (int j = 0; j < kPre * kRowWords / 4; j++) {
+                const uint4 v = ld16<GL>(pa + kChunk * (ii0 * (kRowWords / 4) + j));
                 aw[4 * j] = v.x; aw[4 * j + 1] = v.y; aw[4 * j + 2] = v.z; aw[4 * j + 3] = v.w;
             }
-            int s = 0;
 #pragma unroll
-            for (int p = 0; p < kRowWords; p++)
-                s = (p & 1) ? __dp2a_hi((int)aw[p], (int)qblk[p >> 1], s) : __dp2a_lo((int)aw[p], (int)qblk[p >> 1], s);
-            acc[ii] = (s + rnd) >> sh;
+            for (int i1 = 0; i1 < kPre; i1++) {
+                int s = 0;
+#pragma unroll
+                for (int p = 0; p < kRowWords; p++) {
+                    const uint32_t a = aw[i1 * kRowWords + p];
+                    s = (p & 1) ? __dp2a_hi((int)a, (int)qblk[p >> 1], s) : __dp2a_lo((int)a, (int)qblk[p >> 1], s);
+                }
+                acc[ii0 + i1] = (s + rnd) >> sh;
+            }
         }
     }
     // -- input: table row (cpu/ygg.cpp:334-337) or factored (cpu/ygg.cpp:339-358)

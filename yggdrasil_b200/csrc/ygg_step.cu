@@ -33,6 +33,9 @@ namespace ygg {
 // blocks of 8 warps per SM the register budget is sized for: 4 (64 registers a thread) for n <= 128; n = 256 needs
 // more registers per lane (8 coordinates) and runs 2 blocks
 template <int N> constexpr int blocks_per_sm() { return N >= 256 ? 2 : 4; }
+// The score kernel of a warp per stream runs where streams are few (below 32 768 rows per launch) and each row's
+// latency sets the pace: 3 blocks, so that its row loop, f64 NLL and token pointers stay in registers
+template <int N, int G> constexpr int score_blocks_per_sm() { return N >= 256 ? 2 : G == 32 ? 3 : 4; }
 
 // ------------------------------------------------------------------------------------------------ shared memory
 
@@ -102,30 +105,35 @@ struct TokenCtx {
 
 // The new state of layer l (padding of a narrower model held at exactly 0) into the stream's state, and the debug
 // outputs.
-template <int N, int G>
+template <int N, int G, bool QS>
 __device__ __forceinline__ void finish_state(const DevModel &m, TokenCtx<N / G> &t, int l, int r, int (&acc)[N / G],
                                              LaneQ<N / G> &qn) {
     constexpr int C = N / G;
     const int gl = t.lane & (G - 1);
+    const int qstride = QS ? N : t.qstride;
+    const bool qlane = QS || t.qlane;
     if (m.ns < N && C * gl >= m.ns) {
 #pragma unroll
         for (int i = 0; i < (C >= 4 ? C / 4 : 1); i++) qn.w[i] = 0;
 #pragma unroll
         for (int ii = 0; ii < C; ii++) acc[ii] = 0;
     }
-    if (t.qlane) store_q<C>(t.q_out + (size_t)l * t.qstride + C * gl, qn);
+    if (qlane) store_q<C>(t.q_out + (size_t)l * qstride + C * gl, qn);
+    if (QS) return;   // the score kernel has no debug outputs
     if (t.dbg.routes != nullptr && gl == 0) t.dbg.routes[l] = r;
-    if (t.dbg.acc != nullptr && t.qlane) {
+    if (t.dbg.acc != nullptr && qlane) {
 #pragma unroll
-        for (int ii = 0; ii < C; ii++) t.dbg.acc[(size_t)l * t.qstride + C * gl + ii] = acc[ii];
+        for (int ii = 0; ii < C; ii++) t.dbg.acc[(size_t)l * qstride + C * gl + ii] = acc[ii];
     }
 }
 
 // Layer l of a token (cpu/ygg.cpp:443-458) for the stream of the caller's lane group (G lanes). DIRECT: the expert
-// record is read from global memory after an L2 prefetch; else it is staged in a shared-memory slot by a bulk copy. Returns false if a
-// bounded wait gave up (for every stream of the warp). Always inlined: the warp collectives in it (shuffles, ballots,
-// redux) rely on the caller's converged warp, and both stream groups of a warp run it together.
-template <int N, int BLK, int R, int R2T, int NVT, int G, bool DIRECT>
+// record is read from global memory after an L2 prefetch; else it is staged in a shared-memory slot by a bulk copy.
+// QS: the state is the stream's shared-memory copy in the device layout (stride n, every lane's coordinates; the score
+// kernel). Returns false if a bounded wait gave up (for every stream of the warp). Always inlined: the warp collectives
+// in it (shuffles, ballots, redux) rely on the caller's converged warp, and both stream groups of a warp run it
+// together.
+template <int N, int BLK, int R, int R2T, int NVT, int G, bool DIRECT, bool QS>
 __device__ __forceinline__ bool layer_step(TokenCtx<N / G> &t, const int l, float (&lg)[kMaxClasses<G>]) {
     constexpr int C = N / G;
     const DevModel &m = t.m;
@@ -137,7 +145,7 @@ __device__ __forceinline__ bool layer_step(TokenCtx<N / G> &t, const int l, floa
     LaneQ<C> &qbelow = t.qbelow;
     const DevLayer &y = m.layer[l];
     LaneQ<C> qold = {};
-    if (t.qlane) qold = load_q<C>(t.q_in + (size_t)l * t.qstride + C * gl);
+    if (QS || t.qlane) qold = load_q<C>(t.q_in + (size_t)l * (QS ? N : t.qstride) + C * gl);
     int r = x;
     float rho = 0.0f;
     const bool low = l > 0 && (R2T > 0 || m.R2 > 0);
@@ -167,7 +175,7 @@ __device__ __forceinline__ bool layer_step(TokenCtx<N / G> &t, const int l, floa
         store_q<C>(sc.qold + C * gl, qold);
         __syncwarp();
         leaf_update<N, BLK, R2T, G, true>(m, y, rec, trow, x, sc.qold, sc.zl, low, lane, acc, qn);
-        finish_state<N, G>(m, t, l, r, acc, qn);
+        finish_state<N, G, QS>(m, t, l, r, acc, qn);
         ro = readout_partials<N, R, G, true>(y, rec, qn, lane);
     } else {
         // -- lane 0 claims a unit of slots for the warp (slot unit * P + group for each stream group); each group's
@@ -175,13 +183,8 @@ __device__ __forceinline__ bool layer_step(TokenCtx<N / G> &t, const int l, floa
         // parity to wait for reach the group's lanes in one shuffle
         constexpr int P = 32 / G;
         const int leader = lane & (32 - G);
-        int unit = 0;
-        if (lane == 0) unit = unit_claim(pool, t.home, t.warp);
-        unit = __shfl_sync(kFull, unit, 0);
-        if (unit < 0) return false;
-        __syncwarp();   // the phases the unit's last holder flipped are visible to every group leader
-        int tag = 0;
-        if (gl == 0) {
+        // the group leader's copies into slot unit * P + group (one group, lane 0, when G = 32)
+        auto issue = [&](int unit) {
             const int slot = unit * P + lane / G;
             uint8_t *rec = pool.slots + (size_t)slot * pool.slot_bytes;
             const uint32_t bar = pool.bars + 8u * slot;
@@ -192,9 +195,25 @@ __device__ __forceinline__ bool layer_step(TokenCtx<N / G> &t, const int l, floa
                 const int16_t *src = y.table + ((size_t)r * y.table_rows + (y.table_rows > 1 ? x : 0)) * N;
                 bulk_g2s(smem_addr(rec + pool.slot_bytes - 2 * N), src, 2u * N, bar);
             }
-            tag = 2 * slot + pool.phase[slot];
+            return 2 * slot + pool.phase[slot];
+        };
+        int unit = 0, tag = -1;
+        if constexpr (G == 32) {   // one stream: lane 0 claims and copies in one region, one shuffle
+            if (lane == 0) {
+                unit = unit_claim(pool, t.home, t.warp);
+                if (unit >= 0) tag = issue(unit);
+            }
+            tag = __shfl_sync(kFull, tag, 0);
+            if (tag < 0) return false;
+            unit = tag >> 1;
+        } else {
+            if (lane == 0) unit = unit_claim(pool, t.home, t.warp);
+            unit = __shfl_sync(kFull, unit, 0);
+            if (unit < 0) return false;
+            __syncwarp();   // the phases the unit's last holder flipped are visible to every group leader
+            if (gl == 0) tag = issue(unit);
+            tag = __shfl_sync(kFull, tag, leader);
         }
-        tag = __shfl_sync(kFull, tag, leader);
         const int slot = tag >> 1;
         const uint32_t parity = (uint32_t)(tag & 1);
         const uint8_t *rec = pool.slots + (size_t)slot * pool.slot_bytes;
@@ -206,12 +225,12 @@ __device__ __forceinline__ bool layer_step(TokenCtx<N / G> &t, const int l, floa
         __syncwarp();
         if (!__all_sync(kFull, mbar_wait_bounded(bar, parity))) return false;
         leaf_update<N, BLK, R2T, G>(m, y, rec, has_table ? trow : nullptr, x, sc.qold, sc.zl, low, lane, acc, qn);
-        finish_state<N, G>(m, t, l, r, acc, qn);
+        finish_state<N, G, QS>(m, t, l, r, acc, qn);
         ro = readout_partials<N, R, G>(y, rec, qn, lane);
         // the slots are free once their bytes are used: flip their parities and hand the unit back
         __syncwarp();
         if (gl == 0) pool.phase[slot] = (int)(parity ^ 1u);
-        __syncwarp();
+        if (G < 32) __syncwarp();
         if (lane == 0) {
             __threadfence_block();
             atomicExch(pool.owner + unit, -1);
@@ -233,7 +252,7 @@ __device__ __forceinline__ bool layer_step(TokenCtx<N / G> &t, const int l, floa
 // its warp's collectives company). lg: the logits of the lane's classes (out). Returns false if a bounded wait gave
 // up. Compile-time shape where a fast instance fixes it (0: read from the model at run time): R2T the padded
 // layer-input rank, LT the number of layers, NVT the classes per lane (VP / G).
-template <int N, int BLK, int R, int R2T, int LT, int NVT, int G, bool DIRECT>
+template <int N, int BLK, int R, int R2T, int LT, int NVT, int G, bool DIRECT, bool QS>
 __device__ __forceinline__ bool token_step(const DevModel &m, const Pool &pool, const Scratch &sc, int home, int warp,
                                            int x, const int8_t *q_in, int8_t *q_out, int qstride, bool qlane,
                                            float (&lg)[kMaxClasses<G>], const StepOut &dbg, int lane) {
@@ -249,13 +268,13 @@ __device__ __forceinline__ bool token_step(const DevModel &m, const Pool &pool, 
         // converged at the collectives, and each shuffle / ballot / redux then pays a re-convergence loop
 #pragma unroll 1
         for (int l = 0; l < LT; l++)
-            if (!layer_step<N, BLK, R, R2T, NVT, G, DIRECT>(t, l, lg)) return false;
+            if (!layer_step<N, BLK, R, R2T, NVT, G, DIRECT, QS>(t, l, lg)) return false;
     } else {
 #pragma unroll 1
         for (int l = 0; l < m.L; l++)
-            if (!layer_step<N, BLK, R, R2T, NVT, G, DIRECT>(t, l, lg)) return false;
+            if (!layer_step<N, BLK, R, R2T, NVT, G, DIRECT, QS>(t, l, lg)) return false;
     }
-    if (dbg.logits != nullptr) {
+    if (!QS && dbg.logits != nullptr) {
 #pragma unroll
         for (int c = 0; c < kMaxClasses<G>; c++) {
             const int cls = G * c + gl;
@@ -328,7 +347,7 @@ __global__ void __launch_bounds__(256, blocks_per_sm<N>()) step_kernel(const __g
         float lg[kMaxClasses<G>];
         StepOut o{(live && logits) ? logits + (size_t)s * V : nullptr, (live && routes) ? routes + (size_t)s * L : nullptr,
                   (live && acc_out) ? acc_out + (size_t)se * L * ns : nullptr};
-        if (!token_step<N, BLK, R, R2T, LT, NVT, G, DIRECT>(m, pool, sc, home, warp, bad ? 0 : x, state_in + (size_t)se * L * ns,
+        if (!token_step<N, BLK, R, R2T, LT, NVT, G, DIRECT, false>(m, pool, sc, home, warp, bad ? 0 : x, state_in + (size_t)se * L * ns,
                                                     state_out + (size_t)se * L * ns, ns, live, lg, o, lane)) {
             if (lane == 0) atomicOr(m.status, kStatusTimeout);
             return;
@@ -348,7 +367,7 @@ __global__ void __launch_bounds__(256, blocks_per_sm<N>()) step_kernel(const __g
 // rows at a time; a row past B, or with a token out of range, runs unseen (token 0, nothing written; the bad row
 // scores NaN).
 template <int N, int BLK, int R, int R2T, int LT, int NVT, int G, bool DIRECT>
-__global__ void __launch_bounds__(256, blocks_per_sm<N>()) score_kernel(const __grid_constant__ DevModel m, int B, int T,
+__global__ void __launch_bounds__(256, score_blocks_per_sm<N, G>()) score_kernel(const __grid_constant__ DevModel m, int B, int T,
                                                     const int32_t *__restrict__ tokens, int8_t *state,
                                                     double *__restrict__ bits, uint32_t rec_max, int S) {
     constexpr int P = 32 / G;
@@ -365,17 +384,18 @@ __global__ void __launch_bounds__(256, blocks_per_sm<N>()) score_kernel(const __
     const StepOut none{nullptr, nullptr, nullptr};
     for (int base = (blockIdx.x * W + warp) * P; base < B; base += gridDim.x * W * P) {
         const int s = base + gh;
-        const bool real = s < B;
+        const bool real = G == 32 || s < B;        // a warp per stream: its one row is always real
         const int32_t *tok = tokens + (size_t)(real ? s : base) * T;
         bool bad = false;
         for (int t = gl; t < T; t += G) bad |= tok[t] < 0 || tok[t] >= V;
         const uint32_t bb = __ballot_sync(kFull, bad);
         bad = ((bb >> (lane & (32 - G))) & (G == 32 ? kFull : 0xFFFFu)) != 0;
-        const bool live = real && !bad;
         if (real && bad && gl == 0) {
             atomicOr(m.status, kStatusBadToken);
             bits[s] = __longlong_as_double(0x7ff8000000000000LL);
         }
+        if (G == 32 && bad) continue;              // the whole warp skips its row
+        const bool live = real && !bad;
         // the row's state into the device layout (n per layer; coordinates past the model's ns are 0)
         for (int i = gl; i < L * N; i += G) {
             const int li = i / N, c = i % N;
@@ -386,7 +406,7 @@ __global__ void __launch_bounds__(256, blocks_per_sm<N>()) score_kernel(const __
         for (int t = 0; t + 1 < T; t++) {
             float lg[kMaxClasses<G>];
             const int xt = live ? tok[t] : 0;
-            if (!token_step<N, BLK, R, R2T, LT, NVT, G, DIRECT>(m, pool, sc, home, warp, xt, qs, qs, N, true, lg, none, lane)) {
+            if (!token_step<N, BLK, R, R2T, LT, NVT, G, DIRECT, true>(m, pool, sc, home, warp, xt, qs, qs, N, true, lg, none, lane)) {
                 if (lane == 0) atomicOr(m.status, kStatusTimeout);
                 return;
             }
