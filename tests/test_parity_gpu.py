@@ -269,17 +269,25 @@ def test_extension_state_layout(rec, case_model, torch):
     np.testing.assert_allclose(bits, om.score(x[:, 9:], ost), rtol=BITS_RTOL)
 
 
-@pytest.mark.parametrize("direct", ["0", "1"])
-@pytest.mark.parametrize("lanes", ["16", "32"])
+# the launch configurations the library chooses between by batch, each forced for every batch
+LAUNCH_CONFIGS = {
+    "coop": {"YGG_COOP": "1000000"},                       # 4 warps per stream (n = 128; others keep the policy)
+    "warp-staged": {"YGG_LANES": "32", "YGG_DIRECT": "0"},  # a warp per stream, records staged in shared memory
+    "warp-direct": {"YGG_LANES": "32", "YGG_DIRECT": "1"},  # a warp per stream, records read from global memory
+    "half-staged": {"YGG_LANES": "16", "YGG_DIRECT": "0"},  # two streams per warp (shapes that allow it)
+    "half-direct": {"YGG_LANES": "16", "YGG_DIRECT": "1"},
+}
+
+
+@pytest.mark.parametrize("cfg", list(LAUNCH_CONFIGS))
 @pytest.mark.parametrize("rec", CASES[:6] + CASES[11:14] + EXT_CASES[:2],
                          ids=_ids(CASES[:6] + CASES[11:14]) + [f"ext-{i}" for i in _ids(EXT_CASES[:2])])
-def test_both_lane_layouts_bit_exact(lanes, direct, rec, case_model, torch, monkeypatch):
-    """Every launch configuration: YGG_LANES=16 runs two streams per warp (16 lanes per stream; shapes that allow it,
-    else a warp per stream), 32 a warp per stream; YGG_DIRECT=1 has the fast kernels read records from global memory,
-    0 stages them in shared memory. Each gives the oracle's routes, states and logits, with ragged batches (an odd
-    count leaves a warp's second stream unseen) and the score path."""
-    monkeypatch.setenv("YGG_LANES", lanes)
-    monkeypatch.setenv("YGG_DIRECT", direct)
+def test_every_launch_configuration_bit_exact(cfg, rec, case_model, torch, monkeypatch):
+    """Every launch configuration, forced for every batch (LAUNCH_CONFIGS): each gives the oracle's routes,
+    accumulators, states and logits, with ragged batches (an odd count leaves a warp's second stream unseen) and the
+    score path."""
+    for k, v in LAUNCH_CONFIGS[cfg].items():
+        monkeypatch.setenv(k, v)
     path = case_model(rec)
     model, om = load(path), O.OracleModel(path)
     x = case_tokens(rec)[:7, :12]
@@ -287,16 +295,15 @@ def test_both_lane_layouts_bit_exact(lanes, direct, rec, case_model, torch, monk
     np.testing.assert_allclose(model.score(x), om.score(x), rtol=BITS_RTOL)
 
 
-@pytest.mark.parametrize("direct", ["0", "1"])
-@pytest.mark.parametrize("lanes", ["16", "32"])
+@pytest.mark.parametrize("cfg", list(LAUNCH_CONFIGS))
 @pytest.mark.parametrize("rec", WORKLOADS + EXT_WORKLOADS, ids=[w["workload"] for w in WORKLOADS + EXT_WORKLOADS])
-def test_fast_instances_bit_exact(lanes, direct, rec, tmp_path, torch, monkeypatch):
-    """The benchmark shapes run the fast instances (shape fixed at compile time): every lane layout and record path
-    against the oracle and the reference's digest, with 7 streams (ragged) in the score path."""
+def test_fast_instances_bit_exact(cfg, rec, tmp_path, torch, monkeypatch):
+    """The benchmark shapes run the fast instances (shape fixed at compile time): every launch configuration against
+    the oracle and the reference's digest, with 7 streams (ragged) in the score path."""
     from yggdrasil_b200 import synth
     from yggdrasil_b200.ygg1 import write_model
-    monkeypatch.setenv("YGG_LANES", lanes)
-    monkeypatch.setenv("YGG_DIRECT", direct)
+    for k, v in LAUNCH_CONFIGS[cfg].items():
+        monkeypatch.setenv(k, v)
     w = synth.WORKLOADS[rec["workload"]]
     p = tmp_path / "w.bin"
     write_model(synth.workload_layers(w, seed=7), np.linspace(-1, 1, w.shape.vocab), p, extended=w.extended)

@@ -1,0 +1,512 @@
+// The latency kernels for small batches (n = 128): C = n / 32 = 4 warps serve one stream, one stream per block.
+//
+// With a warp per stream, a token's time at small batches is its chain of dependent steps: 5 router rounds of L2 loads
+// per layer, the DRAM fetch of the leaf's record, and the layer's arithmetic done by one warp. Here, per layer:
+//   - the router resolves 5 tree levels per round: the 31 rows of the 5-level subtree are read by the 4 warps (16 rows
+//     per 16-byte load of the block, 2 loads per lane), each warp ballots its rows' decisions, and the decisions meet in
+//     shared memory after one barrier; depth 13 takes 3 rounds (5 + 5 + 3) instead of 5;
+//   - when the last round starts, the records and table rows of its 2^lv <= 8 candidate leaves are prefetched into L2,
+//     so that the chosen record's bulk copy reads L2 rather than DRAM;
+//   - the layer's arithmetic is split by the warps: warp w computes row 4 l + w of lane l (the 32-lane record layout
+//     keeps each warp's part of a lane in whole 16-byte chunks), the layer-input codes split their chunks over the
+//     warps, and the readout rows are split too; the new state meets in shared memory.
+// Every integer and f32 operation, and its order, is that of the warp-per-stream kernels (ygg_step.cu), so routes,
+// states and logits are the same bits.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "ygg_device.cuh"
+
+namespace ygg {
+
+constexpr int kCoopLook = 5;                         // router levels per round
+constexpr int kCoopWarps = 4;                        // n / 32
+constexpr int kCoopThreads = 32 * kCoopWarps;
+constexpr int kCoopBlocksPerSm = 8;                  // 64 registers a thread
+constexpr int kCoopClasses = kMaxClasses<32> / kCoopWarps;   // class groups a warp holds
+
+// Shared memory of a block: one slot (record, then the table row at its end), its mbarrier, the stream's state vectors
+// and exchange buffers; `qs` holds the whole state [L][n] of a scored row (score kernel only).
+struct CoopSmem {
+    uint8_t *slot;
+    uint32_t slot_bytes;
+    uint32_t bar;
+    int8_t *qold, *qnew, *zl, *zq;
+    int *zpart;          // [4 warps][64] layer-input partial dots
+    uint32_t *dec;       // [2 parities][2 loads][4 warps] router ballots
+    float *red;          // [4 warps] the warps' logit maxima, [4] the target's logit (score)
+    double *exd;         // [8 class groups][32 lanes] exp of the logits (score)
+    int8_t *qs;
+};
+
+__host__ __device__ constexpr uint32_t coop_slot_bytes(uint32_t rec_max, int n) { return (rec_max + 2 * n + 127) / 128 * 128; }
+// slot | bar 16 | qold n | qnew n | zl 64 | zq 32 | zpart 4 x 64 x 4 | dec 16 x 4 | red 32 | exd 8 x 32 x 8 | qs
+__host__ __device__ constexpr uint32_t coop_smem_bytes(uint32_t rec_max, int n, int qs_bytes) {
+    return coop_slot_bytes(rec_max, n) + 16 + 2 * n + 64 + 32 + 4 * 64 * 4 + 16 * 4 + 32 + 8 * 32 * 8 + qs_bytes;
+}
+
+__device__ __forceinline__ CoopSmem coop_carve(uint8_t *smem, uint32_t rec_max, int n) {
+    CoopSmem c;
+    uint8_t *p = smem;
+    c.slot = p;
+    c.slot_bytes = coop_slot_bytes(rec_max, n);
+    p += c.slot_bytes;
+    c.bar = smem_addr(p); p += 16;
+    c.qold = (int8_t *)p; p += n;
+    c.qnew = (int8_t *)p; p += n;
+    c.zl = (int8_t *)p; p += 64;
+    c.zq = (int8_t *)p; p += 32;
+    c.zpart = (int *)p; p += 4 * 64 * 4;
+    c.dec = (uint32_t *)p; p += 16 * 4;
+    c.red = (float *)p; p += 32;
+    c.exd = (double *)p; p += 8 * 32 * 8;
+    c.qs = (int8_t *)p;
+    return c;
+}
+
+// Router descent of the block's stream (cpu/ygg.cpp:271-280), kCoopLook levels per round. Row k < 31 of a round's
+// subtree (heap order under the round's root ix: k = 0 is ix, k = 1-2 its children, ...) is read in load k / 16 by
+// warp (k % 16) / 4, row group k % 4 (the 8 lanes 8 g .. 8 g + 7, 16 bytes each). Each lane also reads its row's
+// threshold; one ballot per load and warp carries the decisions (bit 8 g), which the warps exchange in `dec`. qb: the
+// n new state bytes of the layer below. The records of the last round's candidate leaves go to L2 when there are at
+// most 8 of them. Returns the leaf node index in [E, 2E).
+__device__ __forceinline__ int route_coop(const DevLayer &y, int x, int E, int D, const int8_t *qb, float rho,
+                                          uint32_t *dec, int warp, int lane) {
+    constexpr int N = 128, LPR = 8;
+    const int g = lane / LPR;
+    const int8_t *wl = y.w + 16 * (lane % LPR);
+    const float *thr_x = y.thr + (size_t)x * E;
+    const uint4 qrow = *(const uint4 *)(qb + 16 * (lane % LPR));
+    int kk[2], mul[2], add[2];
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        const int k = 16 * i + 4 * warp + g;
+        const int lvl = 31 - __clz(k + 1);
+        kk[i] = k;
+        mul[i] = 1 << lvl;
+        add[i] = k + 1 - (1 << lvl);
+    }
+    int ix = 1, parity = 0;
+    for (int d = 0; d < D; d += kCoopLook) {
+        const int lv = min(kCoopLook, D - d);
+        const int nrows = (1 << lv) - 1;
+        if (d + lv == D && lv <= 3 && warp == 0 && lane < (1 << lv)) {   // the candidate leaves of the last round
+            const int leaf = ix * (1 << lv) + lane - E;
+            prefetch_l2(y.rec + (size_t)leaf * y.rec_bytes, y.rec_bytes);
+            if (y.table != nullptr)
+                prefetch_l2(y.table + ((size_t)leaf * y.table_rows + (y.table_rows > 1 ? x : 0)) * N, 2u * N);
+        }
+        uint4 v[2];
+        float t[2];
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+            const int row = ix * mul[i] + add[i];
+            v[i] = make_uint4(0, 0, 0, 0);
+            t[i] = 0.0f;
+            if (kk[i] < nrows) {
+                v[i] = __ldg((const uint4 *)(wl + (size_t)row * N));
+                t[i] = __ldg(thr_x + row);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+            int dot = dot16(v[i], qrow, 0);
+#pragma unroll
+            for (int off = 1; off < LPR; off <<= 1) dot += __shfl_xor_sync(kFull, dot, off);
+            const uint32_t bal = __ballot_sync(kFull, __fmul_rn(i2f(dot), rho) > t[i]);
+            if (lane == 0) dec[parity * 8 + i * 4 + warp] = bal;
+        }
+        __syncthreads();
+        // row k's decision: bit 8 g of dec[load][warp] -> bit k = 16 load + 4 warp + g of one mask
+        uint32_t mask = 0;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const uint32_t b = dec[parity * 8 + j];
+            mask |= ((b & 1u) | ((b >> 7) & 2u) | ((b >> 14) & 4u) | ((b >> 21) & 8u)) << (4 * j);
+        }
+        int k = 0;
+#pragma unroll
+        for (int j = 0; j < kCoopLook; j++) {
+            if (j < lv) {
+                const int b = (int)((mask >> k) & 1u);
+                ix = 2 * ix + b;
+                k = 2 * k + 1 + b;
+            }
+        }
+        parity ^= 1;
+    }
+    return ix;
+}
+
+struct CoopOut {
+    int8_t *q_out;       // where the new state goes: [L][ns] (global memory), or the score kernel's shared [L][n]
+    int32_t *routes;     // [L] or null
+    int32_t *acc;        // [L][ns] or null
+};
+
+// One token of the block's stream through every layer. q_in: the stream's state ([L][ns] global memory for the step
+// kernel; the score kernel's shared [L][n] copy, QS, where o.q_out is the same copy). lg: the logits of this lane's
+// classes 32 cg + lane for the class groups cg = warp + 4 c. Returns false if the bounded wait for a copy gave up.
+template <int BLK, int R, int R2T, int LT, int NVT, bool QS>
+__device__ __forceinline__ bool coop_token(const DevModel &m, const CoopSmem &sm, uint32_t &phase, int x,
+                                           const int8_t *q_in, const CoopOut &o, float (&lg)[kCoopClasses],
+                                           int warp, int lane) {
+    constexpr int N = 128, C = kCoopWarps;
+    const int tid = threadIdx.x;
+    const int i = C * lane + warp;               // the state coordinate this thread updates
+    const int L = LT ? LT : m.L, ns = QS ? N : m.ns;
+    const int nv = NVT ? NVT : m.VP / 32;
+#pragma unroll
+    for (int c = 0; c < kCoopClasses; c++) {
+        const int cg = warp + C * c;
+        lg[c] = cg < nv ? __ldg(m.head_b + 32 * cg + lane) : 0.0f;
+    }
+#pragma unroll 1
+    for (int l = 0; l < L; l++) {
+        const DevLayer &y = m.layer[l];
+        const bool low = l > 0 && (R2T > 0 || m.R2 > 0);
+        const bool has_table = y.table != nullptr;
+        // -- this layer's old state; the new state of the layer below is in qnew
+        sm.qold[tid] = (QS || tid < ns) ? q_in[(size_t)l * ns + tid] : (int8_t)0;
+        __syncthreads();
+        int r = x;
+        float rho = 0.0f;
+        if (l > 0) {
+            const LaneQ<C> qb = load_q<C>(sm.qnew + C * lane);
+            rho = rms_rho<N, 32>(qb, y.r2b, y.rms_eps, m.inv_n, lane);
+            r = route_coop(y, x, m.E, m.D, sm.qnew, rho, sm.dec, warp, lane) - m.E;
+        }
+        // -- the record and its table row into the slot (thread 0), while the layer-input codes are formed
+        const int16_t *trow = (const int16_t *)(sm.slot + sm.slot_bytes - 2 * N);
+        if (tid == 0) {
+            fence_proxy_async();
+            mbar_expect_tx(sm.bar, y.rec_bytes + (has_table ? 2u * N : 0u));
+            bulk_g2s(smem_addr(sm.slot), y.rec + (size_t)r * y.rec_bytes, y.rec_bytes, sm.bar);
+            if (has_table)
+                bulk_g2s(smem_addr(trow), y.table + ((size_t)r * y.table_rows + (y.table_rows > 1 ? x : 0)) * N, 2u * N,
+                         sm.bar);
+        }
+        if (low) {   // zl[k] = clamp(rint((f32(V'_k . qb) * mv[k]) * rho)) (cpu/ygg.cpp:285-296); warp w: chunks 2w, 2w+1
+            const int R2P = R2T ? R2T : m.R2P;
+            for (int k = lane; k < R2P; k += 32) {
+                const int8_t *vk = y.vl + (size_t)k * 16;
+                int a = 0;
+#pragma unroll
+                for (int j = 2 * warp; j < 2 * warp + 2; j++)
+                    a = dot16(__ldg((const uint4 *)(vk + (size_t)j * R2P * 16)), *(const uint4 *)(sm.qnew + 16 * j), a);
+                sm.zpart[warp * 64 + k] = a;
+            }
+            __syncthreads();
+            if (warp == 0)
+                for (int k = lane; k < R2P; k += 32) {
+                    const int a = sm.zpart[k] + sm.zpart[64 + k] + sm.zpart[128 + k] + sm.zpart[192 + k];
+                    const float zf = __fmul_rn(__fmul_rn(i2f(a), __ldg(y.mv + k)), rho);
+                    sm.zl[k] = (int8_t)(k < m.R2 ? clampi(cvt_rne(zf), -127, 127) : 0);
+                }
+        }
+        const bool ok = mbar_wait_bounded(sm.bar, phase);
+        phase ^= 1u;
+        if (!__syncthreads_and(ok)) return false;   // every wait ended (or one gave up); zl is ready
+        // -- row i = 4 lane + warp: transition, input, layer input, saturation (cpu/ygg.cpp:312-389); the lane's data
+        // for its row ii = warp sits in whole chunks of the 32-lane layout
+        const uint8_t *rec = sm.slot;
+        int acc;
+        {
+            constexpr int kRowWords = BLK / 2;
+            const uint8_t *pa = rec + y.off_a + 16 * lane;
+            uint32_t aw[kRowWords];
+#pragma unroll
+            for (int j = 0; j < kRowWords / 4; j++) {
+                const uint4 v = *(const uint4 *)(pa + 512 * (warp * (kRowWords / 4) + j));
+                aw[4 * j] = v.x; aw[4 * j + 1] = v.y; aw[4 * j + 2] = v.z; aw[4 * j + 3] = v.w;
+            }
+            const int blk0 = (i / BLK) * BLK;
+            uint32_t qblk[BLK / 4];
+            if constexpr (BLK == 8) {
+                const uint2 v = *(const uint2 *)(sm.qold + blk0);
+                qblk[0] = v.x; qblk[1] = v.y;
+            } else {
+                const uint4 v = *(const uint4 *)(sm.qold + blk0);
+                qblk[0] = v.x; qblk[1] = v.y; qblk[2] = v.z; qblk[3] = v.w;
+            }
+            int s = 0;
+#pragma unroll
+            for (int p = 0; p < kRowWords; p++)
+                s = (p & 1) ? __dp2a_hi((int)aw[p], (int)qblk[p >> 1], s) : __dp2a_lo((int)aw[p], (int)qblk[p >> 1], s);
+            acc = (s + (1 << (m.shift - 1))) >> m.shift;
+        }
+        if (has_table) {
+            acc += trow[i];
+        } else {   // factored (cpu/ygg.cpp:339-358): the lane's row ii = warp of F, chunks warp * KP/16 + j
+            const int KP = m.KP;
+            const uint8_t *pf = rec + y.off_f + 16 * lane;
+            const int8_t *v = y.vt + (size_t)x * KP;
+            int lt = 0;
+            for (int j = 0; j < KP / 16; j++)
+                lt = dot16(*(const uint4 *)(pf + 512 * (warp * (KP / 16) + j)), __ldg((const uint4 *)(v + 16 * j)), lt);
+            const float su = *(const float *)(rec + y.off_su);
+            const float mul = __fmul_rn(su, __ldg(y.mt + i));
+            acc += cvt_rne(__fmul_rn(i2f(lt), mul)) + ((const int16_t *)(rec + y.off_cb))[i];
+        }
+        if (low) {   // (cpu/ygg.cpp:360-377): the lane's row ii = warp of U', chunks warp * R2P/16 + j
+            const int R2P = R2T ? R2T : m.R2P;
+            const uint8_t *pu = rec + y.off_u + 16 * lane;
+            int la = 0;
+#pragma unroll
+            for (int j = 0; j < (R2T ? R2T / 16 : 4); j++)
+                if (R2T || j < R2P / 16)
+                    la = dot16(*(const uint4 *)(pu + 512 * (warp * (R2P / 16) + j)), *(const uint4 *)(sm.zl + 16 * j), la);
+            const float mu = y.mulv ? __ldg(y.mulv + i) : y.layer_input_scale;
+            acc += cvt_rne(__fmul_rn(i2f(la), mu));
+        }
+        if (i >= m.ns) acc = 0;   // padding of a narrower model: held at exactly 0
+        const int8_t qn = (int8_t)clampi(acc, -128, 127);
+        // the readout reads the new state of every lane: every thread has read qold and the slot's rows first
+        sm.qnew[i] = qn;
+        if (!QS && o.acc != nullptr && i < ns) o.acc[(size_t)l * ns + i] = acc;
+        __syncthreads();
+        if (tid < ns) o.q_out[(size_t)l * ns + tid] = sm.qnew[tid];
+        if (!QS && o.routes != nullptr && tid == 0) o.routes[l] = r;
+        // -- readout (cpu/ygg.cpp:395-420): warp w takes rows [w R/4, (w + 1) R/4); the lane's word of row rr is
+        // P[rr][4 lane .. 4 lane + 3], word rr of its readout data
+        {
+            constexpr int RW = R / C;
+            const uint32_t qw = *(const uint32_t *)(sm.qnew + C * lane);
+            const uint32_t *pp = (const uint32_t *)(rec + y.off_p + 16 * lane);
+            int myz = 0;
+#pragma unroll
+            for (int j = 0; j < RW; j++) {
+                const int rr = warp * RW + j;
+                const uint32_t word = pp[128 * (rr / 4) + rr % 4];
+                const int z = __reduce_add_sync(kFull, __dp4a((int)word, (int)qw, 0));
+                if (lane == j) myz = z;
+            }
+            if (lane < RW) {
+                const int rr = warp * RW + lane;
+                const float mz = y.off_mz != kNone ? *(const float *)(rec + y.off_mz + 4 * rr) : y.readout_scale;
+                sm.zq[rr] = (int8_t)clampi(cvt_rne(__fmul_rn(i2f(myz), mz)), -127, 127);
+            }
+        }
+        __syncthreads();   // zq is ready; every read of the slot is done before the next layer's copy
+        // -- the head (cpu/ygg.cpp:421-434) for this warp's class groups
+        {
+            uint32_t zw[R / 4];
+#pragma unroll
+            for (int j = 0; j < R / 4; j++) zw[j] = *(const uint32_t *)(sm.zq + 4 * j);
+#pragma unroll
+            for (int c = 0; c < kCoopClasses; c++) {
+                const int cg = warp + C * c;
+                if (NVT ? (cg < NVT) : (cg < nv)) {
+                    const int cls = 32 * cg + lane;
+                    const int8_t *qrow = y.unembed + (size_t)cls * R;
+                    int a = 0;
+                    if constexpr (R == 8) {
+                        const uint2 v = __ldg((const uint2 *)qrow);
+                        a = __dp4a((int)v.x, (int)zw[0], a);
+                        a = __dp4a((int)v.y, (int)zw[1], a);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < R / 16; j++)
+                            a = dot16(__ldg((const uint4 *)(qrow + 16 * j)),
+                                      make_uint4(zw[4 * j], zw[4 * j + 1], zw[4 * j + 2], zw[4 * j + 3]), a);
+                    }
+                    const float sc = y.sqv ? __ldg(y.sqv + cls) : y.unembed_scale;
+                    lg[c] = __fadd_rn(lg[c], __fmul_rn(i2f(a), sc));
+                }
+            }
+        }
+    }
+    return true;
+}
+
+// -log p(y) in f64 over the V classes of the block's stream (cpu/ygg.cpp:513-517), summed in the order of the
+// warp-per-stream kernels' nll_of: lane l adds the exps of its classes 32 cg + l in class-group order, then a butterfly
+// over the 32 lanes; the exps come from the warps holding each class group through shared memory. Every thread gets it.
+template <int NVT>
+__device__ __forceinline__ double coop_nll(const DevModel &m, const CoopSmem &sm, const float (&lg)[kCoopClasses],
+                                           int y, int warp, int lane) {
+    const int nv = NVT ? NVT : m.VP / 32, V = m.V;
+    float mx = -__int_as_float(0x7f800000);
+#pragma unroll
+    for (int c = 0; c < kCoopClasses; c++) {
+        const int cg = warp + kCoopWarps * c;
+        if (cg < nv && 32 * cg + lane < V) mx = fmaxf(mx, lg[c]);
+        if (32 * cg + lane == y) sm.red[kCoopWarps] = lg[c];
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, off));
+    if (lane == 0) sm.red[warp] = mx;
+    __syncthreads();
+    mx = fmaxf(fmaxf(sm.red[0], sm.red[1]), fmaxf(sm.red[2], sm.red[3]));
+    const float ly = sm.red[kCoopWarps];
+#pragma unroll
+    for (int c = 0; c < kCoopClasses; c++) {
+        const int cg = warp + kCoopWarps * c;
+        if (cg < nv) sm.exd[32 * cg + lane] = 32 * cg + lane < V ? exp((double)lg[c] - (double)mx) : 0.0;
+    }
+    __syncthreads();
+    double se = 0.0;
+    for (int cg = 0; cg < nv; cg++)
+        if (32 * cg + lane < V) se += sm.exd[32 * cg + lane];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) se += __shfl_xor_sync(kFull, se, off);
+    return log(se) + (double)mx - (double)ly;
+}
+
+// ------------------------------------------------------------------------------------------------ kernels
+
+__device__ __forceinline__ CoopSmem coop_init(uint8_t *smem, uint32_t rec_max) {
+    CoopSmem sm = coop_carve(smem, rec_max, 128);
+    if (threadIdx.x == 0) {
+        mbar_init(sm.bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    return sm;
+}
+
+// One decode step of B streams, one stream per block at a time (grid-stride).
+template <int BLK, int R, int R2T, int LT, int NVT>
+__global__ void __launch_bounds__(kCoopThreads, kCoopBlocksPerSm) coop_step_kernel(
+    const __grid_constant__ DevModel m, int B, const int32_t *__restrict__ tokens, const int8_t *state_in,
+    int8_t *state_out, float *__restrict__ logits, int32_t *__restrict__ routes, int32_t *__restrict__ acc_out,
+    uint32_t rec_max) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    const CoopSmem sm = coop_init(smem, rec_max);
+    uint32_t phase = 0;
+    const int L = m.L, V = m.V, ns = m.ns, nv = NVT ? NVT : m.VP / 32;
+    for (int s = blockIdx.x; s < B; s += gridDim.x) {
+        const int x = tokens[s];
+        if (x < 0 || x >= V) {   // cpu/ygg.cpp:493-495 rejects the whole input; here the stream is skipped
+            if (tid == 0) atomicOr(m.status, kStatusBadToken);
+            if (logits != nullptr)
+                for (int c = tid; c < V; c += kCoopThreads) logits[(size_t)s * V + c] = __int_as_float(0x7fc00000);
+            if (state_out != state_in)
+                for (int j = tid; j < L * ns; j += kCoopThreads)
+                    state_out[(size_t)s * L * ns + j] = state_in[(size_t)s * L * ns + j];
+            if (routes != nullptr && tid < L) routes[(size_t)s * L + tid] = -1;
+            continue;
+        }
+        float lg[kCoopClasses];
+        const CoopOut o{state_out + (size_t)s * L * ns, routes ? routes + (size_t)s * L : nullptr,
+                        acc_out ? acc_out + (size_t)s * L * ns : nullptr};
+        if (!coop_token<BLK, R, R2T, LT, NVT, false>(m, sm, phase, x, state_in + (size_t)s * L * ns, o, lg, warp,
+                                                     lane)) {
+            if (tid == 0) atomicOr(m.status, kStatusTimeout);
+            return;
+        }
+        if (logits != nullptr) {
+#pragma unroll
+            for (int c = 0; c < kCoopClasses; c++) {
+                const int cg = warp + kCoopWarps * c, cls = 32 * cg + lane;
+                if (cg < nv && cls < V) logits[(size_t)s * V + cls] = lg[c];
+            }
+        }
+    }
+}
+
+// Rows of T tokens, one row per block at a time: the row's state in shared memory, the f64 NLL of the next token
+// summed on chip (cpu/ygg.cpp:513-517).
+template <int BLK, int R, int R2T, int LT, int NVT>
+__global__ void __launch_bounds__(kCoopThreads, kCoopBlocksPerSm) coop_score_kernel(
+    const __grid_constant__ DevModel m, int B, int T, const int32_t *__restrict__ tokens, int8_t *state,
+    double *__restrict__ bits, uint32_t rec_max) {
+    constexpr int N = 128;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    const CoopSmem sm = coop_init(smem, rec_max);
+    uint32_t phase = 0;
+    const int L = m.L, V = m.V, ns = m.ns;
+    for (int s = blockIdx.x; s < B; s += gridDim.x) {
+        const int32_t *tok = tokens + (size_t)s * T;
+        bool bad = false;
+        for (int t = tid; t < T; t += kCoopThreads) bad |= tok[t] < 0 || tok[t] >= V;
+        if (__syncthreads_or(bad)) {
+            if (tid == 0) {
+                atomicOr(m.status, kStatusBadToken);
+                bits[s] = __longlong_as_double(0x7ff8000000000000LL);
+            }
+            continue;
+        }
+        // the row's state into the device layout (n per layer; coordinates past the model's ns are 0)
+        for (int j = tid; j < L * N; j += kCoopThreads) {
+            const int li = j / N, c = j % N;
+            sm.qs[j] = (state != nullptr && c < ns) ? state[((size_t)s * L + li) * ns + c] : (int8_t)0;
+        }
+        __syncthreads();
+        const CoopOut o{sm.qs, nullptr, nullptr};
+        double nll = 0.0;
+        for (int t = 0; t + 1 < T; t++) {
+            float lg[kCoopClasses];
+            if (!coop_token<BLK, R, R2T, LT, NVT, true>(m, sm, phase, tok[t], sm.qs, o, lg, warp, lane)) {
+                if (tid == 0) atomicOr(m.status, kStatusTimeout);
+                return;
+            }
+            nll += coop_nll<NVT>(m, sm, lg, tok[t + 1], warp, lane);
+        }
+        if (tid == 0) bits[s] = nll / 0.69314718055994530942;
+        if (state != nullptr)
+            for (int j = tid; j < L * N; j += kCoopThreads) {
+                const int li = j / N, c = j % N;
+                if (c < ns) state[((size_t)s * L + li) * ns + c] = sm.qs[j];
+            }
+        __syncthreads();
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ launchers
+
+template <int BLK, int R, int R2T, int LT, int NVT>
+static cudaError_t coop_step_t(const DevModel &dm, int B, const int32_t *tok, const int8_t *sin, int8_t *sout,
+                               float *lg, int32_t *routes, int32_t *acc, uint32_t rec_max, int sm_count,
+                               cudaStream_t st) {
+    const size_t smem = coop_smem_bytes(rec_max, 128, 0);
+    cudaError_t e = cudaFuncSetAttribute(coop_step_kernel<BLK, R, R2T, LT, NVT>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    const int grid = B < sm_count * kCoopBlocksPerSm ? B : sm_count * kCoopBlocksPerSm;
+    coop_step_kernel<BLK, R, R2T, LT, NVT><<<grid, kCoopThreads, smem, st>>>(dm, B, tok, sin, sout, lg, routes, acc,
+                                                                             rec_max);
+    return cudaGetLastError();
+}
+
+template <int BLK, int R, int R2T, int LT, int NVT>
+static cudaError_t coop_score_t(const DevModel &dm, int B, int T, const int32_t *tok, int8_t *state, double *bits,
+                                uint32_t rec_max, int sm_count, cudaStream_t st) {
+    const size_t smem = coop_smem_bytes(rec_max, 128, (dm.L * 128 + 127) / 128 * 128);
+    cudaError_t e = cudaFuncSetAttribute(coop_score_kernel<BLK, R, R2T, LT, NVT>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    const int grid = B < sm_count * kCoopBlocksPerSm ? B : sm_count * kCoopBlocksPerSm;
+    coop_score_kernel<BLK, R, R2T, LT, NVT><<<grid, kCoopThreads, smem, st>>>(dm, B, T, tok, state, bits, rec_max);
+    return cudaGetLastError();
+}
+
+// n = 128 only (the device layout's n; the d_state 96 extension included). Fast instances: c3 (V <= 32) and c4 / c5
+// (V = 256); generic instances read R2, L and the classes at run time.
+#define YGG_COOP_DISPATCH(FN, ...)                                                                            \
+    if (dm.n != 128) return cudaErrorInvalidValue;                                                            \
+    if (dm.b == 16 && dm.R == 16 && dm.R2P == 32 && dm.L == 4 && dm.VP == 32) return FN<16, 16, 32, 4, 1>(__VA_ARGS__); \
+    if (dm.b == 16 && dm.R == 16 && dm.R2P == 32 && dm.L == 4 && dm.VP == 256) return FN<16, 16, 32, 4, 8>(__VA_ARGS__); \
+    switch (dm.b * 100 + dm.R) {                                                                              \
+        case 8 * 100 + 8: return FN<8, 8, 0, 0, 0>(__VA_ARGS__);                                              \
+        case 8 * 100 + 16: return FN<8, 16, 0, 0, 0>(__VA_ARGS__);                                            \
+        case 8 * 100 + 32: return FN<8, 32, 0, 0, 0>(__VA_ARGS__);                                            \
+        case 16 * 100 + 8: return FN<16, 8, 0, 0, 0>(__VA_ARGS__);                                            \
+        case 16 * 100 + 16: return FN<16, 16, 0, 0, 0>(__VA_ARGS__);                                          \
+        case 16 * 100 + 32: return FN<16, 32, 0, 0, 0>(__VA_ARGS__);                                          \
+        default: return cudaErrorInvalidValue;                                                                \
+    }
+
+cudaError_t launch_coop_step(const DevModel &dm, int B, const int32_t *tok, const int8_t *sin, int8_t *sout,
+                             float *lg, int32_t *routes, int32_t *acc, uint32_t rec_max, int sm_count, cudaStream_t st) {
+    YGG_COOP_DISPATCH(coop_step_t, dm, B, tok, sin, sout, lg, routes, acc, rec_max, sm_count, st)
+}
+
+cudaError_t launch_coop_score(const DevModel &dm, int B, int T, const int32_t *tok, int8_t *state, double *bits,
+                              uint32_t rec_max, int sm_count, cudaStream_t st) {
+    YGG_COOP_DISPATCH(coop_score_t, dm, B, T, tok, state, bits, rec_max, sm_count, st)
+}
+
+}  // namespace ygg

@@ -29,6 +29,10 @@ size_t grouped_ws_bytes(const DevModel &m, int B);
 cudaError_t run_grouped(int n, int blk, int r, int r2p, const DevModel &m, int B, int T, const int32_t *tok,
                         int8_t *state, double *bits, void *workspace, int G, int sm_count, cudaStream_t st);
 cudaError_t noalloc_scratch(int device, void **ptr, size_t *bytes);
+cudaError_t launch_coop_step(const DevModel &dm, int B, const int32_t *tok, const int8_t *sin, int8_t *sout,
+                             float *lg, int32_t *routes, int32_t *acc, uint32_t rec_max, int sm_count, cudaStream_t st);
+cudaError_t launch_coop_score(const DevModel &dm, int B, int T, const int32_t *tok, int8_t *state, double *bits,
+                              uint32_t rec_max, int sm_count, cudaStream_t st);
 }  // namespace ygg
 
 using namespace ygg;
@@ -38,6 +42,7 @@ using namespace ygg;
 struct LaunchCfg {
     DevModel dm;
     int slots_step, slots_score;
+    bool coop;           // the step / score runs the latency kernels (ygg_coop.cu): 4 warps per stream
 };
 
 struct ygg_model {
@@ -45,11 +50,11 @@ struct ygg_model {
     LaunchCfg warp;           // a warp per stream (records over 32 lanes): every shape
     LaunchCfg half;           // two streams per warp (records over 16 lanes), when has_half
     bool has_half;
-    // launch policy (ygg_step / ygg_score / grouped, by the batch B): B <= small_max stages records in shared memory
-    // (a warp per stream: the shortest per-token latency at small batches); B >= big_min runs two streams per warp
-    // (fewest instructions per token); in between a warp per stream reads records from global memory. YGG_LANES
-    // (16 / 32) and YGG_DIRECT (0 / 1) fix the choice instead.
-    int small_max, big_min, force_lanes, force_direct;
+    // launch policy (ygg_step / ygg_score / grouped, by the batch B): B <= coop_max (n = 128) runs the latency
+    // kernels, 4 warps per stream; B <= small_max stages records in shared memory (a warp per stream); B >= big_min
+    // runs two streams per warp (fewest instructions per token); in between a warp per stream reads records from
+    // global memory. YGG_COOP (0 or the largest batch), YGG_LANES (16 / 32) and YGG_DIRECT (0 / 1) fix the choice.
+    int coop_max, small_max, big_min, force_lanes, force_direct;
     uint8_t *d_blob;          // every device array
     size_t d_bytes;
     int *d_status;
@@ -471,10 +476,14 @@ int ygg_load(const void *file_bytes, size_t nbytes, int device, ygg_model **out)
     // staging pays below ~2 K streams for n >= 128 (a 10 KB record lands with one bulk copy instead of ~40 loads per
     // lane with few in flight); the smaller records of n = 64 read as fast directly at every batch
     m->small_max = n >= 128 ? 2048 : 0;
+    // the latency kernels win up to ~256 streams (c3 step: 14.2 against 16.5 us at 16 streams, 16.6 against 18.3 at
+    // 256; c5 score rows: +18 % at 256); from ~512 the warp-per-stream kernels fill the GPU better
+    m->coop_max = n == 128 ? 256 : 0;
     m->big_min = 32768;
     m->force_lanes = 0;
     m->force_direct = -1;
     if (const char *e = getenv("YGG_SMALL_BATCH")) m->small_max = atoi(e);
+    if (const char *e = getenv("YGG_COOP")) m->coop_max = n == 128 ? atoi(e) : 0;
     if (const char *e = getenv("YGG_BIG_BATCH")) m->big_min = atoi(e);
     if (const char *e = getenv("YGG_LANES")) m->force_lanes = atoi(e) == 16 ? 16 : atoi(e) == 32 ? 32 : 0;
     if (const char *e = getenv("YGG_DIRECT")) m->force_direct = atoi(e) != 0;
@@ -498,6 +507,7 @@ static LaunchCfg choose(const ygg_model *m, int batch) {
     const bool half = m->has_half && (m->force_lanes == 16 || (m->force_lanes == 0 && batch >= m->big_min));
     LaunchCfg c = half ? m->half : m->warp;
     c.dm.direct = m->force_direct >= 0 ? m->force_direct : (batch > m->small_max ? 1 : 0);
+    c.coop = !half && m->force_lanes == 0 && m->force_direct < 0 && batch <= m->coop_max;
     return c;
 }
 
@@ -520,9 +530,11 @@ int ygg_step_debug(const ygg_model *m, int batch, const int32_t *d_tokens, const
     if (set_device(m, &prev)) return YGG_E_CUDA;
     const LaunchCfg c = choose(m, batch);
     const DevModel &dm = c.dm;
-    const cudaError_t e = launch_step(dm.n, dm.b, dm.R, dm.R2P, dm, batch, d_tokens, d_state_in, d_state_out, d_logits,
-                                      d_routes, d_acc, m->rec_max, m->warps, c.slots_step, m->grid_cap,
-                                      (cudaStream_t)stream);
+    const cudaError_t e =
+        c.coop ? launch_coop_step(dm, batch, d_tokens, d_state_in, d_state_out, d_logits, d_routes, d_acc, m->rec_max,
+                                  m->sm_count, (cudaStream_t)stream)
+               : launch_step(dm.n, dm.b, dm.R, dm.R2P, dm, batch, d_tokens, d_state_in, d_state_out, d_logits, d_routes,
+                             d_acc, m->rec_max, m->warps, c.slots_step, m->grid_cap, (cudaStream_t)stream);
     restore_device(m, prev);
     return e == cudaSuccess ? YGG_OK : YGG_E_CUDA;
 }
@@ -541,8 +553,11 @@ int ygg_score(const ygg_model *m, int batch, int steps, const int32_t *d_tokens,
     if (set_device(m, &prev)) return YGG_E_CUDA;
     const LaunchCfg c = choose(m, batch);
     const DevModel &dm = c.dm;
-    const cudaError_t e = launch_score(dm.n, dm.b, dm.R, dm.R2P, dm, batch, steps, d_tokens, d_state, d_bits,
-                                       m->rec_max, m->warps, c.slots_score, m->grid_cap, (cudaStream_t)stream);
+    const cudaError_t e =
+        c.coop ? launch_coop_score(dm, batch, steps, d_tokens, d_state, d_bits, m->rec_max, m->sm_count,
+                                   (cudaStream_t)stream)
+               : launch_score(dm.n, dm.b, dm.R, dm.R2P, dm, batch, steps, d_tokens, d_state, d_bits, m->rec_max,
+                              m->warps, c.slots_score, m->grid_cap, (cudaStream_t)stream);
     restore_device(m, prev);
     return e == cudaSuccess ? YGG_OK : YGG_E_CUDA;
 }
