@@ -69,7 +69,9 @@ __device__ __forceinline__ CoopSmem coop_carve(uint8_t *smem, uint32_t rec_max, 
 // warp (k % 16) / 4, row group k % 4 (the 8 lanes 8 g .. 8 g + 7, 16 bytes each). Each lane also reads its row's
 // threshold; one ballot per load and warp carries the decisions (bit 8 g), which the warps exchange in `dec`. qb: the
 // n new state bytes of the layer below. The records of the last round's candidate leaves go to L2 when there are at
-// most 8 of them. Returns the leaf node index in [E, 2E).
+// most 8 of them. DT > 0: the depth fixed at compile time (= D), the rounds unrolled. Returns the leaf node index in
+// [E, 2E).
+template <int DT = 0>
 __device__ __forceinline__ int route_coop(const DevLayer &y, int x, int E, int D, const int8_t *qb, float rho,
                                           uint32_t *dec, int warp, int lane) {
     constexpr int N = 128, LPR = 8;
@@ -87,8 +89,8 @@ __device__ __forceinline__ int route_coop(const DevLayer &y, int x, int E, int D
         add[i] = k + 1 - (1 << lvl);
     }
     int ix = 1, parity = 0;
-    for (int d = 0; d < D; d += kCoopLook) {
-        const int lv = min(kCoopLook, D - d);
+    // one round: the lv <= kCoopLook levels under ix, starting at depth d
+    auto round = [&](const int d, const int lv) {
         const int nrows = (1 << lv) - 1;
         if (d + lv == D && lv <= 3 && warp == 0 && lane < (1 << lv)) {   // the candidate leaves of the last round
             const int leaf = ix * (1 << lv) + lane - E;
@@ -134,6 +136,12 @@ __device__ __forceinline__ int route_coop(const DevLayer &y, int x, int E, int D
             }
         }
         parity ^= 1;
+    };
+    if constexpr (DT > 0) {
+#pragma unroll
+        for (int d = 0; d < DT; d += kCoopLook) round(d, DT - d < kCoopLook ? DT - d : kCoopLook);
+    } else {
+        for (int d = 0; d < D; d += kCoopLook) round(d, min(kCoopLook, D - d));
     }
     return ix;
 }
@@ -174,7 +182,8 @@ __device__ __forceinline__ bool coop_token(const DevModel &m, const CoopSmem &sm
         if (l > 0) {
             const LaneQ<C> qb = load_q<C>(sm.qnew + C * lane);
             rho = rms_rho<N, 32>(qb, y.r2b, y.rms_eps, m.inv_n, lane);
-            r = route_coop(y, x, m.E, m.D, sm.qnew, rho, sm.dec, warp, lane) - m.E;
+            r = (m.D == 13 ? route_coop<13>(y, x, m.E, m.D, sm.qnew, rho, sm.dec, warp, lane)
+                           : route_coop(y, x, m.E, m.D, sm.qnew, rho, sm.dec, warp, lane)) - m.E;
         }
         // -- the record and its table row into the slot (thread 0), while the layer-input codes are formed
         const int16_t *trow = (const int16_t *)(sm.slot + sm.slot_bytes - 2 * N);

@@ -166,8 +166,9 @@ __device__ __forceinline__ float rms_rho(const LaneQ<N / G> &qb, const float *r2
 // k + 1 - 2^lvl(k)) is read by the LPR = n/16 lanes of row group k % RPI (RPI = G / LPR) in load k / RPI, 16 bytes
 // each; every lane of the row group also reads the row's threshold (one broadcast transaction), so each lane can
 // decide its row and one ballot per load carries every decision of both stream groups. qrow: the lane's 16 bytes of
-// qb at 16 (gl % LPR). Returns the leaf node index in [E, 2E).
-template <int N, int G>
+// qb at 16 (gl % LPR). DT > 0: the depth fixed at compile time (= depth), which unrolls the rounds with their row
+// counts known. Returns the leaf node index in [E, 2E).
+template <int N, int G, int DT = 0>
 __device__ __forceinline__ int route_look(const int8_t *__restrict__ w, const float *__restrict__ thr_x, int depth,
                                           const uint4 &qrow, float rho, int lane) {
     constexpr int LPR = N / 16;                 // lanes per row
@@ -188,8 +189,8 @@ __device__ __forceinline__ int route_look(const int8_t *__restrict__ w, const fl
         add[i] = k + 1 - (1 << lvl);
     }
     int ix = 1;
-    for (int d = 0; d < depth; d += kLook) {
-        const int lv = min(kLook, depth - d);
+    // one round: the lv <= kLook levels under ix
+    auto round = [&](const int lv) {
         const int nrows = (1 << lv) - 1;
         uint4 v[NI];
         float t[NI];
@@ -246,6 +247,12 @@ __device__ __forceinline__ int route_look(const int8_t *__restrict__ w, const fl
                 k = 2 * k + 1 + b;
             }
         }
+    };
+    if constexpr (DT > 0) {
+#pragma unroll
+        for (int d = 0; d < DT; d += kLook) round(DT - d < kLook ? DT - d : kLook);
+    } else {
+        for (int d = 0; d < depth; d += kLook) round(min(kLook, depth - d));
     }
     return ix;
 }

@@ -147,7 +147,8 @@ __global__ void __launch_bounds__(256) g_route(const __grid_constant__ DevModel 
         store_q<C>(qb_s[sidx] + C * gl, qbelow);
         __syncwarp();
         const uint4 qrow = *(const uint4 *)(qb_s[sidx] + 16 * (gl % (N / 16)));
-        leaf = route_look<N, G>(y.w, y.thr + (size_t)x * m.E, m.D, qrow, rho, lane) - m.E;
+        leaf = (m.D == 13 ? route_look<N, G, 13>(y.w, y.thr + (size_t)x * m.E, m.D, qrow, rho, lane)
+                          : route_look<N, G>(y.w, y.thr + (size_t)x * m.E, m.D, qrow, rho, lane)) - m.E;
         if (R2T > 0 || m.R2 > 0)
             layer_input_codes<N, R2T, G>(m, y, qb_s[sidx], rho, real ? ws.zl + (size_t)s * kZlStride : zl_unseen[sidx],
                                          lane);

@@ -154,7 +154,9 @@ __device__ __forceinline__ bool layer_step(TokenCtx<N / G> &t, const int l, floa
         store_q<C>(sc.qb + C * gl, qbelow);
         __syncwarp();
         const uint4 qrow = *(const uint4 *)(sc.qb + 16 * (gl % (N / 16)));
-        r = route_look<N, G>(y.w, y.thr + (size_t)x * E, D, qrow, rho, lane) - E;
+        // the benchmark depth (13: c3, c4) runs an unrolled copy of the router
+        r = (D == 13 ? route_look<N, G, 13>(y.w, y.thr + (size_t)x * E, D, qrow, rho, lane)
+                     : route_look<N, G>(y.w, y.thr + (size_t)x * E, D, qrow, rho, lane)) - E;
     }
     const uint32_t rec_bytes = y.rec_bytes;
     const bool has_table = y.table != nullptr;
