@@ -1,25 +1,28 @@
-// The int8 decode step and the fused scoring loop of Yggdrasil on sm_100a.
+// The int8 decode step and the fused scoring loop of Yggdrasil on sm_100a, for batches past the latency kernels'
+// (ygg_coop.cu).
 //
-// G lanes serve one stream: a warp per stream (G = 32), or two streams per warp (G = 16, the layout the loader picks
-// for n = 64 / 128 with readout rank <= 16), which shares every per-stream step a lane does not own (the router's
-// decisions, rho, the slot and copy handshakes, the descriptor loads, the loop control) between two streams. Lane gl of
-// a group owns the C = n/G state coordinates [C gl, C gl + C) of every layer (layout in ygg_model.h). Per layer the
-// group
+// G lanes serve one stream: a warp per stream (G = 32), or two streams per warp (G = 16, records interleaved over 16
+// lanes; n <= 128 with readout rank <= 16), which shares every per-stream step a lane does not own (the router's
+// decisions, rho, the copy handshakes, the descriptor loads, the loop control) between two streams. Lane gl of a group
+// owns the C = n/G state coordinates [C gl, C gl + C) of every layer (layout in ygg_model.h). Per layer the group
 //   1. computes rho from the new state of the layer below (exact int32 sum of squares, then the reference's f32 ops),
-//   2. descends the router LOOK = 3 levels per round of loads: the 7 rows of the 3-level subtree under the current
+//   2. descends the router kLook = 3 levels per round of loads: the 7 rows of the 3-level subtree under the current
 //      node are fetched together (16-byte lanes, n/16 lanes per row), their dots reduced within the row's lanes and
-//      compared in f32 with the thresholds of (token, node), so D dependent levels cost ceil(D / 3) L2 round trips,
-//   3. takes a leaf slot from the block's pool (a slot is held only from the copy to the readout, a small part of a
-//      layer's time, so a block runs more streams than it has slots) and has its first lane issue one bulk copy
-//      (cp.async.bulk, the 1-D TMA, no multicast) of the chosen expert's record and one of its table row into it,
-//      completing on the slot's mbarrier,
+//      compared in f32 with the thresholds of (token, node), so D dependent levels cost ceil(D / 3) L2 round trips
+//      (depth 13, the benchmark shapes', runs an unrolled copy),
+//   3. gets the chosen expert's record and table row: staged (DIRECT = 0), a warp claims one slot per stream it serves
+//      from the block's pool (a slot is held only from the copy to the readout, so a block runs more streams than it
+//      has slots) and each group's first lane issues the bulk copies (cp.async.bulk, the 1-D TMA, no multicast) into
+//      its slot, completing on the slot's mbarrier; direct (DIRECT = 1), the first lane asks L2 for the record
+//      (cp.async.bulk.prefetch.L2) and the lanes later read their chunks from global memory,
 //   4. meanwhile computes the layer input zl (lane gl: the dots of down-projection rows gl, gl + G, ... with the state
 //      below),
-//   5. waits on the mbarrier (bounded: it gives up after ~1 s with an error status instead of hanging),
+//   5. (staged) waits on the mbarrier (bounded: it gives up after ~1 s with an error status instead of hanging),
 //   6. runs the block-diagonal int16 x int8 transition (__dp2a), the table / factored input and the layer input in
 //      int32, saturates to the new int8 state and stores it,
-//   7. reads out z = P_r q (per-row partials, the slot released, then redux.sync or a butterfly over the group),
-//      quantises zq, and adds f32(Q zq) * s to the logits each lane holds in registers for its classes G m + gl.
+//   7. reads out z = P_r q (per-row partials, then redux.sync or a butterfly over the group; staged slots are handed
+//      back first), quantises zq, and adds f32(Q zq) * s to the logits each lane holds in registers for its classes
+//      G m + gl.
 // Every f32 operation is the reference's, single-rounded and in the reference's order (__fmul_rn / __fadd_rn /
 // __fsqrt_rn / __fdiv_rn; no contraction), and f32 -> int32 rounds half to even with the x86 out-of-range value, so
 // routes, int32 accumulators, states and logits equal cpu/ygg.cpp bit for bit.
