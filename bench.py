@@ -508,34 +508,52 @@ def main():
     value = tokens / (ms / 1e3)
     per_launch_ms = ms / K
 
-    # ---- end to end through the public API: pinned host tokens in, logits out, every step
-    # (a serving loop: step t+1 runs while the logits of step t travel to the host on a copy stream; the token
-    # upload happens on the compute stream inside step())
+    # ---- end to end through the public API: pinned host tokens in, logits out, every step. A serving loop with two
+    # buffers each way: while step i runs (step_into, in place), the tokens of step i + 1 go up on one copy stream and
+    # the logits of step i - 1 come down on another; events keep each buffer's writer after its last reader.
     ke = min(K, 256)
     h_tok = torch.as_tensor(x[W:W + ke]).pin_memory()
     h_lg = [torch.empty(B, model.vocab, dtype=torch.float32).pin_memory() for _ in range(2)]
-    copy_stream = torch.cuda.Stream(dev)
+    d_tokb = [torch.empty(B, dtype=torch.int32, device=dev) for _ in range(2)]
+    d_lg = [torch.empty(B, model.vocab, dtype=torch.float32, device=dev) for _ in range(2)]
+    up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev = lambda: [torch.cuda.Event() for _ in range(2)]  # noqa: E731
+    uploaded, stepped, downloaded = ev(), ev(), ev()
 
-    def e2e_step(i, st):
-        lg, st = model.step(h_tok[i % ke], st)
-        copy_stream.wait_stream(stream)
-        with torch.cuda.stream(copy_stream):
-            h_lg[i % 2].copy_(lg, non_blocking=True)
-        lg.record_stream(copy_stream)
-        return st
+    def upload(i):
+        j = i % 2
+        up.wait_event(stepped[j])                  # the step that read this buffer (i - 2) is done
+        with torch.cuda.stream(up):
+            d_tokb[j].copy_(h_tok[i % ke], non_blocking=True)
+            uploaded[j].record(up)
+
+    def e2e_loop(n, st):
+        for e in stepped + downloaded:
+            e.record(stream)
+        upload(0)
+        for i in range(n):
+            j = i % 2
+            stream.wait_event(uploaded[j])
+            stream.wait_event(downloaded[j])       # the logits buffer's previous download is done
+            model.step_into(d_tokb[j], st, st, d_lg[j])
+            stepped[j].record(stream)
+            if i + 1 < n:
+                upload(i + 1)
+            down.wait_event(stepped[j])
+            with torch.cuda.stream(down):
+                h_lg[j].copy_(d_lg[j], non_blocking=True)
+                downloaded[j].record(down)
+        stream.wait_stream(down)
 
     st = state.clone()
-    for i in range(W):
-        st = e2e_step(i, st)
+    e2e_loop(W, st)
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
     a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a0.record(stream)
-    for i in range(ke):
-        st = e2e_step(i, st)
-    stream.wait_stream(copy_stream)
+    e2e_loop(ke, st)
     a1.record(stream)
     torch.cuda.synchronize(dev)
     ems = a0.elapsed_time(a1)
