@@ -6,10 +6,12 @@
 // One step is, for every layer l (the per-stream kernels serve a stream with G lanes, the model's lw: a warp, or half
 // a warp with two streams per warp):
 //   g_route    G lanes per stream: rho, router descent, layer-input codes; leaf id and its rank in the leaf's bucket
-//   g_scan     one block: prefix sum of the per-leaf counts, the list of heavy leaves (count >= G), counts zeroed
+//   g_scan     one block: prefix sum of the per-leaf counts, the list of heavy leaves (count >= G) with the first of
+//              their work items (one per tile of 128 of the leaf's streams), counts zeroed
 //   g_scatter  thread per stream: heavy streams into their leaf's bucket, the others into the light list
-//   g_heavy    block per heavy leaf (persistent): the leaf's weights once into shared memory as K-major operands,
-//              then per tile of 128 of its streams (M = streams, N = output features, K = input features):
+//   g_heavy    the work items (leaf, tile) split into contiguous runs over the SMs' blocks, so that a hot leaf's
+//              tiles run on many SMs; a block stages a leaf's weights into shared memory as K-major operands when its
+//              run reaches the leaf, then per tile of 128 of its streams (M = streams, N = output features, K = input):
 //                D_hi = Q_old . hi(A16)^T, D_lo = Q_old . lo(A16)^T          (A16 = 256 hi + lo, exact in int32)
 //                D_u  = ZL . U'^T,  D_f = V(x) . U^T (factored input)
 //              an epilogue per stream (thread = TMEM lane = stream) forms the int32 accumulators as the reference does,
@@ -34,7 +36,8 @@ struct GroupWs {
     int32_t *cnt;       // [Emax] per-leaf counts (kept zero between layers)
     int32_t *off;       // [Emax + 1] bucket offsets
     int32_t *heavy;     // [Emax] heavy leaves
-    int32_t *counts;    // [2] heavy leaves, light streams
+    int32_t *tile_off;  // [Emax + 1] first work item (128-stream tile) of each heavy leaf
+    int32_t *counts;    // [3] heavy leaves, light streams, work items
     int8_t *zl;         // [B][64] layer-input codes
     int8_t *zq;         // [B][L][32] readout codes of every layer
     double *nll;        // [B]
@@ -159,42 +162,52 @@ __global__ void __launch_bounds__(256) g_route(const __grid_constant__ DevModel 
     }
 }
 
-// One block of 1024 threads: exclusive scan of cnt[0, n_leaves) into off, heavy leaves (count >= G) in leaf order,
-// counts zeroed for the next layer.
+// One block of 1024 threads: exclusive scan of cnt[0, n_leaves) into off, heavy leaves (count >= G) in leaf order with
+// the first of their work items (tiles of 128 streams), counts zeroed for the next layer.
 __global__ void __launch_bounds__(1024) g_scan(GroupWs ws, int n_leaves, int G) {
     __shared__ int part[1024];
     __shared__ int hpart[1024];
+    __shared__ int tpart[1024];
     const int tid = threadIdx.x;
     const int per = (n_leaves + 1023) / 1024;
     const int a = min(tid * per, n_leaves), b = min(a + per, n_leaves);
-    int sum = 0, hs = 0;
+    int sum = 0, hs = 0, ts = 0;
     for (int i = a; i < b; i++) {
         const int c = ws.cnt[i];
         sum += c;
         hs += c >= G;
+        ts += c >= G ? (c + 127) / 128 : 0;
     }
     part[tid] = sum;
     hpart[tid] = hs;
+    tpart[tid] = ts;
     __syncthreads();
-    for (int d = 1; d < 1024; d <<= 1) {   // inclusive Hillis-Steele scan of both arrays
-        const int v = tid >= d ? part[tid - d] : 0, h = tid >= d ? hpart[tid - d] : 0;
+    for (int d = 1; d < 1024; d <<= 1) {   // inclusive Hillis-Steele scan of the three arrays
+        const int v = tid >= d ? part[tid - d] : 0, h = tid >= d ? hpart[tid - d] : 0, u = tid >= d ? tpart[tid - d] : 0;
         __syncthreads();
         part[tid] += v;
         hpart[tid] += h;
+        tpart[tid] += u;
         __syncthreads();
     }
-    int run = part[tid] - sum, hrun = hpart[tid] - hs;
+    int run = part[tid] - sum, hrun = hpart[tid] - hs, trun = tpart[tid] - ts;
     for (int i = a; i < b; i++) {
         const int c = ws.cnt[i];
         ws.off[i] = run;
         run += c;
-        if (c >= G) ws.heavy[hrun++] = i;
+        if (c >= G) {
+            ws.tile_off[hrun] = trun;
+            trun += (c + 127) / 128;
+            ws.heavy[hrun++] = i;
+        }
         ws.cnt[i] = 0;
     }
     if (tid == 1023) {
         ws.off[n_leaves] = part[1023];
         ws.counts[0] = hpart[1023];
         ws.counts[1] = 0;
+        ws.counts[2] = tpart[1023];
+        ws.tile_off[hpart[1023]] = tpart[1023];
     }
 }
 
@@ -238,9 +251,9 @@ __global__ void __launch_bounds__(256) g_light(const __grid_constant__ DevModel 
     }
 }
 
-// Block per heavy leaf (persistent over the heavy list), 128 threads; one tile of up to 128 of the leaf's streams at
-// a time. Thread i is TMEM lane i: stream i of the tile in the epilogue, output row i of the leaf when the weights
-// are staged.
+// Work items (heavy leaf, tile of up to 128 of its streams) in contiguous runs per block, 128 threads; a block stages a
+// leaf's weights when its run reaches the leaf (a hot leaf's tiles spread over many blocks). Thread i is TMEM lane i:
+// stream i of the tile in the epilogue, output row i of the leaf when the weights are staged.
 template <int N, int BLK, int R, int R2T, int G>
 __global__ void __launch_bounds__(kHeavyThreads, 1) g_heavy(const __grid_constant__ DevModel m, int l, int T, int t,
                                                              const int32_t *__restrict__ tokens, int8_t *state,
@@ -259,8 +272,10 @@ __global__ void __launch_bounds__(kHeavyThreads, 1) g_heavy(const __grid_constan
     uint32_t *tmem_slot = (uint32_t *)(smem + hp.o_bar + 16);
     float *mzs = (float *)(smem + hp.o_bar + 32);           // the leaf's per-row readout scales
     const uint32_t bar = smem_addr(smem + hp.o_bar);
-    const int nheavy = ws.counts[0];
-    if ((int)blockIdx.x >= nheavy) return;
+    const int nheavy = ws.counts[0], nitems = ws.counts[2];
+    const int per = (nitems + (int)gridDim.x - 1) / (int)gridDim.x;
+    const int it0 = (int)blockIdx.x * per, it1 = min(it0 + per, nitems);
+    if (it0 >= it1) return;
 
     // TMEM: D_hi [0, N), D_lo [N, 2N), D_u [2N, 3N), D_f [3N, 4N); the readout D_p reuses [0, R)
     constexpr uint32_t kCols = N <= 64 ? 256 : 512;
@@ -284,53 +299,64 @@ __global__ void __launch_bounds__(kHeavyThreads, 1) g_heavy(const __grid_constan
     const uint32_t id_ss_r = umma_idesc_i8(true, true, R);
     const int lane_base = (warp * 32) << 16;
 
-    for (int h = blockIdx.x; h < nheavy && ok; h += gridDim.x) {
+    int staged = -1;   // the heavy leaf whose weights are in shared memory
+    for (int it = it0; it < it1 && ok; it++) {
+        // the item's heavy leaf: the last h with tile_off[h] <= it
+        int lo = 0, hi = nheavy - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (ws.tile_off[mid] <= it) lo = mid; else hi = mid - 1;
+        }
+        const int h = lo, base = 128 * (it - ws.tile_off[h]);
         const int r = ws.heavy[h];
         const uint8_t *rec = y.rec + (size_t)r * y.rec_bytes;
         const int first = ws.off[r], count = ws.off[r + 1] - first;
-        // ---- the leaf's weights as K-major B operands (row = output feature)
-        if (tid < N) {
-            const int i = tid, ln = i / C, ii = i % C, c0 = (i / BLK) * BLK;
-            for (int c = 0; c < N / 16; c++) {
-                put_row16(bhi, i, N, c, make_uint4(0, 0, 0, 0));
-                put_row16(blo, i, N, c, make_uint4(0, 0, 0, 0));
-            }
-            const uint8_t *pa = rec + y.off_a;
-            for (int p = 0; p < BLK / 2; p++) {
-                const int lb = (ii * (BLK / 2) + p) * 4;                   // the lane's byte of the int16 pair
-                const uint32_t wv = *(const uint32_t *)(pa + ((lb / 16) * G + ln) * 16 + lb % 16);
-                const int a0 = (int)(int16_t)(wv & 0xFFFFu), a1 = (int)(int16_t)(wv >> 16);
-                bhi[core_off(i, c0 + 2 * p, N)] = (uint8_t)(a0 >> 8);
-                blo[core_off(i, c0 + 2 * p, N)] = (uint8_t)(a0 & 0xFF);
-                bhi[core_off(i, c0 + 2 * p + 1, N)] = (uint8_t)(a1 >> 8);
-                blo[core_off(i, c0 + 2 * p + 1, N)] = (uint8_t)(a1 & 0xFF);
-            }
-            if (low) {
-                const uint8_t *pu = rec + y.off_u;
-                for (int k = 0; k < hp.ku; k++) {
-                    const int lb = ii * R2P + k;
-                    bu[core_off(i, k, hp.ku)] = k < R2P ? pu[((lb / 16) * G + ln) * 16 + lb % 16] : 0;
+        // ---- the leaf's weights as K-major B operands (row = output feature), once per run of its tiles
+        if (h != staged) {
+            staged = h;
+            if (tid < N) {
+                const int i = tid, ln = i / C, ii = i % C, c0 = (i / BLK) * BLK;
+                for (int c = 0; c < N / 16; c++) {
+                    put_row16(bhi, i, N, c, make_uint4(0, 0, 0, 0));
+                    put_row16(blo, i, N, c, make_uint4(0, 0, 0, 0));
+                }
+                const uint8_t *pa = rec + y.off_a;
+                for (int p = 0; p < BLK / 2; p++) {
+                    const int lb = (ii * (BLK / 2) + p) * 4;                   // the lane's byte of the int16 pair
+                    const uint32_t wv = *(const uint32_t *)(pa + ((lb / 16) * G + ln) * 16 + lb % 16);
+                    const int a0 = (int)(int16_t)(wv & 0xFFFFu), a1 = (int)(int16_t)(wv >> 16);
+                    bhi[core_off(i, c0 + 2 * p, N)] = (uint8_t)(a0 >> 8);
+                    blo[core_off(i, c0 + 2 * p, N)] = (uint8_t)(a0 & 0xFF);
+                    bhi[core_off(i, c0 + 2 * p + 1, N)] = (uint8_t)(a1 >> 8);
+                    blo[core_off(i, c0 + 2 * p + 1, N)] = (uint8_t)(a1 & 0xFF);
+                }
+                if (low) {
+                    const uint8_t *pu = rec + y.off_u;
+                    for (int k = 0; k < hp.ku; k++) {
+                        const int lb = ii * R2P + k;
+                        bu[core_off(i, k, hp.ku)] = k < R2P ? pu[((lb / 16) * G + ln) * 16 + lb % 16] : 0;
+                    }
+                }
+                if (fact) {
+                    const uint8_t *pf = rec + y.off_f;
+                    for (int k = 0; k < hp.kf; k++) {
+                        const int lb = ii * KP + k;
+                        bf[core_off(i, k, hp.kf)] = k < KP ? pf[((lb / 16) * G + ln) * 16 + lb % 16] : 0;
+                    }
                 }
             }
-            if (fact) {
-                const uint8_t *pf = rec + y.off_f;
-                for (int k = 0; k < hp.kf; k++) {
-                    const int lb = ii * KP + k;
-                    bf[core_off(i, k, hp.kf)] = k < KP ? pf[((lb / 16) * G + ln) * 16 + lb % 16] : 0;
+            if (tid < R) {
+                const uint8_t *pp = rec + y.off_p;
+                for (int i = 0; i < N; i++) {
+                    const int lb = tid * C + i % C, ln = i / C;
+                    bp[core_off(tid, i, N)] = pp[((lb / 16) * G + ln) * 16 + lb % 16];
                 }
             }
+            if (tid < R) mzs[tid] = y.off_mz != kNone ? *(const float *)(rec + y.off_mz + 4 * tid) : y.readout_scale;
         }
-        if (tid < R) {
-            const uint8_t *pp = rec + y.off_p;
-            for (int i = 0; i < N; i++) {
-                const int lb = tid * C + i % C, ln = i / C;
-                bp[core_off(tid, i, N)] = pp[((lb / 16) * G + ln) * 16 + lb % 16];
-            }
-        }
-        if (tid < R) mzs[tid] = y.off_mz != kNone ? *(const float *)(rec + y.off_mz + 4 * tid) : y.readout_scale;
         const float su = fact ? *(const float *)(rec + y.off_su) : 0.0f;
-        // ---- tiles of up to 128 streams
-        for (int base = 0; base < count && ok; base += 128) {
+        // ---- the item's tile of up to 128 streams
+        {
             const int ntile = min(128, count - base);
             const int s = tid < ntile ? ws.member[first + base + tid] : -1;
             const int x = s >= 0 ? tok_at(tokens, ws, s, T, t) : 0;
@@ -438,7 +464,6 @@ __global__ void __launch_bounds__(kHeavyThreads, 1) g_heavy(const __grid_constan
             __syncthreads();
             tc_fence_after();
         }
-        __syncthreads();
     }
     if (!ok && tid == 0) atomicOr(m.status, kStatusTimeout);
     tc_fence_before();
@@ -503,7 +528,7 @@ __global__ void g_state_unpad(int B, int L, int ns, int N, const int8_t *__restr
 size_t grouped_ws_bytes(const DevModel &m, int B) {
     const size_t Emax = (size_t)(m.E > m.V ? m.E : m.V);
     auto r = [](size_t x) { return (x + 255) / 256 * 256; };
-    return r(4 * (size_t)B) * 5 + r(4 * Emax) * 2 + r(4 * (Emax + 1)) + 256 + r((size_t)B * kZlStride) +
+    return r(4 * (size_t)B) * 5 + r(4 * Emax) * 2 + r(4 * (Emax + 1)) * 2 + 256 + r((size_t)B * kZlStride) +
            r((size_t)B * m.L * kZqStride) + r(8 * (size_t)B) + r((size_t)B * m.L * m.n);
 }
 
@@ -520,6 +545,7 @@ static GroupWs grouped_layout(const DevModel &m, int B, uint8_t *base) {
     ws.bad = (int32_t *)take(4 * (size_t)B);
     ws.cnt = (int32_t *)take(4 * Emax);
     ws.heavy = (int32_t *)take(4 * Emax);
+    ws.tile_off = (int32_t *)take(4 * (Emax + 1));
     ws.off = (int32_t *)take(4 * (Emax + 1));
     ws.counts = (int32_t *)take(256);
     ws.zl = (int8_t *)take((size_t)B * kZlStride);
