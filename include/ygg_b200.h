@@ -121,6 +121,12 @@ YGG_API int ygg_score_grouped_noalloc(const ygg_model *m, int batch, int steps, 
  * wait that gave up). Synchronises `stream`. */
 YGG_API int ygg_status(const ygg_model *m, void *stream, int clear, int *status_out);
 
+/* Self test of the bounded device waits, for failure-detection tests: one warp on `device` waits on an mbarrier that
+ * nothing completes, gives up after `cycles` clock cycles exactly as a wait of the step kernels does after ~1 s, and
+ * *status_out receives YGG_E_TIMEOUT (YGG_OK had the wait ended). Synchronises `stream`; the context stays usable. No
+ * counterpart in the reference (its CPU kernel has no device waits). */
+YGG_API int ygg_selftest_wait(int device, long long cycles, void *stream, int *status_out);
+
 /* Free the device memory of a model; NULL is a no-op. */
 YGG_API void ygg_free(ygg_model *m);
 

@@ -88,3 +88,10 @@ def test_null_arguments():
     assert lib.ygg_step(None, 1, None, None, None, None, None) == _native.YGG_E_ARG
     assert lib.ygg_score(None, 1, 1, None, None, None, None) == _native.YGG_E_ARG
     lib.ygg_free(None)
+
+
+def test_selftest_wait_arguments():
+    lib = _native.lib()
+    status = ctypes.c_int(7)
+    assert lib.ygg_selftest_wait(0, -1, None, ctypes.byref(status)) == _native.YGG_E_ARG
+    assert lib.ygg_selftest_wait(0, 1000, None, None) == _native.YGG_E_ARG

@@ -11,7 +11,8 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "libygg_b200.so"
 
 EXPORTS = ("ygg_load", "ygg_info", "ygg_step", "ygg_step_debug", "ygg_score", "ygg_score_grouped_workspace",
-           "ygg_score_grouped", "ygg_score_grouped_noalloc", "ygg_status", "ygg_free", "ygg_strerror", "ygg_version")
+           "ygg_score_grouped", "ygg_score_grouped_noalloc", "ygg_status", "ygg_selftest_wait", "ygg_free",
+           "ygg_strerror", "ygg_version")
 
 YGG_OK = 0
 YGG_E_ARG, YGG_E_FORMAT, YGG_E_UNSUPPORTED, YGG_E_MISSING, YGG_E_CUDA, YGG_E_OOM, YGG_E_TOKEN, YGG_E_TIMEOUT, \
@@ -53,6 +54,7 @@ def lib() -> ctypes.CDLL:
         l.ygg_score_grouped.argtypes = [vp, i32, i32, vp, vp, vp, i32, vp, sz, vp]
         l.ygg_score_grouped_noalloc.argtypes = [vp, i32, i32, vp, vp, vp, i32, vp]
         l.ygg_status.argtypes = [vp, vp, i32, ctypes.POINTER(ctypes.c_int)]
+        l.ygg_selftest_wait.argtypes = [i32, ctypes.c_longlong, vp, ctypes.POINTER(ctypes.c_int)]
         l.ygg_free.argtypes = [vp]
         l.ygg_free.restype = None
         l.ygg_strerror.argtypes = [i32]
@@ -60,7 +62,7 @@ def lib() -> ctypes.CDLL:
         l.ygg_version.argtypes = []
         l.ygg_version.restype = ctypes.c_char_p
         for f in (l.ygg_load, l.ygg_info, l.ygg_step, l.ygg_step_debug, l.ygg_score, l.ygg_score_grouped,
-                  l.ygg_score_grouped_noalloc, l.ygg_status):
+                  l.ygg_score_grouped_noalloc, l.ygg_status, l.ygg_selftest_wait):
             f.restype = ctypes.c_int
         _lib = l
     return _lib

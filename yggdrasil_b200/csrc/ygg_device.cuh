@@ -72,12 +72,13 @@ template <bool GL> __device__ __forceinline__ uint4 ld16(const void *p) {
     }
 }
 
-// Bounded wait for the phase `parity` of an mbarrier: false after ~1 s (the caller reports a timeout).
-__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+// Bounded wait for the phase `parity` of an mbarrier: false after `limit` cycles (~1 s by default; the caller reports
+// a timeout).
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, long long limit = kWaitCycles) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
     while (!mbar_try_wait(bar, parity))
-        if (clock64() - t0 > kWaitCycles) return false;
+        if (clock64() - t0 > limit) return false;
     return true;
 }
 

@@ -29,6 +29,7 @@ size_t grouped_ws_bytes(const DevModel &m, int B);
 cudaError_t run_grouped(int n, int blk, int r, int r2p, const DevModel &m, int B, int T, const int32_t *tok,
                         int8_t *state, double *bits, void *workspace, int G, int sm_count, cudaStream_t st);
 cudaError_t noalloc_scratch(int device, void **ptr, size_t *bytes);
+cudaError_t launch_wait_selftest(long long limit, int *d_status, cudaStream_t st);
 cudaError_t launch_coop_step(const DevModel &dm, int B, const int32_t *tok, const int8_t *sin, int8_t *sout,
                              float *lg, int32_t *routes, int32_t *acc, uint32_t rec_max, int sm_count, cudaStream_t st);
 cudaError_t launch_coop_score(const DevModel &dm, int B, int T, const int32_t *tok, int8_t *state, double *bits,
@@ -608,6 +609,25 @@ int ygg_score_grouped_noalloc(const ygg_model *m, int batch, int steps, const in
                                       d_state, d_bits, scratch, min_group, m->sm_count, (cudaStream_t)stream);
     restore_device(m, prev);
     return e == cudaSuccess ? YGG_OK : YGG_E_CUDA;
+}
+
+int ygg_selftest_wait(int device, long long cycles, void *stream, int *status_out) {
+    if (!status_out || cycles < 0) return YGG_E_ARG;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) return YGG_E_DEVICE;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    if (cudaSetDevice(device) != cudaSuccess) return YGG_E_DEVICE;
+    int *d = nullptr, v = -1;
+    cudaError_t e = cudaMalloc((void **)&d, sizeof(int));
+    if (e == cudaSuccess) e = launch_wait_selftest(cycles, d, (cudaStream_t)stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&v, d, sizeof v, cudaMemcpyDeviceToHost, (cudaStream_t)stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
+    cudaFree(d);
+    if (prev >= 0) cudaSetDevice(prev);
+    if (e != cudaSuccess) return YGG_E_CUDA;
+    *status_out = (v & kStatusTimeout) ? YGG_E_TIMEOUT : YGG_OK;
+    return YGG_OK;
 }
 
 int ygg_status(const ygg_model *m, void *stream, int clear, int *status_out) {

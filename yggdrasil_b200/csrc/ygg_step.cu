@@ -433,6 +433,28 @@ __global__ void __launch_bounds__(256, score_blocks_per_sm<N, G>()) score_kernel
     }
 }
 
+// ------------------------------------------------------------------------------------------------ self test
+
+// The bounded wait of the kernels, made to run out: one warp waits on an mbarrier that nothing arrives at (its
+// expected arrival never comes), gives up after `limit` cycles as every wait of the step does, and writes the timeout
+// status. Nothing faults or spins forever, and the context stays usable.
+__global__ void wait_selftest_kernel(long long limit, int *status) {
+    __shared__ __align__(8) uint64_t bar_word;
+    const uint32_t bar = smem_addr(&bar_word);
+    if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+    const bool ok = __all_sync(kFull, mbar_wait_bounded(bar, 0, limit));
+    if (threadIdx.x == 0) *status = ok ? (int)kStatusOk : (int)kStatusTimeout;
+}
+
+cudaError_t launch_wait_selftest(long long limit, int *d_status, cudaStream_t st) {
+    wait_selftest_kernel<<<1, 32, 0, st>>>(limit, d_status);
+    return cudaGetLastError();
+}
+
 // ------------------------------------------------------------------------------------------------ launchers
 
 // The dynamic shared-memory limit of a kernel, raised once per device to the largest size asked for so far (the
