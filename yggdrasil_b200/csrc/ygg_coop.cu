@@ -466,13 +466,16 @@ __global__ void __launch_bounds__(kCoopThreads, kCoopBlocksPerSm) coop_score_ker
 
 // ------------------------------------------------------------------------------------------------ launchers
 
+template <int BLK, int R, int R2T, int LT, int NVT> static SmemLimits &coop_step_limit() { static SmemLimits l{}; return l; }
+template <int BLK, int R, int R2T, int LT, int NVT> static SmemLimits &coop_score_limit() { static SmemLimits l{}; return l; }
+
 template <int BLK, int R, int R2T, int LT, int NVT>
 static cudaError_t coop_step_t(const DevModel &dm, int B, const int32_t *tok, const int8_t *sin, int8_t *sout,
                                float *lg, int32_t *routes, int32_t *acc, uint32_t rec_max, int sm_count,
                                cudaStream_t st) {
     const size_t smem = coop_smem_bytes(rec_max, 128, 0);
-    cudaError_t e = cudaFuncSetAttribute(coop_step_kernel<BLK, R, R2T, LT, NVT>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = raise_smem_limit((const void *)coop_step_kernel<BLK, R, R2T, LT, NVT>, smem,
+                                     coop_step_limit<BLK, R, R2T, LT, NVT>());
     if (e != cudaSuccess) return e;
     const int grid = B < sm_count * kCoopBlocksPerSm ? B : sm_count * kCoopBlocksPerSm;
     coop_step_kernel<BLK, R, R2T, LT, NVT><<<grid, kCoopThreads, smem, st>>>(dm, B, tok, sin, sout, lg, routes, acc,
@@ -484,8 +487,8 @@ template <int BLK, int R, int R2T, int LT, int NVT>
 static cudaError_t coop_score_t(const DevModel &dm, int B, int T, const int32_t *tok, int8_t *state, double *bits,
                                 uint32_t rec_max, int sm_count, cudaStream_t st) {
     const size_t smem = coop_smem_bytes(rec_max, 128, (dm.L * 128 + 127) / 128 * 128);
-    cudaError_t e = cudaFuncSetAttribute(coop_score_kernel<BLK, R, R2T, LT, NVT>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = raise_smem_limit((const void *)coop_score_kernel<BLK, R, R2T, LT, NVT>, smem,
+                                     coop_score_limit<BLK, R, R2T, LT, NVT>());
     if (e != cudaSuccess) return e;
     const int grid = B < sm_count * kCoopBlocksPerSm ? B : sm_count * kCoopBlocksPerSm;
     coop_score_kernel<BLK, R, R2T, LT, NVT><<<grid, kCoopThreads, smem, st>>>(dm, B, T, tok, state, bits, rec_max);

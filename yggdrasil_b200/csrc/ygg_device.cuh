@@ -21,6 +21,22 @@ constexpr int kLook = 3;                // router levels per round of loads
 constexpr int kLookRows = (1 << kLook) - 1;
 
 
+// ------------------------------------------------------------------------------------------------ host side
+
+// The dynamic shared-memory limit of a kernel, raised once per device to the largest size asked for so far (the
+// attribute is per device; raising it on every launch would cost a driver call per step). One SmemLimits per kernel.
+constexpr int kMaxDevices = 64;
+struct SmemLimits { size_t set[kMaxDevices]; };
+static inline cudaError_t raise_smem_limit(const void *fn, size_t smem, SmemLimits &lim) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < kMaxDevices && lim.set[dev] >= smem) return cudaSuccess;
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess && dev >= 0 && dev < kMaxDevices) lim.set[dev] = smem;
+    return e;
+}
+
 // ------------------------------------------------------------------------------------------------ PTX helpers
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }

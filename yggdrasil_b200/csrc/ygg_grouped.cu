@@ -578,7 +578,8 @@ static cudaError_t run_grouped_t(const DevModel &m, int B, int T, const int32_t 
     const int Geff = tc ? (G < 1 ? 1 : G) : (1 << 30);
     const HeavyPlan hp(N, m.R2P, m.factored ? m.KP : 0, R);
     if constexpr (tc) {
-        e = cudaFuncSetAttribute(g_heavy<N, BLK, R, R2T, LG>, cudaFuncAttributeMaxDynamicSharedMemorySize, hp.bytes);
+        static SmemLimits lim{};
+        e = raise_smem_limit((const void *)g_heavy<N, BLK, R, R2T, LG>, (size_t)hp.bytes, lim);
         if (e != cudaSuccess) return e;
     }
     constexpr int P = 32 / LG;   // streams per warp

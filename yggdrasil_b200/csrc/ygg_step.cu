@@ -457,21 +457,8 @@ cudaError_t launch_wait_selftest(long long limit, int *d_status, cudaStream_t st
 
 // ------------------------------------------------------------------------------------------------ launchers
 
-// The dynamic shared-memory limit of a kernel, raised once per device to the largest size asked for so far (the
-// attribute is per device; raising it on every launch would cost a driver call per step).
-constexpr int kMaxDevices = 64;
-struct SmemLimits { size_t set[kMaxDevices]; };
 template <int N, int BLK, int R, int R2T, int LT, int NVT, int G, bool D> static SmemLimits &step_limit() { static SmemLimits l{}; return l; }
 template <int N, int BLK, int R, int R2T, int LT, int NVT, int G, bool D> static SmemLimits &score_limit() { static SmemLimits l{}; return l; }
-static cudaError_t raise_smem_limit(const void *fn, size_t smem, SmemLimits &lim) {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
-    if (dev >= 0 && dev < kMaxDevices && lim.set[dev] >= smem) return cudaSuccess;
-    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e == cudaSuccess && dev >= 0 && dev < kMaxDevices) lim.set[dev] = smem;
-    return e;
-}
 
 // blocks for B streams: W warps of P = 32 / G streams each, at most grid_cap blocks
 template <int G> static int grid_for(int B, int warps, int grid_cap) {
