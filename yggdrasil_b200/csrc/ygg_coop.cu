@@ -25,13 +25,14 @@ constexpr int kCoopThreads = 32 * kCoopWarps;
 constexpr int kCoopBlocksPerSm = 8;                  // 64 registers a thread
 constexpr int kCoopClasses = kMaxClasses<32> / kCoopWarps;   // class groups a warp holds
 
-// Shared memory of a block: one slot (record, then the table row at its end), its mbarrier, the stream's state vectors
-// and exchange buffers; `qs` holds the whole state [L][n] of a scored row (score kernel only).
+// Shared memory of a block: one slot (record, then the table row at its end), its mbarrier, the new state of the
+// current layer, exchange buffers, the readout codes of every layer (their heads run after the last layer), and `qs`,
+// the stream's whole state [L][n] (the step kernel's copy of its input; the score kernel's row state).
 struct CoopSmem {
     uint8_t *slot;
     uint32_t slot_bytes;
     uint32_t bar;
-    int8_t *qold, *qnew, *zl, *zq;
+    int8_t *qnew, *zl, *zq;   // zq: [L][32]
     int *zpart;          // [4 warps][64] layer-input partial dots
     uint32_t *dec;       // [2 parities][2 loads][4 warps] router ballots
     float *red;          // [4 warps] the warps' logit maxima, [4] the target's logit (score)
@@ -40,9 +41,9 @@ struct CoopSmem {
 };
 
 __host__ __device__ constexpr uint32_t coop_slot_bytes(uint32_t rec_max, int n) { return (rec_max + 2 * n + 127) / 128 * 128; }
-// slot | bar 16 | qold n | qnew n | zl 64 | zq 32 | zpart 4 x 64 x 4 | dec 16 x 4 | red 32 | exd 8 x 32 x 8 | qs
+// slot | bar 16 | qnew n | zl 64 | zq 8 x 32 | zpart 4 x 64 x 4 | dec 16 x 4 | red 32 | exd 8 x 32 x 8 | qs
 __host__ __device__ constexpr uint32_t coop_smem_bytes(uint32_t rec_max, int n, int qs_bytes) {
-    return coop_slot_bytes(rec_max, n) + 16 + 2 * n + 64 + 32 + 4 * 64 * 4 + 16 * 4 + 32 + 8 * 32 * 8 + qs_bytes;
+    return coop_slot_bytes(rec_max, n) + 16 + n + 64 + 8 * 32 + 4 * 64 * 4 + 16 * 4 + 32 + 8 * 32 * 8 + qs_bytes;
 }
 
 __device__ __forceinline__ CoopSmem coop_carve(uint8_t *smem, uint32_t rec_max, int n) {
@@ -52,10 +53,9 @@ __device__ __forceinline__ CoopSmem coop_carve(uint8_t *smem, uint32_t rec_max, 
     c.slot_bytes = coop_slot_bytes(rec_max, n);
     p += c.slot_bytes;
     c.bar = smem_addr(p); p += 16;
-    c.qold = (int8_t *)p; p += n;
     c.qnew = (int8_t *)p; p += n;
     c.zl = (int8_t *)p; p += 64;
-    c.zq = (int8_t *)p; p += 32;
+    c.zq = (int8_t *)p; p += 8 * 32;
     c.zpart = (int *)p; p += 4 * 64 * 4;
     c.dec = (uint32_t *)p; p += 16 * 4;
     c.red = (float *)p; p += 32;
@@ -152,13 +152,14 @@ struct CoopOut {
     int32_t *acc;        // [L][ns] or null
 };
 
-// One token of the block's stream through every layer. q_in: the stream's state ([L][ns] global memory for the step
-// kernel; the score kernel's shared [L][n] copy, QS, where o.q_out is the same copy). lg: the logits of this lane's
-// classes 32 cg + lane for the class groups cg = warp + 4 c. Returns false if the bounded wait for a copy gave up.
+// One token of the block's stream through every layer. The stream's old state is sm.qs ([L][n], shared memory; the
+// step kernel copies its input there first, in one pass); the new state goes to o.q_out ([L][ns] in global memory
+// for the step kernel; sm.qs itself for the score kernel, QS). lg: the logits of this lane's classes 32 cg + lane for
+// the class groups cg = warp + 4 c; every layer's head is added after the last layer (in layer order), so that no
+// layer waits on the unembedding's loads. Returns false if the bounded wait for a copy gave up.
 template <int BLK, int R, int R2T, int LT, int NVT, bool QS>
 __device__ __forceinline__ bool coop_token(const DevModel &m, const CoopSmem &sm, uint32_t &phase, int x,
-                                           const int8_t *q_in, const CoopOut &o, float (&lg)[kCoopClasses],
-                                           int warp, int lane) {
+                                           const CoopOut &o, float (&lg)[kCoopClasses], int warp, int lane) {
     constexpr int N = 128, C = kCoopWarps;
     const int tid = threadIdx.x;
     const int i = C * lane + warp;               // the state coordinate this thread updates
@@ -174,9 +175,8 @@ __device__ __forceinline__ bool coop_token(const DevModel &m, const CoopSmem &sm
         const DevLayer &y = m.layer[l];
         const bool low = l > 0 && (R2T > 0 || m.R2 > 0);
         const bool has_table = y.table != nullptr;
-        // -- this layer's old state; the new state of the layer below is in qnew
-        sm.qold[tid] = (QS || tid < ns) ? q_in[(size_t)l * ns + tid] : (int8_t)0;
-        __syncthreads();
+        // this layer's old state; the new state of the layer below is in qnew
+        const int8_t *qold = sm.qs + (size_t)l * N;
         int r = x;
         float rho = 0.0f;
         if (l > 0) {
@@ -232,10 +232,10 @@ __device__ __forceinline__ bool coop_token(const DevModel &m, const CoopSmem &sm
             const int blk0 = (i / BLK) * BLK;
             uint32_t qblk[BLK / 4];
             if constexpr (BLK == 8) {
-                const uint2 v = *(const uint2 *)(sm.qold + blk0);
+                const uint2 v = *(const uint2 *)(qold + blk0);
                 qblk[0] = v.x; qblk[1] = v.y;
             } else {
-                const uint4 v = *(const uint4 *)(sm.qold + blk0);
+                const uint4 v = *(const uint4 *)(qold + blk0);
                 qblk[0] = v.x; qblk[1] = v.y; qblk[2] = v.z; qblk[3] = v.w;
             }
             int s = 0;
@@ -270,7 +270,7 @@ __device__ __forceinline__ bool coop_token(const DevModel &m, const CoopSmem &sm
         }
         if (i >= m.ns) acc = 0;   // padding of a narrower model: held at exactly 0
         const int8_t qn = (int8_t)clampi(acc, -128, 127);
-        // the readout reads the new state of every lane: every thread has read qold and the slot's rows first
+        // the readout reads the new state of every lane: every thread has read the old state and the slot's rows first
         sm.qnew[i] = qn;
         if (!QS && o.acc != nullptr && i < ns) o.acc[(size_t)l * ns + i] = acc;
         __syncthreads();
@@ -293,37 +293,45 @@ __device__ __forceinline__ bool coop_token(const DevModel &m, const CoopSmem &sm
             if (lane < RW) {
                 const int rr = warp * RW + lane;
                 const float mz = y.off_mz != kNone ? *(const float *)(rec + y.off_mz + 4 * rr) : y.readout_scale;
-                sm.zq[rr] = (int8_t)clampi(cvt_rne(__fmul_rn(i2f(myz), mz)), -127, 127);
+                sm.zq[l * 32 + rr] = (int8_t)clampi(cvt_rne(__fmul_rn(i2f(myz), mz)), -127, 127);
             }
         }
-        __syncthreads();   // zq is ready; every read of the slot is done before the next layer's copy
-        // -- the head (cpu/ygg.cpp:421-434) for this warp's class groups
-        {
-            uint32_t zw[R / 4];
+        __syncthreads();   // every read of the slot is done before the next layer's copy; zq of layer l is ready
+    }
+    // -- the heads (cpu/ygg.cpp:421-434) of every layer in layer order, for this warp's class groups; with the layer
+    // count fixed, the unembedding rows of every layer load together
+    auto head = [&](const int l) {
+        const DevLayer &y = m.layer[l];
+        uint32_t zw[R / 4];
 #pragma unroll
-            for (int j = 0; j < R / 4; j++) zw[j] = *(const uint32_t *)(sm.zq + 4 * j);
+        for (int j = 0; j < R / 4; j++) zw[j] = *(const uint32_t *)(sm.zq + l * 32 + 4 * j);
 #pragma unroll
-            for (int c = 0; c < kCoopClasses; c++) {
-                const int cg = warp + C * c;
-                if (NVT ? (cg < NVT) : (cg < nv)) {
-                    const int cls = 32 * cg + lane;
-                    const int8_t *qrow = y.unembed + (size_t)cls * R;
-                    int a = 0;
-                    if constexpr (R == 8) {
-                        const uint2 v = __ldg((const uint2 *)qrow);
-                        a = __dp4a((int)v.x, (int)zw[0], a);
-                        a = __dp4a((int)v.y, (int)zw[1], a);
-                    } else {
+        for (int c = 0; c < kCoopClasses; c++) {
+            const int cg = warp + C * c;
+            if (NVT ? (cg < NVT) : (cg < nv)) {
+                const int cls = 32 * cg + lane;
+                const int8_t *qrow = y.unembed + (size_t)cls * R;
+                int a = 0;
+                if constexpr (R == 8) {
+                    const uint2 v = __ldg((const uint2 *)qrow);
+                    a = __dp4a((int)v.x, (int)zw[0], a);
+                    a = __dp4a((int)v.y, (int)zw[1], a);
+                } else {
 #pragma unroll
-                        for (int j = 0; j < R / 16; j++)
-                            a = dot16(__ldg((const uint4 *)(qrow + 16 * j)),
-                                      make_uint4(zw[4 * j], zw[4 * j + 1], zw[4 * j + 2], zw[4 * j + 3]), a);
-                    }
-                    const float sc = y.sqv ? __ldg(y.sqv + cls) : y.unembed_scale;
-                    lg[c] = __fadd_rn(lg[c], __fmul_rn(i2f(a), sc));
+                    for (int j = 0; j < R / 16; j++)
+                        a = dot16(__ldg((const uint4 *)(qrow + 16 * j)),
+                                  make_uint4(zw[4 * j], zw[4 * j + 1], zw[4 * j + 2], zw[4 * j + 3]), a);
                 }
+                const float sc = y.sqv ? __ldg(y.sqv + cls) : y.unembed_scale;
+                lg[c] = __fadd_rn(lg[c], __fmul_rn(i2f(a), sc));
             }
         }
+    };
+    if constexpr (LT > 0) {
+#pragma unroll
+        for (int l = 0; l < LT; l++) head(l);
+    } else {
+        for (int l = 0; l < L; l++) head(l);
     }
     return true;
 }
@@ -397,11 +405,17 @@ __global__ void __launch_bounds__(kCoopThreads, kCoopBlocksPerSm) coop_step_kern
             if (routes != nullptr && tid < L) routes[(size_t)s * L + tid] = -1;
             continue;
         }
+        // the stream's old state, every layer in one pass, into the device layout (coordinates past ns are 0)
+        const int8_t *q_in = state_in + (size_t)s * L * ns;
+        for (int j = tid; j < L * 128; j += kCoopThreads) {
+            const int li = j / 128, c = j % 128;
+            sm.qs[j] = c < ns ? q_in[(size_t)li * ns + c] : (int8_t)0;
+        }
+        __syncthreads();
         float lg[kCoopClasses];
         const CoopOut o{state_out + (size_t)s * L * ns, routes ? routes + (size_t)s * L : nullptr,
                         acc_out ? acc_out + (size_t)s * L * ns : nullptr};
-        if (!coop_token<BLK, R, R2T, LT, NVT, false>(m, sm, phase, x, state_in + (size_t)s * L * ns, o, lg, warp,
-                                                     lane)) {
+        if (!coop_token<BLK, R, R2T, LT, NVT, false>(m, sm, phase, x, o, lg, warp, lane)) {
             if (tid == 0) atomicOr(m.status, kStatusTimeout);
             return;
         }
@@ -448,7 +462,7 @@ __global__ void __launch_bounds__(kCoopThreads, kCoopBlocksPerSm) coop_score_ker
         double nll = 0.0;
         for (int t = 0; t + 1 < T; t++) {
             float lg[kCoopClasses];
-            if (!coop_token<BLK, R, R2T, LT, NVT, true>(m, sm, phase, tok[t], sm.qs, o, lg, warp, lane)) {
+            if (!coop_token<BLK, R, R2T, LT, NVT, true>(m, sm, phase, tok[t], o, lg, warp, lane)) {
                 if (tid == 0) atomicOr(m.status, kStatusTimeout);
                 return;
             }
@@ -473,7 +487,7 @@ template <int BLK, int R, int R2T, int LT, int NVT>
 static cudaError_t coop_step_t(const DevModel &dm, int B, const int32_t *tok, const int8_t *sin, int8_t *sout,
                                float *lg, int32_t *routes, int32_t *acc, uint32_t rec_max, int sm_count,
                                cudaStream_t st) {
-    const size_t smem = coop_smem_bytes(rec_max, 128, 0);
+    const size_t smem = coop_smem_bytes(rec_max, 128, (dm.L * 128 + 127) / 128 * 128);
     cudaError_t e = raise_smem_limit((const void *)coop_step_kernel<BLK, R, R2T, LT, NVT>, smem,
                                      coop_step_limit<BLK, R, R2T, LT, NVT>());
     if (e != cudaSuccess) return e;
