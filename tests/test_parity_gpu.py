@@ -271,7 +271,8 @@ def test_extension_state_layout(rec, case_model, torch):
 
 # the launch configurations the library chooses between by batch, each forced for every batch
 LAUNCH_CONFIGS = {
-    "coop": {"YGG_COOP": "1000000"},                       # 4 warps per stream (n = 128; others keep the policy)
+    "pipe": {"YGG_PIPE": "1000000"},                       # scoring as a layer wavefront (n = 128, L <= 7)
+    "coop": {"YGG_COOP": "1000000", "YGG_PIPE": "0"},      # 4 warps per stream (n = 128; others keep the policy)
     "warp-staged": {"YGG_LANES": "32", "YGG_DIRECT": "0"},  # a warp per stream, records staged in shared memory
     "warp-direct": {"YGG_LANES": "32", "YGG_DIRECT": "1"},  # a warp per stream, records read from global memory
     "half-staged": {"YGG_LANES": "16", "YGG_DIRECT": "0"},  # two streams per warp (shapes that allow it)
@@ -313,3 +314,45 @@ def test_fast_instances_bit_exact(cfg, rec, tmp_path, torch, monkeypatch):
     assert sha(np.ascontiguousarray(lg).tobytes()) == rec["logits_sha256"]
     x7 = synth.workload_tokens(w, 7, 20, seed=3)
     np.testing.assert_allclose(model.score(x7), om.score(x7), rtol=BITS_RTOL)
+
+
+N128 = [c for c in CASES if c["shape"]["d_state"] == 128]
+
+
+@pytest.mark.parametrize("rec", N128, ids=_ids(N128))
+def test_pipe_score_rows_short_sequences_and_state(rec, case_model, torch, monkeypatch):
+    """The layer wavefront (one row per block, L + 1 warp groups): more rows than blocks (a block takes a second
+    row), sequences shorter than the pipeline's depth (T = 1, 2, 3), and a carried state in and out. Its bits must
+    equal the sequential latency kernel's exactly (same operations, same order) and the oracle's within rtol."""
+    path = case_model(rec)
+    om = O.OracleModel(path)
+    rng = np.random.default_rng(5)
+    monkeypatch.setenv("YGG_PIPE", "1000000")
+    pipe = load(path)
+    monkeypatch.setenv("YGG_PIPE", "0")
+    monkeypatch.setenv("YGG_COOP", "1000000")
+    coop = load(path)
+    rows = 150
+    warm = rng.integers(0, pipe.vocab, (rows, 6)).astype(np.int32)
+    st0 = pipe.init_state(rows)
+    ost0 = om.init_state(rows)
+    for i in range(warm.shape[1]):
+        _, st0 = pipe.step(warm[:, i], st0)
+        om.step(warm[:, i], ost0)
+    np.testing.assert_array_equal(st0.cpu().numpy(), ost0)
+    for t in (1, 2, 3, 9):
+        x = rng.integers(0, pipe.vocab, (rows, t)).astype(np.int32)
+        xd = torch.as_tensor(x).cuda()
+        sp, sc = st0.clone(), st0.clone()
+        bp = torch.empty(rows, dtype=torch.float64, device="cuda")
+        bc = torch.empty_like(bp)
+        pipe.score_into(xd, sp, bp)
+        coop.score_into(xd, sc, bc)
+        ost = ost0.copy()
+        ob = om.score(x, ost)
+        np.testing.assert_array_equal(bp.cpu().numpy(), bc.cpu().numpy(), err_msg=f"pipe vs coop bits, T={t}")
+        np.testing.assert_allclose(bp.cpu().numpy(), ob, rtol=BITS_RTOL)
+        np.testing.assert_array_equal(sp.cpu().numpy(), ost, err_msg=f"state after T={t}")
+        bz = torch.empty_like(bp)
+        pipe.score_into(xd, None, bz)
+        np.testing.assert_allclose(bz.cpu().numpy(), om.score(x), rtol=BITS_RTOL)

@@ -25,44 +25,81 @@ constexpr int kCoopThreads = 32 * kCoopWarps;
 constexpr int kCoopBlocksPerSm = 8;                  // 64 registers a thread
 constexpr int kCoopClasses = kMaxClasses<32> / kCoopWarps;   // class groups a warp holds
 
-// Shared memory of a block: one slot (record, then the table row at its end), its mbarrier, the new state of the
-// current layer, exchange buffers, the readout codes of every layer (their heads run after the last layer), and `qs`,
-// the stream's whole state [L][n] (the step kernel's copy of its input; the score kernel's row state).
-struct CoopSmem {
+// What one group of 4 warps needs to run a layer: one slot (record, then the table row at its end), its mbarrier, and
+// exchange buffers.
+struct CoopLayerSmem {
     uint8_t *slot;
     uint32_t slot_bytes;
     uint32_t bar;
-    int8_t *qnew, *zl, *zq;   // zq: [L][32]
+    int8_t *zl;
     int *zpart;          // [4 warps][64] layer-input partial dots
     uint32_t *dec;       // [2 parities][2 loads][4 warps] router ballots
+};
+
+// Shared memory of a latency-kernel block: the layer buffers, the new state of the current layer, the readout codes of
+// every layer (their heads run after the last layer), the NLL's exchange buffers, and `qs`, the stream's whole state
+// [L][n] (the step kernel's copy of its input; the score kernel's row state).
+struct CoopSmem {
+    CoopLayerSmem ly;
+    int8_t *qnew, *zq;   // zq: [L][32]
     float *red;          // [4 warps] the warps' logit maxima, [4] the target's logit (score)
     double *exd;         // [8 class groups][32 lanes] exp of the logits (score)
     int8_t *qs;
 };
 
 __host__ __device__ constexpr uint32_t coop_slot_bytes(uint32_t rec_max, int n) { return (rec_max + 2 * n + 127) / 128 * 128; }
-// slot | bar 16 | qnew n | zl 64 | zq 8 x 32 | zpart 4 x 64 x 4 | dec 16 x 4 | red 32 | exd 8 x 32 x 8 | qs
+// slot | bar 16 | zl 64 | zpart 4 x 64 x 4 | dec 16 x 4
+__host__ __device__ constexpr uint32_t coop_layer_smem_bytes(uint32_t rec_max, int n) {
+    return coop_slot_bytes(rec_max, n) + 16 + 64 + 4 * 64 * 4 + 16 * 4;
+}
+// layer buffers | qnew n | zq 8 x 32 | red 32 | exd 8 x 32 x 8 | qs
 __host__ __device__ constexpr uint32_t coop_smem_bytes(uint32_t rec_max, int n, int qs_bytes) {
-    return coop_slot_bytes(rec_max, n) + 16 + n + 64 + 8 * 32 + 4 * 64 * 4 + 16 * 4 + 32 + 8 * 32 * 8 + qs_bytes;
+    return coop_layer_smem_bytes(rec_max, n) + n + 8 * 32 + 32 + 8 * 32 * 8 + qs_bytes;
+}
+
+__device__ __forceinline__ CoopLayerSmem coop_carve_layer(uint8_t *&p, uint32_t rec_max, int n) {
+    CoopLayerSmem c;
+    c.slot = p;
+    c.slot_bytes = coop_slot_bytes(rec_max, n);
+    p += c.slot_bytes;
+    c.bar = smem_addr(p); p += 16;
+    c.zl = (int8_t *)p; p += 64;
+    c.zpart = (int *)p; p += 4 * 64 * 4;
+    c.dec = (uint32_t *)p; p += 16 * 4;
+    return c;
 }
 
 __device__ __forceinline__ CoopSmem coop_carve(uint8_t *smem, uint32_t rec_max, int n) {
     CoopSmem c;
     uint8_t *p = smem;
-    c.slot = p;
-    c.slot_bytes = coop_slot_bytes(rec_max, n);
-    p += c.slot_bytes;
-    c.bar = smem_addr(p); p += 16;
+    c.ly = coop_carve_layer(p, rec_max, n);
     c.qnew = (int8_t *)p; p += n;
-    c.zl = (int8_t *)p; p += 64;
     c.zq = (int8_t *)p; p += 8 * 32;
-    c.zpart = (int *)p; p += 4 * 64 * 4;
-    c.dec = (uint32_t *)p; p += 16 * 4;
     c.red = (float *)p; p += 32;
     c.exd = (double *)p; p += 8 * 32 * 8;
     c.qs = (int8_t *)p;
     return c;
 }
+
+// How the 4 warps of a stream meet: the whole block (one stream per block), or a named barrier of 128 threads (one
+// warp group of a block that holds several; ids 1-15, id 0 being __syncthreads').
+struct BlockBar {
+    __device__ __forceinline__ void sync() const { __syncthreads(); }
+    __device__ __forceinline__ bool all(bool p) const { return __syncthreads_and(p) != 0; }
+};
+struct GroupBar {
+    uint32_t id;
+    __device__ __forceinline__ void sync() const { asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory"); }
+    __device__ __forceinline__ bool all(bool p) const {
+        uint32_t r;
+        asm volatile(
+            "{\n\t.reg .pred a, q;\n\tsetp.ne.u32 a, %1, 0;\n\tbar.red.and.pred q, %2, 128, a;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+            : "=r"(r)
+            : "r"((uint32_t)p), "r"(id)
+            : "memory");
+        return r != 0;
+    }
+};
 
 // Router descent of the block's stream (cpu/ygg.cpp:271-280), kCoopLook levels per round. Row k < 31 of a round's
 // subtree (heap order under the round's root ix: k = 0 is ix, k = 1-2 its children, ...) is read in load k / 16 by
@@ -71,9 +108,36 @@ __device__ __forceinline__ CoopSmem coop_carve(uint8_t *smem, uint32_t rec_max, 
 // n new state bytes of the layer below. The records of the last round's candidate leaves go to L2 when there are at
 // most 8 of them. DT > 0: the depth fixed at compile time (= D), the rounds unrolled. Returns the leaf node index in
 // [E, 2E).
-template <int DT = 0>
+// The first round without global loads (PRE): `top` holds rows 1-31 of the layer's router (row k + 1 at 128 k, shared
+// memory, copied once per block), and t the lane's two thresholds of token x (rows k + 1 for its k = 16 i + 4 warp +
+// lane / 8), loaded ahead of time by route_first_thr.
+struct RouteFirst {
+    const int8_t *top;
+    float t[2];
+};
+__device__ __forceinline__ void route_first_thr(const DevLayer &y, int x, int E, int D, int warp, int lane,
+                                                float (&t)[2]) {
+    const int nrows = (1 << (D < kCoopLook ? D : kCoopLook)) - 1;
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        const int k = 16 * i + 4 * warp + lane / 8;
+        t[i] = k < nrows ? __ldg(y.thr + (size_t)x * E + k + 1) : 0.0f;
+    }
+}
+
+// Nothing to overlap with a round's loads (see route_coop's `shadow`).
+struct NoShadow {
+    __device__ __forceinline__ void operator()() const {}
+};
+
+//
+// shadow() runs in the second round (the first when D <= 5) between the issue of its loads and their use, and after()
+// once that round's barrier has passed: work that needs neither the loads nor the decisions hides in their latency.
+template <int DT = 0, bool PRE = false, class Bar, class Shadow = NoShadow, class After = NoShadow>
 __device__ __forceinline__ int route_coop(const DevLayer &y, int x, int E, int D, const int8_t *qb, float rho,
-                                          uint32_t *dec, int warp, int lane) {
+                                          uint32_t *dec, const Bar &bar, int warp, int lane,
+                                          const RouteFirst &pre = RouteFirst{}, const Shadow &shadow = Shadow{},
+                                          const After &after = After{}) {
     constexpr int N = 128, LPR = 8;
     const int g = lane / LPR;
     const int8_t *wl = y.w + 16 * (lane % LPR);
@@ -100,16 +164,26 @@ __device__ __forceinline__ int route_coop(const DevLayer &y, int x, int E, int D
         }
         uint4 v[2];
         float t[2];
+        if (PRE && d == 0) {
 #pragma unroll
-        for (int i = 0; i < 2; i++) {
-            const int row = ix * mul[i] + add[i];
-            v[i] = make_uint4(0, 0, 0, 0);
-            t[i] = 0.0f;
-            if (kk[i] < nrows) {
-                v[i] = __ldg((const uint4 *)(wl + (size_t)row * N));
-                t[i] = __ldg(thr_x + row);
+            for (int i = 0; i < 2; i++) {
+                v[i] = kk[i] < nrows ? *(const uint4 *)(pre.top + 128 * kk[i] + 16 * (lane % LPR)) : make_uint4(0, 0, 0, 0);
+                t[i] = pre.t[i];
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 2; i++) {
+                const int row = ix * mul[i] + add[i];
+                v[i] = make_uint4(0, 0, 0, 0);
+                t[i] = 0.0f;
+                if (kk[i] < nrows) {
+                    v[i] = __ldg((const uint4 *)(wl + (size_t)row * N));
+                    t[i] = __ldg(thr_x + row);
+                }
             }
         }
+        const bool hide = d == (D > kCoopLook ? kCoopLook : 0);
+        if (hide) shadow();
 #pragma unroll
         for (int i = 0; i < 2; i++) {
             int dot = dot16(v[i], qrow, 0);
@@ -118,7 +192,8 @@ __device__ __forceinline__ int route_coop(const DevLayer &y, int x, int E, int D
             const uint32_t bal = __ballot_sync(kFull, __fmul_rn(i2f(dot), rho) > t[i]);
             if (lane == 0) dec[parity * 8 + i * 4 + warp] = bal;
         }
-        __syncthreads();
+        bar.sync();
+        if (hide) after();
         // row k's decision: bit 8 g of dec[load][warp] -> bit k = 16 load + 4 warp + g of one mask
         uint32_t mask = 0;
 #pragma unroll
@@ -152,159 +227,172 @@ struct CoopOut {
     int32_t *acc;        // [L][ns] or null
 };
 
-// One token of the block's stream through every layer. The stream's old state is sm.qs ([L][n], shared memory; the
-// step kernel copies its input there first, in one pass); the new state goes to o.q_out ([L][ns] in global memory
-// for the step kernel; sm.qs itself for the score kernel, QS). lg: the logits of this lane's classes 32 cg + lane for
-// the class groups cg = warp + 4 c; every layer's head is added after the last layer (in layer order), so that no
-// layer waits on the unembedding's loads. Returns false if the bounded wait for a copy gave up.
-template <int BLK, int R, int R2T, int LT, int NVT, bool QS>
-__device__ __forceinline__ bool coop_token(const DevModel &m, const CoopSmem &sm, uint32_t &phase, int x,
-                                           const CoopOut &o, float (&lg)[kCoopClasses], int warp, int lane) {
+// Layer l of one token of a group's stream (4 warps; `bar` joins them). PRE: the router's first round reads `pre`
+// (rows in shared memory, thresholds loaded ahead). qb: the new state of the layer below (l > 0;
+// shared memory); qold: this layer's old state (shared); qnew: where the layer's new state goes (shared; it may be qb
+// itself, which is read only before the record wait); q_out (+ acc_out, route_out when not null; QS: q_out is shared
+// memory with stride n): the new state's destination; zq: the layer's 32 readout-code bytes (shared). Returns false
+// (every thread of the group) if the bounded wait for the record's copy gave up.
+template <int BLK, int R, int R2T, bool QS, bool PRE = false, class Bar>
+__device__ __forceinline__ bool coop_layer(const DevModel &m, const CoopLayerSmem &sm, uint32_t &phase, int l, int x,
+                                           const int8_t *qb, const int8_t *qold, int8_t *qnew, int8_t *zq,
+                                           int8_t *q_out, int32_t *acc_out, int32_t *route_out, const Bar &bar,
+                                           int warp, int lane, const RouteFirst &pre = RouteFirst{}) {
     constexpr int N = 128, C = kCoopWarps;
-    const int tid = threadIdx.x;
+    const int tid = 32 * warp + lane;
     const int i = C * lane + warp;               // the state coordinate this thread updates
-    const int L = LT ? LT : m.L, ns = QS ? N : m.ns;
+    const int ns = QS ? N : m.ns;
+    const DevLayer &y = m.layer[l];
+    const bool low = l > 0 && (R2T > 0 || m.R2 > 0);
+    const bool has_table = y.table != nullptr;
+    int r = x;
+    float rho = 0.0f;
+    if (l > 0) {
+        const LaneQ<C> qv = load_q<C>(qb + C * lane);
+        rho = rms_rho<N, 32>(qv, y.r2b, y.rms_eps, m.inv_n, lane);
+        // the layer-input codes zl[k] = clamp(rint((f32(V'_k . qb) * mv[k]) * rho)) (cpu/ygg.cpp:285-296) need only
+        // the state below and rho: formed while a router round's loads are in flight. Warp w dots chunks 2w, 2w+1;
+        // after the round's barrier warp 0 adds the 4 partials.
+        const int R2P = R2T ? R2T : m.R2P;
+        auto zl_part = [&]() {
+            if (!low) return;
+            for (int k = lane; k < R2P; k += 32) {
+                const int8_t *vk = y.vl + (size_t)k * 16;
+                int a = 0;
+#pragma unroll
+                for (int j = 2 * warp; j < 2 * warp + 2; j++)
+                    a = dot16(__ldg((const uint4 *)(vk + (size_t)j * R2P * 16)), *(const uint4 *)(qb + 16 * j), a);
+                sm.zpart[warp * 64 + k] = a;
+            }
+        };
+        auto zl_sum = [&]() {
+            if (!low || warp != 0) return;
+            for (int k = lane; k < R2P; k += 32) {
+                const int a = sm.zpart[k] + sm.zpart[64 + k] + sm.zpart[128 + k] + sm.zpart[192 + k];
+                const float zf = __fmul_rn(__fmul_rn(i2f(a), __ldg(y.mv + k)), rho);
+                sm.zl[k] = (int8_t)(k < m.R2 ? clampi(cvt_rne(zf), -127, 127) : 0);
+            }
+        };
+        r = (m.D == 13 ? route_coop<13, PRE>(y, x, m.E, m.D, qb, rho, sm.dec, bar, warp, lane, pre, zl_part, zl_sum)
+                       : route_coop<0, PRE>(y, x, m.E, m.D, qb, rho, sm.dec, bar, warp, lane, pre, zl_part, zl_sum)) -
+            m.E;
+    }
+    // -- the record and its table row into the slot (the group's thread 0)
+    const int16_t *trow = (const int16_t *)(sm.slot + sm.slot_bytes - 2 * N);
+    if (tid == 0) {
+        fence_proxy_async();
+        mbar_expect_tx(sm.bar, y.rec_bytes + (has_table ? 2u * N : 0u));
+        bulk_g2s(smem_addr(sm.slot), y.rec + (size_t)r * y.rec_bytes, y.rec_bytes, sm.bar);
+        if (has_table)
+            bulk_g2s(smem_addr(trow), y.table + ((size_t)r * y.table_rows + (y.table_rows > 1 ? x : 0)) * N, 2u * N,
+                     sm.bar);
+    }
+    const bool ok = mbar_wait_bounded(sm.bar, phase);
+    phase ^= 1u;
+    if (!bar.all(ok)) return false;   // every wait ended (or one gave up); zl is ready
+    // -- row i = 4 lane + warp: transition, input, layer input, saturation (cpu/ygg.cpp:312-389); the lane's data
+    // for its row ii = warp sits in whole chunks of the 32-lane layout
+    const uint8_t *rec = sm.slot;
+    int acc;
+    {
+        constexpr int kRowWords = BLK / 2;
+        const uint8_t *pa = rec + y.off_a + 16 * lane;
+        uint32_t aw[kRowWords];
+#pragma unroll
+        for (int j = 0; j < kRowWords / 4; j++) {
+            const uint4 v = *(const uint4 *)(pa + 512 * (warp * (kRowWords / 4) + j));
+            aw[4 * j] = v.x; aw[4 * j + 1] = v.y; aw[4 * j + 2] = v.z; aw[4 * j + 3] = v.w;
+        }
+        const int blk0 = (i / BLK) * BLK;
+        uint32_t qblk[BLK / 4];
+        if constexpr (BLK == 8) {
+            const uint2 v = *(const uint2 *)(qold + blk0);
+            qblk[0] = v.x; qblk[1] = v.y;
+        } else {
+            const uint4 v = *(const uint4 *)(qold + blk0);
+            qblk[0] = v.x; qblk[1] = v.y; qblk[2] = v.z; qblk[3] = v.w;
+        }
+        int s = 0;
+#pragma unroll
+        for (int p = 0; p < kRowWords; p++)
+            s = (p & 1) ? __dp2a_hi((int)aw[p], (int)qblk[p >> 1], s) : __dp2a_lo((int)aw[p], (int)qblk[p >> 1], s);
+        acc = (s + (1 << (m.shift - 1))) >> m.shift;
+    }
+    if (has_table) {
+        acc += trow[i];
+    } else {   // factored (cpu/ygg.cpp:339-358): the lane's row ii = warp of F, chunks warp * KP/16 + j
+        const int KP = m.KP;
+        const uint8_t *pf = rec + y.off_f + 16 * lane;
+        const int8_t *v = y.vt + (size_t)x * KP;
+        int lt = 0;
+        for (int j = 0; j < KP / 16; j++)
+            lt = dot16(*(const uint4 *)(pf + 512 * (warp * (KP / 16) + j)), __ldg((const uint4 *)(v + 16 * j)), lt);
+        const float su = *(const float *)(rec + y.off_su);
+        const float mul = __fmul_rn(su, __ldg(y.mt + i));
+        acc += cvt_rne(__fmul_rn(i2f(lt), mul)) + ((const int16_t *)(rec + y.off_cb))[i];
+    }
+    if (low) {   // (cpu/ygg.cpp:360-377): the lane's row ii = warp of U', chunks warp * R2P/16 + j
+        const int R2P = R2T ? R2T : m.R2P;
+        const uint8_t *pu = rec + y.off_u + 16 * lane;
+        int la = 0;
+#pragma unroll
+        for (int j = 0; j < (R2T ? R2T / 16 : 4); j++)
+            if (R2T || j < R2P / 16)
+                la = dot16(*(const uint4 *)(pu + 512 * (warp * (R2P / 16) + j)), *(const uint4 *)(sm.zl + 16 * j), la);
+        const float mu = y.mulv ? __ldg(y.mulv + i) : y.layer_input_scale;
+        acc += cvt_rne(__fmul_rn(i2f(la), mu));
+    }
+    if (i >= m.ns) acc = 0;   // padding of a narrower model: held at exactly 0
+    const int8_t qn = (int8_t)clampi(acc, -128, 127);
+    // the readout reads the new state of every lane: every thread has read the old state and the slot's rows first
+    qnew[i] = qn;
+    if (!QS && acc_out != nullptr && i < ns) acc_out[i] = acc;
+    bar.sync();
+    if (tid < ns) q_out[tid] = qnew[tid];
+    if (!QS && route_out != nullptr && tid == 0) *route_out = r;
+    // -- readout (cpu/ygg.cpp:395-420): warp w takes rows [w R/4, (w + 1) R/4); the lane's word of row rr is
+    // P[rr][4 lane .. 4 lane + 3], word rr of its readout data
+    {
+        constexpr int RW = R / C;
+        const uint32_t qw = *(const uint32_t *)(qnew + C * lane);
+        const uint32_t *pp = (const uint32_t *)(rec + y.off_p + 16 * lane);
+        int myz = 0;
+#pragma unroll
+        for (int j = 0; j < RW; j++) {
+            const int rr = warp * RW + j;
+            const uint32_t word = pp[128 * (rr / 4) + rr % 4];
+            const int z = __reduce_add_sync(kFull, __dp4a((int)word, (int)qw, 0));
+            if (lane == j) myz = z;
+        }
+        if (lane < RW) {
+            const int rr = warp * RW + lane;
+            const float mz = y.off_mz != kNone ? *(const float *)(rec + y.off_mz + 4 * rr) : y.readout_scale;
+            zq[rr] = (int8_t)clampi(cvt_rne(__fmul_rn(i2f(myz), mz)), -127, 127);
+        }
+    }
+    bar.sync();   // every read of the slot is done before the next copy into it; zq is ready
+    return true;
+}
+
+// The logits of a token (cpu/ygg.cpp:421-434): head_b, then every layer's head in layer order, for this warp's class
+// groups cg = warp + 4 c (classes 32 cg + lane). zq: layer l's readout codes at zq + 32 l. With the layer count fixed,
+// the unembedding rows of every layer load together.
+template <int R, int LT, int NVT>
+__device__ __forceinline__ void coop_heads(const DevModel &m, const int8_t *zq, float (&lg)[kCoopClasses], int warp,
+                                           int lane) {
+    constexpr int C = kCoopWarps;
+    const int L = LT ? LT : m.L;
     const int nv = NVT ? NVT : m.VP / 32;
 #pragma unroll
     for (int c = 0; c < kCoopClasses; c++) {
         const int cg = warp + C * c;
         lg[c] = cg < nv ? __ldg(m.head_b + 32 * cg + lane) : 0.0f;
     }
-#pragma unroll 1
-    for (int l = 0; l < L; l++) {
-        const DevLayer &y = m.layer[l];
-        const bool low = l > 0 && (R2T > 0 || m.R2 > 0);
-        const bool has_table = y.table != nullptr;
-        // this layer's old state; the new state of the layer below is in qnew
-        const int8_t *qold = sm.qs + (size_t)l * N;
-        int r = x;
-        float rho = 0.0f;
-        if (l > 0) {
-            const LaneQ<C> qb = load_q<C>(sm.qnew + C * lane);
-            rho = rms_rho<N, 32>(qb, y.r2b, y.rms_eps, m.inv_n, lane);
-            r = (m.D == 13 ? route_coop<13>(y, x, m.E, m.D, sm.qnew, rho, sm.dec, warp, lane)
-                           : route_coop(y, x, m.E, m.D, sm.qnew, rho, sm.dec, warp, lane)) - m.E;
-        }
-        // -- the record and its table row into the slot (thread 0), while the layer-input codes are formed
-        const int16_t *trow = (const int16_t *)(sm.slot + sm.slot_bytes - 2 * N);
-        if (tid == 0) {
-            fence_proxy_async();
-            mbar_expect_tx(sm.bar, y.rec_bytes + (has_table ? 2u * N : 0u));
-            bulk_g2s(smem_addr(sm.slot), y.rec + (size_t)r * y.rec_bytes, y.rec_bytes, sm.bar);
-            if (has_table)
-                bulk_g2s(smem_addr(trow), y.table + ((size_t)r * y.table_rows + (y.table_rows > 1 ? x : 0)) * N, 2u * N,
-                         sm.bar);
-        }
-        if (low) {   // zl[k] = clamp(rint((f32(V'_k . qb) * mv[k]) * rho)) (cpu/ygg.cpp:285-296); warp w: chunks 2w, 2w+1
-            const int R2P = R2T ? R2T : m.R2P;
-            for (int k = lane; k < R2P; k += 32) {
-                const int8_t *vk = y.vl + (size_t)k * 16;
-                int a = 0;
-#pragma unroll
-                for (int j = 2 * warp; j < 2 * warp + 2; j++)
-                    a = dot16(__ldg((const uint4 *)(vk + (size_t)j * R2P * 16)), *(const uint4 *)(sm.qnew + 16 * j), a);
-                sm.zpart[warp * 64 + k] = a;
-            }
-            __syncthreads();
-            if (warp == 0)
-                for (int k = lane; k < R2P; k += 32) {
-                    const int a = sm.zpart[k] + sm.zpart[64 + k] + sm.zpart[128 + k] + sm.zpart[192 + k];
-                    const float zf = __fmul_rn(__fmul_rn(i2f(a), __ldg(y.mv + k)), rho);
-                    sm.zl[k] = (int8_t)(k < m.R2 ? clampi(cvt_rne(zf), -127, 127) : 0);
-                }
-        }
-        const bool ok = mbar_wait_bounded(sm.bar, phase);
-        phase ^= 1u;
-        if (!__syncthreads_and(ok)) return false;   // every wait ended (or one gave up); zl is ready
-        // -- row i = 4 lane + warp: transition, input, layer input, saturation (cpu/ygg.cpp:312-389); the lane's data
-        // for its row ii = warp sits in whole chunks of the 32-lane layout
-        const uint8_t *rec = sm.slot;
-        int acc;
-        {
-            constexpr int kRowWords = BLK / 2;
-            const uint8_t *pa = rec + y.off_a + 16 * lane;
-            uint32_t aw[kRowWords];
-#pragma unroll
-            for (int j = 0; j < kRowWords / 4; j++) {
-                const uint4 v = *(const uint4 *)(pa + 512 * (warp * (kRowWords / 4) + j));
-                aw[4 * j] = v.x; aw[4 * j + 1] = v.y; aw[4 * j + 2] = v.z; aw[4 * j + 3] = v.w;
-            }
-            const int blk0 = (i / BLK) * BLK;
-            uint32_t qblk[BLK / 4];
-            if constexpr (BLK == 8) {
-                const uint2 v = *(const uint2 *)(qold + blk0);
-                qblk[0] = v.x; qblk[1] = v.y;
-            } else {
-                const uint4 v = *(const uint4 *)(qold + blk0);
-                qblk[0] = v.x; qblk[1] = v.y; qblk[2] = v.z; qblk[3] = v.w;
-            }
-            int s = 0;
-#pragma unroll
-            for (int p = 0; p < kRowWords; p++)
-                s = (p & 1) ? __dp2a_hi((int)aw[p], (int)qblk[p >> 1], s) : __dp2a_lo((int)aw[p], (int)qblk[p >> 1], s);
-            acc = (s + (1 << (m.shift - 1))) >> m.shift;
-        }
-        if (has_table) {
-            acc += trow[i];
-        } else {   // factored (cpu/ygg.cpp:339-358): the lane's row ii = warp of F, chunks warp * KP/16 + j
-            const int KP = m.KP;
-            const uint8_t *pf = rec + y.off_f + 16 * lane;
-            const int8_t *v = y.vt + (size_t)x * KP;
-            int lt = 0;
-            for (int j = 0; j < KP / 16; j++)
-                lt = dot16(*(const uint4 *)(pf + 512 * (warp * (KP / 16) + j)), __ldg((const uint4 *)(v + 16 * j)), lt);
-            const float su = *(const float *)(rec + y.off_su);
-            const float mul = __fmul_rn(su, __ldg(y.mt + i));
-            acc += cvt_rne(__fmul_rn(i2f(lt), mul)) + ((const int16_t *)(rec + y.off_cb))[i];
-        }
-        if (low) {   // (cpu/ygg.cpp:360-377): the lane's row ii = warp of U', chunks warp * R2P/16 + j
-            const int R2P = R2T ? R2T : m.R2P;
-            const uint8_t *pu = rec + y.off_u + 16 * lane;
-            int la = 0;
-#pragma unroll
-            for (int j = 0; j < (R2T ? R2T / 16 : 4); j++)
-                if (R2T || j < R2P / 16)
-                    la = dot16(*(const uint4 *)(pu + 512 * (warp * (R2P / 16) + j)), *(const uint4 *)(sm.zl + 16 * j), la);
-            const float mu = y.mulv ? __ldg(y.mulv + i) : y.layer_input_scale;
-            acc += cvt_rne(__fmul_rn(i2f(la), mu));
-        }
-        if (i >= m.ns) acc = 0;   // padding of a narrower model: held at exactly 0
-        const int8_t qn = (int8_t)clampi(acc, -128, 127);
-        // the readout reads the new state of every lane: every thread has read the old state and the slot's rows first
-        sm.qnew[i] = qn;
-        if (!QS && o.acc != nullptr && i < ns) o.acc[(size_t)l * ns + i] = acc;
-        __syncthreads();
-        if (tid < ns) o.q_out[(size_t)l * ns + tid] = sm.qnew[tid];
-        if (!QS && o.routes != nullptr && tid == 0) o.routes[l] = r;
-        // -- readout (cpu/ygg.cpp:395-420): warp w takes rows [w R/4, (w + 1) R/4); the lane's word of row rr is
-        // P[rr][4 lane .. 4 lane + 3], word rr of its readout data
-        {
-            constexpr int RW = R / C;
-            const uint32_t qw = *(const uint32_t *)(sm.qnew + C * lane);
-            const uint32_t *pp = (const uint32_t *)(rec + y.off_p + 16 * lane);
-            int myz = 0;
-#pragma unroll
-            for (int j = 0; j < RW; j++) {
-                const int rr = warp * RW + j;
-                const uint32_t word = pp[128 * (rr / 4) + rr % 4];
-                const int z = __reduce_add_sync(kFull, __dp4a((int)word, (int)qw, 0));
-                if (lane == j) myz = z;
-            }
-            if (lane < RW) {
-                const int rr = warp * RW + lane;
-                const float mz = y.off_mz != kNone ? *(const float *)(rec + y.off_mz + 4 * rr) : y.readout_scale;
-                sm.zq[l * 32 + rr] = (int8_t)clampi(cvt_rne(__fmul_rn(i2f(myz), mz)), -127, 127);
-            }
-        }
-        __syncthreads();   // every read of the slot is done before the next layer's copy; zq of layer l is ready
-    }
-    // -- the heads (cpu/ygg.cpp:421-434) of every layer in layer order, for this warp's class groups; with the layer
-    // count fixed, the unembedding rows of every layer load together
     auto head = [&](const int l) {
         const DevLayer &y = m.layer[l];
         uint32_t zw[R / 4];
 #pragma unroll
-        for (int j = 0; j < R / 4; j++) zw[j] = *(const uint32_t *)(sm.zq + l * 32 + 4 * j);
+        for (int j = 0; j < R / 4; j++) zw[j] = *(const uint32_t *)(zq + l * 32 + 4 * j);
 #pragma unroll
         for (int c = 0; c < kCoopClasses; c++) {
             const int cg = warp + C * c;
@@ -333,38 +421,61 @@ __device__ __forceinline__ bool coop_token(const DevModel &m, const CoopSmem &sm
     } else {
         for (int l = 0; l < L; l++) head(l);
     }
+}
+
+// One token of the block's stream through every layer. The stream's old state is sm.qs ([L][n], shared memory; the
+// step kernel copies its input there first, in one pass); the new state goes to o.q_out ([L][ns] in global memory
+// for the step kernel; sm.qs itself for the score kernel, QS). lg: the logits of this lane's classes 32 cg + lane for
+// the class groups cg = warp + 4 c; every layer's head is added after the last layer (in layer order), so that no
+// layer waits on the unembedding's loads. Returns false if the bounded wait for a copy gave up.
+template <int BLK, int R, int R2T, int LT, int NVT, bool QS>
+__device__ __forceinline__ bool coop_token(const DevModel &m, const CoopSmem &sm, uint32_t &phase, int x,
+                                           const CoopOut &o, float (&lg)[kCoopClasses], int warp, int lane) {
+    constexpr int N = 128;
+    const int L = LT ? LT : m.L, ns = QS ? N : m.ns;
+    const BlockBar bar;
+#pragma unroll 1
+    for (int l = 0; l < L; l++) {
+        // the new state of the layer below is in qnew, and this layer's replaces it
+        if (!coop_layer<BLK, R, R2T, QS>(m, sm.ly, phase, l, x, sm.qnew, sm.qs + (size_t)l * N, sm.qnew,
+                                         sm.zq + l * 32, o.q_out + (size_t)l * ns,
+                                         o.acc ? o.acc + (size_t)l * ns : nullptr, o.routes ? o.routes + l : nullptr,
+                                         bar, warp, lane))
+            return false;
+    }
+    coop_heads<R, LT, NVT>(m, sm.zq, lg, warp, lane);
     return true;
 }
 
 // -log p(y) in f64 over the V classes of the block's stream (cpu/ygg.cpp:513-517), summed in the order of the
 // warp-per-stream kernels' nll_of: lane l adds the exps of its classes 32 cg + l in class-group order, then a butterfly
 // over the 32 lanes; the exps come from the warps holding each class group through shared memory. Every thread gets it.
-template <int NVT>
-__device__ __forceinline__ double coop_nll(const DevModel &m, const CoopSmem &sm, const float (&lg)[kCoopClasses],
-                                           int y, int warp, int lane) {
+template <int NVT, class Bar>
+__device__ __forceinline__ double coop_nll(const DevModel &m, float *red, double *exd, const float (&lg)[kCoopClasses],
+                                           int y, const Bar &bar, int warp, int lane) {
     const int nv = NVT ? NVT : m.VP / 32, V = m.V;
     float mx = -__int_as_float(0x7f800000);
 #pragma unroll
     for (int c = 0; c < kCoopClasses; c++) {
         const int cg = warp + kCoopWarps * c;
         if (cg < nv && 32 * cg + lane < V) mx = fmaxf(mx, lg[c]);
-        if (32 * cg + lane == y) sm.red[kCoopWarps] = lg[c];
+        if (32 * cg + lane == y) red[kCoopWarps] = lg[c];
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFull, mx, off));
-    if (lane == 0) sm.red[warp] = mx;
-    __syncthreads();
-    mx = fmaxf(fmaxf(sm.red[0], sm.red[1]), fmaxf(sm.red[2], sm.red[3]));
-    const float ly = sm.red[kCoopWarps];
+    if (lane == 0) red[warp] = mx;
+    bar.sync();
+    mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    const float ly = red[kCoopWarps];
 #pragma unroll
     for (int c = 0; c < kCoopClasses; c++) {
         const int cg = warp + kCoopWarps * c;
-        if (cg < nv) sm.exd[32 * cg + lane] = 32 * cg + lane < V ? exp((double)lg[c] - (double)mx) : 0.0;
+        if (cg < nv) exd[32 * cg + lane] = 32 * cg + lane < V ? exp((double)lg[c] - (double)mx) : 0.0;
     }
-    __syncthreads();
+    bar.sync();
     double se = 0.0;
     for (int cg = 0; cg < nv; cg++)
-        if (32 * cg + lane < V) se += sm.exd[32 * cg + lane];
+        if (32 * cg + lane < V) se += exd[32 * cg + lane];
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) se += __shfl_xor_sync(kFull, se, off);
     return log(se) + (double)mx - (double)ly;
@@ -375,7 +486,7 @@ __device__ __forceinline__ double coop_nll(const DevModel &m, const CoopSmem &sm
 __device__ __forceinline__ CoopSmem coop_init(uint8_t *smem, uint32_t rec_max) {
     CoopSmem sm = coop_carve(smem, rec_max, 128);
     if (threadIdx.x == 0) {
-        mbar_init(sm.bar, 1);
+        mbar_init(sm.ly.bar, 1);
         fence_mbar_init();
     }
     __syncthreads();
@@ -466,7 +577,7 @@ __global__ void __launch_bounds__(kCoopThreads, kCoopBlocksPerSm) coop_score_ker
                 if (tid == 0) atomicOr(m.status, kStatusTimeout);
                 return;
             }
-            nll += coop_nll<NVT>(m, sm, lg, tok[t + 1], warp, lane);
+            nll += coop_nll<NVT>(m, sm.red, sm.exd, lg, tok[t + 1], BlockBar{}, warp, lane);
         }
         if (tid == 0) bits[s] = nll / 0.69314718055994530942;
         if (state != nullptr)
@@ -478,10 +589,155 @@ __global__ void __launch_bounds__(kCoopThreads, kCoopBlocksPerSm) coop_score_ker
     }
 }
 
+// Rows of T tokens at the smallest batches, one row per block, the layers as a wavefront (cpu/ygg.cpp:500-519 is the
+// sequential loop it reorders). Layer l of token t needs only layer l - 1 of token t (the state it routes on) and
+// layer l of token t - 1 (its own old state), so the block's L + 1 warp groups form a pipeline: group g < L runs layer
+// g of token after token, and group L forms the logits and the NLL of each token once layer L - 1 has it. The new state
+// of layer g goes to group g + 1 through a ring of kPipeHand buffers; the readout codes of a token wait in a ring of
+// kPipeRing slots until group L reads them. Each group publishes how many tokens it has finished (`done`, a release
+// store after the group's last barrier of the token); a group starts token t once the group below has finished it and
+// the groups that read its rings have freed the slots it will write. Nothing else orders the groups, so a token
+// costs about the mean time of the slowest layer rather than the sum over the layers. Every operation and every sum's
+// order are those of the sequential kernels: the bits match.
+constexpr int kPipeRing = 16;   // readout-code slots (tokens between a layer and the NLL group)
+constexpr int kPipeHand = 4;    // new-state buffers between two layers
+
+__host__ __device__ constexpr uint32_t pipe_smem_bytes(uint32_t rec_max, int L) {
+    // L layer groups' buffers | top rows L x 4096 | hand L x kPipeHand x n | qs L x n | zq ring kPipeRing x L x 32 |
+    // red 32 | exd 8 x 32 x 8 | done 8 x 4 | abort 4
+    return L * coop_layer_smem_bytes(rec_max, 128) + L * 4096 + L * kPipeHand * 128 + L * 128 + kPipeRing * L * 32 +
+           32 + 8 * 32 * 8 + 8 * 4 + 16;
+}
+
+__device__ __forceinline__ int ld_acquire_shared(const int *p) {
+    int v;
+    asm volatile("ld.acquire.cta.shared::cta.b32 %0, [%1];" : "=r"(v) : "r"(smem_addr(p)) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_shared(int *p, int v) {
+    asm volatile("st.release.cta.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(p)), "r"(v) : "memory");
+}
+
+template <int BLK, int R, int R2T, int LT, int NVT>
+__global__ void __launch_bounds__(LT > 0 ? 128 * (LT + 1) : 1024, 1) pipe_score_kernel(
+    const __grid_constant__ DevModel m, int B, int T, const int32_t *__restrict__ tokens, int8_t *state,
+    double *__restrict__ bits, uint32_t rec_max) {
+    constexpr int N = 128;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int L = LT ? LT : m.L, V = m.V, ns = m.ns;
+    const int tid = threadIdx.x, nthr = blockDim.x;
+    const int grp = tid >> 7, warp = (tid >> 5) & 3, lane = tid & 31, gtid = tid & 127;
+    // carve: every layer group's own buffers, then what the groups share
+    uint8_t *p = smem;
+    CoopLayerSmem ly{};
+    for (int g = 0; g < L; g++) {
+        const CoopLayerSmem c = coop_carve_layer(p, rec_max, N);
+        if (g == grp) ly = c;
+    }
+    int8_t *top = (int8_t *)p; p += L * 4096;
+    int8_t *hand = (int8_t *)p; p += L * kPipeHand * N;
+    int8_t *qs = (int8_t *)p; p += L * N;
+    int8_t *zqr = (int8_t *)p; p += kPipeRing * L * 32;
+    float *red = (float *)p; p += 32;
+    double *exd = (double *)p; p += 8 * 32 * 8;
+    int *done = (int *)p; p += 8 * 4;
+    int *abort_flag = (int *)p;
+    if (grp < L && gtid == 0) {
+        mbar_init(ly.bar, 1);
+        fence_mbar_init();
+    }
+    {   // rows 1 .. 2^min(5, D) - 1 of every routed layer's router, for the first round of each of its tokens
+        const int nrows = (1 << (m.D < kCoopLook ? m.D : kCoopLook)) - 1;
+        for (int j = tid; j < L * 256; j += nthr) {
+            const int g = j >> 8, c = j & 255;
+            if (g > 0 && c < 8 * nrows)
+                *(uint4 *)(top + 4096 * g + 16 * c) = __ldg((const uint4 *)(m.layer[g].w + N + 16 * c));
+        }
+    }
+    __syncthreads();
+    const GroupBar bar{1u + (uint32_t)grp};
+    const bool routed = grp > 0 && grp < L;
+    uint32_t phase = 0;
+    for (int s = blockIdx.x; s < B; s += gridDim.x) {
+        const int32_t *tok = tokens + (size_t)s * T;
+        bool bad = false;
+        for (int t = tid; t < T; t += nthr) bad |= tok[t] < 0 || tok[t] >= V;
+        if (__syncthreads_or(bad)) {
+            if (tid == 0) {
+                atomicOr(m.status, kStatusBadToken);
+                bits[s] = __longlong_as_double(0x7ff8000000000000LL);
+            }
+            continue;
+        }
+        for (int j = tid; j < L * N; j += nthr) {
+            const int li = j / N, c = j % N;
+            qs[j] = (state != nullptr && c < ns) ? state[((size_t)s * L + li) * ns + c] : (int8_t)0;
+        }
+        if (tid < 8) done[tid] = 0;
+        if (tid == 0) *abort_flag = 0;
+        __syncthreads();
+        double nll = 0.0;
+        bool ok = true;
+        // the first router round's thresholds need only the token: each token's are loaded one token ahead
+        float tn[2] = {0.0f, 0.0f};
+        if (routed && T > 1) route_first_thr(m.layer[grp], tok[0], m.E, m.D, warp, lane, tn);
+        for (int t = 0; t + 1 < T; t++) {
+            const RouteFirst pre{top + 4096 * grp, {tn[0], tn[1]}};
+            if (routed && t + 2 < T) route_first_thr(m.layer[grp], tok[t + 1], m.E, m.D, warp, lane, tn);
+            // wait (the group's thread 0, bounded) until token t's input is ready and the ring slots it writes are
+            // free; the group then agrees on the outcome at its barrier, which also hands the acquired data on
+            if (gtid == 0) {
+                const long long t0 = clock64();
+                for (;;) {
+                    const bool in = grp == 0 || ld_acquire_shared(done + grp - 1) > t;
+                    const bool hand_free = grp >= L - 1 || ld_acquire_shared(done + grp + 1) > t - kPipeHand;
+                    const bool ring_free = grp == L || ld_acquire_shared(done + L) > t - kPipeRing;
+                    if (in && hand_free && ring_free) break;
+                    if (*(volatile int *)abort_flag != 0 || clock64() - t0 > kWaitCycles) {
+                        ok = false;
+                        break;
+                    }
+                }
+            }
+            if (!bar.all(ok)) {
+                ok = false;
+                break;
+            }
+            if (grp < L) {
+                const int8_t *qb = grp > 0 ? hand + ((grp - 1) * kPipeHand + t % kPipeHand) * N : nullptr;
+                int8_t *qnew = hand + (grp * kPipeHand + t % kPipeHand) * N;
+                int8_t *q = qs + grp * N;
+                ok = coop_layer<BLK, R, R2T, true, true>(m, ly, phase, grp, tok[t], qb, q, qnew,
+                                                         zqr + ((t % kPipeRing) * L + grp) * 32, q, nullptr, nullptr,
+                                                         bar, warp, lane, pre);
+                if (!ok) break;
+            } else {
+                float lg[kCoopClasses];
+                coop_heads<R, LT, NVT>(m, zqr + (t % kPipeRing) * L * 32, lg, warp, lane);
+                nll += coop_nll<NVT>(m, red, exd, lg, tok[t + 1], bar, warp, lane);
+            }
+            if (gtid == 0) st_release_shared(done + grp, t + 1);
+        }
+        if (!ok && gtid == 0) atomicExch(abort_flag, 1);
+        if (__syncthreads_or(!ok)) {
+            if (tid == 0) atomicOr(m.status, kStatusTimeout);
+            return;
+        }
+        if (grp == L && gtid == 0) bits[s] = nll / 0.69314718055994530942;
+        if (state != nullptr)
+            for (int j = tid; j < L * N; j += nthr) {
+                const int li = j / N, c = j % N;
+                if (c < ns) state[((size_t)s * L + li) * ns + c] = qs[j];
+            }
+        __syncthreads();
+    }
+}
+
 // ------------------------------------------------------------------------------------------------ launchers
 
 template <int BLK, int R, int R2T, int LT, int NVT> static SmemLimits &coop_step_limit() { static SmemLimits l{}; return l; }
 template <int BLK, int R, int R2T, int LT, int NVT> static SmemLimits &coop_score_limit() { static SmemLimits l{}; return l; }
+template <int BLK, int R, int R2T, int LT, int NVT> static SmemLimits &pipe_score_limit() { static SmemLimits l{}; return l; }
 
 template <int BLK, int R, int R2T, int LT, int NVT>
 static cudaError_t coop_step_t(const DevModel &dm, int B, const int32_t *tok, const int8_t *sin, int8_t *sout,
@@ -509,6 +765,19 @@ static cudaError_t coop_score_t(const DevModel &dm, int B, int T, const int32_t 
     return cudaGetLastError();
 }
 
+template <int BLK, int R, int R2T, int LT, int NVT>
+static cudaError_t pipe_score_t(const DevModel &dm, int B, int T, const int32_t *tok, int8_t *state, double *bits,
+                                uint32_t rec_max, int sm_count, cudaStream_t st) {
+    if (dm.L + 1 > 8) return cudaErrorInvalidValue;   // L + 1 groups of 128 threads in one block
+    const size_t smem = pipe_smem_bytes(rec_max, dm.L);
+    cudaError_t e = raise_smem_limit((const void *)pipe_score_kernel<BLK, R, R2T, LT, NVT>, smem,
+                                     pipe_score_limit<BLK, R, R2T, LT, NVT>());
+    if (e != cudaSuccess) return e;
+    const int grid = B < sm_count ? B : sm_count;
+    pipe_score_kernel<BLK, R, R2T, LT, NVT><<<grid, 128 * (dm.L + 1), smem, st>>>(dm, B, T, tok, state, bits, rec_max);
+    return cudaGetLastError();
+}
+
 // n = 128 only (the device layout's n; the d_state 96 extension included). Fast instances: c3 (V <= 32) and c4 / c5
 // (V = 256); generic instances read R2, L and the classes at run time.
 #define YGG_COOP_DISPATCH(FN, ...)                                                                            \
@@ -533,6 +802,11 @@ cudaError_t launch_coop_step(const DevModel &dm, int B, const int32_t *tok, cons
 cudaError_t launch_coop_score(const DevModel &dm, int B, int T, const int32_t *tok, int8_t *state, double *bits,
                               uint32_t rec_max, int sm_count, cudaStream_t st) {
     YGG_COOP_DISPATCH(coop_score_t, dm, B, T, tok, state, bits, rec_max, sm_count, st)
+}
+
+cudaError_t launch_pipe_score(const DevModel &dm, int B, int T, const int32_t *tok, int8_t *state, double *bits,
+                              uint32_t rec_max, int sm_count, cudaStream_t st) {
+    YGG_COOP_DISPATCH(pipe_score_t, dm, B, T, tok, state, bits, rec_max, sm_count, st)
 }
 
 }  // namespace ygg

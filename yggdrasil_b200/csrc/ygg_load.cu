@@ -34,6 +34,8 @@ cudaError_t launch_coop_step(const DevModel &dm, int B, const int32_t *tok, cons
                              float *lg, int32_t *routes, int32_t *acc, uint32_t rec_max, int sm_count, cudaStream_t st);
 cudaError_t launch_coop_score(const DevModel &dm, int B, int T, const int32_t *tok, int8_t *state, double *bits,
                               uint32_t rec_max, int sm_count, cudaStream_t st);
+cudaError_t launch_pipe_score(const DevModel &dm, int B, int T, const int32_t *tok, int8_t *state, double *bits,
+                              uint32_t rec_max, int sm_count, cudaStream_t st);
 }  // namespace ygg
 
 using namespace ygg;
@@ -44,6 +46,7 @@ struct LaunchCfg {
     DevModel dm;
     int slots_step, slots_score;
     bool coop;           // the step / score runs the latency kernels (ygg_coop.cu): 4 warps per stream
+    bool pipe;           // the score runs the layer wavefront (ygg_coop.cu): L + 1 groups of 4 warps per row
 };
 
 struct ygg_model {
@@ -54,8 +57,9 @@ struct ygg_model {
     // launch policy (ygg_step / ygg_score / grouped, by the batch B): B <= coop_max (n = 128) runs the latency
     // kernels, 4 warps per stream; B <= small_max stages records in shared memory (a warp per stream); B >= big_min
     // runs two streams per warp (fewest instructions per token); in between a warp per stream reads records from
-    // global memory. YGG_COOP (0 or the largest batch), YGG_LANES (16 / 32) and YGG_DIRECT (0 / 1) fix the choice.
-    int coop_max, small_max, big_min, force_lanes, force_direct;
+    // global memory. Scoring runs the layer wavefront up to pipe_max rows (n = 128, L <= 7). YGG_COOP (0 or the
+    // largest batch), YGG_PIPE (likewise), YGG_LANES (16 / 32) and YGG_DIRECT (0 / 1) fix the choice.
+    int coop_max, pipe_max, small_max, big_min, force_lanes, force_direct;
     uint8_t *d_blob;          // every device array
     size_t d_bytes;
     int *d_status;
@@ -480,11 +484,15 @@ int ygg_load(const void *file_bytes, size_t nbytes, int device, ygg_model **out)
     // the latency kernels win up to ~256 streams (c3 step: 14.2 against 16.5 us at 16 streams, 16.6 against 18.3 at
     // 256; c5 score rows: +18 % at 256); from ~512 the warp-per-stream kernels fill the GPU better
     m->coop_max = n == 128 ? 256 : 0;
+    // scoring rows: the layer wavefront (one row per SM at a time) wins up to about two rows per SM (c3 and c4 at
+    // 296 rows: 33 against 22 M tokens/s), the latency kernels from there (592 rows: 45 against 33 M)
+    m->pipe_max = n == 128 && L <= 7 ? 2 * m->sm_count : 0;
     m->big_min = 32768;
     m->force_lanes = 0;
     m->force_direct = -1;
     if (const char *e = getenv("YGG_SMALL_BATCH")) m->small_max = atoi(e);
     if (const char *e = getenv("YGG_COOP")) m->coop_max = n == 128 ? atoi(e) : 0;
+    if (const char *e = getenv("YGG_PIPE")) m->pipe_max = n == 128 && L <= 7 ? atoi(e) : 0;
     if (const char *e = getenv("YGG_BIG_BATCH")) m->big_min = atoi(e);
     if (const char *e = getenv("YGG_LANES")) m->force_lanes = atoi(e) == 16 ? 16 : atoi(e) == 32 ? 32 : 0;
     if (const char *e = getenv("YGG_DIRECT")) m->force_direct = atoi(e) != 0;
@@ -509,6 +517,7 @@ static LaunchCfg choose(const ygg_model *m, int batch) {
     LaunchCfg c = half ? m->half : m->warp;
     c.dm.direct = m->force_direct >= 0 ? m->force_direct : (batch > m->small_max ? 1 : 0);
     c.coop = !half && m->force_lanes == 0 && m->force_direct < 0 && batch <= m->coop_max;
+    c.pipe = !half && m->force_lanes == 0 && m->force_direct < 0 && batch <= m->pipe_max;
     return c;
 }
 
@@ -555,9 +564,11 @@ int ygg_score(const ygg_model *m, int batch, int steps, const int32_t *d_tokens,
     const LaunchCfg c = choose(m, batch);
     const DevModel &dm = c.dm;
     const cudaError_t e =
-        c.coop ? launch_coop_score(dm, batch, steps, d_tokens, d_state, d_bits, m->rec_max, m->sm_count,
-                                   (cudaStream_t)stream)
-               : launch_score(dm.n, dm.b, dm.R, dm.R2P, dm, batch, steps, d_tokens, d_state, d_bits, m->rec_max,
+        c.pipe   ? launch_pipe_score(dm, batch, steps, d_tokens, d_state, d_bits, m->rec_max, m->sm_count,
+                                     (cudaStream_t)stream)
+        : c.coop ? launch_coop_score(dm, batch, steps, d_tokens, d_state, d_bits, m->rec_max, m->sm_count,
+                                     (cudaStream_t)stream)
+                 : launch_score(dm.n, dm.b, dm.R, dm.R2P, dm, batch, steps, d_tokens, d_state, d_bits, m->rec_max,
                               m->warps, c.slots_score, m->grid_cap, (cudaStream_t)stream);
     restore_device(m, prev);
     return e == cudaSuccess ? YGG_OK : YGG_E_CUDA;
