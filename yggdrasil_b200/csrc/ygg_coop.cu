@@ -5,8 +5,9 @@
 //   - the router resolves 5 tree levels per round: the 31 rows of the 5-level subtree are read by the 4 warps (16 rows
 //     per 16-byte load of the block, 2 loads per lane), each warp ballots its rows' decisions, and the decisions meet in
 //     shared memory after one barrier; depth 13 takes 3 rounds (5 + 5 + 3) instead of 5;
-//   - when the last round starts, the records and table rows of its 2^lv <= 8 candidate leaves are prefetched into L2,
-//     so that the chosen record's bulk copy reads L2 rather than DRAM;
+//   - nothing is prefetched: an L2 prefetch of the last round's 8 candidate records cost more than it saved (a bulk
+//     prefetch holds the issuing warp until the copy engine has taken it; one batch-1 token took 3.35 us in the layer
+//     wavefront without it, 3.90 us with it split over the warps, 4.18 us from one warp);
 //   - the layer's arithmetic is split by the warps: warp w computes row 4 l + w of lane l (the 32-lane record layout
 //     keeps each warp's part of a lane in whole 16-byte chunks), the layer-input codes split their chunks over the
 //     warps, and the readout rows are split too; the new state meets in shared memory.
@@ -101,13 +102,6 @@ struct GroupBar {
     }
 };
 
-// Router descent of the block's stream (cpu/ygg.cpp:271-280), kCoopLook levels per round. Row k < 31 of a round's
-// subtree (heap order under the round's root ix: k = 0 is ix, k = 1-2 its children, ...) is read in load k / 16 by
-// warp (k % 16) / 4, row group k % 4 (the 8 lanes 8 g .. 8 g + 7, 16 bytes each). Each lane also reads its row's
-// threshold; one ballot per load and warp carries the decisions (bit 8 g), which the warps exchange in `dec`. qb: the
-// n new state bytes of the layer below. The records of the last round's candidate leaves go to L2 when there are at
-// most 8 of them. DT > 0: the depth fixed at compile time (= D), the rounds unrolled. Returns the leaf node index in
-// [E, 2E).
 // The first round without global loads (PRE): `top` holds rows 1-31 of the layer's router (row k + 1 at 128 k, shared
 // memory, copied once per block), and t the lane's two thresholds of token x (rows k + 1 for its k = 16 i + 4 warp +
 // lane / 8), loaded ahead of time by route_first_thr.
@@ -130,6 +124,12 @@ struct NoShadow {
     __device__ __forceinline__ void operator()() const {}
 };
 
+// Router descent of the block's stream (cpu/ygg.cpp:271-280), kCoopLook levels per round. Row k < 31 of a round's
+// subtree (heap order under the round's root ix: k = 0 is ix, k = 1-2 its children, ...) is read in load k / 16 by
+// warp (k % 16) / 4, row group k % 4 (the 8 lanes 8 g .. 8 g + 7, 16 bytes each). Each lane also reads its row's
+// threshold; one ballot per load and warp carries the decisions (bit 8 g), which the warps exchange in `dec`. qb: the
+// n new state bytes of the layer below. DT > 0: the depth fixed at compile time (= D), the rounds unrolled. Returns the leaf node index in
+// [E, 2E).
 //
 // shadow() runs in the second round (the first when D <= 5) between the issue of its loads and their use, and after()
 // once that round's barrier has passed: work that needs neither the loads nor the decisions hides in their latency.
@@ -156,12 +156,6 @@ __device__ __forceinline__ int route_coop(const DevLayer &y, int x, int E, int D
     // one round: the lv <= kCoopLook levels under ix, starting at depth d
     auto round = [&](const int d, const int lv) {
         const int nrows = (1 << lv) - 1;
-        if (d + lv == D && lv <= 3 && warp == 0 && lane < (1 << lv)) {   // the candidate leaves of the last round
-            const int leaf = ix * (1 << lv) + lane - E;
-            prefetch_l2(y.rec + (size_t)leaf * y.rec_bytes, y.rec_bytes);
-            if (y.table != nullptr)
-                prefetch_l2(y.table + ((size_t)leaf * y.table_rows + (y.table_rows > 1 ? x : 0)) * N, 2u * N);
-        }
         uint4 v[2];
         float t[2];
         if (PRE && d == 0) {
