@@ -271,7 +271,8 @@ def test_extension_state_layout(rec, case_model, torch):
 
 # the launch configurations the library chooses between by batch, each forced for every batch
 LAUNCH_CONFIGS = {
-    "pipe": {"YGG_PIPE": "1000000"},                       # scoring as a layer wavefront (n = 128, L <= 7)
+    "pipe": {"YGG_PIPE": "1000000"},                       # scoring as a layer wavefront, router and update groups
+    "pipe-whole": {"YGG_PIPE": "1000000", "YGG_PIPE_SPLIT": "0"},   # the wavefront with one group per layer
     "coop": {"YGG_COOP": "1000000", "YGG_PIPE": "0"},      # 4 warps per stream (n = 128; others keep the policy)
     "warp-staged": {"YGG_LANES": "32", "YGG_DIRECT": "0"},  # a warp per stream, records staged in shared memory
     "warp-direct": {"YGG_LANES": "32", "YGG_DIRECT": "1"},  # a warp per stream, records read from global memory
@@ -321,14 +322,17 @@ N128 = [c for c in CASES if c["shape"]["d_state"] == 128]
 
 @pytest.mark.parametrize("rec", N128, ids=_ids(N128))
 def test_pipe_score_rows_short_sequences_and_state(rec, case_model, torch, monkeypatch):
-    """The layer wavefront (one row per block, L + 1 warp groups): more rows than blocks (a block takes a second
-    row), sequences shorter than the pipeline's depth (T = 1, 2, 3), and a carried state in and out. Its bits must
-    equal the sequential latency kernel's exactly (same operations, same order) and the oracle's within rtol."""
+    """The layer wavefront (one row per block; a router and an update group per layer for L <= 4, else one group per
+    layer): more rows than blocks (a block takes a second row), sequences shorter than the pipeline's depth (T = 1, 2,
+    3), and a carried state in and out. Its bits must equal the sequential latency kernel's and the one-group-per-layer
+    wavefront's exactly (same operations, same order) and the oracle's within rtol."""
     path = case_model(rec)
     om = O.OracleModel(path)
     rng = np.random.default_rng(5)
     monkeypatch.setenv("YGG_PIPE", "1000000")
     pipe = load(path)
+    monkeypatch.setenv("YGG_PIPE_SPLIT", "0")
+    whole = load(path)
     monkeypatch.setenv("YGG_PIPE", "0")
     monkeypatch.setenv("YGG_COOP", "1000000")
     coop = load(path)
@@ -348,6 +352,10 @@ def test_pipe_score_rows_short_sequences_and_state(rec, case_model, torch, monke
         bc = torch.empty_like(bp)
         pipe.score_into(xd, sp, bp)
         coop.score_into(xd, sc, bc)
+        sw, bw = st0.clone(), torch.empty_like(bp)
+        whole.score_into(xd, sw, bw)
+        np.testing.assert_array_equal(bp.cpu().numpy(), bw.cpu().numpy(), err_msg=f"split vs whole bits, T={t}")
+        np.testing.assert_array_equal(sp.cpu().numpy(), sw.cpu().numpy(), err_msg=f"split vs whole state, T={t}")
         ost = ost0.copy()
         ob = om.score(x, ost)
         np.testing.assert_array_equal(bp.cpu().numpy(), bc.cpu().numpy(), err_msg=f"pipe vs coop bits, T={t}")

@@ -221,17 +221,98 @@ struct CoopOut {
     int32_t *acc;        // [L][ns] or null
 };
 
-// Layer l of one token of a group's stream (4 warps; `bar` joins them). PRE: the router's first round reads `pre`
-// (rows in shared memory, thresholds loaded ahead). qb: the new state of the layer below (l > 0;
-// shared memory); qold: this layer's old state (shared); qnew: where the layer's new state goes (shared; it may be qb
-// itself, which is read only before the record wait); q_out (+ acc_out, route_out when not null; QS: q_out is shared
-// memory with stride n): the new state's destination; zq: the layer's 32 readout-code bytes (shared). Returns false
-// (every thread of the group) if the bounded wait for the record's copy gave up.
-template <int BLK, int R, int R2T, bool QS, bool PRE = false, class Bar>
-__device__ __forceinline__ bool coop_layer(const DevModel &m, const CoopLayerSmem &sm, uint32_t &phase, int l, int x,
-                                           const int8_t *qb, const int8_t *qold, int8_t *qnew, int8_t *zq,
-                                           int8_t *q_out, int32_t *acc_out, int32_t *route_out, const Bar &bar,
-                                           int warp, int lane, const RouteFirst &pre = RouteFirst{}) {
+// Where a layer's record lands: the slot (record, then the table row at its end) and the mbarrier of its copy.
+struct CoopSlot {
+    uint8_t *slot;
+    uint32_t slot_bytes;
+    uint32_t bar;
+};
+
+// The layer-input codes zl[k] = clamp(rint((f32(V'_k . qb) * mv[k]) * rho)) (cpu/ygg.cpp:285-296) of layer y from qb,
+// the new state of the layer below: warp w dots chunks 2w, 2w+1 into zpart (coop_zl_partial); after a barrier of the
+// group, warp 0 adds the 4 partials (coop_zl_finish).
+template <int R2T>
+__device__ __forceinline__ void coop_zl_partial(const DevModel &m, const DevLayer &y, const int8_t *qb, int *zpart,
+                                                int warp, int lane) {
+    const int R2P = R2T ? R2T : m.R2P;
+    for (int k = lane; k < R2P; k += 32) {
+        const int8_t *vk = y.vl + (size_t)k * 16;
+        int a = 0;
+#pragma unroll
+        for (int j = 2 * warp; j < 2 * warp + 2; j++)
+            a = dot16(__ldg((const uint4 *)(vk + (size_t)j * R2P * 16)), *(const uint4 *)(qb + 16 * j), a);
+        zpart[warp * 64 + k] = a;
+    }
+}
+template <int R2T>
+__device__ __forceinline__ void coop_zl_finish(const DevModel &m, const DevLayer &y, float rho, const int *zpart,
+                                               int8_t *zl, int warp, int lane) {
+    if (warp != 0) return;
+    const int R2P = R2T ? R2T : m.R2P;
+    for (int k = lane; k < R2P; k += 32) {
+        const int a = zpart[k] + zpart[64 + k] + zpart[128 + k] + zpart[192 + k];
+        const float zf = __fmul_rn(__fmul_rn(i2f(a), __ldg(y.mv + k)), rho);
+        zl[k] = (int8_t)(k < m.R2 ? clampi(cvt_rne(zf), -127, 127) : 0);
+    }
+}
+
+// The copy of leaf r's record and its table row (for token x) into sl, issued by the calling thread; the slot's
+// earlier readers are done (the caller has synchronised with them).
+__device__ __forceinline__ void coop_issue_copy(const DevLayer &y, int x, int r, const CoopSlot &sl) {
+    constexpr int N = 128;
+    const bool has_table = y.table != nullptr;
+    uint8_t *trow = sl.slot + sl.slot_bytes - 2 * N;
+    fence_proxy_async();
+    mbar_expect_tx(sl.bar, y.rec_bytes + (has_table ? 2u * N : 0u));
+    bulk_g2s(smem_addr(sl.slot), y.rec + (size_t)r * y.rec_bytes, y.rec_bytes, sl.bar);
+    if (has_table)
+        bulk_g2s(smem_addr(trow), y.table + ((size_t)r * y.table_rows + (y.table_rows > 1 ? x : 0)) * N, 2u * N,
+                 sl.bar);
+}
+
+// The first half of layer l of one token of a group's stream (4 warps; `bar` joins them): for l > 0 rho, the router
+// (PRE: its first round reads `pre`, rows in shared memory and thresholds loaded ahead) and, in the shadow of its
+// loads, the layer-input codes into zl (zpart and dec are scratch); then the group's thread 0 starts the copy of the
+// chosen record and its table row into `sl` (l = 0: the token's own record). qb: the new state of the layer below
+// (shared memory). Returns the leaf r in [0, E).
+template <int R2T, bool PRE, class Bar>
+__device__ __forceinline__ int coop_route_part(const DevModel &m, int l, int x, const int8_t *qb, int8_t *zl,
+                                               int *zpart, uint32_t *dec, const CoopSlot &sl, const Bar &bar,
+                                               int warp, int lane, const RouteFirst &pre) {
+    constexpr int N = 128, C = kCoopWarps;
+    const DevLayer &y = m.layer[l];
+    const bool low = l > 0 && (R2T > 0 || m.R2 > 0);
+    int r = x;
+    float rho = 0.0f;
+    if (l > 0) {
+        const LaneQ<C> qv = load_q<C>(qb + C * lane);
+        rho = rms_rho<N, 32>(qv, y.r2b, y.rms_eps, m.inv_n, lane);
+        // the layer-input codes need only the state below and rho: formed while a router round's loads are in flight
+        auto zl_part = [&]() {
+            if (low) coop_zl_partial<R2T>(m, y, qb, zpart, warp, lane);
+        };
+        auto zl_sum = [&]() {
+            if (low) coop_zl_finish<R2T>(m, y, rho, zpart, zl, warp, lane);
+        };
+        r = (m.D == 13 ? route_coop<13, PRE>(y, x, m.E, m.D, qb, rho, dec, bar, warp, lane, pre, zl_part, zl_sum)
+                       : route_coop<0, PRE>(y, x, m.E, m.D, qb, rho, dec, bar, warp, lane, pre, zl_part, zl_sum)) -
+            m.E;
+    }
+    // -- the record and its table row into the slot (the group's thread 0)
+    if (warp == 0 && lane == 0) coop_issue_copy(y, x, r, sl);
+    return r;
+}
+
+// The second half: the wait (bounded) for the copy into `sl` (its mbarrier's phase `parity`), then row i = 4 lane +
+// warp of the update and the readout. zl: the layer-input codes; qold: this layer's old state (shared); qnew: where
+// the layer's new state goes (shared); q_out (+ acc_out, route_out = r when not null; QS: q_out is shared memory with
+// stride n): the new state's destination; zq: the layer's 32 readout-code bytes (shared). Returns false (every thread
+// of the group) if the wait gave up.
+template <int BLK, int R, int R2T, bool QS, class Bar>
+__device__ __forceinline__ bool coop_update_part(const DevModel &m, int l, int x, int r, const CoopSlot &sl,
+                                                 uint32_t parity, const int8_t *zl, const int8_t *qold, int8_t *qnew,
+                                                 int8_t *zq, int8_t *q_out, int32_t *acc_out, int32_t *route_out,
+                                                 const Bar &bar, int warp, int lane) {
     constexpr int N = 128, C = kCoopWarps;
     const int tid = 32 * warp + lane;
     const int i = C * lane + warp;               // the state coordinate this thread updates
@@ -239,54 +320,12 @@ __device__ __forceinline__ bool coop_layer(const DevModel &m, const CoopLayerSme
     const DevLayer &y = m.layer[l];
     const bool low = l > 0 && (R2T > 0 || m.R2 > 0);
     const bool has_table = y.table != nullptr;
-    int r = x;
-    float rho = 0.0f;
-    if (l > 0) {
-        const LaneQ<C> qv = load_q<C>(qb + C * lane);
-        rho = rms_rho<N, 32>(qv, y.r2b, y.rms_eps, m.inv_n, lane);
-        // the layer-input codes zl[k] = clamp(rint((f32(V'_k . qb) * mv[k]) * rho)) (cpu/ygg.cpp:285-296) need only
-        // the state below and rho: formed while a router round's loads are in flight. Warp w dots chunks 2w, 2w+1;
-        // after the round's barrier warp 0 adds the 4 partials.
-        const int R2P = R2T ? R2T : m.R2P;
-        auto zl_part = [&]() {
-            if (!low) return;
-            for (int k = lane; k < R2P; k += 32) {
-                const int8_t *vk = y.vl + (size_t)k * 16;
-                int a = 0;
-#pragma unroll
-                for (int j = 2 * warp; j < 2 * warp + 2; j++)
-                    a = dot16(__ldg((const uint4 *)(vk + (size_t)j * R2P * 16)), *(const uint4 *)(qb + 16 * j), a);
-                sm.zpart[warp * 64 + k] = a;
-            }
-        };
-        auto zl_sum = [&]() {
-            if (!low || warp != 0) return;
-            for (int k = lane; k < R2P; k += 32) {
-                const int a = sm.zpart[k] + sm.zpart[64 + k] + sm.zpart[128 + k] + sm.zpart[192 + k];
-                const float zf = __fmul_rn(__fmul_rn(i2f(a), __ldg(y.mv + k)), rho);
-                sm.zl[k] = (int8_t)(k < m.R2 ? clampi(cvt_rne(zf), -127, 127) : 0);
-            }
-        };
-        r = (m.D == 13 ? route_coop<13, PRE>(y, x, m.E, m.D, qb, rho, sm.dec, bar, warp, lane, pre, zl_part, zl_sum)
-                       : route_coop<0, PRE>(y, x, m.E, m.D, qb, rho, sm.dec, bar, warp, lane, pre, zl_part, zl_sum)) -
-            m.E;
-    }
-    // -- the record and its table row into the slot (the group's thread 0)
-    const int16_t *trow = (const int16_t *)(sm.slot + sm.slot_bytes - 2 * N);
-    if (tid == 0) {
-        fence_proxy_async();
-        mbar_expect_tx(sm.bar, y.rec_bytes + (has_table ? 2u * N : 0u));
-        bulk_g2s(smem_addr(sm.slot), y.rec + (size_t)r * y.rec_bytes, y.rec_bytes, sm.bar);
-        if (has_table)
-            bulk_g2s(smem_addr(trow), y.table + ((size_t)r * y.table_rows + (y.table_rows > 1 ? x : 0)) * N, 2u * N,
-                     sm.bar);
-    }
-    const bool ok = mbar_wait_bounded(sm.bar, phase);
-    phase ^= 1u;
+    const bool ok = mbar_wait_bounded(sl.bar, parity);
     if (!bar.all(ok)) return false;   // every wait ended (or one gave up); zl is ready
     // -- row i = 4 lane + warp: transition, input, layer input, saturation (cpu/ygg.cpp:312-389); the lane's data
     // for its row ii = warp sits in whole chunks of the 32-lane layout
-    const uint8_t *rec = sm.slot;
+    const uint8_t *rec = sl.slot;
+    const int16_t *trow = (const int16_t *)(sl.slot + sl.slot_bytes - 2 * N);
     int acc;
     {
         constexpr int kRowWords = BLK / 2;
@@ -332,7 +371,7 @@ __device__ __forceinline__ bool coop_layer(const DevModel &m, const CoopLayerSme
 #pragma unroll
         for (int j = 0; j < (R2T ? R2T / 16 : 4); j++)
             if (R2T || j < R2P / 16)
-                la = dot16(*(const uint4 *)(pu + 512 * (warp * (R2P / 16) + j)), *(const uint4 *)(sm.zl + 16 * j), la);
+                la = dot16(*(const uint4 *)(pu + 512 * (warp * (R2P / 16) + j)), *(const uint4 *)(zl + 16 * j), la);
         const float mu = y.mulv ? __ldg(y.mulv + i) : y.layer_input_scale;
         acc += cvt_rne(__fmul_rn(i2f(la), mu));
     }
@@ -366,6 +405,21 @@ __device__ __forceinline__ bool coop_layer(const DevModel &m, const CoopLayerSme
     }
     bar.sync();   // every read of the slot is done before the next copy into it; zq is ready
     return true;
+}
+
+// Layer l of one token of a group's stream: both halves, one after the other, through the group's one slot. qnew may
+// be qb itself (qb is read only before the record wait).
+template <int BLK, int R, int R2T, bool QS, bool PRE = false, class Bar>
+__device__ __forceinline__ bool coop_layer(const DevModel &m, const CoopLayerSmem &sm, uint32_t &phase, int l, int x,
+                                           const int8_t *qb, const int8_t *qold, int8_t *qnew, int8_t *zq,
+                                           int8_t *q_out, int32_t *acc_out, int32_t *route_out, const Bar &bar,
+                                           int warp, int lane, const RouteFirst &pre = RouteFirst{}) {
+    const CoopSlot sl{sm.slot, sm.slot_bytes, sm.bar};
+    const int r = coop_route_part<R2T, PRE>(m, l, x, qb, sm.zl, sm.zpart, sm.dec, sl, bar, warp, lane, pre);
+    const uint32_t parity = phase;
+    phase ^= 1u;
+    return coop_update_part<BLK, R, R2T, QS>(m, l, x, r, sl, parity, sm.zl, qold, qnew, zq, q_out, acc_out, route_out,
+                                             bar, warp, lane);
 }
 
 // The logits of a token (cpu/ygg.cpp:421-434): head_b, then every layer's head in layer order, for this warp's class
@@ -727,11 +781,226 @@ __global__ void __launch_bounds__(LT > 0 ? 128 * (LT + 1) : 1024, 1) pipe_score_
     }
 }
 
+// Rows of T tokens at the smallest batches, L <= 4: the layer wavefront with each routed layer split in two groups.
+// The update of layer l at token t needs only the leaf of token t (its record), the layer-input codes and the layer's
+// own state after token t - 1, while the route of token t + 1 needs only the state below of token t + 1. So a router
+// group (R_l) only routes, token after token, and the update group (U_l) does the rest: it copies the record of the
+// leaf R_l left in the token's slot, updates, reads out, and then forms what R_{l+1} and U_{l+1} need from the state it
+// just made (rho and the layer-input codes of layer l + 1), while R_l already routes the next tokens (up to
+// kSplitSlots ahead). Groups: U_0 (the token layer), R_1, U_1, ..., R_{L-1}, U_{L-1}, then the NLL group: 2L groups
+// of 128 threads. Progress counters (doneR, doneU, doneN) order them as in pipe_score_kernel:
+//   R_l waits until U_{l-1} has finished the token (its state, rho) and U_l has freed the token's slot;
+//   U_l waits until R_l has left the leaf, and until the readers of what it writes (the hand ring, the readout-code
+//   ring, the next layer's slot) are far enough;
+//   the NLL group waits for U_{L-1}.
+// A token then costs about the time of the router's rounds alone. Operations and sums in the same order as the
+// sequential kernels: the same bits.
+constexpr int kSplitSlots = 3;
+
+// a routed layer's slot for one token: record and table row | mbarrier 16 | layer-input codes 64 | leaf, rho 16
+__host__ __device__ constexpr uint32_t split_slot_bytes(uint32_t rec_max) { return coop_slot_bytes(rec_max, 128) + 96; }
+__host__ __device__ constexpr uint32_t split_smem_bytes(uint32_t rec_max, int L) {
+    // slots: U_0's one, then kSplitSlots per routed layer | zpart 1024 + dec 64 per layer | top rows L x 4096 |
+    // hand L x kPipeHand x n | qs L x n | zq ring kPipeRing x L x 32 | red 32 | exd 8 x 32 x 8 | doneR 8 x 4 |
+    // doneU 8 x 4 | doneN, abort 16
+    return (1 + (L - 1) * kSplitSlots) * split_slot_bytes(rec_max) + L * (1024 + 64) + L * 4096 +
+           L * kPipeHand * 128 + L * 128 + kPipeRing * L * 32 + 32 + 8 * 32 * 8 + 8 * 4 + 8 * 4 + 16;
+}
+
+template <int BLK, int R, int R2T, int LT, int NVT>
+__global__ void __launch_bounds__(LT > 0 ? 256 * LT : 1024, 1) split_score_kernel(
+    const __grid_constant__ DevModel m, int B, int T, const int32_t *__restrict__ tokens, int8_t *state,
+    double *__restrict__ bits, uint32_t rec_max) {
+    constexpr int N = 128, C = kCoopWarps;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int L = LT ? LT : m.L, V = m.V, ns = m.ns;
+    const int tid = threadIdx.x, nthr = blockDim.x;
+    const int grp = tid >> 7, warp = (tid >> 5) & 3, lane = tid & 31, gtid = tid & 127;
+    // the group's role: U_0 = 0, R_l = 2 l - 1, U_l = 2 l, NLL = 2 L - 1
+    const bool is_nll = grp == 2 * L - 1;
+    const bool is_r = !is_nll && (grp & 1);
+    const int layer = is_r ? (grp + 1) >> 1 : grp >> 1;
+    // carve. Slots and their mbarrier phases follow the block's running token count g (the phases carry over from row
+    // to row): layer l's slot for token g, and the parity of that use
+    const uint32_t cs = coop_slot_bytes(rec_max, N), sb = split_slot_bytes(rec_max);
+    uint8_t *slots = smem;
+    auto slot_base = [&](int l, int g) {
+        return slots + (size_t)sb * (l == 0 ? 0 : 1 + (l - 1) * kSplitSlots + g % kSplitSlots);
+    };
+    auto slot_of = [&](int l, int g) {
+        uint8_t *b = slot_base(l, g);
+        return CoopSlot{b, cs, smem_addr(b + cs)};
+    };
+    auto zl_of = [&](int l, int g) { return (int8_t *)(slot_base(l, g) + cs + 16); };
+    auto leaf_of = [&](int l, int g) { return (int *)(slot_base(l, g) + cs + 80); };
+    auto rho_of = [&](int l, int g) { return (float *)(slot_base(l, g) + cs + 84); };
+    auto parity_of = [&](int l, int g) { return (uint32_t)(l == 0 ? g : g / kSplitSlots) & 1u; };
+    uint8_t *p = slots + (size_t)sb * (1 + (L - 1) * kSplitSlots);
+    int *zpart = (int *)(p + (size_t)(layer < L ? layer : 0) * (1024 + 64));   // U_l's
+    uint32_t *dec = (uint32_t *)((uint8_t *)zpart + 1024);                      // R_l's
+    p += (size_t)L * (1024 + 64);
+    int8_t *top = (int8_t *)p; p += L * 4096;
+    int8_t *hand = (int8_t *)p; p += L * kPipeHand * N;
+    int8_t *qs = (int8_t *)p; p += L * N;
+    int8_t *zqr = (int8_t *)p; p += kPipeRing * L * 32;
+    float *red = (float *)p; p += 32;
+    double *exd = (double *)p; p += 8 * 32 * 8;
+    int *done_r = (int *)p; p += 8 * 4;
+    int *done_u = (int *)p; p += 8 * 4;
+    int *done_n = (int *)p;
+    int *abort_flag = done_n + 1;
+    // every slot's mbarrier (U_0's, then the routed layers')
+    for (int j = tid; j < 1 + (L - 1) * kSplitSlots; j += nthr) {
+        mbar_init(smem_addr(slots + (size_t)sb * j + cs), 1);
+        fence_mbar_init();
+    }
+    {   // rows 1 .. 2^min(5, D) - 1 of every routed layer's router, for the first round of each of its tokens
+        const int nrows = (1 << (m.D < kCoopLook ? m.D : kCoopLook)) - 1;
+        for (int j = tid; j < L * 256; j += nthr) {
+            const int g = j >> 8, c = j & 255;
+            if (g > 0 && c < 8 * nrows)
+                *(uint4 *)(top + 4096 * g + 16 * c) = __ldg((const uint4 *)(m.layer[g].w + N + 16 * c));
+        }
+    }
+    __syncthreads();
+    const GroupBar bar{1u + (uint32_t)grp};
+    int g0 = 0;   // tokens the block has run before this row
+    for (int s = blockIdx.x; s < B; s += gridDim.x) {
+        const int32_t *tok = tokens + (size_t)s * T;
+        bool bad = false;
+        for (int t = tid; t < T; t += nthr) bad |= tok[t] < 0 || tok[t] >= V;
+        if (__syncthreads_or(bad)) {
+            if (tid == 0) {
+                atomicOr(m.status, kStatusBadToken);
+                bits[s] = __longlong_as_double(0x7ff8000000000000LL);
+            }
+            continue;
+        }
+        for (int j = tid; j < L * N; j += nthr) {
+            const int li = j / N, c = j % N;
+            qs[j] = (state != nullptr && c < ns) ? state[((size_t)s * L + li) * ns + c] : (int8_t)0;
+        }
+        if (tid < 8) {
+            done_r[tid] = 0;
+            done_u[tid] = 0;
+        }
+        if (tid == 0) {
+            *done_n = 0;
+            *abort_flag = 0;
+        }
+        __syncthreads();
+        double nll = 0.0;
+        bool ok = true;
+        int inflight = -1;   // (an update group's thread 0) the token whose copy it issued and has not seen land
+        float tn[2] = {0.0f, 0.0f};
+        if (is_r && T > 1) route_first_thr(m.layer[layer], tok[0], m.E, m.D, warp, lane, tn);
+        for (int t = 0; t + 1 < T; t++) {
+            const int g = g0 + t;
+            const RouteFirst pre{top + 4096 * layer, {tn[0], tn[1]}};
+            if (is_r && t + 2 < T) route_first_thr(m.layer[layer], tok[t + 1], m.E, m.D, warp, lane, tn);
+            // wait (the group's thread 0, bounded) for this role's inputs and free ring slots; the group agrees at its
+            // barrier, which also hands the acquired data to its other threads
+            if (gtid == 0) {
+                const long long t0 = clock64();
+                for (;;) {
+                    bool go;
+                    if (is_nll) {
+                        go = ld_acquire_shared(done_u + L - 1) > t;
+                    } else if (is_r) {
+                        go = ld_acquire_shared(done_u + layer - 1) > t &&
+                             ld_acquire_shared(done_u + layer) > t - kSplitSlots;
+                    } else {
+                        go = (layer == 0 || ld_acquire_shared(done_r + layer) > t) &&
+                             (layer == L - 1 || (ld_acquire_shared(done_r + layer + 1) > t - kPipeHand &&
+                                                 ld_acquire_shared(done_u + layer + 1) > t - kSplitSlots)) &&
+                             ld_acquire_shared(done_n) > t - kPipeRing;
+                    }
+                    if (go) break;
+                    if (*(volatile int *)abort_flag != 0 || clock64() - t0 > kWaitCycles) {
+                        ok = false;
+                        break;
+                    }
+                }
+            }
+            if (!bar.all(ok)) {
+                ok = false;
+                break;
+            }
+            const int x = tok[t];
+            if (is_nll) {
+                float lg[kCoopClasses];
+                coop_heads<R, LT, NVT>(m, zqr + (t % kPipeRing) * L * 32, lg, warp, lane);
+                nll += coop_nll<NVT>(m, red, exd, lg, tok[t + 1], bar, warp, lane);
+                if (gtid == 0) st_release_shared(done_n, t + 1);
+            } else if (is_r) {
+                // the route alone (cpu/ygg.cpp:271-280): the state below and rho come from U_{l-1}
+                const DevLayer &y = m.layer[layer];
+                const int8_t *qb = hand + ((layer - 1) * kPipeHand + t % kPipeHand) * N;
+                const float rho = *rho_of(layer, g);
+                const int r = (m.D == 13 ? route_coop<13, true>(y, x, m.E, m.D, qb, rho, dec, bar, warp, lane, pre)
+                                         : route_coop<0, true>(y, x, m.E, m.D, qb, rho, dec, bar, warp, lane, pre)) -
+                              m.E;
+                if (gtid == 0) {
+                    *leaf_of(layer, g) = r;
+                    st_release_shared(done_r + layer, t + 1);
+                }
+            } else {
+                const DevLayer &y = m.layer[layer];
+                const CoopSlot sl = slot_of(layer, g);
+                // the record of the leaf (the token's own for the token layer) into the token's slot
+                if (gtid == 0) {
+                    coop_issue_copy(y, x, layer == 0 ? x : *leaf_of(layer, g), sl);
+                    inflight = t;
+                }
+                int8_t *q = qs + layer * N;
+                int8_t *qnew = hand + (layer * kPipeHand + t % kPipeHand) * N;
+                ok = coop_update_part<BLK, R, R2T, true>(m, layer, x, 0, sl, parity_of(layer, g), zl_of(layer, g), q,
+                                                         qnew, zqr + ((t % kPipeRing) * L + layer) * 32, q, nullptr,
+                                                         nullptr, bar, warp, lane);
+                if (!ok) break;
+                inflight = -1;
+                if (layer + 1 < L) {   // rho and the layer-input codes of layer + 1 from the new state (cpu/ygg.cpp:248-296)
+                    const DevLayer &yn = m.layer[layer + 1];
+                    const LaneQ<C> qv = load_q<C>(qnew + C * lane);
+                    const float rho = rms_rho<N, 32>(qv, yn.r2b, yn.rms_eps, m.inv_n, lane);
+                    if (gtid == 0) *rho_of(layer + 1, g) = rho;
+                    if (R2T > 0 || m.R2 > 0) {
+                        coop_zl_partial<R2T>(m, yn, qnew, zpart, warp, lane);
+                        bar.sync();
+                        coop_zl_finish<R2T>(m, yn, rho, zpart, zl_of(layer + 1, g), warp, lane);
+                    }
+                }
+                __syncwarp();   // warp 0 wrote the codes; its lane 0 publishes them
+                if (gtid == 0) st_release_shared(done_u + layer, t + 1);
+            }
+        }
+        if (!ok && gtid == 0) atomicExch(abort_flag, 1);
+        if (__syncthreads_or(!ok)) {
+            // every group has left its loop: an update group whose copy did not land waits for it (bounded), so that
+            // none is in flight into shared memory when the block exits (a copy is issued and awaited by the same
+            // group, token by token)
+            if (inflight >= 0)
+                mbar_wait_bounded(slot_of(layer, g0 + inflight).bar, parity_of(layer, g0 + inflight));
+            if (tid == 0) atomicOr(m.status, kStatusTimeout);
+            return;
+        }
+        if (is_nll && gtid == 0) bits[s] = nll / 0.69314718055994530942;
+        if (state != nullptr)
+            for (int j = tid; j < L * N; j += nthr) {
+                const int li = j / N, c = j % N;
+                if (c < ns) state[((size_t)s * L + li) * ns + c] = qs[j];
+            }
+        g0 += T > 1 ? T - 1 : 0;
+        __syncthreads();
+    }
+}
+
 // ------------------------------------------------------------------------------------------------ launchers
 
 template <int BLK, int R, int R2T, int LT, int NVT> static SmemLimits &coop_step_limit() { static SmemLimits l{}; return l; }
 template <int BLK, int R, int R2T, int LT, int NVT> static SmemLimits &coop_score_limit() { static SmemLimits l{}; return l; }
 template <int BLK, int R, int R2T, int LT, int NVT> static SmemLimits &pipe_score_limit() { static SmemLimits l{}; return l; }
+template <int BLK, int R, int R2T, int LT, int NVT> static SmemLimits &split_score_limit() { static SmemLimits l{}; return l; }
 
 template <int BLK, int R, int R2T, int LT, int NVT>
 static cudaError_t coop_step_t(const DevModel &dm, int B, const int32_t *tok, const int8_t *sin, int8_t *sout,
@@ -761,13 +1030,21 @@ static cudaError_t coop_score_t(const DevModel &dm, int B, int T, const int32_t 
 
 template <int BLK, int R, int R2T, int LT, int NVT>
 static cudaError_t pipe_score_t(const DevModel &dm, int B, int T, const int32_t *tok, int8_t *state, double *bits,
-                                uint32_t rec_max, int sm_count, cudaStream_t st) {
+                                uint32_t rec_max, int sm_count, bool split, cudaStream_t st) {
+    const int grid = B < sm_count ? B : sm_count;
+    if (split && 2 * dm.L <= 8) {   // 2L groups of 128 threads: a router and an update group per routed layer
+        const size_t smem = split_smem_bytes(rec_max, dm.L);
+        cudaError_t e = raise_smem_limit((const void *)split_score_kernel<BLK, R, R2T, LT, NVT>, smem,
+                                         split_score_limit<BLK, R, R2T, LT, NVT>());
+        if (e != cudaSuccess) return e;
+        split_score_kernel<BLK, R, R2T, LT, NVT><<<grid, 256 * dm.L, smem, st>>>(dm, B, T, tok, state, bits, rec_max);
+        return cudaGetLastError();
+    }
     if (dm.L + 1 > 8) return cudaErrorInvalidValue;   // L + 1 groups of 128 threads in one block
     const size_t smem = pipe_smem_bytes(rec_max, dm.L);
     cudaError_t e = raise_smem_limit((const void *)pipe_score_kernel<BLK, R, R2T, LT, NVT>, smem,
                                      pipe_score_limit<BLK, R, R2T, LT, NVT>());
     if (e != cudaSuccess) return e;
-    const int grid = B < sm_count ? B : sm_count;
     pipe_score_kernel<BLK, R, R2T, LT, NVT><<<grid, 128 * (dm.L + 1), smem, st>>>(dm, B, T, tok, state, bits, rec_max);
     return cudaGetLastError();
 }
@@ -799,8 +1076,8 @@ cudaError_t launch_coop_score(const DevModel &dm, int B, int T, const int32_t *t
 }
 
 cudaError_t launch_pipe_score(const DevModel &dm, int B, int T, const int32_t *tok, int8_t *state, double *bits,
-                              uint32_t rec_max, int sm_count, cudaStream_t st) {
-    YGG_COOP_DISPATCH(pipe_score_t, dm, B, T, tok, state, bits, rec_max, sm_count, st)
+                              uint32_t rec_max, int sm_count, bool split, cudaStream_t st) {
+    YGG_COOP_DISPATCH(pipe_score_t, dm, B, T, tok, state, bits, rec_max, sm_count, split, st)
 }
 
 }  // namespace ygg

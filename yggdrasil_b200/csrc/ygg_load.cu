@@ -35,7 +35,7 @@ cudaError_t launch_coop_step(const DevModel &dm, int B, const int32_t *tok, cons
 cudaError_t launch_coop_score(const DevModel &dm, int B, int T, const int32_t *tok, int8_t *state, double *bits,
                               uint32_t rec_max, int sm_count, cudaStream_t st);
 cudaError_t launch_pipe_score(const DevModel &dm, int B, int T, const int32_t *tok, int8_t *state, double *bits,
-                              uint32_t rec_max, int sm_count, cudaStream_t st);
+                              uint32_t rec_max, int sm_count, bool split, cudaStream_t st);
 }  // namespace ygg
 
 using namespace ygg;
@@ -57,9 +57,11 @@ struct ygg_model {
     // launch policy (ygg_step / ygg_score / grouped, by the batch B): B <= coop_max (n = 128) runs the latency
     // kernels, 4 warps per stream; B <= small_max stages records in shared memory (a warp per stream); B >= big_min
     // runs two streams per warp (fewest instructions per token); in between a warp per stream reads records from
-    // global memory. Scoring runs the layer wavefront up to pipe_max rows (n = 128, L <= 7). YGG_COOP (0 or the
-    // largest batch), YGG_PIPE (likewise), YGG_LANES (16 / 32) and YGG_DIRECT (0 / 1) fix the choice.
+    // global memory. Scoring runs the layer wavefront up to pipe_max rows (n = 128, L <= 7), with a router and an
+    // update group per layer when L <= 4 (pipe_split). YGG_COOP (0 or the largest batch), YGG_PIPE (likewise),
+    // YGG_PIPE_SPLIT (0 / 1), YGG_LANES (16 / 32) and YGG_DIRECT (0 / 1) fix the choice.
     int coop_max, pipe_max, small_max, big_min, force_lanes, force_direct;
+    bool pipe_split;
     uint8_t *d_blob;          // every device array
     size_t d_bytes;
     int *d_status;
@@ -493,6 +495,8 @@ int ygg_load(const void *file_bytes, size_t nbytes, int device, ygg_model **out)
     if (const char *e = getenv("YGG_SMALL_BATCH")) m->small_max = atoi(e);
     if (const char *e = getenv("YGG_COOP")) m->coop_max = n == 128 ? atoi(e) : 0;
     if (const char *e = getenv("YGG_PIPE")) m->pipe_max = n == 128 && L <= 7 ? atoi(e) : 0;
+    m->pipe_split = true;
+    if (const char *e = getenv("YGG_PIPE_SPLIT")) m->pipe_split = atoi(e) != 0;
     if (const char *e = getenv("YGG_BIG_BATCH")) m->big_min = atoi(e);
     if (const char *e = getenv("YGG_LANES")) m->force_lanes = atoi(e) == 16 ? 16 : atoi(e) == 32 ? 32 : 0;
     if (const char *e = getenv("YGG_DIRECT")) m->force_direct = atoi(e) != 0;
@@ -565,7 +569,7 @@ int ygg_score(const ygg_model *m, int batch, int steps, const int32_t *d_tokens,
     const DevModel &dm = c.dm;
     const cudaError_t e =
         c.pipe   ? launch_pipe_score(dm, batch, steps, d_tokens, d_state, d_bits, m->rec_max, m->sm_count,
-                                     (cudaStream_t)stream)
+                                     m->pipe_split, (cudaStream_t)stream)
         : c.coop ? launch_coop_score(dm, batch, steps, d_tokens, d_state, d_bits, m->rec_max, m->sm_count,
                                      (cudaStream_t)stream)
                  : launch_score(dm.n, dm.b, dm.R, dm.R2P, dm, batch, steps, d_tokens, d_state, d_bits, m->rec_max,
