@@ -13,6 +13,12 @@
 //     warps, and the readout rows are split too; the new state meets in shared memory.
 // Every integer and f32 operation, and its order, is that of the warp-per-stream kernels (ygg_step.cu), so routes,
 // states and logits are the same bits.
+//
+// Scoring rows (tokens known in advance) at the smallest batches runs the layers of one row as a wavefront instead:
+// layer l of token t needs only layer l - 1 of token t and layer l of token t - 1, so one block holds a warp group per
+// layer role, each on its own token, ordered by progress counters in shared memory. split_score_kernel (L <= 4) gives
+// every routed layer a router group and an update group; pipe_score_kernel (L <= 7) one group per layer. A token of a
+// row then costs about one layer's route instead of all layers (c3: 2.8 against 8.6 us per token at batch 1).
 #include <cuda_runtime.h>
 #include <stdint.h>
 

@@ -486,9 +486,10 @@ int ygg_load(const void *file_bytes, size_t nbytes, int device, ygg_model **out)
     // the latency kernels win up to ~256 streams (c3 step: 14.2 against 16.5 us at 16 streams, 16.6 against 18.3 at
     // 256; c5 score rows: +18 % at 256); from ~512 the warp-per-stream kernels fill the GPU better
     m->coop_max = n == 128 ? 256 : 0;
-    // scoring rows: the layer wavefront (one row per SM at a time) wins up to about two rows per SM (c3 and c4 at
-    // 296 rows: 33 against 22 M tokens/s), the latency kernels from there (592 rows: 45 against 33 M)
-    m->pipe_max = n == 128 && L <= 7 ? 2 * m->sm_count : 0;
+    // scoring rows: the layer wavefront (one row per SM at a time, ~54 M tokens/s on c3 at any count of rows) wins up
+    // to about four rows per SM (592 rows: 53.5 against 45.4 M tokens/s), the other kernels from there (888 rows:
+    // 68.3 against 53.8 M)
+    m->pipe_max = n == 128 && L <= 7 ? 4 * m->sm_count : 0;
     m->big_min = 32768;
     m->force_lanes = 0;
     m->force_direct = -1;
