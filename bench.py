@@ -563,9 +563,9 @@ def main():
         ems = float(t.item())
     e2e = B * ke * world / (ems / 1e3)
 
-    # ---- batch 1, rank 0 only: (a) device time per token of one stream through the fused score kernel (state on
-    # chip, the f64 softmax/NLL of every token included, as `ygg time` includes its softmax); (b) one step() launch
-    # per token through the C-ABI from Python (launch-bound). The warm-up runs other tokens than the timed ones, so
+    # ---- batch 1, rank 0 only: (a) device time per token of one stream scoring a row (the launch policy runs the
+    # layer wavefront for n = 128; state on chip, the f64 softmax/NLL of every token included, as `ygg time` includes
+    # its softmax); (b) one step() launch per token through the C-ABI from Python (launch-bound). The warm-up runs other tokens than the timed ones, so
     # the timed tokens find their leaves' records where a new stream would (mostly not in L2).
     b1 = b1_step = None
     if rank == 0 and args.batch1_steps:
