@@ -53,55 +53,23 @@ def peaks():
 
 
 def build_model_file(workload, seed, rank, world, dist):
-    """The workload's model file, written once (rank 0) into a shared temp dir."""
+    """The workload's model file, written once (rank 0) into a shared temp dir. The Zipf-calibrated models (c4, c4f;
+    c5 scores c4's) take their router thresholds from tests/golden/zipf_thresholds.npz, the same fixture the parity
+    tests pin to the reference's int_forward (tests/golden/make_golden.py calibrates them)."""
     from yggdrasil_b200 import synth
     from yggdrasil_b200.ygg1 import write_model
     w = synth.WORKLOADS[workload]
     d = Path(os.environ.get("YGG_BENCH_DIR", tempfile.gettempdir())) / "ygg_bench"
     d.mkdir(parents=True, exist_ok=True)
-    path = d / f"{w.model or workload}_s{seed}.bin"
+    path = d / f"{w.model or workload}_s{seed}_v2.bin"
     if rank == 0 and not path.exists():
         tmp = path.with_suffix(f".tmp{os.getpid()}")
-        layers = synth.workload_layers(w, seed=seed)
-        ob = np.linspace(-1, 1, w.shape.vocab)
-        if w.leaves == "zipf":
-            calibrate_zipf(w, layers, ob, tmp, seed)
-        write_model(layers, ob, tmp, extended=w.extended)
+        layers = synth.workload_layers(w, seed=seed, thresholds=synth.zipf_thresholds_of(w, ROOT))
+        write_model(layers, np.linspace(-1, 1, w.shape.vocab), tmp, extended=w.extended)
         os.replace(tmp, path)
     if world > 1:
         dist.barrier()
     return w, path
-
-
-def calibrate_zipf(w, layers, ob, tmp, seed, streams=65536, prime=48, snapshots=(48, 56, 64), s=1.1):
-    """Set each routed layer's thresholds (the same for every token) so that its leaf usage follows Zipf(s) over a
-    seeded random leaf order: layer by layer, run the model on the GPU (this library's step) to sample the new state
-    of the layer below in steady state, then place each node's threshold at the score quantile that sends the Zipf
-    share of its subtree mass to the right (synth.zipf_thresholds). Untimed set-up of the benchmark model."""
-    import torch
-
-    from yggdrasil_b200 import Yggdrasil, synth
-    from yggdrasil_b200.ygg1 import write_model
-    E = 2 ** w.shape.router_depth
-    for l in range(1, len(layers)):
-        write_model(layers, ob, tmp, extended=w.extended)
-        model = Yggdrasil.load(tmp, backend="b200")
-        dev = model.device
-        x = torch.as_tensor(synth.workload_tokens(w, max(snapshots), streams, seed=77)).to(dev)
-        st = model.init_state(streams)
-        lg = torch.empty(streams, model.vocab, dtype=torch.float32, device=dev)
-        qb = []
-        for t in range(max(snapshots)):
-            model.step_into(x[t], st, st, lg)
-            if t + 1 in snapshots:
-                qb.append(st[:, l - 1].cpu().numpy())
-        del model
-        torch.cuda.empty_cache()
-        qb = np.concatenate(qb)
-        q = layers[l]
-        rho = synth.rho_f32(qb, q.rms_eps, q.state_r2)
-        thr = synth.zipf_thresholds(q.router_weight, qb, rho, synth.zipf_leaf_probs(E, s, seed + 100 + l))
-        q.router_threshold = np.ascontiguousarray(np.broadcast_to(thr, (w.shape.vocab, E - 1)), dtype=np.float32)
 
 
 class ClockSampler:
@@ -430,6 +398,10 @@ def main():
     ap.add_argument("--grouped", action="store_true", help="score mode: also time the leaf-grouped tensor-core path")
     ap.add_argument("--min-group", type=int, default=64, help="streams a leaf needs for the tensor-core path")
     ap.add_argument("--sweep", default="", help="comma-separated streams per GPU: a batch sweep, one line per size")
+    ap.add_argument("--global-streams", type=int, default=65536,
+                    help="strong scaling: also time this many streams split over the N GPUs (0: off)")
+    ap.add_argument("--extra", default="c4", help="also measure this workload at 65 536 and 262 144 streams per GPU "
+                    "(and 262 144 global under torchrun), with its e2e through step(); '' to skip")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -458,149 +430,58 @@ def main():
     B = args.streams or min(w.streams, 65536)
     K, W = args.steps, args.warmup
     dev = torch.device("cuda", local)
-    model = Yggdrasil.load(path, backend="b200", device=dev)
     stream = torch.cuda.current_stream(dev)
-
-    # ---- inputs resident in HBM: K + W steps of tokens for this rank's streams
-    x = synth.workload_tokens(w, K + W, B, seed=rank)            # (steps, B)
-    d_tok = torch.as_tensor(x).to(dev)
-    state = model.init_state(B)
-    logits = torch.empty(B, model.vocab, dtype=torch.float32, device=dev)
-
-    # steady state: streams carry `prime` tokens of history before anything is timed (from a zero state the first
-    # steps route on the token alone); then the realised leaf usage of the routed layers, as the effective number
-    # of leaves per layer (exp of the entropy of the leaf histogram)
-    xp = torch.as_tensor(synth.workload_tokens(w, max(args.prime, 1), B, seed=10_000 + rank)).to(dev)
-    for i in range(args.prime):
-        model.step_into(xp[i], state, state, logits)
-    _, _, routes, _ = model.step_debug(d_tok[0], state)
-    r = routes.cpu().numpy()
-    eff = []
-    for l in range(1, model.layers):
-        h = np.bincount(r[:, l], minlength=1 << model.depth).astype(np.float64)
-        p = h[h > 0] / h.sum()
-        eff.append(round(float(np.exp(-(p * np.log(p)).sum())), 1))
-
-    for i in range(W):
-        model.step_into(d_tok[i], state, state, logits)
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     try:
         gpu_id = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
     except Exception:  # noqa: BLE001
         gpu_id = str(local)
+    peak, kind = peaks()
+    traffic_tab = load_traffic()
+
+    # ---- the headline: the workload at B streams per GPU (weak scaling), kernel-only, clocks sampled
     with ClockSampler(gpu_id) as clk:
-        e0.record(stream)
-        for i in range(K):
-            model.step_into(d_tok[W + i], state, state, logits)
-        e1.record(stream)
-        torch.cuda.synchronize(dev)
-    ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    model.status()
-    tokens = B * K * world
-    value = tokens / (ms / 1e3)
-    per_launch_ms = ms / K
+        head = measure_step(args, w, path, B, K, W, rank, world, dist, dev, stream, keep_model=True)
+    model = head.pop("model")
 
-    # ---- end to end through the public API: pinned host tokens in, logits out, every step. A serving loop with two
-    # buffers each way: while step i runs (step_into, in place), the tokens of step i + 1 go up on one copy stream and
-    # the logits of step i - 1 come down on another; events keep each buffer's writer after its last reader.
-    ke = min(K, 256)
-    h_tok = torch.as_tensor(x[W:W + ke]).pin_memory()
-    h_lg = [torch.empty(B, model.vocab, dtype=torch.float32).pin_memory() for _ in range(2)]
-    d_tokb = [torch.empty(B, dtype=torch.int32, device=dev) for _ in range(2)]
-    d_lg = [torch.empty(B, model.vocab, dtype=torch.float32, device=dev) for _ in range(2)]
-    up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    ev = lambda: [torch.cuda.Event() for _ in range(2)]  # noqa: E731
-    uploaded, stepped, downloaded = ev(), ev(), ev()
+    # ---- end to end through the public API, host-logits serving loop (the headline's e2e)
+    e2e, ke = e2e_serving_loop(model, w, head["state"], B, K, W, rank, world, dist, dev, stream)
 
-    def upload(i):
-        j = i % 2
-        up.wait_event(stepped[j])                  # the step that read this buffer (i - 2) is done
-        with torch.cuda.stream(up):
-            d_tokb[j].copy_(h_tok[i % ke], non_blocking=True)
-            uploaded[j].record(up)
-
-    def e2e_loop(n, st):
-        for e in stepped + downloaded:
-            e.record(stream)
-        upload(0)
-        for i in range(n):
-            j = i % 2
-            stream.wait_event(uploaded[j])
-            stream.wait_event(downloaded[j])       # the logits buffer's previous download is done
-            model.step_into(d_tokb[j], st, st, d_lg[j])
-            stepped[j].record(stream)
-            if i + 1 < n:
-                upload(i + 1)
-            down.wait_event(stepped[j])
-            with torch.cuda.stream(down):
-                h_lg[j].copy_(d_lg[j], non_blocking=True)
-                downloaded[j].record(down)
-        stream.wait_stream(down)
-
-    st = state.clone()
-    e2e_loop(W, st)
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
-    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a0.record(stream)
-    e2e_loop(ke, st)
-    a1.record(stream)
-    torch.cuda.synchronize(dev)
-    ems = a0.elapsed_time(a1)
-    if world > 1:
-        t = torch.tensor([ems], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ems = float(t.item())
-    e2e = B * ke * world / (ems / 1e3)
-
-    # ---- batch 1, rank 0 only: (a) device time per token of one stream scoring a row (the launch policy runs the
-    # layer wavefront for n = 128; state on chip, the f64 softmax/NLL of every token included, as `ygg time` includes
-    # its softmax); (b) one step() launch per token through the C-ABI from Python (launch-bound). The warm-up runs other tokens than the timed ones, so
-    # the timed tokens find their leaves' records where a new stream would (mostly not in L2).
+    # ---- batch 1 (rank 0): a row scored through the layer wavefront, and one step() call per token
     b1 = b1_step = None
     if rank == 0 and args.batch1_steps:
-        n1 = args.batch1_steps
-        t1 = torch.as_tensor(synth.workload_tokens(w, 1, n1 + 1, seed=99)).to(dev)
-        t1w = torch.as_tensor(synth.workload_tokens(w, 1, n1 + 1, seed=98)).to(dev)
-        bits1 = torch.empty(1, dtype=torch.float64, device=dev)
-        for i in range(W):
-            model.score_into(t1w, None, bits1)
-        torch.cuda.synchronize(dev)
-        b0, b1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        b0.record(stream)
-        model.score_into(t1, None, bits1)
-        b1e.record(stream)
-        torch.cuda.synchronize(dev)
-        b1 = b0.elapsed_time(b1e) * 1e3 / n1
-        s1 = model.init_state(1)
-        lg1 = torch.empty(1, model.vocab, dtype=torch.float32, device=dev)
-        for i in range(W):
-            model.step_into(t1w[0, i:i + 1], s1, s1, lg1)
-        torch.cuda.synchronize(dev)
-        b0.record(stream)
-        for i in range(n1):
-            model.step_into(t1[0, i:i + 1], s1, s1, lg1)
-        b1e.record(stream)
-        torch.cuda.synchronize(dev)
-        b1_step = b0.elapsed_time(b1e) * 1e3 / n1
+        b1, b1_step = batch1(model, w, args.batch1_steps, W, dev, stream)
+    del head["state"], model
+    torch.cuda.empty_cache()
 
-    bpt = synth.gathered_bytes_per_token(w.shape)
-    peak, kind = peaks()
-    achieved = bpt * B / (per_launch_ms / 1e3) / 1e9
-    traffic = None
-    tf = ROOT / "profiles" / "traffic.json"
-    if tf.exists():
-        traffic = json.loads(tf.read_text()).get(f"{args.workload}_B{B}")
+    # ---- strong scaling at the configuration's fixed global batch (c3: 65 536 streams over the N GPUs)
+    strong = {}
+    if world > 1 and args.global_streams:
+        r = measure_step(args, w, path, args.global_streams // world, K, W, rank, world, dist, dev, stream)
+        strong[args.workload] = strong_entry(r, args.global_streams, world)
+    elif args.global_streams:
+        strong[args.workload] = strong_entry(head, B * world, world)
+
+    # ---- the north-star model (c4, 730M shape, Zipf-calibrated) at 65 536 and 262 144 streams per GPU, its strong
+    # scaling at 262 144 global streams, and its e2e through step(tokens, state) with host or device consumers
+    extra = {}
+    if args.extra and args.workload != args.extra:
+        xw, xpath = build_model_file(args.extra, 7, rank, world, dist)
+        xk = min(K, 256)
+        for xb in (65536, 262144):
+            keep = xb == 65536
+            r = measure_step(args, xw, xpath, xb, xk, W, rank, world, dist, dev, stream, keep_model=keep)
+            if keep:
+                xmodel, xstate = r.pop("model"), r.pop("state")
+                r["e2e_step_api"] = e2e_step_api(xmodel, xw, xstate, xb, W, rank, world, dist, dev, stream)
+                del xmodel, xstate
+                torch.cuda.empty_cache()
+            extra[f"B{xb}"] = summarise(r, xw, xb, world, peak, kind, traffic_tab.get(f"{args.extra}_B{xb}"))
+        if world > 1:
+            r = measure_step(args, xw, xpath, 262144 // world, xk, W, rank, world, dist, dev, stream)
+            strong[args.extra] = strong_entry(r, 262144, world)
+        else:
+            strong[args.extra] = {"global_streams": 262144, "streams_per_gpu": 262144,
+                                  "value": extra["B262144"]["value"], "ms_per_step": extra["B262144"]["ms_per_step"]}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -622,29 +503,303 @@ def main():
         dist.destroy_process_group()
     if rank != 0:
         return 0
-    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
-            "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
-            "data": "synthetic",
+    hs = summarise(head, w, B, world, peak, kind, traffic_tab.get(f"{args.workload}_B{B}"))
+    line = {"metric": METRIC, "value": hs["value"], "unit": UNIT, "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": hs["ms_per_step"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8", "data": "synthetic",
             "config": {"workload": w.name, "streams_per_gpu": B, "global_streams": B * world,
-                       "model_bytes": path.stat().st_size, "bytes_per_token": bpt,
+                       "model_bytes": path.stat().st_size, "bytes_per_token": synth.gathered_bytes_per_token(w.shape),
                        "tokens": "i.i.d. DNA bases p=(0.295,0.205,0.205,0.295,0.0001)" if w.tokens == "dna"
                        else "uniform bytes", "l2": "inputs larger than L2 (model file > 126 MB)",
                        "parallelism": f"streams sharded, {world} replica(s)", "primed_steps": args.prime,
-                       "effective_leaves_per_layer": eff,
-                       "leaf_usage": w.leaves if w.leaves != "zipf" else
-                       f"Zipf(1.1) over a seeded leaf order (target {synth.effective_leaves(synth.zipf_leaf_probs(1 << model.depth, 1.1, 0)):.0f} effective leaves)",
-                       "note": w.note},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": traffic, "peak_kind": kind},
+                       "effective_leaves_per_layer": hs["effective_leaves_per_layer"],
+                       "distinct_leaves_per_layer": hs["distinct_leaves_per_layer"],
+                       "leaf_usage": leaf_usage_note(w), "note": w.note},
+            "roofline": hs["roofline"],
             "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": int(B * 4),
-                    "d2h_bytes_per_step": int(B * model.vocab * 4), "steps": ke},
+                    "d2h_bytes_per_step": int(B * w.shape.vocab * 4), "steps": ke,
+                    "path": "step_into serving loop: pinned host tokens up, logits down every step, copies "
+                            "overlapped on two streams"},
             "gpu_launches": K,
             "batch1_us_per_token": b1,
             "batch1_step_api_us_per_token": b1_step,
+            "strong_scaling": strong or None,
             "cpu_baseline": cpu,
             "clocks": clk.summary()}
+    if extra:
+        line[args.extra] = {"workload": synth.WORKLOADS[args.extra].name, **extra}
     print(json.dumps(line))
     return 0
+
+
+def load_traffic():
+    """Per-launch DRAM bytes of the step kernel by workload and batch, from the ncu captures summarised in
+    profiles/ (profiles/traffic.json: each entry names the capture's command)."""
+    tf = ROOT / "profiles" / "traffic.json"
+    if not tf.exists():
+        return {}
+    return {k: v for k, v in json.loads(tf.read_text()).items() if isinstance(v, dict)}
+
+
+def leaf_usage_note(w):
+    from yggdrasil_b200 import synth
+    if w.leaves != "zipf":
+        return w.leaves
+    return (f"Zipf(1.1) over a seeded leaf order (target {synth.effective_leaves(synth.zipf_leaf_probs(8192, 1.1, 0)):.0f}"
+            f" effective leaves); thresholds from tests/golden/zipf_thresholds.npz")
+
+
+def compulsory_bytes(model, shape, tokens, routes):
+    """Bytes one step must move at least, whatever the order of the streams: every distinct record it touches once
+    (the token layer's record of each distinct token; each routed layer's record of each distinct leaf), each distinct
+    table row once (leaf, token), each router row on a visited path once and each (token, node) threshold once, the
+    launch's shared weights (layer-input down projection and its scales, unembedding, output bias), and per stream its
+    token, its state in and out and its logits."""
+    n, b, D, V = shape.d_state, shape.block_size, shape.router_depth, shape.vocab
+    R, R2, k, L = shape.readout_rank, shape.layer_input_rank, shape.input_rank, shape.n_layers
+    E, VP = 1 << D, (V + 31) // 32 * 32
+    x = np.asarray(tokens, np.int64)
+    B = len(x)
+    total = len(np.unique(x)) * (2 * n * b + R * n + 2 * n)            # token layer: A, P and its own table row
+    total += VP * 4 + L * VP * R                                          # output bias, unembeddings
+    per_leaf = 2 * n * b + n * R2 + R * n + ((n * k + 2 * n + 4) if k else 0)
+    for l in range(1, L):
+        r = np.asarray(routes[:, l], np.int64)
+        total += len(np.unique(r)) * per_leaf
+        if not k:
+            total += len(np.unique(r * V + x)) * 2 * n                   # table rows T_r[x]
+        node = r + E
+        nodes, pairs = [], []
+        for _ in range(D):
+            node = node >> 1
+            nodes.append(node)
+            pairs.append(x * E + node)
+        total += len(np.unique(np.concatenate(nodes))) * n               # router rows on the visited paths
+        total += len(np.unique(np.concatenate(pairs))) * 4               # thresholds thr[x][node]
+        total += R2 * n + 4 * R2                                         # down projection and its scales
+    total += B * (4 + 2 * L * n + 4 * V)                                  # token, state in and out, logits
+    return int(total)
+
+
+def measure_step(args, w, path, B, K, W, rank, world, dist, dev, stream, keep_model=False):
+    """Kernel-only decode steps of B streams per GPU: prime every stream with `prime` untimed steps (from a zero
+    state the first steps route on the token alone), record the leaf usage and the compulsory bytes of one step,
+    run W warm-up steps, then time K steps on the launch stream with CUDA events (max over ranks). Tokens are
+    resident in HBM (a ring of at most K + W steps)."""
+    import torch
+
+    from yggdrasil_b200 import Yggdrasil, synth
+    model = Yggdrasil.load(path, backend="b200", device=dev)
+    ring = min(K + W, max(64, (1 << 28) // (4 * B)))
+    d_tok = torch.as_tensor(synth.workload_tokens(w, ring, B, seed=rank)).to(dev)   # (steps, B)
+    state = model.init_state(B)
+    logits = torch.empty(B, model.vocab, dtype=torch.float32, device=dev)
+    xp = torch.as_tensor(synth.workload_tokens(w, max(args.prime, 1), B, seed=10_000 + rank)).to(dev)
+    for i in range(args.prime):
+        model.step_into(xp[i], state, state, logits)
+    del xp
+    _, _, routes, _ = model.step_debug(d_tok[0], state)
+    r = routes.cpu().numpy()
+    eff, distinct = [], []
+    for l in range(1, model.layers):
+        h = np.bincount(r[:, l], minlength=1 << model.depth).astype(np.float64)
+        p = h[h > 0] / h.sum()
+        eff.append(round(float(np.exp(-(p * np.log(p)).sum())), 1))
+        distinct.append(int((h > 0).sum()))
+    comp = compulsory_bytes(model, w.shape, d_tok[0].cpu().numpy(), r)
+    for i in range(W):
+        model.step_into(d_tok[i % ring], state, state, logits)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(K):
+        model.step_into(d_tok[(W + i) % ring], state, state, logits)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = max_over_ranks(e0.elapsed_time(e1), world, dist, dev)
+    model.status()
+    out = {"ms_per_step": ms / K, "value": B * K * world / (ms / 1e3), "steps": K,
+           "effective_leaves_per_layer": eff, "distinct_leaves_per_layer": distinct, "compulsory_bytes": comp}
+    if keep_model:
+        out["model"], out["state"] = model, state
+    else:
+        del model, state
+    del d_tok, logits
+    torch.cuda.empty_cache()
+    return out
+
+
+def max_over_ranks(ms, world, dist, dev):
+    if world > 1:
+        import torch
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def summarise(r, w, B, world, peak, kind, traffic):
+    """The JSON entry of one measurement: tokens/s (whole job), and the roofline of the step kernel on two bases.
+    frac: compulsory bytes of one launch (compulsory_bytes) / launch time / the measured HBM copy peak; algorithmic:
+    the survey's gathered bytes per token x B (counts every stream's leaf bytes, also those that L2 serves to the
+    streams sharing a leaf, so it is not an HBM bound); traffic: the DRAM bytes ncu measured for one launch of this
+    workload and batch (profiles/traffic.json), and its ratio to the compulsory bytes."""
+    from yggdrasil_b200 import synth
+    sec = r["ms_per_step"] / 1e3
+    comp = r["compulsory_bytes"]
+    bpt = synth.gathered_bytes_per_token(w.shape)
+    roof = {"bound": "hbm", "basis": "compulsory bytes per launch", "achieved": comp / sec / 1e9, "peak": peak,
+            "unit": "GB/s", "frac": comp / sec / 1e9 / peak, "peak_kind": kind, "compulsory_bytes": comp,
+            "traffic": None,
+            "algorithmic": {"bytes_per_token": bpt, "bytes_per_launch": bpt * B, "achieved": bpt * B / sec / 1e9,
+                            "frac": bpt * B / sec / 1e9 / peak}}
+    if traffic:
+        t = float(traffic["dram_bytes_per_launch"])
+        roof.update(traffic=t, traffic_source=traffic.get("source"), dram_achieved=t / sec / 1e9,
+                    dram_frac=t / sec / 1e9 / peak, dram_over_compulsory=t / comp)
+    return {"value": r["value"], "ms_per_step": r["ms_per_step"], "streams_per_gpu": B,
+            "effective_leaves_per_layer": r["effective_leaves_per_layer"],
+            "distinct_leaves_per_layer": r["distinct_leaves_per_layer"], "roofline": roof,
+            **({"e2e_step_api": r["e2e_step_api"]} if "e2e_step_api" in r else {})}
+
+
+def strong_entry(r, global_streams, world):
+    return {"global_streams": global_streams, "streams_per_gpu": global_streams // world, "value": r["value"],
+            "ms_per_step": r["ms_per_step"]}
+
+
+def e2e_serving_loop(model, w, state, B, K, W, rank, world, dist, dev, stream):
+    """End to end through step_into with pinned host tokens in and logits out every step: a serving loop with two
+    buffers each way; while step i runs (in place), the tokens of step i + 1 go up on one copy stream and the logits of
+    step i - 1 come down on another; events keep each buffer's writer after its last reader. Returns (tokens/s, steps)."""
+    import torch
+
+    from yggdrasil_b200 import synth
+    ke = min(K, 256)
+    h_tok = torch.as_tensor(synth.workload_tokens(w, ke, B, seed=20_000 + rank)).pin_memory()
+    h_lg = [torch.empty(B, model.vocab, dtype=torch.float32).pin_memory() for _ in range(2)]
+    d_tokb = [torch.empty(B, dtype=torch.int32, device=dev) for _ in range(2)]
+    d_lg = [torch.empty(B, model.vocab, dtype=torch.float32, device=dev) for _ in range(2)]
+    up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev = lambda: [torch.cuda.Event() for _ in range(2)]  # noqa: E731
+    uploaded, stepped, downloaded = ev(), ev(), ev()
+
+    def upload(i):
+        j = i % 2
+        up.wait_event(stepped[j])                  # the step that read this buffer (i - 2) is done
+        with torch.cuda.stream(up):
+            d_tokb[j].copy_(h_tok[i % ke], non_blocking=True)
+            uploaded[j].record(up)
+
+    def loop(n, st):
+        for e in stepped + downloaded:
+            e.record(stream)
+        upload(0)
+        for i in range(n):
+            j = i % 2
+            stream.wait_event(uploaded[j])
+            stream.wait_event(downloaded[j])       # the logits buffer's previous download is done
+            model.step_into(d_tokb[j], st, st, d_lg[j])
+            stepped[j].record(stream)
+            if i + 1 < n:
+                upload(i + 1)
+            down.wait_event(stepped[j])
+            with torch.cuda.stream(down):
+                h_lg[j].copy_(d_lg[j], non_blocking=True)
+                downloaded[j].record(down)
+        stream.wait_stream(down)
+
+    st = state.clone()
+    loop(W, st)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    loop(ke, st)
+    a1.record(stream)
+    torch.cuda.synchronize(dev)
+    ems = max_over_ranks(a0.elapsed_time(a1), world, dist, dev)
+    return B * ke * world / (ems / 1e3), ke
+
+
+def e2e_step_api(model, w, state, B, W, rank, world, dist, dev, stream, steps=64):
+    """The reference-shaped call, `logits, state = model.step(tokens, state)` with host (pinned) tokens, one call after
+    the other, timed with events on the launch stream around `steps` calls (max over ranks), with two consumers of the
+    logits: "host" copies the (B, V) float32 logits to the host every step; "device" keeps them on the GPU and brings
+    back only the greedy next token of each stream (argmax on the device, B int32), as generate() and a sampling
+    server do."""
+    import torch
+
+    from yggdrasil_b200 import synth
+    h_tok = torch.as_tensor(synth.workload_tokens(w, steps, B, seed=30_000 + rank)).pin_memory()
+    out = {}
+    for consumer in ("host", "device"):
+        st = state.clone()
+        h_out = (torch.empty(B, model.vocab, dtype=torch.float32) if consumer == "host"
+                 else torch.empty(B, dtype=torch.int64)).pin_memory()
+
+        def one(i):
+            nonlocal st
+            lg, st = model.step(h_tok[i % steps], st)
+            h_out.copy_(lg if consumer == "host" else lg.argmax(-1), non_blocking=True)
+
+        for i in range(W):
+            one(i)
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        for i in range(steps):
+            one(i)
+        a1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = max_over_ranks(a0.elapsed_time(a1), world, dist, dev)
+        per_step_out = B * model.vocab * 4 if consumer == "host" else B * 8
+        out[consumer] = {"value": B * steps * world / (ms / 1e3), "unit": UNIT, "steps": steps,
+                         "h2d_bytes_per_step": B * 4, "d2h_bytes_per_step": per_step_out}
+    return out
+
+
+def batch1(model, w, n1, W, dev, stream):
+    """Batch 1 on rank 0: (a) device time per token of one stream scoring a row (the launch policy runs the layer
+    wavefront for n = 128; state on chip, the f64 softmax/NLL of every token included, as `ygg time` includes its
+    softmax); (b) one step() call per token through the public API (CUDA-graph replay at batch 1, host tokens). The
+    warm-up runs other tokens than the timed ones, so the timed tokens find their leaves' records where a new stream
+    would (mostly not in L2)."""
+    import torch
+
+    from yggdrasil_b200 import synth
+    t1 = torch.as_tensor(synth.workload_tokens(w, 1, n1 + 1, seed=99)).to(dev)
+    t1w = torch.as_tensor(synth.workload_tokens(w, 1, n1 + 1, seed=98)).to(dev)
+    bits1 = torch.empty(1, dtype=torch.float64, device=dev)
+    for i in range(W):
+        model.score_into(t1w, None, bits1)
+    torch.cuda.synchronize(dev)
+    b0, b1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    b0.record(stream)
+    model.score_into(t1, None, bits1)
+    b1e.record(stream)
+    torch.cuda.synchronize(dev)
+    b1 = b0.elapsed_time(b1e) * 1e3 / n1
+    h1 = t1.cpu()
+    h1w = t1w.cpu()
+    s1 = model.init_state(1)
+    for i in range(W):
+        _, s1 = model.step(h1w[0, i:i + 1], s1)
+    torch.cuda.synchronize(dev)
+    b0.record(stream)
+    for i in range(n1):
+        _, s1 = model.step(h1[0, i:i + 1], s1)
+    b1e.record(stream)
+    torch.cuda.synchronize(dev)
+    return b1, b0.elapsed_time(b1e) * 1e3 / n1
 
 
 if __name__ == "__main__":

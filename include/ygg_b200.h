@@ -109,7 +109,8 @@ YGG_API int ygg_score_grouped(const ygg_model *m, int batch, int steps, const in
  * takes no workspace: its scratch is one fixed 16 MiB array in device memory that every GPU loading this library holds
  * until the process exits, so it calls no allocator at all. A batch whose scratch (ygg_score_grouped_workspace)
  * exceeds 16 MiB is refused with YGG_E_CAPACITY (22 738 rows at n = 128, L = 4, 8192 leaves). The first call on a device
- * looks up the array's device address (once per device); make that first call before any stream capture. Every call
+ * looks up the array's device address (once per device and context: after the device's primary context is reset, or
+ * under another context, the next call looks it up again); make that first call before any stream capture. Every call
  * shares the array and clears what must start at zero; calls whose work overlaps on the GPU (other streams, other
  * threads) race on it, so run them one after another. Same arguments (less the workspace) and the same results as
  * ygg_score_grouped. No counterpart in the reference: it is an addition of this library. */

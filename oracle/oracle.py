@@ -40,9 +40,9 @@ def lib():
         l.orc_free.argtypes = [ctypes.c_void_p]
         l.orc_info.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
         l.orc_step.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
-                               ctypes.c_void_p]
+                               ctypes.c_void_p, ctypes.c_void_p]
         l.orc_logits.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
-                                 ctypes.c_void_p]
+                                 ctypes.c_void_p, ctypes.c_void_p]
         l.orc_score.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p,
                                 ctypes.c_void_p]
         for f in (l.orc_step, l.orc_logits, l.orc_score):
@@ -78,25 +78,31 @@ class OracleModel:
     def init_state(self, batch: int) -> np.ndarray:
         return np.zeros((batch, self.n_layers, self.n), np.int8)
 
-    def step(self, tokens, state, routes: bool = False):
-        """tokens (B,), state (B, L, n) int8 (updated in place) -> logits (B, V) f32 [, routes (B, L)]."""
+    def step(self, tokens, state, routes: bool = False, acc: bool = False):
+        """tokens (B,), state (B, L, n) int8 (updated in place) -> logits (B, V) f32 [, routes (B, L)] [, acc (B, L, n)
+        int32: the accumulators before saturation to the new state]."""
         tok = np.ascontiguousarray(tokens, np.int32)
         assert state.dtype == np.int8 and state.flags.c_contiguous and state.shape == (len(tok), self.n_layers, self.n)
         lg = np.empty((len(tok), self.vocab), np.float32)
         rt = np.empty((len(tok), self.n_layers), np.int32) if routes else None
-        if lib().orc_step(self._h, len(tok), _ptr(tok), _ptr(state), _ptr(lg), _ptr(rt)):
+        ac = np.empty((len(tok), self.n_layers, self.n), np.int32) if acc else None
+        if lib().orc_step(self._h, len(tok), _ptr(tok), _ptr(state), _ptr(lg), _ptr(rt), _ptr(ac)):
             raise ValueError("token out of range")
-        return (lg, rt) if routes else lg
+        out = (lg,) + ((rt,) if routes else ()) + ((ac,) if acc else ())
+        return out if len(out) > 1 else lg
 
-    def logits(self, tokens, routes: bool = False):
-        """windows (S, T), zero state per window -> logits (S, T, V) f32 [, routes (S, T, L)]."""
+    def logits(self, tokens, routes: bool = False, acc: bool = False):
+        """windows (S, T), zero state per window -> logits (S, T, V) f32 [, routes (S, T, L)] [, acc (S, T, L, n) int32
+        before saturation]."""
         tok = np.ascontiguousarray(tokens, np.int32)
         s, t = tok.shape
         lg = np.empty((s, t, self.vocab), np.float32)
         rt = np.empty((s, t, self.n_layers), np.int32) if routes else None
-        if lib().orc_logits(self._h, s, t, _ptr(tok), _ptr(lg), _ptr(rt)):
+        ac = np.empty((s, t, self.n_layers, self.n), np.int32) if acc else None
+        if lib().orc_logits(self._h, s, t, _ptr(tok), _ptr(lg), _ptr(rt), _ptr(ac)):
             raise ValueError("token out of range")
-        return (lg, rt) if routes else lg
+        out = (lg,) + ((rt,) if routes else ()) + ((ac,) if acc else ())
+        return out if len(out) > 1 else lg
 
     def score(self, tokens, state=None):
         """bits of tokens[:, 1:] per row (f64); state (S, L, n) int8 updated in place, or None (zero)."""

@@ -168,8 +168,10 @@ static void layer_input(const orc_model *m, const OLayer *y, const int8_t *qb, f
     }
 }
 
-/* q <- sat8((A16 q + 2^(shift-1)) >> shift + input + rint(f32(U' zl) m_ul)) (cpu/ygg.cpp:312-389) */
-static void update(const orc_model *m, const OLayer *y, int r, int x, int8_t *q, const int8_t *zl) {
+/* q <- sat8((A16 q + 2^(shift-1)) >> shift + input + rint(f32(U' zl) m_ul)) (cpu/ygg.cpp:312-389); acc_out (n) or
+ * NULL receives the int32 accumulator before the saturation (the `acc` that cpu/ygg.cpp:388 narrows with
+ * cvtsepi32_epi8; `drive` in cpu/export.py:307-310) */
+static void update(const orc_model *m, const OLayer *y, int r, int x, int8_t *q, const int8_t *zl, int32_t *acc_out) {
     const int n = m->n, b = m->b;
     const uint8_t *rec = y->rec + (size_t)r * y->rec_bytes;
     const int16_t *A = (const int16_t *)(rec + y->off_a);
@@ -205,6 +207,7 @@ static void update(const orc_model *m, const OLayer *y, int r, int x, int8_t *q,
             acc[i] += rne((float)la * mu);
         }
     }
+    if (acc_out) memcpy(acc_out, acc, 4 * (size_t)n);
     for (int i = 0; i < n; i++) q[i] = (int8_t)clampi(acc[i], -128, 127);
 }
 
@@ -233,11 +236,13 @@ static void readout(const orc_model *m, const OLayer *y, int r, const int8_t *q,
     }
 }
 
-/* one token of one stream over every layer (cpu/ygg.cpp:441-459); q: L*n int8, lg: VP floats */
-static void step1(const orc_model *m, int x, int8_t *q, float *lg, int32_t *routes) {
+/* one token of one stream over every layer (cpu/ygg.cpp:441-459); q: L*n int8, lg: VP floats; routes (L) and acc
+ * (L*n, the accumulators before saturation) or NULL */
+static void step1(const orc_model *m, int x, int8_t *q, float *lg, int32_t *routes, int32_t *acc) {
     for (int l = 0; l < m->L; l++) {
         const OLayer *y = &m->y[l];
         int8_t *ql = q + (size_t)l * m->n;
+        int32_t *al = acc ? acc + (size_t)l * m->n : NULL;
         int r = x;
         if (l > 0) {
             const int8_t *qb = ql - m->n;
@@ -246,9 +251,9 @@ static void step1(const orc_model *m, int x, int8_t *q, float *lg, int32_t *rout
             if (m->R2) {
                 int8_t zl[64];
                 layer_input(m, y, qb, rho, zl);
-                update(m, y, r, x, ql, zl);
-            } else update(m, y, r, x, ql, NULL);
-        } else update(m, y, r, x, ql, NULL);
+                update(m, y, r, x, ql, zl, al);
+            } else update(m, y, r, x, ql, NULL, al);
+        } else update(m, y, r, x, ql, NULL, al);
         if (routes) routes[l] = r;
         readout(m, y, r, ql, lg, l == 0 ? m->head_b : lg);
     }
@@ -259,20 +264,23 @@ static int check_tokens(const orc_model *m, size_t cnt, const int32_t *tok) {
     return 0;
 }
 
-/* one step of B streams: state (B, L, n) in/out, logits (B, V) or NULL, routes (B, L) or NULL */
-int orc_step(const orc_model *m, int B, const int32_t *tok, int8_t *state, float *logits, int32_t *routes) {
+/* one step of B streams: state (B, L, n) in/out, logits (B, V) or NULL, routes (B, L) or NULL, acc (B, L, n) or NULL
+ * (the int32 accumulators before saturation) */
+int orc_step(const orc_model *m, int B, const int32_t *tok, int8_t *state, float *logits, int32_t *routes,
+             int32_t *acc) {
     if (check_tokens(m, (size_t)B, tok)) return -1;
     float lg[256];
     for (int s = 0; s < B; s++) {
-        step1(m, tok[s], state + (size_t)s * m->L * m->n, lg, routes ? routes + (size_t)s * m->L : NULL);
+        step1(m, tok[s], state + (size_t)s * m->L * m->n, lg, routes ? routes + (size_t)s * m->L : NULL,
+              acc ? acc + (size_t)s * m->L * m->n : NULL);
         if (logits) memcpy(logits + (size_t)s * m->V, lg, 4 * (size_t)m->V);
     }
     return 0;
 }
 
-/* windows of tokens (S, T) from a zero state each: logits (S, T, V), routes (S, T, L) or NULL
- * (cpu/ygg.cpp:500-512, the logits command) */
-int orc_logits(const orc_model *m, int S, int T, const int32_t *tok, float *logits, int32_t *routes) {
+/* windows of tokens (S, T) from a zero state each: logits (S, T, V), routes (S, T, L) or NULL, acc (S, T, L, n) or
+ * NULL (cpu/ygg.cpp:500-512, the logits command) */
+int orc_logits(const orc_model *m, int S, int T, const int32_t *tok, float *logits, int32_t *routes, int32_t *acc) {
     if (check_tokens(m, (size_t)S * T, tok)) return -1;
     int8_t *q = (int8_t *)calloc((size_t)m->L * m->n, 1);
     float lg[256];
@@ -280,7 +288,7 @@ int orc_logits(const orc_model *m, int S, int T, const int32_t *tok, float *logi
         memset(q, 0, (size_t)m->L * m->n);
         for (int t = 0; t < T; t++) {
             const size_t i = (size_t)s * T + t;
-            step1(m, tok[i], q, lg, routes ? routes + i * m->L : NULL);
+            step1(m, tok[i], q, lg, routes ? routes + i * m->L : NULL, acc ? acc + i * m->L * m->n : NULL);
             memcpy(logits + i * m->V, lg, 4 * (size_t)m->V);
         }
     }
@@ -299,7 +307,7 @@ int orc_score(const orc_model *m, int S, int T, const int32_t *tok, int8_t *stat
         if (!state) memset(own, 0, (size_t)m->L * m->n);
         double nll = 0.0;
         for (int t = 0; t + 1 < T; t++) {
-            step1(m, tok[(size_t)s * T + t], q, lg, NULL);
+            step1(m, tok[(size_t)s * T + t], q, lg, NULL, NULL);
             double mx = -1e300;
             for (int c = 0; c < m->V; c++) mx = lg[c] > mx ? lg[c] : mx;
             double se = 0.0;

@@ -83,6 +83,40 @@ def case_model(model_dir):
     return get
 
 
+@pytest.fixture(scope="session")
+def workload_model(model_dir):
+    """path of a benchmark workload's model (synth.WORKLOADS key; the Zipf-calibrated ones with their fixture
+    thresholds), written once per session: c4's table-storage file is 1.9 GB."""
+    from yggdrasil_b200 import synth
+    from yggdrasil_b200.ygg1 import write_model
+    cache = {}
+
+    def get(key):
+        w = synth.WORKLOADS[key]
+        name = w.model or key
+        if name not in cache:
+            p = model_dir / f"workload_{name}.bin"
+            layers = synth.workload_layers(w, seed=7, thresholds=synth.zipf_thresholds_of(w, ROOT))
+            write_model(layers, np.linspace(-1, 1, w.shape.vocab), p, extended=w.extended)
+            cache[name] = p
+        return cache[name]
+    return get
+
+
+@pytest.fixture(scope="session")
+def oracle_of():
+    """The C oracle of a model path, loaded once per session (a c4 oracle holds the 1.9 GB file)."""
+    from oracle import oracle as O
+    cache = {}
+
+    def get(path):
+        key = str(path)
+        if key not in cache:
+            cache[key] = O.OracleModel(path)
+        return cache[key]
+    return get
+
+
 def ygg_step_logp(ygg, tokens):
     """Feed tokens (T,) one at a time through ygg.step (one stream, from ygg.init_state(1)) -> log-probabilities
     (T, classes) of the next token."""

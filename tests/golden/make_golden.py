@@ -1,6 +1,6 @@
 """Regenerate tests/golden/*.json from the reference implementation (run in a container that has the reference tree).
 
-    python tests/golden/make_golden.py [--ref /path/to/yggdrasil]
+    python tests/golden/make_golden.py [--ref /path/to/yggdrasil] [--only cases,zipf,workloads,ext,checkpoints]
 
 The fixtures pin this repository's generator and oracle to the reference:
   kernel_cases.json  for every shape of the reference's kernel test (cpu/tests/test_kernel.py:22-33): the sha256 of
@@ -9,12 +9,21 @@ The fixtures pin this repository's generator and oracle to the reference:
                      the test's tokens (default_rng(0), 8 streams x 64 steps), the per-row bits derived from them in
                      float64, and a few logits in clear for reading a failure;
   long_cases.json    two shapes run for 512 steps (deep state dynamics, saturation);
-  workloads.json     the benchmark shapes (yggdrasil_b200.synth WORKLOADS c1-c3) written by the reference's writer, with
-                     int_forward logits on a few streams;
+  workloads.json     the benchmark shapes (yggdrasil_b200.synth WORKLOADS c1-c4f) written by the reference's writer,
+                     with int_forward logits on a few streams;
+  zipf_thresholds.npz  the router thresholds of the Zipf(1.1)-calibrated models (c4, c4f; c5 scores the c4 model):
+                     layer by layer, the C oracle (itself pinned to the reference here) runs 16 384 streams of uniform
+                     bytes for 64 steps, and each node's threshold is set at the quantile of the sampled scores that
+                     sends the Zipf share of its subtree to the right (synth.zipf_thresholds). The calibrated models
+                     are then written by the reference's writer and run by its int_forward like the other workloads.
   extended_cases.json  shapes of this repository's d_state 96 format extension, which the reference's writer and ygg
                      refuse: the reference's random_model (seed 7) and int_forward logits on the kernel test's tokens,
                      and the c3n96 benchmark shape's int_forward logits on a few streams. The model digests here are
                      this repository's writer's (a regression check, not a pin); the logits are the pin.
+  checkpoints.json   digests of the files the reference's quantize + write make from seeded synthetic checkpoints.
+Every record of the first four also carries acc_sha256: the digest of the int32 accumulators before saturation,
+(S, T, L, n), taken from int_forward's own `drive` array (cpu/export.py:300-310; the value cpu/ygg.cpp:388 narrows with
+cvtsepi32_epi8) by watching its saturating np.clip(drive, -128, 127) calls.
 The reference sources are read in place and never copied; only digests and a few numbers land here.
 """
 from __future__ import annotations
@@ -47,10 +56,93 @@ def bits_from_logits(lg: np.ndarray, x: np.ndarray) -> np.ndarray:
     return (lse - tgt).sum(-1) / np.log(2.0)
 
 
+class AccCapture:
+    """Records the array of every np.clip(a, -128, 127) call while active: in the reference's int_forward that is
+    the saturation of each layer's accumulator `drive` into the new int8 state, once per (step, layer), in order."""
+
+    def __enter__(self):
+        self.arrays, self._clip = [], np.clip
+
+        def clip(a, lo=None, hi=None, *args, **kw):
+            if isinstance(lo, int) and isinstance(hi, int) and (lo, hi) == (-128, 127):
+                self.arrays.append(np.array(a, copy=True))
+            return self._clip(a, lo, hi, *args, **kw)
+        np.clip = clip
+        return self
+
+    def __exit__(self, *exc):
+        np.clip = self._clip
+
+    def acc(self, S, T, L):
+        """The accumulators as int32 (S, T, L, n); checks that no value left the int32 range of cpu/ygg.cpp."""
+        a = np.stack(self.arrays).reshape(T, L, S, -1)
+        assert np.abs(a).max() < 2 ** 31
+        return np.ascontiguousarray(a.transpose(2, 0, 1, 3).astype(np.int32))
+
+
+def forward_with_acc(E, layers, ob, x):
+    """int_forward's logits and its accumulators before saturation."""
+    with AccCapture() as cap:
+        lg = E.int_forward(layers, ob, x)
+    return lg, cap.acc(x.shape[0], x.shape[1], len(layers))
+
+
+def oracle_layer_states(path, w, streams, snapshots, layer, procs=8):
+    """States of `layer` (int8, (streams * len(snapshots), n)) after each step in snapshots, running the C oracle on
+    `streams` streams of the workload's tokens (seed 77) from zero, split over processes."""
+    from multiprocessing import get_context
+
+    from yggdrasil_b200 import synth
+    x = synth.workload_tokens(w, streams, max(snapshots), seed=77)
+    chunks = np.array_split(np.arange(streams), procs)
+    with get_context("spawn").Pool(procs) as pool:
+        parts = pool.starmap(_oracle_chunk, [(str(path), x[c], tuple(snapshots), layer) for c in chunks])
+    return np.concatenate([np.concatenate(p) for p in zip(*parts)])
+
+
+def _oracle_chunk(path, x, snapshots, layer):
+    sys.path.insert(0, str(ROOT))
+    from oracle import oracle as O
+    om = O.OracleModel(path)
+    st = om.init_state(x.shape[0])
+    out = []
+    for t in range(max(snapshots)):
+        om.step(x[:, t], st)
+        if t + 1 in snapshots:
+            out.append(st[:, layer].copy())
+    return out
+
+
+def calibrate_zipf(key, tmp, streams=16384, snapshots=(48, 56, 64), s=1.1, seed=7):
+    """Per-node router thresholds (L - 1, 2^D - 1) of workload `key` for Zipf(s) leaf usage over a seeded leaf order
+    (synth.zipf_leaf_probs, seed + 100 + l), layer by layer on the states the layers below produce."""
+    from yggdrasil_b200 import synth
+    from yggdrasil_b200.ygg1 import write_model
+    w = synth.WORKLOADS[key]
+    layers = synth.workload_layers(w, seed=seed)
+    ob = np.linspace(-1, 1, w.shape.vocab)
+    E = 2 ** w.shape.router_depth
+    thr = np.zeros((len(layers) - 1, E - 1), np.float32)
+    path = os.path.join(tmp, f"{key}_cal.bin")
+    for l in range(1, len(layers)):
+        write_model(layers, ob, path)
+        qb = oracle_layer_states(path, w, streams, snapshots, l - 1)
+        q = layers[l]
+        rho = synth.rho_f32(qb, q.rms_eps, q.state_r2)
+        thr[l - 1] = synth.zipf_thresholds(q.router_weight, qb, rho, synth.zipf_leaf_probs(E, s, seed + 100 + l))
+        synth.apply_thresholds(layers, thr, only=l)
+        print(f"calibrated {key} layer {l}", flush=True)
+    os.remove(path)
+    return thr
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("YGG_REFERENCE", "/root/reference"))
+    ap.add_argument("--only", default="cases,workloads,zipf,ext,checkpoints",
+                    help="comma-separated parts to regenerate (zipf recalibrates c4/c4f; workloads reads the .npz)")
     a = ap.parse_args()
+    parts = set(a.only.split(","))
     ref = Path(a.ref)
     sys.path.insert(0, str(ref / "cpu"))
     sys.path.insert(0, str(ref))
@@ -70,10 +162,11 @@ def main():
         path = os.path.join(tmp, "m.bin")
         E.write(layers, ob, path)
         x = np.random.default_rng(0).integers(0, cfg.vocab, (streams, steps)).astype(np.int32)
-        lg = E.int_forward(layers, ob, x)
+        lg, acc = forward_with_acc(E, layers, ob, x)
         rec = dict(shape={k: getattr(cfg, k) for k in fields}, seed=7, streams=streams, steps=steps, token_seed=0,
                    model_sha256=sha(Path(path).read_bytes()), model_bytes=os.path.getsize(path),
-                   logits_sha256=sha(np.ascontiguousarray(lg, np.float32).tobytes()),
+                   logits_sha256=sha(np.ascontiguousarray(lg, np.float32).tobytes()), acc_sha256=sha(acc.tobytes()),
+                   acc_range=[int(acc.min()), int(acc.max())],
                    bits=[float(v) for v in bits_from_logits(lg, x)],
                    logits_head=np.asarray(lg[0, :4, :8], np.float64).tolist())
         if ygg.exists():   # the reference binary agrees with int_forward (the reference test's own assertion)
@@ -84,99 +177,113 @@ def main():
             rec["ygg_equal"] = bool(np.array_equal(np.fromfile(of, np.float32).reshape(lg.shape), lg))
         return rec
 
-    with tempfile.TemporaryDirectory() as tmp:
-        cases = [run_case(c, STREAMS, STEPS, tmp) for c in CASES]
-        (HERE / "kernel_cases.json").write_text(json.dumps(cases, indent=1) + "\n")
-        longs = [run_case(CASES[i], 4, 512, tmp) for i in (1, 12)]
-        (HERE / "long_cases.json").write_text(json.dumps(longs, indent=1) + "\n")
-        works = []
-        for key in ("c1", "c2", "c3"):
-            w = synth.WORKLOADS[key]
-            layers = synth.workload_layers(w, seed=7)
-            ob = np.linspace(-1, 1, w.shape.vocab)
-            path = os.path.join(tmp, "w.bin")
-            E.write(layers, ob, path)            # the reference's writer on this repository's layers
-            x = synth.workload_tokens(w, 4, 32, seed=0)
-            lg = E.int_forward(layers, ob, x)
-            works.append(dict(workload=key, model_sha256=sha(Path(path).read_bytes()),
-                              model_bytes=os.path.getsize(path), streams=4, steps=32, token_seed=0,
-                              logits_sha256=sha(np.ascontiguousarray(lg, np.float32).tobytes()),
-                              bits=[float(v) for v in bits_from_logits(lg, x)]))
-        (HERE / "workloads.json").write_text(json.dumps(works, indent=1) + "\n")
-
-        # the d_state 96 extension: int_forward works at any shape; the file is this repository's writer's
-        from yggdrasil_b200.synth import ModelShape, write_random_model
-        from yggdrasil_b200.ygg1 import write_model
-        ext_cfgs = [E.KernelConfig(96, 16, 8, 256, 2, 12, 24), E.KernelConfig(96, 8, 6, 5, 3, 12, 24, group=True),
-                    E.KernelConfig(96, 16, 7, 27, 3, 12, 24, input_rank=24, group=True),
-                    E.KernelConfig(96, 16, 6, 256, 2, 16, 32), E.KernelConfig(96, 8, 5, 5, 2, 8, 0)]
-        ext = []
-        for cfg in ext_cfgs:
-            layers = E.random_model(cfg, seed=7)
-            ob = np.linspace(-1, 1, cfg.vocab)
-            path = os.path.join(tmp, "x.bin")
-            shape = ModelShape(**{k: getattr(cfg, k) for k in fields})
-            write_random_model(shape, path, seed=7, extended=True)
-            x = np.random.default_rng(0).integers(0, cfg.vocab, (STREAMS, STEPS)).astype(np.int32)
-            lg = E.int_forward(layers, ob, x)
-            ext.append(dict(shape={k: getattr(cfg, k) for k in fields}, seed=7, streams=STREAMS, steps=STEPS,
-                            token_seed=0, extended=True, model_sha256=sha(Path(path).read_bytes()),
-                            model_bytes=os.path.getsize(path),
-                            logits_sha256=sha(np.ascontiguousarray(lg, np.float32).tobytes()),
-                            bits=[float(v) for v in bits_from_logits(lg, x)],
-                            logits_head=np.asarray(lg[0, :4, :8], np.float64).tolist()))
-        w = synth.WORKLOADS["c3n96"]
-        layers = synth.workload_layers(w, seed=7)
-        ob = np.linspace(-1, 1, w.shape.vocab)
-        path = os.path.join(tmp, "w.bin")
-        write_model(layers, ob, path, extended=True)
-        x = synth.workload_tokens(w, 4, 32, seed=0)
-        lg = E.int_forward(layers, ob, x)
-        ext.append(dict(workload="c3n96", extended=True, model_sha256=sha(Path(path).read_bytes()),
-                        model_bytes=os.path.getsize(path), streams=4, steps=32, token_seed=0,
-                        logits_sha256=sha(np.ascontiguousarray(lg, np.float32).tobytes()),
-                        bits=[float(v) for v in bits_from_logits(lg, x)]))
-        (HERE / "extended_cases.json").write_text(json.dumps(ext, indent=1) + "\n")
-
-        # checkpoints: the reference's read (yggdrasil/inference.py:129-139), FloatLayer, quantize and write
-        # (cpu/export.py:68-96,216-265,461-468) on seeded synthetic checkpoints and export records; the float64
-        # transitions come from torch.linalg.matrix_exp (the reference's exporter uses JAX, absent here), checked
-        # against the reference Triton backend's own transitions (yggdrasil/inference_triton.py:109-114)
-        sys.path.insert(0, str(HERE.parent))
-        import checkpoints as C
-        from yggdrasil import inference as I
-        from yggdrasil import inference_triton as IT
-        from yggdrasil_b200.checkpoint import transitions64
-        ckpts = []
-        for seed, old in ((0, False), (1, True)):
-            npz = os.path.join(tmp, f"ck{seed}.npz")
-            C.synthetic_checkpoint(npz, seed=seed, old_keys=old)
-            raw, ob = I.read(npz)
-            raw = [{k: v.astype(np.float64) for k, v in p.items()} for p in raw]
-            tr_ok = all(np.array_equal(transitions64(p["rotation"], p["decay"]).astype(np.float32),
-                                       IT._transitions(p).numpy()) for p in raw)
-            depth = I.router_depth(raw[1])
-            fl = []
-            for i, p in enumerate(raw):
-                table = np.einsum("lkr,vr->lvk", p["input_proj"], p["token_embed"]) + p["bias"][:, None]
-                kw = {k: p[k] for k in ("router_embed", "router_weight", "router_bias", "layer_input_down",
-                                        "layer_input_proj") if k in p}
-                fl.append(E.FloatLayer(token_layer=i == 0, depth=depth if i else 0,
-                                       transition=transitions64(p["rotation"], p["decay"]), table=table,
-                                       input_proj=p["input_proj"], token_embed=p["token_embed"], bias=p["bias"],
-                                       readout=p["readout"], unembed=p["unembed"], **kw))
-            for rs, (hm, group, fac) in enumerate(((0.85, False, False), (1.0, True, True))):
-                rec = C.synthetic_record(seed=rs, hmargin=hm, group=group, factored=fac)
-                stats = [E.LayerStats(**{k: (np.asarray(v) if isinstance(v, list) else v) for k, v in s.items()})
-                         for s in rec["stats"]]
-                q = E.quantize(fl, stats, **rec["quantize"])
-                out = os.path.join(tmp, "ck.bin")
-                E.write(q, ob, out, router_token_dim=fl[-1].router_token_dim, input_rank=fl[0].token_embed.shape[1])
-                ckpts.append(dict(seed=seed, old_keys=old, record_seed=rs, quantize=rec["quantize"],
-                                  model_sha256=sha(Path(out).read_bytes()), model_bytes=os.path.getsize(out),
-                                  transitions_match_reference_triton_backend=bool(tr_ok)))
-        (HERE / "checkpoints.json").write_text(json.dumps(ckpts, indent=1) + "\n")
+    with tempfile.TemporaryDirectory(dir=os.environ.get("YGG_GOLDEN_TMP")) as tmp:
+        if "cases" in parts:
+            cases = [run_case(c, STREAMS, STEPS, tmp) for c in CASES]
+            (HERE / "kernel_cases.json").write_text(json.dumps(cases, indent=1) + "\n")
+            longs = [run_case(CASES[i], 4, 512, tmp) for i in (1, 12)]
+            (HERE / "long_cases.json").write_text(json.dumps(longs, indent=1) + "\n")
+        if "zipf" in parts:
+            thr = {key: calibrate_zipf(key, tmp) for key in ("c4", "c4f")}
+            np.savez(HERE / "zipf_thresholds.npz", **thr)
+        if "workloads" in parts:
+            works = []
+            for key in ("c1", "c2", "c3", "c4", "c4f"):
+                w = synth.WORKLOADS[key]
+                layers = synth.workload_layers(w, seed=7, thresholds=synth.zipf_thresholds_of(w, ROOT))
+                ob = np.linspace(-1, 1, w.shape.vocab)
+                path = os.path.join(tmp, "w.bin")
+                E.write(layers, ob, path)            # the reference's writer on this repository's layers
+                x = synth.workload_tokens(w, 4, 32, seed=0)
+                lg, acc = forward_with_acc(E, layers, ob, x)
+                works.append(dict(workload=key, model_sha256=sha(Path(path).read_bytes()),
+                                  model_bytes=os.path.getsize(path), streams=4, steps=32, token_seed=0,
+                                  logits_sha256=sha(np.ascontiguousarray(lg, np.float32).tobytes()),
+                                  acc_sha256=sha(acc.tobytes()), acc_range=[int(acc.min()), int(acc.max())],
+                                  bits=[float(v) for v in bits_from_logits(lg, x)]))
+                os.remove(path)
+                del layers
+            (HERE / "workloads.json").write_text(json.dumps(works, indent=1) + "\n")
+        if "ext" in parts:
+            make_extended(E, synth, fields, tmp, STREAMS, STEPS)
+        if "checkpoints" in parts:
+            make_checkpoints(E, tmp)
     print("wrote", [p.name for p in HERE.glob("*.json")])
+
+
+def make_extended(E, synth, fields, tmp, STREAMS, STEPS):
+    """The d_state 96 extension: int_forward works at any shape; the file is this repository's writer's."""
+    from yggdrasil_b200.synth import ModelShape, write_random_model
+    from yggdrasil_b200.ygg1 import write_model
+    ext_cfgs = [E.KernelConfig(96, 16, 8, 256, 2, 12, 24), E.KernelConfig(96, 8, 6, 5, 3, 12, 24, group=True),
+                E.KernelConfig(96, 16, 7, 27, 3, 12, 24, input_rank=24, group=True),
+                E.KernelConfig(96, 16, 6, 256, 2, 16, 32), E.KernelConfig(96, 8, 5, 5, 2, 8, 0)]
+    ext = []
+    for cfg in ext_cfgs:
+        layers = E.random_model(cfg, seed=7)
+        ob = np.linspace(-1, 1, cfg.vocab)
+        path = os.path.join(tmp, "x.bin")
+        shape = ModelShape(**{k: getattr(cfg, k) for k in fields})
+        write_random_model(shape, path, seed=7, extended=True)
+        x = np.random.default_rng(0).integers(0, cfg.vocab, (STREAMS, STEPS)).astype(np.int32)
+        lg, acc = forward_with_acc(E, layers, ob, x)
+        ext.append(dict(shape={k: getattr(cfg, k) for k in fields}, seed=7, streams=STREAMS, steps=STEPS,
+                        token_seed=0, extended=True, model_sha256=sha(Path(path).read_bytes()),
+                        model_bytes=os.path.getsize(path),
+                        logits_sha256=sha(np.ascontiguousarray(lg, np.float32).tobytes()),
+                        acc_sha256=sha(acc.tobytes()), acc_range=[int(acc.min()), int(acc.max())],
+                        bits=[float(v) for v in bits_from_logits(lg, x)],
+                        logits_head=np.asarray(lg[0, :4, :8], np.float64).tolist()))
+    w = synth.WORKLOADS["c3n96"]
+    layers = synth.workload_layers(w, seed=7)
+    ob = np.linspace(-1, 1, w.shape.vocab)
+    path = os.path.join(tmp, "w.bin")
+    write_model(layers, ob, path, extended=True)
+    x = synth.workload_tokens(w, 4, 32, seed=0)
+    lg, acc = forward_with_acc(E, layers, ob, x)
+    ext.append(dict(workload="c3n96", extended=True, model_sha256=sha(Path(path).read_bytes()),
+                    model_bytes=os.path.getsize(path), streams=4, steps=32, token_seed=0,
+                    logits_sha256=sha(np.ascontiguousarray(lg, np.float32).tobytes()),
+                    acc_sha256=sha(acc.tobytes()), acc_range=[int(acc.min()), int(acc.max())],
+                    bits=[float(v) for v in bits_from_logits(lg, x)]))
+    (HERE / "extended_cases.json").write_text(json.dumps(ext, indent=1) + "\n")
+
+
+def make_checkpoints(E, tmp):
+    """Checkpoints: the reference's read (yggdrasil/inference.py:129-139), FloatLayer, quantize and write
+    (cpu/export.py:68-96,216-265,461-468) on seeded synthetic checkpoints and export records. The float64
+    transitions come from this repository's transitions64 (the reference's exporter uses JAX, absent here);
+    tests/test_checkpoint.py checks them against scipy's float64 expm at test time."""
+    sys.path.insert(0, str(HERE.parent))
+    import checkpoints as C
+    from yggdrasil import inference as I
+    from yggdrasil_b200.checkpoint import transitions64
+    ckpts = []
+    for seed, old in ((0, False), (1, True)):
+        npz = os.path.join(tmp, f"ck{seed}.npz")
+        C.synthetic_checkpoint(npz, seed=seed, old_keys=old)
+        raw, ob = I.read(npz)
+        raw = [{k: v.astype(np.float64) for k, v in p.items()} for p in raw]
+        depth = I.router_depth(raw[1])
+        fl = []
+        for i, p in enumerate(raw):
+            table = np.einsum("lkr,vr->lvk", p["input_proj"], p["token_embed"]) + p["bias"][:, None]
+            kw = {k: p[k] for k in ("router_embed", "router_weight", "router_bias", "layer_input_down",
+                                    "layer_input_proj") if k in p}
+            fl.append(E.FloatLayer(token_layer=i == 0, depth=depth if i else 0,
+                                   transition=transitions64(p["rotation"], p["decay"]), table=table,
+                                   input_proj=p["input_proj"], token_embed=p["token_embed"], bias=p["bias"],
+                                   readout=p["readout"], unembed=p["unembed"], **kw))
+        for rs, (hm, group, fac) in enumerate(((0.85, False, False), (1.0, True, True))):
+            rec = C.synthetic_record(seed=rs, hmargin=hm, group=group, factored=fac)
+            stats = [E.LayerStats(**{k: (np.asarray(v) if isinstance(v, list) else v) for k, v in s.items()})
+                     for s in rec["stats"]]
+            q = E.quantize(fl, stats, **rec["quantize"])
+            out = os.path.join(tmp, "ck.bin")
+            E.write(q, ob, out, router_token_dim=fl[-1].router_token_dim, input_rank=fl[0].token_embed.shape[1])
+            ckpts.append(dict(seed=seed, old_keys=old, record_seed=rs, quantize=rec["quantize"],
+                              model_sha256=sha(Path(out).read_bytes()), model_bytes=os.path.getsize(out)))
+    (HERE / "checkpoints.json").write_text(json.dumps(ckpts, indent=1) + "\n")
 
 
 if __name__ == "__main__":

@@ -81,16 +81,15 @@ def test_grouped_from_state(rec, case_model, torch):
     assert torch.equal(s1, s2)
 
 
-@pytest.mark.parametrize("key", ["c3", "c3n96"])
-def test_grouped_benchmark_shape(key, tmp_path, torch):
-    """The c3 shape (n128 b16 R16 R2=32, 4 layers, V = 5; and the d 96 extension, padded to n 128 on the device) at
-    4096 streams: DNA tokens make the token layer's five leaves and the hot routed leaves heavy."""
+@pytest.mark.parametrize("key", ["c3", "c3n96", "c4", "c4f"])
+def test_grouped_benchmark_shape(key, workload_model, torch):
+    """The benchmark shapes at 4096 streams: c3 (n128 b16 R16 R2=32, 4 layers, V = 5; and the d 96 extension, padded
+    to n 128 on the device), where DNA tokens make the token layer's five leaves and the hot routed leaves heavy, and
+    c4 / c4f (V = 256, table and factored storage), whose Zipf-calibrated routers concentrate the routed layers on a
+    few hundred leaves."""
     from yggdrasil_b200 import synth
-    from yggdrasil_b200.ygg1 import write_model
     w = synth.WORKLOADS[key]
-    p = tmp_path / "c3.bin"
-    write_model(synth.workload_layers(w, seed=7), np.linspace(-1, 1, w.shape.vocab), p, extended=w.extended)
-    model = load(p)
+    model = load(workload_model(key))
     x = synth.workload_tokens(w, 4096, 16, seed=2)
     for g in (1, 32):
         b1, b2, s1, s2 = run_both(model, x, g, torch)

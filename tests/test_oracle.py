@@ -33,13 +33,23 @@ def test_generator_bytes_match_reference(rec, case_model):
 
 @pytest.mark.parametrize("rec", CASES + LONG, ids=_ids(CASES) + [f"long-{i}" for i in _ids(LONG)])
 def test_oracle_logits_match_reference(rec, case_model):
+    """Logits, and the int32 accumulators before saturation (the reference int_forward's `drive`, which cpu/ygg.cpp
+    narrows with cvtsepi32_epi8): the oracle's equal the reference's bit for bit."""
     om = O.OracleModel(case_model(rec))
     x = case_tokens(rec)
-    lg = om.logits(x)
+    lg, acc = om.logits(x, acc=True)
     assert lg.dtype == np.float32 and lg.shape == (rec["streams"], rec["steps"], rec["shape"]["vocab"])
     if sha(np.ascontiguousarray(lg).tobytes()) != rec["logits_sha256"]:
         np.testing.assert_array_equal(lg[0, :4, :8], np.asarray(rec["logits_head"], np.float32))
         pytest.fail("oracle logits differ from the reference's")
+    assert [int(acc.min()), int(acc.max())] == rec["acc_range"]
+    assert sha(acc.tobytes()) == rec["acc_sha256"], "oracle accumulators differ from the reference's"
+
+
+def test_accumulators_leave_the_int8_range():
+    """The accumulator pins mean something only if they are not already int8: most shapes saturate."""
+    wide = [r["acc_range"][0] < -128 or r["acc_range"][1] > 127 for r in CASES + LONG]
+    assert sum(wide) >= 0.75 * len(wide) and any(wide[len(CASES):])
 
 
 @pytest.mark.parametrize("rec", CASES[:6], ids=_ids(CASES[:6]))
@@ -77,19 +87,31 @@ def test_reference_binary_matches_oracle(rec, case_model, tmp_path):
 
 
 @pytest.mark.parametrize("rec", WORKLOADS, ids=[w["workload"] for w in WORKLOADS])
-def test_workload_models_match_reference_writer(rec, tmp_path):
-    """The benchmark models: this repository's writer equals the reference's writer on the same layers, and the
-    oracle's logits equal the reference's int_forward on them."""
+def test_workload_models_match_reference_writer(rec, workload_model):
+    """The benchmark models (c4 and c4f with their Zipf-calibrated thresholds from tests/golden/zipf_thresholds.npz):
+    this repository's writer equals the reference's writer on the same layers, and the oracle's logits and
+    accumulators equal the reference's int_forward on them."""
     from yggdrasil_b200 import synth
     w = synth.WORKLOADS[rec["workload"]]
-    p = tmp_path / "w.bin"
-    layers = synth.workload_layers(w, seed=7)
-    from yggdrasil_b200.ygg1 import write_model
-    write_model(layers, np.linspace(-1, 1, w.shape.vocab), p)
+    p = workload_model(rec["workload"])
+    assert p.stat().st_size == rec["model_bytes"]
     assert sha(p.read_bytes()) == rec["model_sha256"]
     x = synth.workload_tokens(w, rec["streams"], rec["steps"], seed=rec["token_seed"])
-    lg = O.OracleModel(p).logits(x)
+    lg, acc = O.OracleModel(p).logits(x, acc=True)
     assert sha(np.ascontiguousarray(lg).tobytes()) == rec["logits_sha256"]
+    assert sha(acc.tobytes()) == rec["acc_sha256"]
+
+
+def test_zipf_fixture_shapes():
+    """The calibrated thresholds: one row per routed layer, one per tree node, finite, not all equal."""
+    from yggdrasil_b200 import synth
+    for key in ("c4", "c4f"):
+        w = synth.WORKLOADS[key]
+        thr = synth.zipf_thresholds_of(w, ROOT)
+        assert thr.shape == (w.shape.n_layers - 1, 2 ** w.shape.router_depth - 1) and thr.dtype == np.float32
+        assert np.isfinite(thr).all() and len(np.unique(thr)) > 1000
+    assert synth.zipf_thresholds_of(synth.WORKLOADS["c5"], ROOT).shape == synth.zipf_thresholds_of(
+        synth.WORKLOADS["c4"], ROOT).shape
 
 
 @pytest.mark.parametrize("rec", EXT_CASES, ids=_ids(EXT_CASES))
@@ -98,10 +120,11 @@ def test_extension_oracle_matches_reference_int_forward(rec, case_model):
     equals the reference's int_forward on the same random model, bit for bit."""
     p = case_model(rec)
     assert sha(p.read_bytes()) == rec["model_sha256"] and p.stat().st_size == rec["model_bytes"]
-    lg = O.OracleModel(p).logits(case_tokens(rec))
+    lg, acc = O.OracleModel(p).logits(case_tokens(rec), acc=True)
     if sha(np.ascontiguousarray(lg).tobytes()) != rec["logits_sha256"]:
         np.testing.assert_array_equal(lg[0, :4, :8], np.asarray(rec["logits_head"], np.float32))
         pytest.fail("oracle logits differ from the reference's int_forward")
+    assert sha(acc.tobytes()) == rec["acc_sha256"]
     np.testing.assert_allclose(O.OracleModel(p).score(case_tokens(rec)), rec["bits"], rtol=1e-12)
 
 
@@ -114,4 +137,6 @@ def test_extension_workload_matches_reference_int_forward(rec, tmp_path):
     write_model(synth.workload_layers(w, seed=7), np.linspace(-1, 1, w.shape.vocab), p, extended=w.extended)
     assert sha(p.read_bytes()) == rec["model_sha256"]
     x = synth.workload_tokens(w, rec["streams"], rec["steps"], seed=rec["token_seed"])
-    assert sha(np.ascontiguousarray(O.OracleModel(p).logits(x)).tobytes()) == rec["logits_sha256"]
+    lg, acc = O.OracleModel(p).logits(x, acc=True)
+    assert sha(np.ascontiguousarray(lg).tobytes()) == rec["logits_sha256"]
+    assert sha(acc.tobytes()) == rec["acc_sha256"]

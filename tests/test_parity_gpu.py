@@ -1,9 +1,11 @@
 """The CUDA path against the oracle and the reference's golden digests, through the C-ABI (GPU).
 
-The bar is bit-exact: routes (the leaf of every layer), the int32 accumulators before saturation, the int8 states and
-the f32 logits must equal the oracle's (the C restatement pinned to cpu/ygg.cpp / cpu/export.py:int_forward by
-tests/test_oracle.py) on every shape of the reference's kernel test, and the logits' sha256 must equal the reference's.
-Score bits are float64 sums in another order than the oracle's: rtol 1e-10 (the north-star bar is 1e-4).
+The bar is bit-exact: routes (the leaf of every layer), the raw int32 accumulators before saturation (compared
+unclamped: most shapes carry values far outside the int8 range), the int8 states and the f32 logits must equal the
+oracle's (the C restatement pinned to cpu/ygg.cpp / cpu/export.py:int_forward by tests/test_oracle.py, accumulators
+included) on every shape of the reference's kernel test and on every benchmark workload (c1-c4f, c4 and c4f with their
+Zipf-calibrated thresholds), and the digests of the logits and of the accumulators must equal the reference's. Score
+bits are float64 sums in another order than the oracle's: rtol 1e-10 (the north-star bar is 1e-4).
 """
 import numpy as np
 import pytest
@@ -38,24 +40,25 @@ def load(path, **kw):
     return Yggdrasil.load(path, backend="b200", **kw)
 
 
-def run_windows(model, om, x, torch):
-    """Step the GPU model and the oracle over windows x (S, T) from zero; compare everything at every step.
-    Returns the GPU logits (S, T, V)."""
+def run_windows(model, om, x, torch, with_acc=False):
+    """Step the GPU model and the oracle over windows x (S, T) from zero; compare routes, raw accumulators, states
+    and logits at every step. Returns the GPU logits (S, T, V) [and accumulators (S, T, L, n)]."""
     s, t = x.shape
     st = model.init_state(s)
     ost = om.init_state(s)
     out = np.empty((s, t, model.vocab), np.float32)
+    accs = np.empty((s, t, model.layers, model.n), np.int32)
     for i in range(t):
         lg, nst, rt, acc = model.step_debug(x[:, i], st)
-        olg, ort = om.step(x[:, i], ost, routes=True)
+        olg, ort, oacc = om.step(x[:, i], ost, routes=True, acc=True)
         np.testing.assert_array_equal(rt.cpu().numpy(), ort, err_msg=f"routes at step {i}")
+        np.testing.assert_array_equal(acc.cpu().numpy(), oacc, err_msg=f"raw accumulators at step {i}")
         np.testing.assert_array_equal(nst.cpu().numpy(), ost, err_msg=f"states at step {i}")
-        got = acc.cpu().numpy()
-        np.testing.assert_array_equal(np.clip(got, -128, 127).astype(np.int8), ost, err_msg=f"acc at step {i}")
         np.testing.assert_array_equal(lg.cpu().numpy(), olg, err_msg=f"logits at step {i}")
-        out[:, i] = olg
+        out[:, i] = lg.cpu().numpy()
+        accs[:, i] = acc.cpu().numpy()
         st = nst
-    return out
+    return (out, accs) if with_acc else out
 
 
 @pytest.mark.parametrize("rec", CASES + EXT_CASES, ids=_ids(CASES) + [f"ext-{i}" for i in _ids(EXT_CASES)])
@@ -63,23 +66,30 @@ def test_step_bit_exact(rec, case_model, torch):
     path = case_model(rec)
     model, om = load(path), O.OracleModel(path)
     x = case_tokens(rec)
-    lg = run_windows(model, om, x, torch)
+    lg, acc = run_windows(model, om, x, torch, with_acc=True)
     assert sha(np.ascontiguousarray(lg).tobytes()) == rec["logits_sha256"]
+    assert sha(acc.tobytes()) == rec["acc_sha256"], "accumulators differ from the reference int_forward's"
     model.status()
 
 
 @pytest.mark.parametrize("rec", LONG, ids=_ids(LONG))
 def test_long_sequences_bit_exact(rec, case_model, torch):
+    """512 steps (deep state dynamics, long runs of saturation): the logits and the raw accumulators of every step
+    against the reference's digests."""
     path = case_model(rec)
     model = load(path)
     x = case_tokens(rec)
     st = model.init_state(x.shape[0])
-    out = []
+    out, accs = [], []
     for i in range(x.shape[1]):
-        lg, st = model.step(x[:, i], st)
+        lg, st, _, acc = model.step_debug(x[:, i], st)
         out.append(lg.cpu().numpy())
+        accs.append(acc.cpu().numpy())
     lg = np.stack(out, 1)
+    acc = np.stack(accs, 1)
     assert sha(np.ascontiguousarray(lg).tobytes()) == rec["logits_sha256"]
+    assert [int(acc.min()), int(acc.max())] == rec["acc_range"]
+    assert sha(np.ascontiguousarray(acc).tobytes()) == rec["acc_sha256"]
 
 
 @pytest.mark.parametrize("rec", CASES[::2] + EXT_CASES,
@@ -210,29 +220,30 @@ def test_generate_greedy_matches_oracle(case_model, torch):
 
 
 @pytest.mark.parametrize("rec", WORKLOADS + EXT_WORKLOADS, ids=[w["workload"] for w in WORKLOADS + EXT_WORKLOADS])
-def test_benchmark_workloads_bit_exact(rec, tmp_path, torch):
+def test_benchmark_workloads_bit_exact(rec, workload_model, oracle_of, torch):
+    """Every benchmark model, c4 (the north-star 730M shape, table storage, Zipf-calibrated) and c4f (factored)
+    included: routes, raw accumulators, states and logits at every step against the oracle, and the digests of the
+    logits and accumulators and the score bits against the reference's int_forward."""
     from yggdrasil_b200 import synth
-    from yggdrasil_b200.ygg1 import write_model
     w = synth.WORKLOADS[rec["workload"]]
-    p = tmp_path / "w.bin"
-    write_model(synth.workload_layers(w, seed=7), np.linspace(-1, 1, w.shape.vocab), p, extended=w.extended)
-    model, om = load(p), O.OracleModel(p)
+    p = workload_model(rec["workload"])
+    model, om = load(p), oracle_of(p)
     x = synth.workload_tokens(w, rec["streams"], rec["steps"], seed=rec["token_seed"])
-    lg = run_windows(model, om, x, torch)
+    lg, acc = run_windows(model, om, x, torch, with_acc=True)
     assert sha(np.ascontiguousarray(lg).tobytes()) == rec["logits_sha256"]
+    assert sha(acc.tobytes()) == rec["acc_sha256"]
     np.testing.assert_allclose(model.score(x), rec["bits"], rtol=BITS_RTOL)
 
 
-@pytest.mark.parametrize("key", ["c3", "c3n96"])
-def test_large_batch_sampled_streams(key, tmp_path, torch):
-    """At the benchmark batch (65536 streams of the c3 shape, at d 128 and d 96), a checksum over all streams' states
-    and logits is reproducible, and a sample of streams equals the oracle exactly after 3 steps."""
+@pytest.mark.parametrize("key", ["c3", "c3n96", "c4", "c4f"])
+def test_large_batch_sampled_streams(key, workload_model, oracle_of, torch):
+    """At the benchmark batch (65536 streams of the c3 shape at d 128 and d 96, and of the c4 and c4f shapes with
+    their Zipf-calibrated routers), a checksum over all streams' states and logits is reproducible, and a sample of
+    streams equals the oracle exactly after 3 steps."""
     from yggdrasil_b200 import synth
-    from yggdrasil_b200.ygg1 import write_model
     w = synth.WORKLOADS[key]
-    p = tmp_path / "c3.bin"
-    write_model(synth.workload_layers(w, seed=7), np.linspace(-1, 1, w.shape.vocab), p, extended=w.extended)
-    model, om = load(p), O.OracleModel(p)
+    p = workload_model(key)
+    model, om = load(p), oracle_of(p)
     B = 65536
     x = synth.workload_tokens(w, B, 3, seed=0)
     st = model.init_state(B)
@@ -299,20 +310,20 @@ def test_every_launch_configuration_bit_exact(cfg, rec, case_model, torch, monke
 
 @pytest.mark.parametrize("cfg", list(LAUNCH_CONFIGS))
 @pytest.mark.parametrize("rec", WORKLOADS + EXT_WORKLOADS, ids=[w["workload"] for w in WORKLOADS + EXT_WORKLOADS])
-def test_fast_instances_bit_exact(cfg, rec, tmp_path, torch, monkeypatch):
-    """The benchmark shapes run the fast instances (shape fixed at compile time): every launch configuration against
-    the oracle and the reference's digest, with 7 streams (ragged) in the score path."""
+def test_fast_instances_bit_exact(cfg, rec, workload_model, oracle_of, torch, monkeypatch):
+    """The benchmark shapes run the fast instances (shape fixed at compile time; c4 and c4f are the n128 L4 R2=32
+    V256 instances, the north-star target): every launch configuration against the oracle and the reference's
+    digests, with 7 streams (ragged) in the score path."""
     from yggdrasil_b200 import synth
-    from yggdrasil_b200.ygg1 import write_model
     for k, v in LAUNCH_CONFIGS[cfg].items():
         monkeypatch.setenv(k, v)
     w = synth.WORKLOADS[rec["workload"]]
-    p = tmp_path / "w.bin"
-    write_model(synth.workload_layers(w, seed=7), np.linspace(-1, 1, w.shape.vocab), p, extended=w.extended)
-    model, om = load(p), O.OracleModel(p)
+    p = workload_model(rec["workload"])
+    model, om = load(p), oracle_of(p)
     x = synth.workload_tokens(w, rec["streams"], rec["steps"], seed=rec["token_seed"])
-    lg = run_windows(model, om, x, torch)
+    lg, acc = run_windows(model, om, x, torch, with_acc=True)
     assert sha(np.ascontiguousarray(lg).tobytes()) == rec["logits_sha256"]
+    assert sha(acc.tobytes()) == rec["acc_sha256"]
     x7 = synth.workload_tokens(w, 7, 20, seed=3)
     np.testing.assert_allclose(model.score(x7), om.score(x7), rtol=BITS_RTOL)
 

@@ -25,12 +25,17 @@ def _ptr(t):
     return ctypes.c_void_p(t.data_ptr()) if t is not None else None
 
 
-def test_no_alloc_equals_workspace_entry_on_two_calls(case_model):
+NO_ALLOC_CASES = [golden("kernel_cases.json")[0], [r for r in golden("extended_cases.json") if "shape" in r][0]]
+
+
+@pytest.mark.parametrize("rec", NO_ALLOC_CASES, ids=["n128", "ext-n96"])
+def test_no_alloc_equals_workspace_entry_on_two_calls(rec, case_model):
+    """n128, and a d_state 96 model, whose padded state copy (the grouped path pads the caller's 96 coordinates to
+    the device layout's 128) also lives in the fixed scratch: with a carried state and with a zero start state."""
     import torch
 
     from yggdrasil_b200 import Yggdrasil, _native
     lib = _native.lib()
-    rec = golden("kernel_cases.json")[0]
     model = Yggdrasil.load(case_model(rec), backend="b200")
     dev, v = model.device, rec["shape"]["vocab"]
     stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)

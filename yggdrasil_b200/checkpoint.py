@@ -11,9 +11,14 @@ From a checkpoint and that record, the int8 model can be rebuilt without calibra
 does. This module does that rebuild with numpy and torch.
 
 Transitions: blockdiag expm((G - G^T) / 2) uses torch.linalg.matrix_exp in float64 (the reference's Triton backend
-computes the same matrix the same way, yggdrasil/inference_triton.py:109-114). The reference's exporter uses JAX's
-expm; the two agree to ~1e-15, so a transition coefficient rint(2^14 A) could differ only where A lies within ~1e-11
-of a half step.
+computes the same matrix with torch, yggdrasil/inference_triton.py:109-114; its exporter uses JAX's expm). Two float64
+expm implementations agree to ~1e-15, so a transition coefficient rint(2^14 A) could differ only where A lies within
+~1e-11 of a half step; the tests compare transitions64 with scipy's float64 expm.
+
+Quantisation (`quantize`) is organised as a scale plan per layer (`scale_plans`: every state, reference and readout
+scale, decided from the calibration maxima before any weight is touched), then one function per kind of weight
+(readout and head, token input, router, layer input) that folds the planned scales in and rounds. The rounding
+steps themselves are the reference's (cpu/export.py:158-265), since the rebuilt file must equal its export.
 """
 from __future__ import annotations
 
@@ -150,78 +155,132 @@ class LayerStats:
     readout_row_max: np.ndarray
 
 
-def _qrow(w):
-    s = np.maximum(np.abs(w).max(-1, keepdims=True), SCALE_FLOOR) / INT8_MAX
-    return np.rint(w / s).astype(np.int64), s[..., 0]
+@dataclasses.dataclass
+class ScalePlan:
+    """The quantisation scales of one layer, fixed before any tensor is quantised.
+
+    state: the f64 scale of each state coordinate (n,): one value for the layer (tensor mode) or one per group of 16
+    coordinates; ref: the layer's reference scale (the largest group scale); readout: the scale of the readout codes
+    zq; below, below_ref: the state scales of the layer underneath relative to its reference scale, and that reference
+    (None, 1.0 for the token layer). A layer's state is stored in units of `state`, so every weight that reads or
+    writes a state has the state scales folded into it."""
+    state: np.ndarray
+    ref: float
+    readout: float
+    below: np.ndarray | None
+    below_ref: float
 
 
-def _qten(w):
-    s = max(np.abs(w).max(), SCALE_FLOOR) / INT8_MAX
-    return np.rint(w / s).astype(np.int64), s
+def scale_plans(layers, stats, hmargin=1.0, group=False) -> list:
+    """The ScalePlan of every layer, from the calibration maxima: state range x hmargin over 127, per layer or per
+    group of 16 coordinates (a group's maximum is floored at 1e-3 of the layer's), and the readout range over 127."""
+    plans = []
+    below, below_ref = None, 1.0
+    for fl, st in zip(layers, stats):
+        if group:
+            gmax = np.asarray(st.state_group_max, np.float64)
+            floor = GROUP_SCALE_FLOOR * max(np.max(gmax), SCALE_FLOOR)
+            per_group = np.maximum(gmax, floor) * hmargin / INT8_MAX
+            state, ref = np.repeat(per_group, STATE_GROUP), float(per_group.max())
+        else:
+            ref = st.state_max * hmargin / INT8_MAX
+            state = np.full(fl.n, ref)
+        plans.append(ScalePlan(state=state, ref=ref, readout=max(st.readout_max, SCALE_FLOOR) / INT8_MAX,
+                               below=below, below_ref=below_ref))
+        below, below_ref = state / ref, ref
+    return plans
 
 
-def _sat16(x):
-    return np.clip(np.rint(x), -32768, 32767)
+def int8_codes(w, per_row: bool):
+    """Symmetric int8 codes of w and their scale: one per row (over the last axis; an array) or one for the tensor (a
+    float). scale = max(|w|, 1e-12) / 127 and code = rint(w / scale), in float64."""
+    w = np.asarray(w, np.float64)
+    if per_row:
+        scale = np.maximum(np.abs(w).max(-1), SCALE_FLOOR) / INT8_MAX
+        return np.rint(w / scale[..., None]).astype(np.int64), scale
+    scale = max(np.abs(w).max(), SCALE_FLOOR) / INT8_MAX
+    return np.rint(w / scale).astype(np.int64), scale
 
 
-def _factor(fl, sc):
-    vt, s_vt = _qten(fl.token_embed)
-    su = np.maximum(np.abs(fl.input_proj).reshape(len(fl.input_proj), -1).max(-1), SCALE_FLOOR) / INT8_MAX
-    return FactoredInput(input_proj=np.rint(fl.input_proj / su[:, None, None]).astype(np.int64),
-                         input_scale=su.astype(f32), bias=_sat16(fl.bias / sc).astype(np.int16), token_code=vt,
-                         token_scale=(s_vt / sc).astype(f32))
+def int16_saturated(x, rows_per_pass: int = EXPERT_CHUNK):
+    """rint(x) saturated to int16, computed `rows_per_pass` leading rows at a time (the tables are large)."""
+    out = np.empty(x.shape, np.int16)
+    for a in range(0, len(x), rows_per_pass):
+        out[a:a + rows_per_pass] = np.clip(np.rint(x[a:a + rows_per_pass]), -32768, 32767)
+    return out
+
+
+def _readout_and_head(fl, plan, group):
+    """Readout codes P and the scale of zq = rint(f32(P q) * scale); unembedding codes Q and their scale. With group
+    scales the state scales go into the readout rows (one scale per expert and row), and Q has one scale per class."""
+    if group:
+        codes, row_scale = int8_codes(fl.readout * plan.state[None, None, :], per_row=True)
+        readout_scale = (row_scale / plan.readout).astype(f32)
+    else:
+        codes, s = int8_codes(fl.readout, per_row=False)
+        readout_scale = f32(s * plan.ref / plan.readout)
+    head, head_scale = int8_codes(fl.unembed, per_row=group)
+    return codes, readout_scale, head, f32(head_scale * plan.readout)
+
+
+def _input_part(fl, plan, factored):
+    """The token input in state units: the token layer keeps T_x[x] only; a routed layer keeps T_r[x] as int16 tables
+    or, factored, int8 U_r (one scale per expert) and token codes v[x] (one scale) plus an int16 bias c_r."""
+    if fl.token_layer:
+        diag = fl.table[np.arange(fl.table.shape[1]), np.arange(fl.table.shape[1])]
+        return {"table": int16_saturated(diag / plan.state)[:, None]}
+    if not factored:
+        return {"table": int16_saturated(fl.table / plan.state)}
+    codes, code_scale = int8_codes(fl.token_embed, per_row=False)
+    expert_scale = np.maximum(np.abs(fl.input_proj).reshape(len(fl.input_proj), -1).max(-1), SCALE_FLOOR) / INT8_MAX
+    return {"factored": FactoredInput(
+        input_proj=np.rint(fl.input_proj / expert_scale[:, None, None]).astype(np.int64),
+        input_scale=expert_scale.astype(f32), bias=int16_saturated(fl.bias / plan.state), token_code=codes,
+        token_scale=(code_scale / plan.state).astype(f32))}
+
+
+def _router_part(fl, plan, group):
+    """Router rows on the layer below's stored state (its relative scales folded in, one int8 scale per node), the
+    token part of each node test folded into per-(token, node) thresholds in those units, and rho's epsilon in the
+    units of the layer below."""
+    F = fl.router_token_dim
+    token_part = fl.router_embed @ fl.router_weight[:, :F].T + fl.router_bias[None, :]
+    rows, node_scale = int8_codes(fl.router_weight[:, F:] * plan.below[None, :], per_row=True)
+    out = {"router_weight": rows, "router_threshold": (-token_part / node_scale[None, :]).astype(f32),
+           "rms_eps": f32(RMS_EPS / plan.below_ref ** 2)}
+    if group:
+        out["state_r2"] = (plan.below[::STATE_GROUP] ** 2).astype(f32)
+    return out
+
+
+def _layer_input_part(fl, plan, st, group):
+    """The low-rank input from the layer below: V' rows on its stored state (per-row scales, over the layer-input
+    range), and U'_r (one scale) mapped into this layer's state units, per coordinate with group scales."""
+    down, row_scale = int8_codes(fl.layer_input_down * plan.below[None, :], per_row=True)
+    code_scale = max(st.layer_input_max, SCALE_FLOOR) / INT8_MAX
+    proj, proj_scale = int8_codes(fl.layer_input_proj, per_row=False)
+    to_state = proj_scale * code_scale / plan.state
+    return {"layer_input_down": down, "layer_input_down_scale": (row_scale / code_scale).astype(f32),
+            "layer_input_proj": proj, "layer_input_scale": to_state.astype(f32) if group else f32(to_state[0])}
 
 
 def quantize(layers, stats, hmargin=1.0, group=False, factored=False):
-    """Int8 layers from float layers and calibration maxima, one state scale per layer or per 16 coordinates
-    (group). The steps of cpu/export.py:216-265, so that a file rebuilt here equals the reference's export."""
-    out, rel_prev, s_prev = [], None, 1.0
-    for fl, st in zip(layers, stats):
-        if group:
-            g = np.maximum(np.asarray(st.state_group_max, np.float64),
-                           GROUP_SCALE_FLOOR * max(np.max(st.state_group_max), SCALE_FLOOR))
-            sg = g * hmargin / INT8_MAX
-            sc, s_ref = np.repeat(sg, STATE_GROUP), float(sg.max())
-        else:
-            s_ref = st.state_max * hmargin / INT8_MAX
-            sc = np.full(fl.n, s_ref)
-        s_z = max(st.readout_max, SCALE_FLOOR) / INT8_MAX
-        if group:
-            readout, s_p = _qrow(fl.readout * sc[None, None, :])
-            readout_scale = (s_p / s_z).astype(f32)
-        else:
-            readout, s_p = _qten(fl.readout)
-            readout_scale = f32(s_p * s_ref / s_z)
-        unembed, s_q = (_qrow if group else _qten)(fl.unembed)
-        q = IntLayer(token_layer=fl.token_layer, n=fl.n, block=fl.block, depth=fl.depth,
-                     transition=np.rint(fl.transition * 2.0 ** SHIFT).astype(np.int64), readout=readout,
-                     readout_scale=readout_scale, unembed=unembed, unembed_scale=f32(s_q * s_z))
-        if fl.token_layer:
-            ar = np.arange(fl.table.shape[1])
-            q.table = _sat16(fl.table[ar, ar] / sc).astype(np.int16)[:, None]
-        elif factored:
-            q.factored = _factor(fl, sc)
-        else:
-            q.table = np.empty(fl.table.shape, np.int16)
-            for j in range(0, len(fl.table), EXPERT_CHUNK):
-                q.table[j:j + EXPERT_CHUNK] = _sat16(fl.table[j:j + EXPERT_CHUNK] / sc)
+    """Int8 layers from float layers and calibration maxima: the scales of every layer first (scale_plans), then
+    each part of each layer quantised on its own. Every rounding is the reference's (cpu/export.py:158-265: the same
+    float64 quotients, rint, int8 and int16 saturation, and the f32 casts of the stored scales), so that a file
+    rebuilt here equals the reference's export byte for byte."""
+    plans = scale_plans(layers, stats, hmargin, group)
+    out = []
+    for fl, st, plan in zip(layers, stats, plans):
+        readout, readout_scale, head, head_scale = _readout_and_head(fl, plan, group)
+        kw = _input_part(fl, plan, factored)
         if not fl.token_layer:
-            F = fl.router_token_dim
-            token_part = fl.router_embed @ fl.router_weight[:, :F].T + fl.router_bias[None, :]
-            q.router_weight, sw = _qrow(fl.router_weight[:, F:] * rel_prev[None, :])
-            q.router_threshold = (-token_part / sw[None, :]).astype(f32)
-            q.rms_eps = f32(RMS_EPS / s_prev ** 2)
-            if group:
-                q.state_r2 = (rel_prev[::STATE_GROUP] ** 2).astype(f32)
+            kw.update(_router_part(fl, plan, group))
             if fl.layer_input_down is not None:
-                q.layer_input_down, sv = _qrow(fl.layer_input_down * rel_prev[None, :])
-                s_v = max(st.layer_input_max, SCALE_FLOOR) / INT8_MAX
-                q.layer_input_down_scale = (sv / s_v).astype(f32)
-                q.layer_input_proj, s_u = _qten(fl.layer_input_proj)
-                scale = s_u * s_v / sc
-                q.layer_input_scale = scale.astype(f32) if group else f32(scale[0])
-        rel_prev, s_prev = sc / s_ref, s_ref
-        out.append(q)
+                kw.update(_layer_input_part(fl, plan, st, group))
+        out.append(IntLayer(token_layer=fl.token_layer, n=fl.n, block=fl.block, depth=fl.depth,
+                            transition=np.rint(fl.transition * 2.0 ** SHIFT).astype(np.int64), readout=readout,
+                            readout_scale=readout_scale, unembed=head, unembed_scale=head_scale, **kw))
     return out
 
 

@@ -654,19 +654,41 @@ static __device__ __align__(256) uint8_t g_noalloc_scratch[ygg::kNoAllocScratchB
 
 namespace ygg {
 
-// The device address of the fixed scratch on `device`, which must be the current device. Resolved once per device
-// (the array's name is only a host-side handle); later calls return the cached address.
+// The context current on this thread (the driver's cuCtxGetCurrent, reached through the runtime's entry-point query
+// so that the library needs no link against the driver library); null when it cannot be asked.
+static void *current_context() {
+    using CtxGetCurrent = int (*)(void **);
+    static CtxGetCurrent fn = [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return (CtxGetCurrent) nullptr;
+        return (CtxGetCurrent)f;
+    }();
+    void *ctx = nullptr;
+    if (fn == nullptr || fn(&ctx) != 0) return nullptr;
+    return ctx;
+}
+
+// The device address of the fixed scratch on `device`, which must be the current device. The array's name is only a
+// host-side handle, so the address is looked up (cudaGetSymbolAddress) the first time a device is seen and cached
+// with the context it belongs to; when the device's context is another one by the next call (the primary context
+// was reset, or a different context was made current), the address is looked up again.
 cudaError_t noalloc_scratch(int device, void **ptr, size_t *bytes) {
     constexpr int kMaxDev = 64;
     static std::mutex mu;
     static void *addr[kMaxDev] = {};
+    static void *owner[kMaxDev] = {};
     if (device < 0 || device >= kMaxDev) return cudaErrorInvalidDevice;
     std::lock_guard<std::mutex> lock(mu);
-    if (addr[device] == nullptr) {
+    void *ctx = current_context();
+    if (addr[device] == nullptr || ctx == nullptr || ctx != owner[device]) {
         void *p = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess) return e;
         addr[device] = p;
+        owner[device] = current_context();   // the lookup above made the device's context current if it was not
     }
     *ptr = addr[device];
     *bytes = kNoAllocScratchBytes;

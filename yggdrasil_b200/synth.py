@@ -156,9 +156,48 @@ WORKLOADS = {
 }
 
 
-def workload_layers(w: Workload, seed: int = 7):
-    """Layers of a benchmark workload: the random generator plus N(0, 0.02) int8 router rows."""
-    return gaussian_router_rows(random_layers(w.shape, seed), seed + 1)
+def workload_layers(w: Workload, seed: int = 7, thresholds=None):
+    """Layers of a benchmark workload: the random generator plus N(0, 0.02) int8 router rows. thresholds: the
+    per-node router thresholds of the routed layers, (L - 1, 2^D - 1) f32, shared by every token (the Zipf-calibrated
+    workloads c4, c4f and c5 take them from their fixture, ZIPF_FIXTURE); None keeps the generator's."""
+    layers = gaussian_router_rows(random_layers(w.shape, seed), seed + 1)
+    if thresholds is not None:
+        apply_thresholds(layers, thresholds)
+    return layers
+
+
+def apply_thresholds(layers, thresholds, only: int = 0):
+    """Set the router thresholds of the routed layers to per-node values shared by every token: thresholds (L - 1,
+    2^D - 1) f32, row l - 1 for layer l; only > 0 sets that layer alone."""
+    thr = np.asarray(thresholds, f32)
+    for l in range(1, len(layers)):
+        if only and l != only:
+            continue
+        q = layers[l]
+        q.router_threshold = np.ascontiguousarray(np.broadcast_to(thr[l - 1], (q_vocab(layers), thr.shape[1])),
+                                                  dtype=f32)
+    return layers
+
+
+def q_vocab(layers) -> int:
+    """Vocabulary of a model's layers (the token layer has one expert per token)."""
+    return int(layers[0].transition.shape[0])
+
+
+# Router thresholds of the Zipf-calibrated workloads (tests/golden/make_golden.py computes them with the C oracle and
+# pins the resulting models to the reference's writer and int_forward): an .npz with one (L - 1, 2^D - 1) f32 array
+# per model key (c4, c4f). c5 scores the c4 model.
+ZIPF_FIXTURE = "tests/golden/zipf_thresholds.npz"
+
+
+def zipf_thresholds_of(w: Workload, root) -> np.ndarray | None:
+    """The fixture thresholds of a Zipf-calibrated workload (None for the others); root: the repository root."""
+    if w.leaves != "zipf":
+        return None
+    from pathlib import Path
+    key = w.model or next(k for k, v in WORKLOADS.items() if v is w)
+    with np.load(Path(root) / ZIPF_FIXTURE) as z:
+        return z[key]
 
 
 def workload_tokens(w: Workload, streams: int, steps: int, seed: int = 0) -> np.ndarray:
