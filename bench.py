@@ -770,7 +770,8 @@ def e2e_step_api(model, w, state, B, W, rank, world, dist, dev, stream, steps=64
 def batch1(model, w, n1, W, dev, stream):
     """Batch 1 on rank 0: (a) device time per token of one stream scoring a row (the launch policy runs the layer
     wavefront for n = 128; state on chip, the f64 softmax/NLL of every token included, as `ygg time` includes its
-    softmax); (b) one step() call per token through the public API (CUDA-graph replay at batch 1, host tokens). The
+    softmax); (b) one step(tokens, state) call per token through the public API, tokens already on the device (as
+generate() keeps them), each call returning new logits and state tensors. The
     warm-up runs other tokens than the timed ones, so the timed tokens find their leaves' records where a new stream
     would (mostly not in L2)."""
     import torch
@@ -788,15 +789,13 @@ def batch1(model, w, n1, W, dev, stream):
     b1e.record(stream)
     torch.cuda.synchronize(dev)
     b1 = b0.elapsed_time(b1e) * 1e3 / n1
-    h1 = t1.cpu()
-    h1w = t1w.cpu()
     s1 = model.init_state(1)
     for i in range(W):
-        _, s1 = model.step(h1w[0, i:i + 1], s1)
+        _, s1 = model.step(t1w[0, i:i + 1], s1)
     torch.cuda.synchronize(dev)
     b0.record(stream)
     for i in range(n1):
-        _, s1 = model.step(h1[0, i:i + 1], s1)
+        _, s1 = model.step(t1[0, i:i + 1], s1)
     b1e.record(stream)
     torch.cuda.synchronize(dev)
     return b1, b0.elapsed_time(b1e) * 1e3 / n1
