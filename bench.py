@@ -400,6 +400,8 @@ def main():
     ap.add_argument("--sweep", default="", help="comma-separated streams per GPU: a batch sweep, one line per size")
     ap.add_argument("--global-streams", type=int, default=65536,
                     help="strong scaling: also time this many streams split over the N GPUs (0: off)")
+    ap.add_argument("--no-float", dest="float", action="store_false",
+                    help="skip the fp32 float step measurement (backend b200f, one-GPU runs)")
     ap.add_argument("--extra", default="c4", help="also measure this workload at 65 536 and 262 144 streams per GPU "
                     "(and 262 144 global under torchrun), with its e2e through step(); '' to skip")
     args = ap.parse_args()
@@ -473,6 +475,11 @@ def main():
             if keep:
                 xmodel, xstate = r.pop("model"), r.pop("state")
                 r["e2e_step_api"] = e2e_step_api(xmodel, xw, xstate, xb, W, rank, world, dist, dev, stream)
+                for consumer in ("host", "device"):
+                    v, ks = e2e_serving_loop(xmodel, xw, xstate, xb, xk, W, rank, world, dist, dev, stream, consumer)
+                    r.setdefault("e2e_serving", {})[consumer] = {
+                        "value": v, "unit": UNIT, "steps": ks, "h2d_bytes_per_step": xb * 4,
+                        "d2h_bytes_per_step": xb * (xw.shape.vocab * 4 if consumer == "host" else 4)}
                 del xmodel, xstate
                 torch.cuda.empty_cache()
             extra[f"B{xb}"] = summarise(r, xw, xb, world, peak, kind, traffic_tab.get(f"{args.extra}_B{xb}"))
@@ -482,6 +489,12 @@ def main():
         else:
             strong[args.extra] = {"global_streams": 262144, "streams_per_gpu": 262144,
                                   "value": extra["B262144"]["value"], "ms_per_step": extra["B262144"]["ms_per_step"]}
+
+    # ---- the fp32 float step (backend "b200f") on the reference's enwik8 large float model, next to the reference's
+    # published 80.1 us/token at batch 1 (its Triton backend, README.md:43); rank 0 of a one-GPU run
+    flt = None
+    if rank == 0 and world == 1 and args.float:
+        flt = run_float(dev, stream, W)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -528,8 +541,83 @@ def main():
             "clocks": clk.summary()}
     if extra:
         line[args.extra] = {"workload": synth.WORKLOADS[args.extra].name, **extra}
+    if flt:
+        line["float_step"] = flt
     print(json.dumps(line))
     return 0
+
+
+def run_float(dev, stream, W, n1=512, big=16384):
+    """The fp32 step of backend "b200f" on a random float model of the enwik8 large shape (synth.FLOAT_ENWIK8_LARGE):
+    (a) batch 1 through step(tokens, state) with cuda_graph=True, the reference Triton backend's own fastest setting
+    (one graph replay per token, host tokens), per token; (b) the device time of one batch-1 step, from a CUDA graph
+    of 32 steps replayed; (c) tokens/s at `big` streams (kernel time, tokens resident)."""
+    import torch
+
+    from yggdrasil_b200 import synth
+    from yggdrasil_b200.float_backend import B200FloatYggdrasil
+    shape = synth.FLOAT_ENWIK8_LARGE
+    layers, ob = synth.random_float_layers(shape, seed=0)
+    model = B200FloatYggdrasil(layers, ob, device=dev, cuda_graph=True)
+    del layers
+    rng = np.random.default_rng(5)
+    toks = rng.integers(0, shape["vocab"], n1 + W).astype(np.int32)
+    st = model.init_state(1)
+    for i in range(W):
+        _, st = model.step(toks[i:i + 1], st)
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    for i in range(n1):
+        _, st = model.step(toks[W + i:W + i + 1], st)
+    torch.cuda.synchronize(dev)
+    api_us = (time.perf_counter() - t0) / n1 * 1e6
+    # device time per step: a graph of G step_into launches at batch 1
+    G = 32
+    d_tok = torch.as_tensor(toks[:G]).to(dev)
+    s1 = model.init_state(1)
+    lg = torch.empty(1, model.classes, device=dev)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        for i in range(G):
+            model.step_into(d_tok[i:i + 1], s1, s1, lg)
+    stream.wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(G):
+            model.step_into(d_tok[i:i + 1], s1, s1, lg)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    reps = 16
+    for _ in range(reps):
+        graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    dev_us = e0.elapsed_time(e1) * 1e3 / (reps * G)
+    del graph
+    # throughput at `big` streams
+    xb = torch.as_tensor(rng.integers(0, shape["vocab"], (16, big)).astype(np.int32)).to(dev)
+    sb = model.init_state(big)
+    lb = torch.empty(big, model.classes, device=dev)
+    for i in range(W):
+        model.step_into(xb[i % 16], sb, sb, lb)
+    torch.cuda.synchronize(dev)
+    K = 32
+    e0.record(stream)
+    for i in range(K):
+        model.step_into(xb[i % 16], sb, sb, lb)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    tps = big * K / (e0.elapsed_time(e1) / 1e3)
+    model.status()
+    return {"model": "enwik8 large float shape (V256 L5 d256 b16 D10 F16 k64 R32 R2=64), random weights, fp32",
+            "batch1_step_api_us_per_token": api_us, "batch1_step_device_us": dev_us,
+            "reference_published_us_per_token": 80.1,
+            "reference_published_note": "Triton backend, batch 1, one GPU (README.md:43)",
+            "streams": big, "tokens_per_s": tps}
 
 
 def load_traffic():
@@ -663,7 +751,7 @@ def summarise(r, w, B, world, peak, kind, traffic):
     return {"value": r["value"], "ms_per_step": r["ms_per_step"], "streams_per_gpu": B,
             "effective_leaves_per_layer": r["effective_leaves_per_layer"],
             "distinct_leaves_per_layer": r["distinct_leaves_per_layer"], "roofline": roof,
-            **({"e2e_step_api": r["e2e_step_api"]} if "e2e_step_api" in r else {})}
+            **{k: r[k] for k in ("e2e_step_api", "e2e_serving") if k in r}}
 
 
 def strong_entry(r, global_streams, world):
@@ -671,16 +759,22 @@ def strong_entry(r, global_streams, world):
             "ms_per_step": r["ms_per_step"]}
 
 
-def e2e_serving_loop(model, w, state, B, K, W, rank, world, dist, dev, stream):
-    """End to end through step_into with pinned host tokens in and logits out every step: a serving loop with two
-    buffers each way; while step i runs (in place), the tokens of step i + 1 go up on one copy stream and the logits of
-    step i - 1 come down on another; events keep each buffer's writer after its last reader. Returns (tokens/s, steps)."""
+def e2e_serving_loop(model, w, state, B, K, W, rank, world, dist, dev, stream, consumer="host"):
+    """End to end through step_into with pinned host tokens in and a result out every step: a serving loop with two
+    buffers each way; while step i runs (in place), the tokens of step i + 1 go up on one copy stream and the result of
+    step i - 1 comes down on another; events keep each buffer's writer after its last reader. consumer "host": the
+    (B, V) float32 logits come down; "device": the logits stay on the GPU and only each stream's greedy next token
+    (argmax on the device, int32) comes down. Returns (tokens/s, steps)."""
     import torch
 
     from yggdrasil_b200 import synth
     ke = min(K, 256)
     h_tok = torch.as_tensor(synth.workload_tokens(w, ke, B, seed=20_000 + rank)).pin_memory()
-    h_lg = [torch.empty(B, model.vocab, dtype=torch.float32).pin_memory() for _ in range(2)]
+    if consumer == "host":
+        h_lg = [torch.empty(B, model.vocab, dtype=torch.float32).pin_memory() for _ in range(2)]
+    else:
+        h_lg = [torch.empty(B, dtype=torch.int32).pin_memory() for _ in range(2)]
+        d_next = [torch.empty(B, dtype=torch.int32, device=dev) for _ in range(2)]
     d_tokb = [torch.empty(B, dtype=torch.int32, device=dev) for _ in range(2)]
     d_lg = [torch.empty(B, model.vocab, dtype=torch.float32, device=dev) for _ in range(2)]
     up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
@@ -703,12 +797,14 @@ def e2e_serving_loop(model, w, state, B, K, W, rank, world, dist, dev, stream):
             stream.wait_event(uploaded[j])
             stream.wait_event(downloaded[j])       # the logits buffer's previous download is done
             model.step_into(d_tokb[j], st, st, d_lg[j])
+            if consumer != "host":
+                d_next[j].copy_(d_lg[j].argmax(-1))
             stepped[j].record(stream)
             if i + 1 < n:
                 upload(i + 1)
             down.wait_event(stepped[j])
             with torch.cuda.stream(down):
-                h_lg[j].copy_(d_lg[j], non_blocking=True)
+                h_lg[j].copy_(d_lg[j] if consumer == "host" else d_next[j], non_blocking=True)
                 downloaded[j].record(down)
         stream.wait_stream(down)
 

@@ -128,6 +128,54 @@ YGG_API int ygg_status(const ygg_model *m, void *stream, int clear, int *status_
  * counterpart in the reference (its CPU kernel has no device waits). */
 YGG_API int ygg_selftest_wait(int device, long long cycles, void *stream, int *status_out);
 
+/* ---- the fp32 float step (backend "b200f") ------------------------------------------------------------------------
+ * The reference's float inference model: yggdrasil/inference.py:42-75 (route, update, step) as its Triton backend
+ * fuses it (yggdrasil/inference_triton.py:21-106 and the torch.addmm head, :187-194). Weights are float32 arrays in
+ * the checkpoint's own shapes, with the tables T_r[x] = U_r v(x) + c_r and the transitions
+ * A_r = diag(clip(decay, -1, 1)) blockdiag(expm((G - G^T) / 2)) already formed (inference_triton.py:109-120). */
+typedef struct ygg_fmodel ygg_fmodel;
+
+typedef struct {
+    int32_t n_layers, d_state, block_size, vocab, classes, router_depth, router_token_dim, readout_rank,
+        layer_input_rank;
+    int32_t route_on_state;      /* 1: the router reads [router_embed(x); rms(h_below)] (router_input token_state), 0:
+                                    the token part only (router_input token) */
+    int32_t token_transition;    /* 1: the token layer has transitions A_x */
+    int32_t routed_transition;   /* 1: the routed layers have transitions A_r (expert_type transition) */
+} ygg_fshape_t;
+
+/* Host arrays of ygg_fload: YGG_F_ARRAYS_PER_LAYER pointers per layer l, at arrays[l * YGG_F_ARRAYS_PER_LAYER + k],
+ * then the output bias (classes) at arrays[n_layers * YGG_F_ARRAYS_PER_LAYER]. E = 2^router_depth, F =
+ * router_token_dim, FIN = F + d_state (route_on_state) or F:
+ *   k = 0 table: token layer [vocab][d_state] (T_x[x], its own rows); routed [E][vocab][d_state]
+ *   k = 1 transition [experts][d_state / block][block][block], or NULL without transitions
+ *   k = 2 readout [experts][readout_rank][d_state]      k = 3 unembed [classes][readout_rank]
+ *   routed layers only: k = 4 router_embed [vocab][F], k = 5 router_weight [E - 1][FIN], k = 6 router_bias [E - 1],
+ *   k = 7 layer_input_down [layer_input_rank][d_state] and k = 8 layer_input_proj [E][d_state][layer_input_rank]
+ *   (both NULL when layer_input_rank is 0); k = 4..8 of the token layer are ignored.
+ * Limits: d_state 64 / 128 / 256, an even block size <= 32, readout rank <= 32, layer-input rank <= d_state,
+ * router_token_dim <= d_state, depth <= 20, 2..16 layers. Replaces TritonYggdrasil.__init__
+ * (yggdrasil/inference_triton.py:123-151): the library copies the arrays into its own device layout. */
+#define YGG_F_ARRAYS_PER_LAYER 9
+YGG_API int ygg_fload(const ygg_fshape_t *shape, const float *const *arrays, int device, ygg_fmodel **out);
+
+/* One fp32 step of `batch` streams (yggdrasil/inference.py:66-75, inference_triton.py:187-194):
+ *   d_tokens    int32 [batch]
+ *   d_state_in  float [batch][n_layers][d_state]   (may equal d_state_out)
+ *   d_state_out float [batch][n_layers][d_state]
+ *   d_logits    float [batch][classes]
+ *   d_experts   int32 [batch][n_layers] the expert of every layer (the token for the token layer), or NULL
+ * A token outside [0, vocab) skips its stream (NaN logits, state copied through) and is reported by ygg_fstatus. */
+YGG_API int ygg_fstep(const ygg_fmodel *m, int batch, const int32_t *d_tokens, const float *d_state_in,
+                      float *d_state_out, float *d_logits, int32_t *d_experts, void *stream);
+
+/* YGG_E_TOKEN if a step since the last call met a device token out of range (then cleared), else YGG_OK.
+ * Synchronises `stream`. */
+YGG_API int ygg_fstatus(const ygg_fmodel *m, void *stream, int *status_out);
+
+/* Free a float model; NULL is a no-op. */
+YGG_API void ygg_ffree(ygg_fmodel *m);
+
 /* Free the device memory of a model; NULL is a no-op. */
 YGG_API void ygg_free(ygg_model *m);
 

@@ -23,8 +23,8 @@ def synthetic_checkpoint(path, seed=0, old_keys=False, shape=SHAPE):
     def layer(prefix, E, routed):
         p = {"token_embed": rng.normal(0, 1, (V, k)), "input_proj": rng.normal(0, 0.3, (E, n, k)),
              "bias": rng.normal(0, 0.5, (E, n)), "rotation": rng.normal(0, 0.4, (E, n // b, b, b)),
-             "decay": rng.uniform(0.6, 1.05, (E, n)), "readout": rng.normal(0, 0.2, (E, R, n)),
-             "unembed": rng.normal(0, 0.3, (V, R))}
+             "decay": rng.uniform(0.6, 1.05, (E, n)), "readout": rng.normal(0, shape.get("readout_std", 0.2), (E, R, n)),
+             "unembed": rng.normal(0, shape.get("unembed_std", 0.3), (V, R))}
         if routed:
             p.update(router_embed=rng.normal(0, 1, (V, F)), router_weight=rng.normal(0, 0.3, (E - 1, F + n)),
                      router_bias=rng.normal(0, 0.1, E - 1), layer_input_down=rng.normal(0, 0.2, (R2, n)),

@@ -21,6 +21,11 @@ The fixtures pin this repository's generator and oracle to the reference:
                      and the c3n96 benchmark shape's int_forward logits on a few streams. The model digests here are
                      this repository's writer's (a regression check, not a pin); the logits are the pin.
   checkpoints.json   digests of the files the reference's quantize + write make from seeded synthetic checkpoints.
+  float_cases.json/.npz  the reference's own fp32 GPU step (yggdrasil/inference_triton.py: its Triton kernel _ygg_step
+                     and its torch.addmm head, run on the CPU by Triton's interpreter, TRITON_INTERPRET=1) on seeded
+                     synthetic float checkpoints of three shapes: per step the logits, the experts and the new state,
+                     from a zero state, and the score bits of the windows (TritonYggdrasil.score); the pin of the float
+                     oracle (oracle/float_oracle.py) and of the B200 float step (backend "b200f").
 Every record of the first four also carries acc_sha256: the digest of the int32 accumulators before saturation,
 (S, T, L, n), taken from int_forward's own `drive` array (cpu/export.py:300-310; the value cpu/ygg.cpp:388 narrows with
 cvtsepi32_epi8) by watching its saturating np.clip(drive, -128, 127) calls.
@@ -140,9 +145,12 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("YGG_REFERENCE", "/root/reference"))
     ap.add_argument("--only", default="cases,workloads,zipf,ext,checkpoints",
-                    help="comma-separated parts to regenerate (zipf recalibrates c4/c4f; workloads reads the .npz)")
+                    help="comma-separated parts to regenerate (zipf recalibrates c4/c4f; workloads reads the .npz; "
+                         "float runs the reference's Triton step under the interpreter)")
     a = ap.parse_args()
     parts = set(a.only.split(","))
+    if "float" in parts:
+        os.environ["TRITON_INTERPRET"] = "1"      # before anything imports triton: the kernel runs on the CPU
     ref = Path(a.ref)
     sys.path.insert(0, str(ref / "cpu"))
     sys.path.insert(0, str(ref))
@@ -208,7 +216,63 @@ def main():
             make_extended(E, synth, fields, tmp, STREAMS, STEPS)
         if "checkpoints" in parts:
             make_checkpoints(E, tmp)
+        if "float" in parts:
+            make_float(tmp)
     print("wrote", [p.name for p in HERE.glob("*.json")])
+
+
+# shapes of the float cases: the synthetic checkpoint's (n 64, b 16), a DNA-like one (V 5, n 128, b 8, 3 routed
+# layers, old keys) and one of the enwik8 large family (V 256, n 256, b 16, R 32, R2 64, k 64) at depth 6; the larger
+# two draw smaller readouts and unembeddings so that their logits stay in the range of a trained model's (|logit| of
+# order 10), where the reference's fp32 tolerance on log-probabilities (1e-4) is meant to hold
+FLOAT_CASES = [
+    dict(name="n64", seed=0, old_keys=False, streams=8, steps=12, shape=None),
+    dict(name="n128-b8", seed=1, old_keys=True, streams=6, steps=8,
+         shape=dict(vocab=5, n=128, block=8, depth=5, readout=16, layer_input=32, input_rank=32, router_token=16,
+                    routed=3, readout_std=0.07, unembed_std=0.15)),
+    dict(name="n256", seed=2, old_keys=False, streams=4, steps=6,
+         shape=dict(vocab=256, n=256, block=16, depth=6, readout=32, layer_input=64, input_rank=64, router_token=16,
+                    routed=2, readout_std=0.04, unembed_std=0.1)),
+]
+
+
+def make_float(tmp):
+    """The reference's Triton float step on the CPU (see the module docstring)."""
+    import torch
+    sys.path.insert(0, str(HERE.parent))
+    import checkpoints as C
+    from yggdrasil import inference as I
+    from yggdrasil import inference_triton as IT
+    arrays, recs = {}, []
+    for case in FLOAT_CASES:
+        npz = os.path.join(tmp, f"f{case['name']}.npz")
+        kw = {} if case["shape"] is None else {"shape": case["shape"]}
+        C.synthetic_checkpoint(npz, seed=case["seed"], old_keys=case["old_keys"], **kw)
+        layers, ob = I.read(npz)
+        m = IT.TritonYggdrasil(layers, ob, device="cpu")
+        S, T = case["streams"], case["steps"]
+        x = np.random.default_rng(case["seed"]).integers(0, m.vocab, (S, T))
+        h = m.init_state(S)
+        logits, experts, states = [], [], []
+        for t in range(T):
+            xt = torch.as_tensor(np.ascontiguousarray(x[:, t]))   # the kernel reads the tokens flat
+            h_out, z = torch.empty_like(h), torch.empty(S, m.layers, m.ro)
+            ex = torch.empty(S, m.layers, dtype=torch.int32)
+            m._launch(xt, h, h_out, z, ex, 1, 3)           # the reference's _step, less its GPU-timed tuning
+            logits.append(torch.addmm(m.output_bias, z.view(S, -1), m.unembed).numpy())
+            experts.append(ex.numpy())
+            states.append(h_out.numpy())
+            h = h_out
+        m._config[S] = (1, 3)                               # score() steps through _step without tuning
+        bits = m.score(x)
+        p = case["name"]
+        arrays.update({f"{p}/tokens": x.astype(np.int32), f"{p}/logits": np.stack(logits, 1).astype(np.float32),
+                       f"{p}/experts": np.stack(experts, 1).astype(np.int16),
+                       f"{p}/states": np.stack(states, 1).astype(np.float32), f"{p}/bits": np.asarray(bits)})
+        recs.append({k: v for k, v in case.items()} | {"classes": int(m.classes), "layers": int(m.layers)})
+        print(f"float case {p}: done", flush=True)
+    np.savez_compressed(HERE / "float_cases.npz", **arrays)
+    (HERE / "float_cases.json").write_text(json.dumps(recs, indent=1) + "\n")
 
 
 def make_extended(E, synth, fields, tmp, STREAMS, STEPS):

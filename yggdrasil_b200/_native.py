@@ -12,7 +12,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libygg_b200.so"
 
 EXPORTS = ("ygg_load", "ygg_info", "ygg_step", "ygg_step_debug", "ygg_score", "ygg_score_grouped_workspace",
            "ygg_score_grouped", "ygg_score_grouped_noalloc", "ygg_status", "ygg_selftest_wait", "ygg_free",
-           "ygg_strerror", "ygg_version")
+           "ygg_strerror", "ygg_version", "ygg_fload", "ygg_fstep", "ygg_fstatus", "ygg_ffree")
 
 YGG_OK = 0
 YGG_E_ARG, YGG_E_FORMAT, YGG_E_UNSUPPORTED, YGG_E_MISSING, YGG_E_CUDA, YGG_E_OOM, YGG_E_TOKEN, YGG_E_TIMEOUT, \
@@ -66,6 +66,27 @@ def lib() -> ctypes.CDLL:
             f.restype = ctypes.c_int
         _lib = l
     return _lib
+
+
+_float_bound = False
+
+
+def flib() -> ctypes.CDLL:
+    """The loaded library with the entry points of the fp32 float step (ygg_fload, ygg_fstep, ygg_fstatus,
+    ygg_ffree) bound; raises if the library lacks them."""
+    global _float_bound
+    l = lib()
+    if not _float_bound:
+        vp, i32 = ctypes.c_void_p, ctypes.c_int
+        l.ygg_fload.argtypes = [vp, ctypes.POINTER(vp), i32, ctypes.POINTER(vp)]
+        l.ygg_fstep.argtypes = [vp, i32, vp, vp, vp, vp, vp, vp]
+        l.ygg_fstatus.argtypes = [vp, vp, ctypes.POINTER(ctypes.c_int)]
+        l.ygg_ffree.argtypes = [vp]
+        l.ygg_ffree.restype = None
+        for f in (l.ygg_fload, l.ygg_fstep, l.ygg_fstatus):
+            f.restype = ctypes.c_int
+        _float_bound = True
+    return l
 
 
 def strerror(code: int) -> str:

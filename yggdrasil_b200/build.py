@@ -15,7 +15,8 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libygg_b200.so"
-SOURCES = [CSRC / "ygg_load.cu", CSRC / "ygg_step.cu", CSRC / "ygg_coop.cu", CSRC / "ygg_grouped.cu"]
+SOURCES = [CSRC / "ygg_load.cu", CSRC / "ygg_step.cu", CSRC / "ygg_coop.cu", CSRC / "ygg_grouped.cu",
+           CSRC / "ygg_float.cu"]
 HEADERS = [CSRC / "ygg_model.h", CSRC / "ygg_device.cuh", ROOT / "include" / "ygg_b200.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 # no --use_fast_math and no FMA contraction: every f32 op of the step is single-rounded as in the reference

@@ -1,0 +1,430 @@
+// The fp32 streaming step of Yggdrasil on sm_100a: the reference's float inference model (yggdrasil/inference.py:42-75;
+// its Triton backend fuses the same step, yggdrasil/inference_triton.py:21-106, and adds the head with torch.addmm,
+// :187-194), as the backend "b200f".
+//
+// One block of n threads serves one stream at a time (grid-stride over the streams); thread t owns state coordinate t
+// of every layer. Per layer:
+//   1. the router (routed layers): f = [router_embed(x); rms(h_below)], node j goes right iff f . W_j + b_j > 0,
+//      descended kLook = 4 levels per round: the 15 rows of the subtree under the current node are read together,
+//      thread t multiplying coordinate t of each row (and token feature t, t < F), and one block reduction of the 15
+//      partial sums decides the round (inference.py:42-52);
+//   2. the layer input v = V' rms(h_below) (thread k < R2 sums row k over the state below in shared memory), then
+//      h_t = T_r[x][t] + sum_k U'_r[t][k] v_k + sum_j A_r[t][j] h_prev[block(t) + j] (inference.py:55-63); every
+//      expert array is stored transposed so that each of these loads is coalesced over the block's threads;
+//   3. the readout z = P_r h (one block reduction of the R partial products, a reduce-scatter within each warp) and
+//      rms(h) for the layer above.
+// The logits are output_bias + sum_l z_l Q_l^T, in layer order, one class per thread. Everything is fp32 with fused
+// multiply-adds; the reference's own fp32 sums run in other orders, so parity is a tolerance (the reference's own:
+// log-probabilities within 1e-4, cpu/tests/test_triton.py:29-30).
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <vector>
+
+#include "../../include/ygg_b200.h"
+
+namespace ygg {
+namespace fstep {
+
+constexpr unsigned kFull = 0xFFFFFFFFu;
+constexpr int kMaxLayers = 16;
+constexpr int kLook = 4;                       // router levels per round
+constexpr float kRmsEps = 1e-6f;               // yggdrasil/config.py:8
+
+struct FLayer {
+    const float *table;   // token layer [V][n] (T_x[x]); routed [E][V][n]
+    const float *at;      // [E][b][n]: at[e][j][i] = A_e[i][block(i) b + j]; null: no transition
+    const float *pt;      // readout [E][R][n]
+    const float *qt;      // unembedding, transposed [R][C]
+    const float *embed;   // router_embed [V][F] (routed layers)
+    const float *w;       // router rows [E - 1][FIN], heap order from node 0
+    const float *bias;    // [E - 1]
+    const float *vt;      // layer-input down projection, transposed [n][R2]; null: no layer input
+    const float *ut;      // layer-input projection [E][R2][n]
+};
+
+struct FModel {
+    int L, n, b, V, C, D, F, FIN, R, R2;
+    int route_on_state;
+    const float *out_bias;   // [C]
+    FLayer layer[kMaxLayers];
+};
+
+template <int K> struct Log2 { static constexpr int value = K <= 1 ? 0 : 1 + Log2<K / 2>::value; };
+template <> struct Log2<1> { static constexpr int value = 0; };
+
+// Warp reduce-scatter of K values (K a power of two <= 32): halving exchanges from offset 16 down leave lane l with the
+// warp sum of v[l >> (5 - log2 K)], then plain butterflies over the lower offsets.
+template <int K> __device__ __forceinline__ float reduce_scatter(float (&v)[K], int lane) {
+    constexpr int LK = Log2<K>::value;
+#pragma unroll
+    for (int s = 0; s < LK; s++) {
+        const int off = 16 >> s;
+        const int half = K >> (s + 1);
+        const bool hi = (lane & off) != 0;
+#pragma unroll
+        for (int i = 0; i < half; i++) {
+            const float keep = hi ? v[i + half] : v[i], send = hi ? v[i] : v[i + half];
+            v[i] = keep + __shfl_xor_sync(kFull, send, off);
+        }
+    }
+    float r = v[0];
+#pragma unroll
+    for (int off = 16 >> LK; off > 0; off >>= 1) r += __shfl_xor_sync(kFull, r, off);
+    return r;
+}
+
+// Block sums of K per-thread values into out[0, K) (shared memory); red: NW * K floats of shared scratch. Ends
+// synchronised, so out[] is visible to every thread.
+template <int K, int NW>
+__device__ __forceinline__ void block_sum(float (&v)[K], float *red, float *out, int tid) {
+    constexpr int LK = Log2<K>::value;
+    const int lane = tid & 31, warp = tid >> 5;
+    const float r = reduce_scatter<K>(v, lane);
+    if ((lane & ((32 >> LK) - 1)) == 0) red[warp * K + (lane >> (5 - LK))] = r;
+    __syncthreads();
+    if (tid < K) {
+        float s = 0.0f;
+#pragma unroll
+        for (int w = 0; w < NW; w++) s += red[w * K + tid];
+        out[tid] = s;
+    }
+    __syncthreads();
+}
+
+// One stream per block of N threads at a time. state [B][L][n] (in may equal out), logits [B][C], experts [B][L] or
+// null. RP: the readout rank rounded up to a power of two (<= 32).
+template <int N, int RP>
+__global__ void __launch_bounds__(N) fstep_kernel(const __grid_constant__ FModel m, int B, const int32_t *__restrict__ tokens,
+                                                  const float *state_in, float *state_out, float *__restrict__ logits,
+                                                  int32_t *__restrict__ experts, int *__restrict__ bad) {
+    constexpr int NW = N / 32;
+    __shared__ float hp[N], below[N], vv[N], emb[N], red[NW * 32], sums[32];
+    __shared__ float zs[kMaxLayers][32];
+    const int t = threadIdx.x;
+    const int L = m.L, V = m.V, C = m.C, R = m.R, R2 = m.R2, F = m.F, FIN = m.FIN, bsz = m.b;
+    for (int s = blockIdx.x; s < B; s += gridDim.x) {
+        const int x = tokens[s];
+        if (x < 0 || x >= V) {   // the whole stream is skipped: NaN logits, state unchanged
+            if (t == 0) atomicOr(bad, 1);
+            for (int c = t; c < C; c += N) logits[(size_t)s * C + c] = __int_as_float(0x7fc00000);
+            for (int i = t; i < L * N; i += N) state_out[(size_t)s * L * N + i] = state_in[(size_t)s * L * N + i];
+            if (experts != nullptr && t < L) experts[(size_t)s * L + t] = -1;
+            continue;
+        }
+        for (int l = 0; l < L; l++) {
+            const FLayer &y = m.layer[l];
+            hp[t] = state_in[((size_t)s * L + l) * N + t];
+            int r = x;
+            if (l > 0) {
+                if (t < F) emb[t] = __ldg(y.embed + (size_t)x * F + t);
+                __syncthreads();   // hp, emb; below was written before the last barrier of the layer below
+                // layer input v = V' rms(h_below), thread k < R2
+                if (y.vt != nullptr && t < R2) {
+                    float a0 = 0.0f, a1 = 0.0f;
+#pragma unroll 4
+                    for (int i = 0; i < N; i += 2) {
+                        a0 = fmaf(__ldg(y.vt + (size_t)i * R2 + t), below[i], a0);
+                        a1 = fmaf(__ldg(y.vt + (size_t)(i + 1) * R2 + t), below[i + 1], a1);
+                    }
+                    vv[t] = a0 + a1;
+                }
+                // router: rounds of kLook levels, node j (0-based heap) right iff f . W_j + b_j > 0
+                int node = 0;
+                for (int d0 = 0; d0 < m.D; d0 += kLook) {
+                    const int lv = min(kLook, m.D - d0);
+                    const int nrows = (1 << lv) - 1;
+                    float part[16];
+                    const float bt = below[t];
+                    const float et = t < F ? emb[t] : 0.0f;
+#pragma unroll
+                    for (int k = 0; k < 16; k++) {
+                        part[k] = 0.0f;
+                        if (k < nrows) {
+                            const int lvl = k == 0 ? 0 : k < 3 ? 1 : k < 7 ? 2 : 3;
+                            const int row = node * (1 << lvl) + k;
+                            const float *wr = y.w + (size_t)row * FIN;
+                            float p = m.route_on_state ? __ldg(wr + F + t) * bt : 0.0f;
+                            if (t < F) p = fmaf(__ldg(wr + t), et, p);
+                            part[k] = p;
+                        }
+                    }
+                    block_sum<16, NW>(part, red, sums, t);
+                    int rr = 0;
+                    for (int j = 0; j < lv; j++) {
+                        const int lvl = j;
+                        const int row = node * (1 << lvl) + rr;
+                        const bool right = sums[rr] + __ldg(y.bias + row) > 0.0f;
+                        rr = 2 * rr + 1 + (right ? 1 : 0);
+                    }
+                    node = node * (1 << lv) + rr;
+                }
+                r = node - ((1 << m.D) - 1);
+                __syncthreads();   // vv
+            } else {
+                __syncthreads();   // hp
+            }
+            // h = T_r[x] + U'_r v + A_r h_prev
+            float h = __ldg(y.table + (l == 0 ? (size_t)x * N : ((size_t)r * V + x) * N) + t);
+            if (l > 0 && y.ut != nullptr) {
+                const float *u = y.ut + (size_t)r * R2 * N + t;
+                float a0 = 0.0f, a1 = 0.0f;
+                int k = 0;
+                for (; k + 1 < R2; k += 2) {
+                    a0 = fmaf(__ldg(u + (size_t)k * N), vv[k], a0);
+                    a1 = fmaf(__ldg(u + (size_t)(k + 1) * N), vv[k + 1], a1);
+                }
+                if (k < R2) a0 = fmaf(__ldg(u + (size_t)k * N), vv[k], a0);
+                h += a0 + a1;
+            }
+            if (y.at != nullptr) {
+                const float *a = y.at + (size_t)r * bsz * N + t;
+                const int blk0 = (t / bsz) * bsz;
+                float a0 = 0.0f, a1 = 0.0f;
+                for (int j = 0; j < bsz; j += 2) {
+                    a0 = fmaf(__ldg(a + (size_t)j * N), hp[blk0 + j], a0);
+                    a1 = fmaf(__ldg(a + (size_t)(j + 1) * N), hp[blk0 + j + 1], a1);
+                }
+                h += a0 + a1;
+            }
+            state_out[((size_t)s * L + l) * N + t] = h;
+            if (experts != nullptr && t == 0) experts[(size_t)s * L + l] = r;
+            // readout z = P_r h, and sum h^2 for rms(h)
+            {
+                float part[RP];
+                const float *p = y.pt + (size_t)r * R * N + t;
+#pragma unroll
+                for (int k = 0; k < RP; k++) part[k] = k < R ? __ldg(p + (size_t)k * N) * h : 0.0f;
+                block_sum<RP, NW>(part, red, sums, t);
+                if (t < R) zs[l][t] = sums[t];
+                float sq[1] = {h * h};
+                block_sum<1, NW>(sq, red, sums, t);
+                below[t] = h * rsqrtf(sums[0] / (float)N + kRmsEps);
+            }
+            __syncthreads();   // below, zs
+        }
+        // logits = output_bias + sum_l z_l Q_l^T, one class per thread
+        for (int c = t; c < C; c += N) {
+            float lg = __ldg(m.out_bias + c);
+            for (int l = 0; l < L; l++) {
+                const float *q = m.layer[l].qt + c;
+                for (int k = 0; k < R; k++) lg = fmaf(zs[l][k], __ldg(q + (size_t)k * C), lg);
+            }
+            logits[(size_t)s * C + c] = lg;
+        }
+        __syncthreads();   // zs, hp before the next stream
+    }
+}
+
+}  // namespace fstep
+}  // namespace ygg
+
+using namespace ygg::fstep;
+
+struct ygg_fmodel {
+    int device;
+    FModel dm;
+    ygg_fshape_t shape;
+    float *d_blob;
+    int *d_bad;
+    int sm_count;
+};
+
+namespace {
+
+size_t align_floats(size_t x) { return (x + 63) / 64 * 64; }   // 256-byte aligned sub-arrays
+
+template <int N, int RP>
+cudaError_t launch_t(const FModel &dm, int B, const int32_t *tok, const float *sin, float *sout, float *lg, int32_t *ex,
+                     int *bad, int grid, cudaStream_t st) {
+    fstep_kernel<N, RP><<<grid, N, 0, st>>>(dm, B, tok, sin, sout, lg, ex, bad);
+    return cudaGetLastError();
+}
+
+template <int N>
+cudaError_t launch_n(const FModel &dm, int B, const int32_t *tok, const float *sin, float *sout, float *lg, int32_t *ex,
+                     int *bad, int grid, cudaStream_t st) {
+    if (dm.R <= 8) return launch_t<N, 8>(dm, B, tok, sin, sout, lg, ex, bad, grid, st);
+    if (dm.R <= 16) return launch_t<N, 16>(dm, B, tok, sin, sout, lg, ex, bad, grid, st);
+    return launch_t<N, 32>(dm, B, tok, sin, sout, lg, ex, bad, grid, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+int ygg_fload(const ygg_fshape_t *sh, const float *const *arrays, int device, ygg_fmodel **out) {
+    if (!sh || !arrays || !out) return YGG_E_ARG;
+    *out = nullptr;
+    const int L = sh->n_layers, n = sh->d_state, b = sh->block_size, V = sh->vocab, C = sh->classes;
+    const int D = sh->router_depth, F = sh->router_token_dim, R = sh->readout_rank, R2 = sh->layer_input_rank;
+    if (L < 2 || L > kMaxLayers || (n != 64 && n != 128 && n != 256) || b < 2 || b > 32 || (b & 1) || n % b ||
+        V < 1 || C < 1 || D < 1 || D > 20 || F < 1 || F > n || R < 1 || R > 32 || R2 < 0 || R2 > n)
+        return YGG_E_UNSUPPORTED;
+    const int E = 1 << D, FIN = F + (sh->route_on_state ? n : 0);
+    for (int l = 0; l < L; l++) {
+        const float *const *a = arrays + (size_t)l * YGG_F_ARRAYS_PER_LAYER;
+        if (!a[0] || !a[2] || !a[3]) return YGG_E_MISSING;
+        if ((l == 0 ? sh->token_transition : sh->routed_transition) && !a[1]) return YGG_E_MISSING;
+        if (l > 0 && (!a[4] || !a[5] || !a[6] || (R2 > 0 && (!a[7] || !a[8])))) return YGG_E_MISSING;
+    }
+    if (!arrays[(size_t)L * YGG_F_ARRAYS_PER_LAYER]) return YGG_E_MISSING;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) return YGG_E_DEVICE;
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess || prop.major < 10) return YGG_E_DEVICE;
+    // host staging of the device layout: one blob, every sub-array 256-byte aligned
+    std::vector<float> blob;
+    auto take = [&](size_t count) {
+        const size_t off = blob.size();
+        blob.resize(off + align_floats(count), 0.0f);
+        return off;
+    };
+    struct Off { size_t table, at, pt, qt, embed, w, bias, vt, ut; bool has_at, has_v; };
+    std::vector<Off> offs(L);
+    for (int l = 0; l < L; l++) {
+        const float *const *a = arrays + (size_t)l * YGG_F_ARRAYS_PER_LAYER;
+        const bool tok = l == 0;
+        const size_t Ex = tok ? (size_t)V : (size_t)E;
+        Off &o = offs[l];
+        // table: token layer its own rows T_x[x] (V, n); routed (E, V, n)
+        const size_t tcount = tok ? (size_t)V * n : (size_t)E * V * n;
+        o.table = take(tcount);
+        memcpy(blob.data() + o.table, a[0], tcount * sizeof(float));
+        o.has_at = (tok ? sh->token_transition : sh->routed_transition) != 0;
+        if (o.has_at) {   // (E, n/b, b, b) -> (E, b, n)
+            o.at = take(Ex * b * n);
+            for (size_t e = 0; e < Ex; e++)
+                for (int i = 0; i < n; i++)
+                    for (int j = 0; j < b; j++)
+                        blob[o.at + (e * b + j) * n + i] = a[1][((e * (n / b) + i / b) * b + i % b) * b + j];
+        }
+        o.pt = take(Ex * R * n);
+        memcpy(blob.data() + o.pt, a[2], Ex * R * n * sizeof(float));
+        o.qt = take((size_t)R * C);   // (C, R) -> (R, C)
+        for (int c = 0; c < C; c++)
+            for (int k = 0; k < R; k++) blob[o.qt + (size_t)k * C + c] = a[3][(size_t)c * R + k];
+        o.has_v = false;
+        if (!tok) {
+            o.embed = take((size_t)V * F);
+            memcpy(blob.data() + o.embed, a[4], (size_t)V * F * sizeof(float));
+            o.w = take((size_t)(E - 1) * FIN);
+            memcpy(blob.data() + o.w, a[5], (size_t)(E - 1) * FIN * sizeof(float));
+            o.bias = take(E - 1);
+            memcpy(blob.data() + o.bias, a[6], (size_t)(E - 1) * sizeof(float));
+            o.has_v = R2 > 0;
+            if (o.has_v) {
+                o.vt = take((size_t)n * R2);   // (R2, n) -> (n, R2)
+                for (int k = 0; k < R2; k++)
+                    for (int i = 0; i < n; i++) blob[o.vt + (size_t)i * R2 + k] = a[7][(size_t)k * n + i];
+                o.ut = take((size_t)E * R2 * n);   // (E, n, R2) -> (E, R2, n)
+                for (size_t e = 0; e < (size_t)E; e++)
+                    for (int i = 0; i < n; i++)
+                        for (int k = 0; k < R2; k++)
+                            blob[o.ut + (e * R2 + k) * n + i] = a[8][(e * n + i) * R2 + k];
+            }
+        }
+    }
+    const size_t ob = take(C);
+    memcpy(blob.data() + ob, arrays[(size_t)L * YGG_F_ARRAYS_PER_LAYER], (size_t)C * sizeof(float));
+
+    int prev = -1;
+    cudaGetDevice(&prev);
+    if (cudaSetDevice(device) != cudaSuccess) return YGG_E_DEVICE;
+    ygg_fmodel *m = new ygg_fmodel();
+    m->device = device;
+    m->shape = *sh;
+    m->sm_count = prop.multiProcessorCount;
+    int rc = YGG_OK;
+    if (cudaMalloc((void **)&m->d_blob, blob.size() * sizeof(float)) != cudaSuccess ||
+        cudaMalloc((void **)&m->d_bad, sizeof(int)) != cudaSuccess) {
+        rc = YGG_E_OOM;
+    } else if (cudaMemcpy(m->d_blob, blob.data(), blob.size() * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess ||
+               cudaMemset(m->d_bad, 0, sizeof(int)) != cudaSuccess) {
+        rc = YGG_E_CUDA;
+    }
+    if (rc != YGG_OK) {
+        cudaFree(m->d_blob);
+        cudaFree(m->d_bad);
+        delete m;
+        if (prev >= 0) cudaSetDevice(prev);
+        return rc;
+    }
+    FModel &dm = m->dm;
+    memset(&dm, 0, sizeof dm);
+    dm.L = L; dm.n = n; dm.b = b; dm.V = V; dm.C = C; dm.D = D; dm.F = F; dm.FIN = FIN; dm.R = R; dm.R2 = R2;
+    dm.route_on_state = sh->route_on_state != 0;
+    const float *d = m->d_blob;
+    dm.out_bias = d + ob;
+    for (int l = 0; l < L; l++) {
+        const Off &o = offs[l];
+        FLayer &y = dm.layer[l];
+        y.table = d + o.table;
+        y.at = o.has_at ? d + o.at : nullptr;
+        y.pt = d + o.pt;
+        y.qt = d + o.qt;
+        if (l > 0) {
+            y.embed = d + o.embed;
+            y.w = d + o.w;
+            y.bias = d + o.bias;
+            y.vt = o.has_v ? d + o.vt : nullptr;
+            y.ut = o.has_v ? d + o.ut : nullptr;
+        }
+    }
+    if (prev >= 0) cudaSetDevice(prev);
+    *out = m;
+    return YGG_OK;
+}
+
+int ygg_fstep(const ygg_fmodel *m, int batch, const int32_t *d_tokens, const float *d_state_in, float *d_state_out,
+              float *d_logits, int32_t *d_experts, void *stream) {
+    if (!m || batch < 0) return YGG_E_ARG;
+    if (batch == 0) return YGG_OK;
+    if (!d_tokens || !d_state_in || !d_state_out || !d_logits) return YGG_E_ARG;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    if (prev != m->device && cudaSetDevice(m->device) != cudaSuccess) return YGG_E_CUDA;
+    const FModel &dm = m->dm;
+    // a block per stream; up to 32 blocks of 64-256 threads an SM, streams beyond that in a grid-stride loop
+    const int grid = batch < 32 * m->sm_count ? batch : 32 * m->sm_count;
+    const cudaStream_t st = (cudaStream_t)stream;
+    cudaError_t e;
+    switch (dm.n) {
+        case 64: e = launch_n<64>(dm, batch, d_tokens, d_state_in, d_state_out, d_logits, d_experts, m->d_bad, grid, st); break;
+        case 128: e = launch_n<128>(dm, batch, d_tokens, d_state_in, d_state_out, d_logits, d_experts, m->d_bad, grid, st); break;
+        default: e = launch_n<256>(dm, batch, d_tokens, d_state_in, d_state_out, d_logits, d_experts, m->d_bad, grid, st); break;
+    }
+    if (prev >= 0 && prev != m->device) cudaSetDevice(prev);
+    return e == cudaSuccess ? YGG_OK : YGG_E_CUDA;
+}
+
+int ygg_fstatus(const ygg_fmodel *m, void *stream, int *status_out) {
+    if (!m || !status_out) return YGG_E_ARG;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    if (prev != m->device && cudaSetDevice(m->device) != cudaSuccess) return YGG_E_CUDA;
+    int v = 0;
+    cudaError_t e = cudaMemcpyAsync(&v, m->d_bad, sizeof v, cudaMemcpyDeviceToHost, (cudaStream_t)stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
+    if (e == cudaSuccess && v) e = cudaMemsetAsync(m->d_bad, 0, sizeof(int), (cudaStream_t)stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
+    if (prev >= 0 && prev != m->device) cudaSetDevice(prev);
+    if (e != cudaSuccess) return YGG_E_CUDA;
+    *status_out = v ? YGG_E_TOKEN : YGG_OK;
+    return YGG_OK;
+}
+
+void ygg_ffree(ygg_fmodel *m) {
+    if (!m) return;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(m->device);
+    cudaFree(m->d_blob);
+    cudaFree(m->d_bad);
+    if (prev >= 0) cudaSetDevice(prev);
+    delete m;
+}
+
+}  // extern "C"

@@ -38,13 +38,18 @@ class Yggdrasil:
 
     @classmethod
     def load(cls, path, backend="b200", **kw):
-        """A YGG1 int8 model file. backend "b200": the sm_100a int8 step; kw device="cuda", cuda_graph=False."""
+        """backend "b200": the sm_100a int8 step of a YGG1 file (or of an .npz with its export record); "b200f": the
+        sm_100a fp32 step of a training checkpoint (.npz), the float model of the reference's jax and triton
+        backends. kw device="cuda", cuda_graph=False."""
         if backend == "b200":
             return B200Yggdrasil(path, **kw)
+        if backend == "b200f":
+            from .float_backend import B200FloatYggdrasil
+            return B200FloatYggdrasil.from_checkpoint(path, **kw)
         if backend in ("jax", "triton"):
-            raise ValueError(f"backend {backend!r} is a float backend of the reference package; "
-                             "yggdrasil_b200 provides backend='b200' (the int8 step)")
-        raise ValueError(f"backend {backend!r}: b200")
+            raise ValueError(f"backend {backend!r} is a backend of the reference package; yggdrasil_b200 provides "
+                             "backend='b200' (the int8 step) and backend='b200f' (the fp32 step)")
+        raise ValueError(f"backend {backend!r}: b200 or b200f")
 
 
 class B200Yggdrasil:

@@ -281,3 +281,41 @@ def gathered_bytes_per_token(shape: ModelShape, with_io: bool = True) -> int:
     g_rt = d * n + 4 * d + 2 * n * b + n * r2 + r * n + s
     io = 2 * L * n + 4 * v + 4 if with_io else 0
     return g_tok + (L - 1) * g_rt + io
+
+
+# ------------------------------------------------------------------------------------------------- float models
+
+# The float model of the reference's enwik8 large configuration (configs/enwik8/large.yaml: 5 layers, d_state 256,
+# blocks of 16, router depth 10, router token dim 16, input rank 64, readout rank 32, layer-input rank 64, V 256), the
+# model its published fp32 GPU time is quoted on (80.1 us/token at batch 1, README.md:43).
+FLOAT_ENWIK8_LARGE = dict(vocab=256, n=256, block=16, depth=10, readout=32, layer_input=64, input_rank=64,
+                          router_token=16, routed=4)
+
+
+def random_float_layers(shape: dict, seed: int = 0):
+    """Random parameters of a float model with the checkpoint's keys and shapes (yggdrasil/config.py PARAMS):
+    (layers [token layer, routed layers...] as dicts of float32 arrays, output bias), as read_checkpoint returns them.
+    Scales keep the state and the logits in a trained model's range: decays U[0.6, 1], rotation generators N(0, 0.4),
+    the readout and unembedding scaled by 1/sqrt of their fan-in."""
+    rng = np.random.default_rng(seed)
+    V, n, b, D = shape["vocab"], shape["n"], shape["block"], shape["depth"]
+    R, R2, k, F = shape["readout"], shape["layer_input"], shape["input_rank"], shape["router_token"]
+
+    def layer(E, routed):
+        p = {"token_embed": rng.standard_normal((V, k), dtype=f32),
+             "input_proj": (rng.standard_normal((E, n, k), dtype=f32) * f32(0.3 / np.sqrt(k / 16))),
+             "bias": rng.standard_normal((E, n), dtype=f32) * f32(0.5),
+             "rotation": rng.standard_normal((E, n // b, b, b), dtype=f32) * f32(0.4),
+             "decay": rng.uniform(0.6, 1.0, (E, n)).astype(f32),
+             "readout": rng.standard_normal((E, R, n), dtype=f32) * f32(1.0 / n),
+             "unembed": rng.standard_normal((V, R), dtype=f32) * f32(2.0 / np.sqrt(R))}
+        if routed:
+            p.update(router_embed=rng.standard_normal((V, F), dtype=f32),
+                     router_weight=rng.standard_normal((E - 1, F + n), dtype=f32) * f32(0.3),
+                     router_bias=rng.standard_normal(E - 1, dtype=f32) * f32(0.1),
+                     layer_input_down=rng.standard_normal((R2, n), dtype=f32) * f32(1.0 / np.sqrt(n)),
+                     layer_input_proj=rng.standard_normal((E, n, R2), dtype=f32) * f32(0.2 / np.sqrt(R2 / 16)))
+        return p
+
+    layers = [layer(V, False)] + [layer(2 ** D, True) for _ in range(shape["routed"])]
+    return layers, rng.standard_normal(V, dtype=f32) * f32(0.5)
