@@ -169,6 +169,15 @@ YGG_API int ygg_fload(const ygg_fshape_t *shape, const float *const *arrays, int
 YGG_API int ygg_fstep(const ygg_fmodel *m, int batch, const int32_t *d_tokens, const float *d_state_in,
                       float *d_state_out, float *d_logits, int32_t *d_experts, void *stream);
 
+/* ygg_fstep that also accumulates the calibration maxima of the reference's exporter (cpu/export.py:120-153,
+ * `LayerStats` and `calibrate`: |h| per group of 16 coordinates, |V' rms(h_below)|, |P_r h| per readout row) over the
+ * batch, into d_stats: float [n_layers][d_state / 16 + 1 + readout_rank], per layer the group maxima, the layer-input
+ * maximum (0 for the token layer) and the row maxima. Each value is the running maximum across every call that passes
+ * the same buffer (zero it first); a calibration is a loop of these calls over the steps of its windows. Replaces the
+ * JAX scan of `calibrate` (cpu/export.py:129-153) with the fp32 step on the GPU. */
+YGG_API int ygg_fstep_stats(const ygg_fmodel *m, int batch, const int32_t *d_tokens, const float *d_state_in,
+                            float *d_state_out, float *d_logits, int32_t *d_experts, float *d_stats, void *stream);
+
 /* YGG_E_TOKEN if a step since the last call met a device token out of range (then cleared), else YGG_OK.
  * Synchronises `stream`. */
 YGG_API int ygg_fstatus(const ygg_fmodel *m, void *stream, int *status_out);

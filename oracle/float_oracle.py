@@ -9,7 +9,9 @@ It follows yggdrasil/inference.py of the reference:
   Yggdrasil.__init__ :142-152  T_r[x] = U_r v(x) + c_r and A_r = diag(clip(decay, -1, 1)) blockdiag(expm((G - G^T)/2))
                   (yggdrasil/experts.py:8-11), here with scipy's float64 expm;
   rms     yggdrasil/model.py:92-93, eps 1e-6 (yggdrasil/config.py:8);
-  score   :179-188  bits of tokens[:, 1:] per row, float64.
+  score   :179-188  bits of tokens[:, 1:] per row, float64;
+  calibrate  cpu/export.py:120-153  the maxima over windows of |h| per group of 16 coordinates, |V' rms(h_below)| and
+                  |P_r h| per readout row, per layer (LayerStats), from a zero state.
 Only the tests use this module (and tests/golden/make_golden.py, which pins it to the reference's own Triton step);
 the product never imports it.
 """
@@ -65,26 +67,52 @@ class FloatOracle:
             node = 2 * node + 1 + (s > 0)
         return node - (2 ** depth - 1)
 
-    def step(self, tokens, state):
-        """tokens (B,), state (B, L, n) -> logits (B, classes), new state (B, L, n), experts (B, L)."""
+    def calibrate(self, windows):
+        """Per layer (group maxima of |h| (n/16,), max |V' rms(h_below)|, row maxima of |P_r h| (R,)) over the steps
+        of windows (S, T) run from a zero state (cpu/export.py:129-153)."""
+        x = np.atleast_2d(np.asarray(windows, np.int64))
+        st = self.init_state(len(x))
+        L, n = self.n_layers, self.n
+        groups = np.zeros((L, n // 16))
+        rows = [np.zeros(p["readout"].shape[1]) for p in self.layers]
+        vmax = np.zeros(L)
+        for t in range(x.shape[1]):
+            _, st, _, extra = self.step(x[:, t], st, with_readout=True)
+            groups = np.maximum(groups, np.abs(st).reshape(len(x), L, n // 16, 16).max((0, 3)))
+            for l in range(L):
+                rows[l] = np.maximum(rows[l], np.abs(extra["z"][l]).max(0))
+                if extra["v"][l] is not None:
+                    vmax[l] = max(vmax[l], np.abs(extra["v"][l]).max())
+        return [(groups[l], vmax[l], rows[l]) for l in range(L)]
+
+    def step(self, tokens, state, with_readout=False):
+        """tokens (B,), state (B, L, n) -> logits (B, classes), new state (B, L, n), experts (B, L) [, the readouts z
+        and the layer inputs V' rms(h_below) of every layer]."""
         x = np.asarray(tokens, np.int64)
         logits = np.broadcast_to(self.output_bias, (len(x), self.classes)).copy()
         new = np.empty_like(state, dtype=np.float64)
         experts = np.empty((len(x), self.n_layers), np.int64)
         below = None
+        zs, vs = [], []
         for i, p in enumerate(self.layers):
             r = x if i == 0 else self._route(p, x, below)
             h = p["table"][r, x]
+            v = None
             if "layer_input_down" in p and below is not None:
-                h = h + np.einsum("bkr,br->bk", p["layer_input_proj"][r], below @ p["layer_input_down"].T)
+                v = below @ p["layer_input_down"].T
+                h = h + np.einsum("bkr,br->bk", p["layer_input_proj"][r], v)
+            vs.append(v)
             if "transition" in p:
                 a = p["transition"][r]
                 h = h + np.einsum("bgij,bgj->bgi", a, state[:, i].reshape(a.shape[:-1])).reshape(h.shape)
             new[:, i] = h
             experts[:, i] = r
             z = np.einsum("brk,bk->br", p["readout"][r], h)
+            zs.append(z)
             logits = logits + z @ p["unembed"].T
             below = rms(h)
+        if with_readout:
+            return logits, new, experts, {"z": zs, "v": vs}
         return logits, new, experts
 
     def score(self, tokens, state=None):

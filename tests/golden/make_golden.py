@@ -24,8 +24,10 @@ The fixtures pin this repository's generator and oracle to the reference:
   float_cases.json/.npz  the reference's own fp32 GPU step (yggdrasil/inference_triton.py: its Triton kernel _ygg_step
                      and its torch.addmm head, run on the CPU by Triton's interpreter, TRITON_INTERPRET=1) on seeded
                      synthetic float checkpoints of three shapes: per step the logits, the experts and the new state,
-                     from a zero state, and the score bits of the windows (TritonYggdrasil.score); the pin of the float
-                     oracle (oracle/float_oracle.py) and of the B200 float step (backend "b200f").
+                     from a zero state, and the score bits of the windows (TritonYggdrasil.score); and the calibration
+                     maxima of cpu/export.py:129-153 (LayerStats: |h| per group of 16, |V' rms(h_below)|, |P_r h| per
+                     row) over those steps; the pin of the float oracle (oracle/float_oracle.py), of the B200 float step
+                     (backend "b200f") and of its calibration (yggdrasil_b200/calibration.py).
 Every record of the first four also carries acc_sha256: the digest of the int32 accumulators before saturation,
 (S, T, L, n), taken from int_forward's own `drive` array (cpu/export.py:300-310; the value cpu/ygg.cpp:388 narrows with
 cvtsepi32_epi8) by watching its saturating np.clip(drive, -128, 127) calls.
@@ -254,6 +256,8 @@ def make_float(tmp):
         x = np.random.default_rng(case["seed"]).integers(0, m.vocab, (S, T))
         h = m.init_state(S)
         logits, experts, states = [], [], []
+        L, n = m.layers, m.n
+        groups, rows, vmax = np.zeros((L, n // 16)), np.zeros((L, m.ro)), np.zeros(L)
         for t in range(T):
             xt = torch.as_tensor(np.ascontiguousarray(x[:, t]))   # the kernel reads the tokens flat
             h_out, z = torch.empty_like(h), torch.empty(S, m.layers, m.ro)
@@ -262,13 +266,23 @@ def make_float(tmp):
             logits.append(torch.addmm(m.output_bias, z.view(S, -1), m.unembed).numpy())
             experts.append(ex.numpy())
             states.append(h_out.numpy())
+            # the calibration maxima of cpu/export.py:129-153 (LayerStats) over this step's states and readouts
+            hs, zs = h_out.numpy().astype(np.float64), z.numpy().astype(np.float64)
+            groups = np.maximum(groups, np.abs(hs).reshape(S, L, n // 16, 16).max((0, 3)))
+            rows = np.maximum(rows, np.abs(zs).max(0))
+            for l in range(1, L):
+                if "layer_input_down" in layers[l]:
+                    below = hs[:, l - 1] / np.sqrt((hs[:, l - 1] ** 2).mean(-1, keepdims=True) + 1e-6)
+                    v = below @ np.asarray(layers[l]["layer_input_down"], np.float64).T
+                    vmax[l] = max(vmax[l], np.abs(v).max())
             h = h_out
         m._config[S] = (1, 3)                               # score() steps through _step without tuning
         bits = m.score(x)
         p = case["name"]
         arrays.update({f"{p}/tokens": x.astype(np.int32), f"{p}/logits": np.stack(logits, 1).astype(np.float32),
                        f"{p}/experts": np.stack(experts, 1).astype(np.int16),
-                       f"{p}/states": np.stack(states, 1).astype(np.float32), f"{p}/bits": np.asarray(bits)})
+                       f"{p}/states": np.stack(states, 1).astype(np.float32), f"{p}/bits": np.asarray(bits),
+                       f"{p}/stats_groups": groups, f"{p}/stats_rows": rows, f"{p}/stats_layer_input": vmax})
         recs.append({k: v for k, v in case.items()} | {"classes": int(m.classes), "layers": int(m.layers)})
         print(f"float case {p}: done", flush=True)
     np.savez_compressed(HERE / "float_cases.npz", **arrays)

@@ -47,3 +47,16 @@ def test_float_oracle_matches_reference_triton_step(rec, tmp_path):
         st = ref["states"][:, t].astype(np.float64)
     assert off <= FLIPS * total
     np.testing.assert_allclose(om.score(x), ref["bits"], rtol=BITS_RTOL)
+
+
+@pytest.mark.parametrize("rec", FLOAT, ids=[r["name"] for r in FLOAT])
+def test_float_oracle_calibration_matches_reference(rec, tmp_path):
+    """The calibration maxima of cpu/export.py:129-153 (|h| per group of 16, |V' rms(h_below)|, |P_r h| per row), from
+    the float oracle's float64 steps, against the same maxima of the reference's fp32 Triton steps on the same
+    windows: within 1e-5 relative (fp32 against float64)."""
+    from yggdrasil_b200.checkpoint import read_checkpoint
+    npz, ref = float_case(rec, tmp_path)
+    stats = FloatOracle(*read_checkpoint(npz)).calibrate(ref["tokens"])
+    np.testing.assert_allclose(np.stack([s[0] for s in stats]), ref["stats_groups"], rtol=1e-5)
+    np.testing.assert_allclose(np.array([s[1] for s in stats]), ref["stats_layer_input"], rtol=1e-5)
+    np.testing.assert_allclose(np.stack([s[2] for s in stats]), ref["stats_rows"], rtol=1e-5)

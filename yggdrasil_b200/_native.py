@@ -12,7 +12,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libygg_b200.so"
 
 EXPORTS = ("ygg_load", "ygg_info", "ygg_step", "ygg_step_debug", "ygg_score", "ygg_score_grouped_workspace",
            "ygg_score_grouped", "ygg_score_grouped_noalloc", "ygg_status", "ygg_selftest_wait", "ygg_free",
-           "ygg_strerror", "ygg_version", "ygg_fload", "ygg_fstep", "ygg_fstatus", "ygg_ffree")
+           "ygg_strerror", "ygg_version", "ygg_fload", "ygg_fstep", "ygg_fstep_stats", "ygg_fstatus", "ygg_ffree")
 
 YGG_OK = 0
 YGG_E_ARG, YGG_E_FORMAT, YGG_E_UNSUPPORTED, YGG_E_MISSING, YGG_E_CUDA, YGG_E_OOM, YGG_E_TOKEN, YGG_E_TIMEOUT, \
@@ -80,10 +80,11 @@ def flib() -> ctypes.CDLL:
         vp, i32 = ctypes.c_void_p, ctypes.c_int
         l.ygg_fload.argtypes = [vp, ctypes.POINTER(vp), i32, ctypes.POINTER(vp)]
         l.ygg_fstep.argtypes = [vp, i32, vp, vp, vp, vp, vp, vp]
+        l.ygg_fstep_stats.argtypes = [vp, i32, vp, vp, vp, vp, vp, vp, vp]
         l.ygg_fstatus.argtypes = [vp, vp, ctypes.POINTER(ctypes.c_int)]
         l.ygg_ffree.argtypes = [vp]
         l.ygg_ffree.restype = None
-        for f in (l.ygg_fload, l.ygg_fstep, l.ygg_fstatus):
+        for f in (l.ygg_fload, l.ygg_fstep, l.ygg_fstep_stats, l.ygg_fstatus):
             f.restype = ctypes.c_int
         _float_bound = True
     return l

@@ -134,6 +134,49 @@ template <int C> __device__ __forceinline__ void store_q(int8_t *p, const LaneQ<
     else if constexpr (C == 8) *(uint2 *)p = make_uint2(q.w[0], q.w[1]);
     else *(uint4 *)p = make_uint4(q.w[0], q.w[1], q.w[2], q.w[3]);
 }
+// The same for a stream's state in global memory, read and written once per step: cache-streaming loads and stores
+// (ld/st.global.cs, evict first), so that the states a step streams through L2 do not displace the leaf records that
+// many streams share (c3: +4 % tokens/s; the logits stay plain stores, which measured 1 % faster on c4).
+#ifndef YGG_STREAM_HINTS
+#define YGG_STREAM_HINTS 1
+#endif
+template <int C> __device__ __forceinline__ LaneQ<C> load_q_stream(const int8_t *p) {
+#if YGG_STREAM_HINTS
+    LaneQ<C> q;
+    if constexpr (C == 2) {
+        unsigned short v;
+        asm volatile("ld.global.cs.u16 %0, [%1];" : "=h"(v) : "l"(p));
+        q.w[0] = v;
+    } else if constexpr (C == 4) {
+        asm volatile("ld.global.cs.u32 %0, [%1];" : "=r"(q.w[0]) : "l"(p));
+    } else if constexpr (C == 8) {
+        asm volatile("ld.global.cs.v2.u32 {%0, %1}, [%2];" : "=r"(q.w[0]), "=r"(q.w[1]) : "l"(p));
+    } else {
+        asm volatile("ld.global.cs.v4.u32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(q.w[0]), "=r"(q.w[1]), "=r"(q.w[2]), "=r"(q.w[3]) : "l"(p));
+    }
+    return q;
+#else
+    return load_q<C>(p);
+#endif
+}
+template <int C> __device__ __forceinline__ void store_q_stream(int8_t *p, const LaneQ<C> &q) {
+#if YGG_STREAM_HINTS
+    if constexpr (C == 2) {
+        asm volatile("st.global.cs.u16 [%0], %1;" ::"l"(p), "h"((unsigned short)q.w[0]) : "memory");
+    } else if constexpr (C == 4) {
+        asm volatile("st.global.cs.u32 [%0], %1;" ::"l"(p), "r"(q.w[0]) : "memory");
+    } else if constexpr (C == 8) {
+        asm volatile("st.global.cs.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(q.w[0]), "r"(q.w[1]) : "memory");
+    } else {
+        asm volatile("st.global.cs.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(q.w[0]), "r"(q.w[1]), "r"(q.w[2]),
+                     "r"(q.w[3])
+                     : "memory");
+    }
+#else
+    store_q<C>(p, q);
+#endif
+}
 template <int C> __device__ __forceinline__ int dot_q(const LaneQ<C> &a, const LaneQ<C> &b) {
     int s = 0;
 #pragma unroll
@@ -181,20 +224,29 @@ __device__ __forceinline__ float rms_rho(const LaneQ<N / G> &qb, const float *r2
 // Heap-order descent from node 1, right iff f32(w_ix . qb) * rho > thr[x][ix] (cpu/ygg.cpp:271-280), kLook levels
 // per round of loads. Row k of a round's subtree (k = 0: ix; 1-2: 2ix + k-1; 3-6: 4ix + k-3, i.e. ix * 2^lvl(k) +
 // k + 1 - 2^lvl(k)) is read by the LPR = n/16 lanes of row group k % RPI (RPI = G / LPR) in load k / RPI, 16 bytes
-// each; every lane of the row group also reads the row's threshold (one broadcast transaction), so each lane can
-// decide its row and one ballot per load carries every decision of both stream groups. qrow: the lane's 16 bytes of
-// qb at 16 (gl % LPR). DT > 0: the depth fixed at compile time (= depth), which unrolls the rounds with their row
-// counts known. Returns the leaf node index in [E, 2E).
+// each (qrow: the lane's 16 bytes of qb at 16 (gl % LPR)). The NI partial dots of a lane are then reduce-scattered
+// over its row group: halving exchanges leave each lane the whole dot of one load i, then plain butterflies finish
+// the sum; so each lane converts and compares one row, loads only that row's threshold, and one ballot per round
+// carries every decision of both stream groups. DT > 0: the depth fixed at compile time (= depth), which unrolls the
+// rounds with their row counts known. Returns the leaf node index in [E, 2E).
 template <int N, int G, int DT = 0>
 __device__ __forceinline__ int route_look(const int8_t *__restrict__ w, const float *__restrict__ thr_x, int depth,
                                           const uint4 &qrow, float rho, int lane) {
     constexpr int LPR = N / 16;                 // lanes per row
     constexpr int RPI = G / LPR;                // rows of one stream per warp-wide 16-byte load
     constexpr int NI = (kLookRows + RPI - 1) / RPI;
+    constexpr int LS = LPR == 4 ? 2 : LPR == 8 ? 3 : 4;     // log2 LPR
+    constexpr int LN = NI == 1 ? 0 : NI == 2 ? 1 : 2;       // log2 NI
     static_assert(G == 32 || N <= 128, "two streams per warp need rows of at most 8 lanes");
+    static_assert((1 << LN) == NI && NI <= LPR, "NI a power of two within a row group");
     const int gl = lane & (G - 1);
     const int g = gl / LPR;
     const int8_t *wl = w + 16 * (gl % LPR);
+    // the load whose whole dot this lane holds after the reduce-scatter, and that row's subtree index
+    const int mine = (gl % LPR) >> (LS - LN);
+    const int kmine = mine * RPI + g;
+    const int lvm = kmine == 0 ? 0 : kmine < 3 ? 1 : 2;
+    const int mulm = 1 << lvm, addm = kmine + 1 - mulm;
     // per-lane constants of the subtree rows this lane reads: row = ix * mul + add
     int mul[NI], add[NI], kk[NI];
 #pragma unroll
@@ -209,57 +261,48 @@ __device__ __forceinline__ int route_look(const int8_t *__restrict__ w, const fl
     // one round: the lv <= kLook levels under ix
     auto round = [&](const int lv) {
         const int nrows = (1 << lv) - 1;
-        uint4 v[NI];
-        float t[NI];
+        int dot[NI];
 #pragma unroll
         for (int i = 0; i < NI; i++) {
-            const int row = ix * mul[i] + add[i];
-            v[i] = make_uint4(0, 0, 0, 0);
-            t[i] = 0.0f;
+            dot[i] = 0;
             if (kk[i] < nrows) {
-                v[i] = __ldg((const uint4 *)(wl + (size_t)row * N));
-                t[i] = __ldg(thr_x + row);
+                const uint4 v = __ldg((const uint4 *)(wl + (size_t)(ix * mul[i] + add[i]) * N));
+                dot[i] = dot16(v, qrow, 0);
             }
         }
-        // decisions of rows k = RPI i + g, as bit LPR (RPI i + g) of a 64-bit word (each row's LPR lanes agree): the
-        // group's G-bit slice of load i's ballot goes to bits [G i, G i + G)
-        uint64_t bits = 0;
-        constexpr int kFirst = LPR == 16 ? 2 : NI;      // loads whose ballots go into `bits` directly
+        const bool live = kmine < nrows;
+        const float t = live ? __ldg(thr_x + ix * mulm + addm) : 0.0f;
+        // reduce-scatter over the row group: offsets LPR/2, LPR/4, ... halve the values a lane keeps (the upper half
+        // where the lane's offset bit is set), then the remaining offsets sum the last value
+        int cnt = NI;
 #pragma unroll
-        for (int i = 0; i < kFirst; i++) {
-            int dot = dot16(v[i], qrow, 0);
+        for (int st = 0; st < LS; st++) {
+            const int off = LPR >> (st + 1);
+            if (st < LN) {
+                const int half = cnt >> 1;
+                const bool hi = (gl & off) != 0;
 #pragma unroll
-            for (int off = 1; off < LPR; off <<= 1) dot += __shfl_xor_sync(kFull, dot, off);
-            const uint32_t bal = __ballot_sync(kFull, __fmul_rn(i2f(dot), rho) > t[i]);
-            if constexpr (G == 16) {
-                bits |= (uint64_t)((bal >> (lane & 16)) & 0xFFFFu) << (16 * i);
-            } else if constexpr (LPR >= 8) {
-                bits |= (uint64_t)bal << (32 * i);      // row k at bit 8 k (N = 128) or 16 k (N = 256, i < 2)
+                for (int i = 0; i < NI / 2; i++) {
+                    if (i < half) {
+                        const int keep = hi ? dot[i + half] : dot[i], send = hi ? dot[i] : dot[i + half];
+                        dot[i] = keep + __shfl_xor_sync(kFull, send, off);
+                    }
+                }
+                cnt = half;
             } else {
-                bits |= bal;                            // N = 64: one load, row k at bit 4 k
+                dot[0] += __shfl_xor_sync(kFull, dot[0], off);
             }
         }
-        if constexpr (LPR == 16) {                      // N = 256 (G = 32): rows 4-6 sit in loads 2-3; fold them in
-            uint32_t hi = 0;
-#pragma unroll
-            for (int i = 2; i < NI; i++) {
-                int dot = dot16(v[i], qrow, 0);
-#pragma unroll
-                for (int off = 1; off < LPR; off <<= 1) dot += __shfl_xor_sync(kFull, dot, off);
-                const uint32_t bal = __ballot_sync(kFull, __fmul_rn(i2f(dot), rho) > t[i]);
-                hi |= ((bal & 1u) | ((bal >> 15) & 2u)) << (2 * (i - 2));
-            }
-            // rows 0-3 from loads 0-1 at bits 0, 16, 32, 48 -> compact to bits 0-3, then rows 4-6
-            const uint32_t lo = (uint32_t)(bits & 1u) | (uint32_t)((bits >> 15) & 2u) | (uint32_t)((bits >> 30) & 4u) |
-                                (uint32_t)((bits >> 45) & 8u);
-            bits = lo | (hi << 4);
-        }
-        constexpr int kStride = LPR == 16 ? 1 : LPR;   // bit distance between consecutive rows in `bits`
+        const bool right = live && __fmul_rn(i2f(dot[0]), rho) > t;
+        uint32_t bits = __ballot_sync(kFull, right);
+        if constexpr (G == 16) bits = (bits >> (lane & 16)) & 0xFFFFu;
+        // row k's decision sits at lane (k % RPI) LPR + (k / RPI) 2^(LS - LN) of the group
         int k = 0;
 #pragma unroll
         for (int j = 0; j < kLook; j++) {
             if (j < lv) {
-                const int b = (int)((bits >> (kStride * k)) & 1u);
+                const int pos = (k % RPI) * LPR + ((k / RPI) << (LS - LN));
+                const int b = (int)((bits >> pos) & 1u);
                 ix = 2 * ix + b;
                 k = 2 * k + 1 + b;
             }
@@ -321,9 +364,9 @@ __device__ __forceinline__ void leaf_update(const DevModel &m, const DevLayer &y
         constexpr int kRowWords = BLK / 2;             // int16 pairs of one row
         const uint8_t *pa = rec + y.off_a + 16 * gl;
         const int rnd = 1 << (m.shift - 1), sh = m.shift;
-        // G = 32 (C <= 4 rows): every word of the lane first, so that the loads overlap; G = 16 (8 rows): row by row,
-        // which keeps the registers of one row live
-        constexpr int kPre = G == 32 ? C : 1;
+        // G = 32 (C <= 4 rows): every word of the lane first, so that the loads overlap; G = 16 (8 rows): four rows'
+        // words at a time (c4: +7 % tokens/s over row by row; c3 the same)
+        constexpr int kPre = G == 32 ? C : (C >= 4 ? 4 : C);
         uint32_t aw[kPre * kRowWords];
 #pragma unroll
         for (int ii0 = 0; ii0 < C; ii0 += kPre) {

@@ -94,12 +94,18 @@ __device__ __forceinline__ void block_sum(float (&v)[K], float *red, float *out,
     __syncthreads();
 }
 
+// atomicMax of a non-negative float through its bits (the order of non-negative floats is that of their bits)
+__device__ __forceinline__ void max_into(unsigned *p, float v) { atomicMax(p, __float_as_uint(fabsf(v))); }
+
 // One stream per block of N threads at a time. state [B][L][n] (in may equal out), logits [B][C], experts [B][L] or
-// null. RP: the readout rank rounded up to a power of two (<= 32).
+// null. RP: the readout rank rounded up to a power of two (<= 32). stats: null, or the calibration maxima of
+// cpu/export.py:129-153 accumulated over the launch's streams, per layer [n/16 group maxima of |h|][max |V' rms(h_below)|]
+// [R row maxima of |P_r h|] as float bits (the caller zeroes them; an atomicMax per value and block).
 template <int N, int RP>
 __global__ void __launch_bounds__(N) fstep_kernel(const __grid_constant__ FModel m, int B, const int32_t *__restrict__ tokens,
                                                   const float *state_in, float *state_out, float *__restrict__ logits,
-                                                  int32_t *__restrict__ experts, int *__restrict__ bad) {
+                                                  int32_t *__restrict__ experts, int *__restrict__ bad,
+                                                  unsigned *__restrict__ stats) {
     constexpr int NW = N / 32;
     __shared__ float hp[N], below[N], vv[N], emb[N], red[NW * 32], sums[32];
     __shared__ float zs[kMaxLayers][32];
@@ -163,6 +169,12 @@ __global__ void __launch_bounds__(N) fstep_kernel(const __grid_constant__ FModel
                 }
                 r = node - ((1 << m.D) - 1);
                 __syncthreads();   // vv
+                if (stats != nullptr && y.vt != nullptr) {
+                    float a = t < R2 ? fabsf(vv[t]) : 0.0f;
+#pragma unroll
+                    for (int off = 16; off > 0; off >>= 1) a = fmaxf(a, __shfl_xor_sync(kFull, a, off));
+                    if ((t & 31) == 0 && t < R2) max_into(stats + (size_t)l * (N / 16 + 1 + R) + N / 16, a);
+                }
             } else {
                 __syncthreads();   // hp
             }
@@ -191,6 +203,12 @@ __global__ void __launch_bounds__(N) fstep_kernel(const __grid_constant__ FModel
             }
             state_out[((size_t)s * L + l) * N + t] = h;
             if (experts != nullptr && t == 0) experts[(size_t)s * L + l] = r;
+            if (stats != nullptr) {   // group maxima of |h|: the 16 coordinates of a group are 16 lanes of one warp
+                float a = fabsf(h);
+#pragma unroll
+                for (int off = 8; off > 0; off >>= 1) a = fmaxf(a, __shfl_xor_sync(kFull, a, off));
+                if ((t & 15) == 0) max_into(stats + (size_t)l * (N / 16 + 1 + R) + t / 16, a);
+            }
             // readout z = P_r h, and sum h^2 for rms(h)
             {
                 float part[RP];
@@ -198,7 +216,10 @@ __global__ void __launch_bounds__(N) fstep_kernel(const __grid_constant__ FModel
 #pragma unroll
                 for (int k = 0; k < RP; k++) part[k] = k < R ? __ldg(p + (size_t)k * N) * h : 0.0f;
                 block_sum<RP, NW>(part, red, sums, t);
-                if (t < R) zs[l][t] = sums[t];
+                if (t < R) {
+                    zs[l][t] = sums[t];
+                    if (stats != nullptr) max_into(stats + (size_t)l * (N / 16 + 1 + R) + N / 16 + 1 + t, sums[t]);
+                }
                 float sq[1] = {h * h};
                 block_sum<1, NW>(sq, red, sums, t);
                 below[t] = h * rsqrtf(sums[0] / (float)N + kRmsEps);
@@ -238,17 +259,17 @@ size_t align_floats(size_t x) { return (x + 63) / 64 * 64; }   // 256-byte align
 
 template <int N, int RP>
 cudaError_t launch_t(const FModel &dm, int B, const int32_t *tok, const float *sin, float *sout, float *lg, int32_t *ex,
-                     int *bad, int grid, cudaStream_t st) {
-    fstep_kernel<N, RP><<<grid, N, 0, st>>>(dm, B, tok, sin, sout, lg, ex, bad);
+                     int *bad, unsigned *stats, int grid, cudaStream_t st) {
+    fstep_kernel<N, RP><<<grid, N, 0, st>>>(dm, B, tok, sin, sout, lg, ex, bad, stats);
     return cudaGetLastError();
 }
 
 template <int N>
 cudaError_t launch_n(const FModel &dm, int B, const int32_t *tok, const float *sin, float *sout, float *lg, int32_t *ex,
-                     int *bad, int grid, cudaStream_t st) {
-    if (dm.R <= 8) return launch_t<N, 8>(dm, B, tok, sin, sout, lg, ex, bad, grid, st);
-    if (dm.R <= 16) return launch_t<N, 16>(dm, B, tok, sin, sout, lg, ex, bad, grid, st);
-    return launch_t<N, 32>(dm, B, tok, sin, sout, lg, ex, bad, grid, st);
+                     int *bad, unsigned *stats, int grid, cudaStream_t st) {
+    if (dm.R <= 8) return launch_t<N, 8>(dm, B, tok, sin, sout, lg, ex, bad, stats, grid, st);
+    if (dm.R <= 16) return launch_t<N, 16>(dm, B, tok, sin, sout, lg, ex, bad, stats, grid, st);
+    return launch_t<N, 32>(dm, B, tok, sin, sout, lg, ex, bad, stats, grid, st);
 }
 
 }  // namespace
@@ -378,8 +399,8 @@ int ygg_fload(const ygg_fshape_t *sh, const float *const *arrays, int device, yg
     return YGG_OK;
 }
 
-int ygg_fstep(const ygg_fmodel *m, int batch, const int32_t *d_tokens, const float *d_state_in, float *d_state_out,
-              float *d_logits, int32_t *d_experts, void *stream) {
+int ygg_fstep_stats(const ygg_fmodel *m, int batch, const int32_t *d_tokens, const float *d_state_in,
+                    float *d_state_out, float *d_logits, int32_t *d_experts, float *d_stats, void *stream) {
     if (!m || batch < 0) return YGG_E_ARG;
     if (batch == 0) return YGG_OK;
     if (!d_tokens || !d_state_in || !d_state_out || !d_logits) return YGG_E_ARG;
@@ -390,14 +411,20 @@ int ygg_fstep(const ygg_fmodel *m, int batch, const int32_t *d_tokens, const flo
     // a block per stream; up to 32 blocks of 64-256 threads an SM, streams beyond that in a grid-stride loop
     const int grid = batch < 32 * m->sm_count ? batch : 32 * m->sm_count;
     const cudaStream_t st = (cudaStream_t)stream;
+    unsigned *stats = (unsigned *)d_stats;
     cudaError_t e;
     switch (dm.n) {
-        case 64: e = launch_n<64>(dm, batch, d_tokens, d_state_in, d_state_out, d_logits, d_experts, m->d_bad, grid, st); break;
-        case 128: e = launch_n<128>(dm, batch, d_tokens, d_state_in, d_state_out, d_logits, d_experts, m->d_bad, grid, st); break;
-        default: e = launch_n<256>(dm, batch, d_tokens, d_state_in, d_state_out, d_logits, d_experts, m->d_bad, grid, st); break;
+        case 64: e = launch_n<64>(dm, batch, d_tokens, d_state_in, d_state_out, d_logits, d_experts, m->d_bad, stats, grid, st); break;
+        case 128: e = launch_n<128>(dm, batch, d_tokens, d_state_in, d_state_out, d_logits, d_experts, m->d_bad, stats, grid, st); break;
+        default: e = launch_n<256>(dm, batch, d_tokens, d_state_in, d_state_out, d_logits, d_experts, m->d_bad, stats, grid, st); break;
     }
     if (prev >= 0 && prev != m->device) cudaSetDevice(prev);
     return e == cudaSuccess ? YGG_OK : YGG_E_CUDA;
+}
+
+int ygg_fstep(const ygg_fmodel *m, int batch, const int32_t *d_tokens, const float *d_state_in, float *d_state_out,
+              float *d_logits, int32_t *d_experts, void *stream) {
+    return ygg_fstep_stats(m, batch, d_tokens, d_state_in, d_state_out, d_logits, d_experts, nullptr, stream);
 }
 
 int ygg_fstatus(const ygg_fmodel *m, void *stream, int *status_out) {

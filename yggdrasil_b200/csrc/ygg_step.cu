@@ -59,9 +59,23 @@ struct Scratch {
 
 __host__ __device__ constexpr uint32_t pool_slot_bytes(uint32_t rec_max, int n) { return (rec_max + 2 * n + 127) / 128 * 128; }
 __host__ __device__ constexpr uint32_t pool_meta_bytes(int S) { return (16u * S + 127) / 128 * 128; }
-__host__ __device__ constexpr uint32_t scratch_bytes(int n) { return (2 * n + 64 + 32 + 127) / 128 * 128; }
-__host__ __device__ constexpr uint32_t block_smem(uint32_t rec_max, int n, int S, int streams, int state_bytes) {
-    return S * pool_slot_bytes(rec_max, n) + pool_meta_bytes(S) + streams * (scratch_bytes(n) + state_bytes);
+// readout codes zq: one 32-byte slot, or one per layer when the head runs after the last layer (defer_head); the
+// scratch is kept to what a kernel uses, since its shared memory comes out of the SM's L1
+constexpr int kZqSlot = 32;
+__host__ __device__ constexpr uint32_t scratch_bytes(int n, int zq_bytes) {
+    return (2 * n + 64 + zq_bytes + 127) / 128 * 128;
+}
+// Whether the head runs after the last layer (true) or layer by layer inside the layer loop: after, when a lane holds
+// many classes (a wide vocabulary, or a shape not fixed at compile time), so that its logits take no registers across
+// the layer loop (c4, V 256: +11 % tokens/s); inside, for the few classes of a small vocabulary (c3, V 5), where the
+// loop's register allocation came out better with it.
+template <int NVT, int G> __host__ __device__ constexpr bool defer_head() { return NVT == 0 || NVT * G > 64; }
+template <int NVT, int G> __host__ __device__ constexpr int zq_bytes() {
+    return defer_head<NVT, G>() ? kMaxLayers * kZqSlot : kZqSlot;
+}
+__host__ __device__ constexpr uint32_t block_smem(uint32_t rec_max, int n, int S, int streams, int state_bytes,
+                                                  int zqb) {
+    return S * pool_slot_bytes(rec_max, n) + pool_meta_bytes(S) + streams * (scratch_bytes(n, zqb) + state_bytes);
 }
 
 // Lane 0 claims a free unit of P slots for its warp, one slot per stream of the warp (CAS of the warp's id into the
@@ -121,8 +135,11 @@ __device__ __forceinline__ void finish_state(const DevModel &m, TokenCtx<N / G> 
 #pragma unroll
         for (int ii = 0; ii < C; ii++) acc[ii] = 0;
     }
-    if (qlane) store_q<C>(t.q_out + (size_t)l * qstride + C * gl, qn);
-    if (QS) return;   // the score kernel has no debug outputs
+    if (QS) {   // the score kernel's state lives in shared memory, and it has no debug outputs
+        store_q<C>(t.q_out + (size_t)l * qstride + C * gl, qn);
+        return;
+    }
+    if (qlane) store_q_stream<C>(t.q_out + (size_t)l * qstride + C * gl, qn);
     if (t.dbg.routes != nullptr && gl == 0) t.dbg.routes[l] = r;
     if (t.dbg.acc != nullptr && qlane) {
 #pragma unroll
@@ -148,7 +165,8 @@ __device__ __forceinline__ bool layer_step(TokenCtx<N / G> &t, const int l, floa
     LaneQ<C> &qbelow = t.qbelow;
     const DevLayer &y = m.layer[l];
     LaneQ<C> qold = {};
-    if (QS || t.qlane) qold = load_q<C>(t.q_in + (size_t)l * (QS ? N : t.qstride) + C * gl);
+    if (QS) qold = load_q<C>(t.q_in + (size_t)l * N + C * gl);
+    else if (t.qlane) qold = load_q_stream<C>(t.q_in + (size_t)l * t.qstride + C * gl);
     int r = x;
     float rho = 0.0f;
     const bool low = l > 0 && (R2T > 0 || m.R2 > 0);
@@ -243,9 +261,13 @@ __device__ __forceinline__ bool layer_step(TokenCtx<N / G> &t, const int l, floa
     }
     const int zq = readout_code<N, R, G>(ro, lane);
     const int row = readout_row<R, G>(gl);
-    if (row >= 0 && (G == 32 || R == 16 || (gl & 1) == 0)) sc.zq[row] = (int8_t)zq;
-    __syncwarp();
-    head_accumulate<R, NVT, G>(m, y, sc.zq, lg, lane);
+    constexpr bool kDefer = defer_head<NVT, G>();
+    int8_t *zqs = sc.zq + (kDefer ? l * kZqSlot : 0);
+    if (row >= 0 && (G == 32 || R == 16 || (gl & 1) == 0)) zqs[row] = (int8_t)zq;
+    if constexpr (!kDefer) {
+        __syncwarp();
+        head_accumulate<R, NVT, G>(m, y, zqs, lg, lane);
+    }
     qbelow = qn;
     __syncwarp();
     return true;
@@ -264,10 +286,13 @@ __device__ __forceinline__ bool token_step(const DevModel &m, const Pool &pool, 
     const int V = m.V;
     const int nv = NVT ? NVT : m.VP / G;
     const int gl = lane & (G - 1);
-#pragma unroll
-    for (int c = 0; c < kMaxClasses<G>; c++) lg[c] = c < nv ? __ldg(m.head_b + G * c + gl) : 0.0f;
     TokenCtx<N / G> t{m, pool, sc, home, warp, lane, x, q_in, q_out, qstride, qlane && (N / G) * gl < qstride,
                       dbg, {}};
+    constexpr bool kDefer = defer_head<NVT, G>();
+    if constexpr (!kDefer) {
+#pragma unroll
+        for (int c = 0; c < kMaxClasses<G>; c++) lg[c] = c < nv ? __ldg(m.head_b + G * c + gl) : 0.0f;
+    }
     if constexpr (LT > 0 && DIRECT && N <= 64) {
         // the direct path has no early exit (no slot claims, no waits): its fixed layer loop unrolls (n = 64: +8 % on
         // c1; at n = 128 the unrolled body spills)
@@ -284,7 +309,22 @@ __device__ __forceinline__ bool token_step(const DevModel &m, const Pool &pool, 
         for (int l = 0; l < m.L; l++)
             if (!layer_step<N, BLK, R, R2T, NVT, G, DIRECT, QS>(t, l, lg)) return false;
     }
-    if (!QS && dbg.logits != nullptr) {
+    // a deferred head after the last layer, from every layer's readout codes in shared memory: the lane's classes
+    // start at the output bias and add f32(Q_l zq_l) s_l layer by layer (cpu/ygg.cpp:421-434, the reference's order),
+    // so the logits take registers only here; skipped when nothing reads them
+    if constexpr (kDefer) {
+        if (!QS && dbg.logits == nullptr) return true;
+#pragma unroll
+        for (int c = 0; c < kMaxClasses<G>; c++) lg[c] = c < nv ? __ldg(m.head_b + G * c + gl) : 0.0f;
+        if constexpr (LT > 0) {
+#pragma unroll 1
+            for (int l = 0; l < LT; l++) head_accumulate<R, NVT, G>(m, m.layer[l], sc.zq + l * kZqSlot, lg, lane);
+        } else {
+#pragma unroll 1
+            for (int l = 0; l < m.L; l++) head_accumulate<R, NVT, G>(m, m.layer[l], sc.zq + l * kZqSlot, lg, lane);
+        }
+    }
+    if (!QS) {
 #pragma unroll
         for (int c = 0; c < kMaxClasses<G>; c++) {
             const int cls = G * c + gl;
@@ -299,7 +339,7 @@ __device__ __forceinline__ bool token_step(const DevModel &m, const Pool &pool, 
 // Pool and the scratch of this block's stream `sidx` (warp * P + group); the first thread initialises the slots'
 // mbarriers and phases and the units' owners.
 __device__ __forceinline__ void block_init(uint8_t *smem, uint32_t rec_max, int n, int S, int P, int state_bytes,
-                                           int sidx, Pool &pool, Scratch &sc, int8_t *&state) {
+                                           int zqb, int sidx, Pool &pool, Scratch &sc, int8_t *&state) {
     pool.slot_bytes = pool_slot_bytes(rec_max, n);
     pool.slots = smem;
     uint8_t *meta = smem + (size_t)S * pool.slot_bytes;
@@ -308,12 +348,12 @@ __device__ __forceinline__ void block_init(uint8_t *smem, uint32_t rec_max, int 
     pool.phase = (int *)(meta + 12 * S);
     pool.S = S;
     pool.units = S / P;   // 0: no slots (records read from global memory)
-    uint8_t *ws = meta + pool_meta_bytes(S) + (size_t)sidx * (scratch_bytes(n) + state_bytes);
+    uint8_t *ws = meta + pool_meta_bytes(S) + (size_t)sidx * (scratch_bytes(n, zqb) + state_bytes);
     sc.qold = (int8_t *)ws;
     sc.qb = sc.qold + n;
     sc.zl = sc.qb + n;
-    sc.zq = sc.zl + 64;
-    state = (int8_t *)(ws + scratch_bytes(n));
+    sc.zq = sc.zl + 64;        // zq_bytes: one or kMaxLayers slots of kZqSlot codes
+    state = (int8_t *)(ws + scratch_bytes(n, zqb));
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; i++) {
             mbar_init(pool.bars + 8u * i, 1);
@@ -341,7 +381,7 @@ __global__ void __launch_bounds__(256, blocks_per_sm<N>()) step_kernel(const __g
     Pool pool;
     Scratch sc;
     int8_t *unused;
-    block_init(smem, rec_max, N, S, P, 0, sidx, pool, sc, unused);
+    block_init(smem, rec_max, N, S, P, 0, zq_bytes<NVT, G>(), sidx, pool, sc, unused);
     const int home = pool.units ? warp % pool.units : 0;
     const int L = m.L, V = m.V, ns = m.ns;
     for (int base = (blockIdx.x * W + warp) * P; base < B; base += gridDim.x * W * P) {
@@ -389,7 +429,7 @@ __global__ void __launch_bounds__(256, score_blocks_per_sm<N, G>()) score_kernel
     Pool pool;
     Scratch sc;
     int8_t *qs;
-    block_init(smem, rec_max, N, S, P, (L * N + 127) / 128 * 128, sidx, pool, sc, qs);
+    block_init(smem, rec_max, N, S, P, (L * N + 127) / 128 * 128, zq_bytes<NVT, G>(), sidx, pool, sc, qs);
     const int home = pool.units ? warp % pool.units : 0;
     const StepOut none{nullptr, nullptr, nullptr};
     for (int base = (blockIdx.x * W + warp) * P; base < B; base += gridDim.x * W * P) {
@@ -473,7 +513,7 @@ static cudaError_t launch_step_t(const DevModel &dm, int B, const int32_t *tok, 
                                  float *lg, int32_t *routes, int32_t *acc, uint32_t rec_max, int warps, int slots,
                                  int grid_cap, cudaStream_t st) {
     const int S = D ? 0 : slots;
-    const size_t smem = block_smem(rec_max, N, S, warps * (32 / G), 0);
+    const size_t smem = block_smem(rec_max, N, S, warps * (32 / G), 0, zq_bytes<NVT, G>());
     cudaError_t e = raise_smem_limit((const void *)step_kernel<N, BLK, R, R2T, LT, NVT, G, D>, smem,
                                      step_limit<N, BLK, R, R2T, LT, NVT, G, D>());
     if (e != cudaSuccess) return e;
@@ -486,7 +526,7 @@ template <int N, int BLK, int R, int R2T, int LT, int NVT, int G, bool D>
 static cudaError_t launch_score_t(const DevModel &dm, int B, int T, const int32_t *tok, int8_t *state, double *bits,
                                   uint32_t rec_max, int warps, int slots, int grid_cap, cudaStream_t st) {
     const int S = D ? 0 : slots;
-    const size_t smem = block_smem(rec_max, N, S, warps * (32 / G), (dm.L * N + 127) / 128 * 128);
+    const size_t smem = block_smem(rec_max, N, S, warps * (32 / G), (dm.L * N + 127) / 128 * 128, zq_bytes<NVT, G>());
     cudaError_t e = raise_smem_limit((const void *)score_kernel<N, BLK, R, R2T, LT, NVT, G, D>, smem,
                                      score_limit<N, BLK, R, R2T, LT, NVT, G, D>());
     if (e != cudaSuccess) return e;
@@ -555,8 +595,9 @@ cudaError_t launch_score(int n, int blk, int r, int r2p, const DevModel &dm, int
     YGG_DISPATCH(launch_score_t, dm, B, T, tok, state, bits, rec_max, warps, slots, grid_cap, st)
 }
 
+// the largest shared memory of a block of the step or score kernels (the deferred head's zq slots), for the slot sizing
 size_t block_smem_bytes(uint32_t rec_max, int n, int slots, int warps, int state_bytes) {
-    return block_smem(rec_max, n, slots, warps, state_bytes);
+    return block_smem(rec_max, n, slots, warps, state_bytes, kMaxLayers * kZqSlot);
 }
 
 }  // namespace ygg

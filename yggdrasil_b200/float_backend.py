@@ -72,6 +72,7 @@ class B200FloatYggdrasil:
         r0 = rt[0]
         self.layers, self.n = len(layers), np.asarray(tk["bias"]).shape[1]
         self.vocab, self.classes = np.asarray(tk["token_embed"]).shape[0], len(output_bias)
+        self.readout_rank = np.asarray(tk["readout"]).shape[1]
         F = np.asarray(r0["router_embed"]).shape[1]
         fin = np.asarray(r0["router_weight"]).shape[1]
         self.depth = (np.asarray(r0["router_weight"]).shape[0] + 1).bit_length() - 1

@@ -149,24 +149,31 @@ class B200Yggdrasil:
         torch = _torch()
         b = tokens.shape[0]
         stream = torch.cuda.current_stream(self.device).cuda_stream
-        p = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None  # noqa: E731
         if routes is None and acc is None:
-            code = lib().ygg_step(self._h, b, p(tokens), p(state_in), p(state_out), p(logits), ctypes.c_void_p(stream))
+            # pointers as plain ints (the bound argtypes convert them): the per-token path of step()
+            code = lib().ygg_step(self._h, b, tokens.data_ptr(), state_in.data_ptr(), state_out.data_ptr(),
+                                  logits.data_ptr() if logits is not None else None, stream)
         else:
+            p = lambda t: t.data_ptr() if t is not None else None  # noqa: E731
             code = lib().ygg_step_debug(self._h, b, p(tokens), p(state_in), p(state_out), p(logits), p(routes),
-                                        p(acc), ctypes.c_void_p(stream))
+                                        p(acc), stream)
         check(code, "ygg_step")
 
     def _step(self, x, h):
         torch = _torch()
         out = torch.empty_like(h)
-        logits = torch.empty(x.shape[0], self.vocab, dtype=torch.float32, device=self.device)
+        logits = torch.empty((x.shape[0], self.vocab), dtype=torch.float32, device=self.device)
         self.step_into(x, h, out, logits)
         return logits, out
 
     def step(self, tokens, state):
         """One token per stream: tokens (B,) -> logits (B, classes) of the next token, and the new state."""
         torch = _torch()
+        if not self.cuda_graph and type(tokens) is torch.Tensor and tokens.is_cuda and tokens.dtype == torch.int32 \
+                and tokens.device == self.device and tokens.is_contiguous() and type(state) is torch.Tensor \
+                and state.dtype == torch.int8 and state.device == self.device and state.is_contiguous() \
+                and state.shape == (tokens.shape[0], self.layers, self.n):
+            return self._step(tokens, state)   # device tokens and state as they are: no device switch, no copies
         with torch.cuda.device(self.device):
             x = self._tokens(tokens)
             state = self._check_state(state, x.shape[0])
