@@ -490,7 +490,9 @@ int ygg_load(const void *file_bytes, size_t nbytes, int device, ygg_model **out)
     // to about four rows per SM (592 rows: 53.5 against 45.4 M tokens/s), the other kernels from there (888 rows:
     // 68.3 against 53.8 M)
     m->pipe_max = n == 128 && L <= 7 ? 4 * m->sm_count : 0;
-    m->big_min = 32768;
+    // two streams per warp from 8 192 streams at n = 128 (c3: 184.5 against 164.3 M tokens/s at 8 192, 208.3 against
+    // 187.6 at 16 384; c4: 160.2 against 153.6 at 8 192; at 4 096 a warp per stream wins, 141.6 against 128.5)
+    m->big_min = n == 128 ? 8192 : 32768;
     m->force_lanes = 0;
     m->force_direct = -1;
     if (const char *e = getenv("YGG_SMALL_BATCH")) m->small_max = atoi(e);
