@@ -549,26 +549,27 @@ def main():
 
 def run_float(dev, stream, W, n1=512, big=16384):
     """The fp32 step of backend "b200f" on a random float model of the enwik8 large shape (synth.FLOAT_ENWIK8_LARGE):
-    (a) batch 1 through step(tokens, state) with cuda_graph=True, the reference Triton backend's own fastest setting
-    (one graph replay per token, host tokens), per token; (b) the device time of one batch-1 step, from a CUDA graph
-    of 32 steps replayed; (c) tokens/s at `big` streams (kernel time, tokens resident)."""
+    (a) batch 1 through step(tokens, state), one call per token with the token already on the device (as generate()
+    keeps it), timed on the host clock; (b) the device time of one batch-1 step, from a CUDA graph of 32 steps
+    replayed; (c) tokens/s at `big` streams (kernel time, tokens resident)."""
     import torch
 
     from yggdrasil_b200 import synth
     from yggdrasil_b200.float_backend import B200FloatYggdrasil
     shape = synth.FLOAT_ENWIK8_LARGE
     layers, ob = synth.random_float_layers(shape, seed=0)
-    model = B200FloatYggdrasil(layers, ob, device=dev, cuda_graph=True)
+    model = B200FloatYggdrasil(layers, ob, device=dev)
     del layers
     rng = np.random.default_rng(5)
     toks = rng.integers(0, shape["vocab"], n1 + W).astype(np.int32)
+    d_toks = torch.as_tensor(toks).to(dev)
     st = model.init_state(1)
     for i in range(W):
-        _, st = model.step(toks[i:i + 1], st)
+        _, st = model.step(d_toks[i:i + 1], st)
     torch.cuda.synchronize(dev)
     t0 = time.perf_counter()
     for i in range(n1):
-        _, st = model.step(toks[W + i:W + i + 1], st)
+        _, st = model.step(d_toks[W + i:W + i + 1], st)
     torch.cuda.synchronize(dev)
     api_us = (time.perf_counter() - t0) / n1 * 1e6
     # device time per step: a graph of G step_into launches at batch 1

@@ -289,6 +289,9 @@ LAUNCH_CONFIGS = {
     "warp-direct": {"YGG_LANES": "32", "YGG_DIRECT": "1"},  # a warp per stream, records read from global memory
     "half-staged": {"YGG_LANES": "16", "YGG_DIRECT": "0"},  # two streams per warp (shapes that allow it)
     "half-direct": {"YGG_LANES": "16", "YGG_DIRECT": "1"},
+    # the layer-phased step (one launch per layer over all streams), a warp and half a warp per stream
+    "phased": {"YGG_PHASED": "1", "YGG_LANES": "32", "YGG_DIRECT": "1"},
+    "phased-half": {"YGG_PHASED": "1", "YGG_LANES": "16", "YGG_DIRECT": "1"},
 }
 
 

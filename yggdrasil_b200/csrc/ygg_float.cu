@@ -2,15 +2,17 @@
 // its Triton backend fuses the same step, yggdrasil/inference_triton.py:21-106, and adds the head with torch.addmm,
 // :187-194), as the backend "b200f".
 //
-// One block of n threads serves one stream at a time (grid-stride over the streams); thread t owns state coordinate t
-// of every layer. Per layer:
+// One block serves one stream at a time (grid-stride over the streams): n threads, thread t owning state coordinate t
+// of every layer, for large batches; 4 n threads, 4 per coordinate each taking every fourth term of its sums, for a
+// batch of at most two streams per SM, where a step's time is its chain of dependent loads. Per layer:
 //   1. the router (routed layers): f = [router_embed(x); rms(h_below)], node j goes right iff f . W_j + b_j > 0,
 //      descended kLook = 4 levels per round: the 15 rows of the subtree under the current node are read together,
 //      thread t multiplying coordinate t of each row (and token feature t, t < F), and one block reduction of the 15
 //      partial sums decides the round (inference.py:42-52);
-//   2. the layer input v = V' rms(h_below) (thread k < R2 sums row k over the state below in shared memory), then
-//      h_t = T_r[x][t] + sum_k U'_r[t][k] v_k + sum_j A_r[t][j] h_prev[block(t) + j] (inference.py:55-63); every
-//      expert array is stored transposed so that each of these loads is coalesced over the block's threads;
+//   2. the layer input v = V' rms(h_below) (before the router; the inputs split over the whole block, then the parts
+//      added), an L2 prefetch of the chosen expert's arrays, then h_t = T_r[x][t] + sum_k U'_r[t][k] v_k +
+//      sum_j A_r[t][j] h_prev[block(t) + j] (inference.py:55-63); every expert array is stored transposed so that each
+//      of these loads is coalesced over the block's threads;
 //   3. the readout z = P_r h (one block reduction of the R partial products, a reduce-scatter within each warp) and
 //      rms(h) for the layer above.
 // The logits are output_bias + sum_l z_l Q_l^T, in layer order, one class per thread. Everything is fp32 with fused
@@ -94,140 +96,171 @@ __device__ __forceinline__ void block_sum(float (&v)[K], float *red, float *out,
     __syncthreads();
 }
 
+// Bulk prefetch of `bytes` (16-aligned, a multiple of 16) of global memory into L2; nothing waits for it.
+__device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // atomicMax of a non-negative float through its bits (the order of non-negative floats is that of their bits)
 __device__ __forceinline__ void max_into(unsigned *p, float v) { atomicMax(p, __float_as_uint(fabsf(v))); }
 
-// One stream per block of N threads at a time. state [B][L][n] (in may equal out), logits [B][C], experts [B][L] or
-// null. RP: the readout rank rounded up to a power of two (<= 32). stats: null, or the calibration maxima of
-// cpu/export.py:129-153 accumulated over the launch's streams, per layer [n/16 group maxima of |h|][max |V' rms(h_below)|]
-// [R row maxima of |P_r h|] as float bits (the caller zeroes them; an atomicMax per value and block).
-template <int N, int RP>
-__global__ void __launch_bounds__(N) fstep_kernel(const __grid_constant__ FModel m, int B, const int32_t *__restrict__ tokens,
-                                                  const float *state_in, float *state_out, float *__restrict__ logits,
-                                                  int32_t *__restrict__ experts, int *__restrict__ bad,
-                                                  unsigned *__restrict__ stats) {
-    constexpr int NW = N / 32;
-    __shared__ float hp[N], below[N], vv[N], emb[N], red[NW * 32], sums[32];
+// One stream per block of N * TPR threads at a time: thread t works on state coordinate t / TPR and takes part t % TPR
+// of that coordinate's sums (TPR = 1 for throughput at large batches, 4 for the latency of small ones). state
+// [B][L][n] (in may equal out), logits [B][C], experts [B][L] or null. RP: the readout rank rounded up to a power of
+// two (<= 32). stats: null, or the calibration maxima of cpu/export.py:129-153 accumulated over the launch's streams,
+// per layer [n/16 group maxima of |h|][max |V' rms(h_below)|][R row maxima of |P_r h|] as float bits (the caller
+// zeroes them; an atomicMax per value and warp).
+template <int N, int RP, int TPR>
+__global__ void __launch_bounds__(N * TPR) fstep_kernel(const __grid_constant__ FModel m, int B,
+                                                        const int32_t *__restrict__ tokens, const float *state_in,
+                                                        float *state_out, float *__restrict__ logits,
+                                                        int32_t *__restrict__ experts, int *__restrict__ bad,
+                                                        unsigned *__restrict__ stats) {
+    constexpr int NT = N * TPR, NW = NT / 32;
+    constexpr int GL = 16 * TPR < 32 ? 16 * TPR : 32;   // lanes of one warp that hold one group of 16 coordinates
+    __shared__ float hp[N], below[N], vv[N], vpart[NT], emb[N], red[NW * 32], sums[32];
     __shared__ float zs[kMaxLayers][32];
-    const int t = threadIdx.x;
+    const int t = threadIdx.x, row = t / TPR, sub = t % TPR;
     const int L = m.L, V = m.V, C = m.C, R = m.R, R2 = m.R2, F = m.F, FIN = m.FIN, bsz = m.b;
+    const int SW = N / 16 + 1 + R;
     for (int s = blockIdx.x; s < B; s += gridDim.x) {
         const int x = tokens[s];
         if (x < 0 || x >= V) {   // the whole stream is skipped: NaN logits, state unchanged
             if (t == 0) atomicOr(bad, 1);
-            for (int c = t; c < C; c += N) logits[(size_t)s * C + c] = __int_as_float(0x7fc00000);
-            for (int i = t; i < L * N; i += N) state_out[(size_t)s * L * N + i] = state_in[(size_t)s * L * N + i];
+            for (int c = t; c < C; c += NT) logits[(size_t)s * C + c] = __int_as_float(0x7fc00000);
+            for (int i = t; i < L * N; i += NT) state_out[(size_t)s * L * N + i] = state_in[(size_t)s * L * N + i];
             if (experts != nullptr && t < L) experts[(size_t)s * L + t] = -1;
             continue;
         }
         for (int l = 0; l < L; l++) {
             const FLayer &y = m.layer[l];
-            hp[t] = state_in[((size_t)s * L + l) * N + t];
+            if (sub == 0) hp[row] = state_in[((size_t)s * L + l) * N + row];
             int r = x;
             if (l > 0) {
                 if (t < F) emb[t] = __ldg(y.embed + (size_t)x * F + t);
                 __syncthreads();   // hp, emb; below was written before the last barrier of the layer below
-                // layer input v = V' rms(h_below), thread k < R2
-                if (y.vt != nullptr && t < R2) {
-                    float a0 = 0.0f, a1 = 0.0f;
-#pragma unroll 4
-                    for (int i = 0; i < N; i += 2) {
-                        a0 = fmaf(__ldg(y.vt + (size_t)i * R2 + t), below[i], a0);
-                        a1 = fmaf(__ldg(y.vt + (size_t)(i + 1) * R2 + t), below[i + 1], a1);
+                // layer input v = V' rms(h_below): the n inputs split into NP parts, thread (part, k) sums its part of
+                // row k, then thread k adds the parts
+                const int NP = R2 > 0 ? max(1, NT / R2) : 1, span = (N + NP - 1) / NP;
+                if (y.vt != nullptr && t < NP * R2) {
+                    const int k = t % R2, i0 = (t / R2) * span, i1 = min(N, i0 + span);
+                    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+                    int i = i0;
+                    for (; i + 3 < i1; i += 4) {
+                        a0 = fmaf(__ldg(y.vt + (size_t)i * R2 + k), below[i], a0);
+                        a1 = fmaf(__ldg(y.vt + (size_t)(i + 1) * R2 + k), below[i + 1], a1);
+                        a2 = fmaf(__ldg(y.vt + (size_t)(i + 2) * R2 + k), below[i + 2], a2);
+                        a3 = fmaf(__ldg(y.vt + (size_t)(i + 3) * R2 + k), below[i + 3], a3);
                     }
-                    vv[t] = a0 + a1;
+                    for (; i < i1; i++) a0 = fmaf(__ldg(y.vt + (size_t)i * R2 + k), below[i], a0);
+                    vpart[t] = (a0 + a1) + (a2 + a3);
                 }
-                // router: rounds of kLook levels, node j (0-based heap) right iff f . W_j + b_j > 0
+                // router: rounds of kLook levels, node j (0-based heap) right iff f . W_j + b_j > 0; thread t takes the
+                // features t, t + NT, ... of f = [router_embed(x); rms(h_below)]
+                float f0 = 0.0f, f1 = 0.0f;
+                if (t < FIN) f0 = t < F ? emb[t] : below[t - F];
+                if (t + NT < FIN) f1 = t + NT < F ? emb[t + NT] : below[t + NT - F];
                 int node = 0;
                 for (int d0 = 0; d0 < m.D; d0 += kLook) {
                     const int lv = min(kLook, m.D - d0);
                     const int nrows = (1 << lv) - 1;
                     float part[16];
-                    const float bt = below[t];
-                    const float et = t < F ? emb[t] : 0.0f;
 #pragma unroll
                     for (int k = 0; k < 16; k++) {
                         part[k] = 0.0f;
                         if (k < nrows) {
                             const int lvl = k == 0 ? 0 : k < 3 ? 1 : k < 7 ? 2 : 3;
-                            const int row = node * (1 << lvl) + k;
-                            const float *wr = y.w + (size_t)row * FIN;
-                            float p = m.route_on_state ? __ldg(wr + F + t) * bt : 0.0f;
-                            if (t < F) p = fmaf(__ldg(wr + t), et, p);
+                            const float *wr = y.w + (size_t)(node * (1 << lvl) + k) * FIN;
+                            float p = t < FIN ? __ldg(wr + t) * f0 : 0.0f;
+                            if (t + NT < FIN) p = fmaf(__ldg(wr + t + NT), f1, p);
                             part[k] = p;
                         }
                     }
                     block_sum<16, NW>(part, red, sums, t);
                     int rr = 0;
                     for (int j = 0; j < lv; j++) {
-                        const int lvl = j;
-                        const int row = node * (1 << lvl) + rr;
-                        const bool right = sums[rr] + __ldg(y.bias + row) > 0.0f;
+                        const bool right = sums[rr] + __ldg(y.bias + node * (1 << j) + rr) > 0.0f;
                         rr = 2 * rr + 1 + (right ? 1 : 0);
                     }
                     node = node * (1 << lv) + rr;
                 }
                 r = node - ((1 << m.D) - 1);
+                // the chosen expert's arrays towards L2 while the layer input is finished (one thread each)
+                if (t == 0) prefetch_l2(y.table + ((size_t)r * V + x) * N, N * 4u);
+                if (t == 32 && y.ut != nullptr) prefetch_l2(y.ut + (size_t)r * R2 * N, (uint32_t)R2 * N * 4u);
+                if (t == 64 % NT && y.at != nullptr) prefetch_l2(y.at + (size_t)r * bsz * N, (uint32_t)bsz * N * 4u);
+                if (t == 96 % NT) prefetch_l2(y.pt + (size_t)r * R * N, (uint32_t)R * N * 4u);
+                if (y.vt != nullptr && t < R2) {
+                    float a = 0.0f;
+                    for (int q = 0; q < NP; q++) a += vpart[q * R2 + t];
+                    vv[t] = a;
+                }
                 __syncthreads();   // vv
                 if (stats != nullptr && y.vt != nullptr) {
                     float a = t < R2 ? fabsf(vv[t]) : 0.0f;
 #pragma unroll
                     for (int off = 16; off > 0; off >>= 1) a = fmaxf(a, __shfl_xor_sync(kFull, a, off));
-                    if ((t & 31) == 0 && t < R2) max_into(stats + (size_t)l * (N / 16 + 1 + R) + N / 16, a);
+                    if ((t & 31) == 0 && t < R2) max_into(stats + (size_t)l * SW + N / 16, a);
                 }
             } else {
                 __syncthreads();   // hp
             }
-            // h = T_r[x] + U'_r v + A_r h_prev
-            float h = __ldg(y.table + (l == 0 ? (size_t)x * N : ((size_t)r * V + x) * N) + t);
+            // h = T_r[x] + U'_r v + A_r h_prev: each of the TPR threads of a coordinate sums every TPR-th term
+            float h = sub == 0 ? __ldg(y.table + (l == 0 ? (size_t)x * N : ((size_t)r * V + x) * N) + row) : 0.0f;
             if (l > 0 && y.ut != nullptr) {
-                const float *u = y.ut + (size_t)r * R2 * N + t;
-                float a0 = 0.0f, a1 = 0.0f;
-                int k = 0;
-                for (; k + 1 < R2; k += 2) {
+                const float *u = y.ut + (size_t)r * R2 * N + row;
+                float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+                int k = sub;
+#pragma unroll 2
+                for (; k + 3 * TPR < R2; k += 4 * TPR) {
                     a0 = fmaf(__ldg(u + (size_t)k * N), vv[k], a0);
-                    a1 = fmaf(__ldg(u + (size_t)(k + 1) * N), vv[k + 1], a1);
+                    a1 = fmaf(__ldg(u + (size_t)(k + TPR) * N), vv[k + TPR], a1);
+                    a2 = fmaf(__ldg(u + (size_t)(k + 2 * TPR) * N), vv[k + 2 * TPR], a2);
+                    a3 = fmaf(__ldg(u + (size_t)(k + 3 * TPR) * N), vv[k + 3 * TPR], a3);
                 }
-                if (k < R2) a0 = fmaf(__ldg(u + (size_t)k * N), vv[k], a0);
-                h += a0 + a1;
+                for (; k < R2; k += TPR) a0 = fmaf(__ldg(u + (size_t)k * N), vv[k], a0);
+                h += (a0 + a1) + (a2 + a3);
             }
             if (y.at != nullptr) {
-                const float *a = y.at + (size_t)r * bsz * N + t;
-                const int blk0 = (t / bsz) * bsz;
+                const float *a = y.at + (size_t)r * bsz * N + row;
+                const int blk0 = (row / bsz) * bsz;
                 float a0 = 0.0f, a1 = 0.0f;
-                for (int j = 0; j < bsz; j += 2) {
+#pragma unroll 4
+                for (int j = sub; j < bsz; j += 2 * TPR) {
                     a0 = fmaf(__ldg(a + (size_t)j * N), hp[blk0 + j], a0);
-                    a1 = fmaf(__ldg(a + (size_t)(j + 1) * N), hp[blk0 + j + 1], a1);
+                    if (j + TPR < bsz) a1 = fmaf(__ldg(a + (size_t)(j + TPR) * N), hp[blk0 + j + TPR], a1);
                 }
                 h += a0 + a1;
             }
-            state_out[((size_t)s * L + l) * N + t] = h;
+#pragma unroll
+            for (int off = 1; off < TPR; off <<= 1) h += __shfl_xor_sync(kFull, h, off);
+            if (sub == 0) state_out[((size_t)s * L + l) * N + row] = h;
             if (experts != nullptr && t == 0) experts[(size_t)s * L + l] = r;
-            if (stats != nullptr) {   // group maxima of |h|: the 16 coordinates of a group are 16 lanes of one warp
+            if (stats != nullptr) {   // group maxima of |h|, a warp's share of each group of 16 coordinates at a time
                 float a = fabsf(h);
 #pragma unroll
-                for (int off = 8; off > 0; off >>= 1) a = fmaxf(a, __shfl_xor_sync(kFull, a, off));
-                if ((t & 15) == 0) max_into(stats + (size_t)l * (N / 16 + 1 + R) + t / 16, a);
+                for (int off = TPR; off < GL; off <<= 1) a = fmaxf(a, __shfl_xor_sync(kFull, a, off));
+                if ((t & (GL - 1)) == 0) max_into(stats + (size_t)l * SW + row / 16, a);
             }
-            // readout z = P_r h, and sum h^2 for rms(h)
+            // readout z = P_r h (thread sub takes the rows k = sub mod TPR), and sum h^2 for rms(h)
             {
                 float part[RP];
-                const float *p = y.pt + (size_t)r * R * N + t;
+                const float *p = y.pt + (size_t)r * R * N + row;
 #pragma unroll
-                for (int k = 0; k < RP; k++) part[k] = k < R ? __ldg(p + (size_t)k * N) * h : 0.0f;
+                for (int k = 0; k < RP; k++) part[k] = (k < R && k % TPR == sub) ? __ldg(p + (size_t)k * N) * h : 0.0f;
                 block_sum<RP, NW>(part, red, sums, t);
                 if (t < R) {
                     zs[l][t] = sums[t];
-                    if (stats != nullptr) max_into(stats + (size_t)l * (N / 16 + 1 + R) + N / 16 + 1 + t, sums[t]);
+                    if (stats != nullptr) max_into(stats + (size_t)l * SW + N / 16 + 1 + t, sums[t]);
                 }
-                float sq[1] = {h * h};
+                float sq[1] = {sub == 0 ? h * h : 0.0f};
                 block_sum<1, NW>(sq, red, sums, t);
-                below[t] = h * rsqrtf(sums[0] / (float)N + kRmsEps);
+                if (sub == 0) below[row] = h * rsqrtf(sums[0] / (float)N + kRmsEps);
             }
             __syncthreads();   // below, zs
         }
         // logits = output_bias + sum_l z_l Q_l^T, one class per thread
-        for (int c = t; c < C; c += N) {
+        for (int c = t; c < C; c += NT) {
             float lg = __ldg(m.out_bias + c);
             for (int l = 0; l < L; l++) {
                 const float *q = m.layer[l].qt + c;
@@ -257,19 +290,29 @@ namespace {
 
 size_t align_floats(size_t x) { return (x + 63) / 64 * 64; }   // 256-byte aligned sub-arrays
 
-template <int N, int RP>
+template <int N, int RP, int TPR>
 cudaError_t launch_t(const FModel &dm, int B, const int32_t *tok, const float *sin, float *sout, float *lg, int32_t *ex,
                      int *bad, unsigned *stats, int grid, cudaStream_t st) {
-    fstep_kernel<N, RP><<<grid, N, 0, st>>>(dm, B, tok, sin, sout, lg, ex, bad, stats);
+    fstep_kernel<N, RP, TPR><<<grid, N * TPR, 0, st>>>(dm, B, tok, sin, sout, lg, ex, bad, stats);
     return cudaGetLastError();
 }
 
-template <int N>
+template <int N, int TPR>
 cudaError_t launch_n(const FModel &dm, int B, const int32_t *tok, const float *sin, float *sout, float *lg, int32_t *ex,
                      int *bad, unsigned *stats, int grid, cudaStream_t st) {
-    if (dm.R <= 8) return launch_t<N, 8>(dm, B, tok, sin, sout, lg, ex, bad, stats, grid, st);
-    if (dm.R <= 16) return launch_t<N, 16>(dm, B, tok, sin, sout, lg, ex, bad, stats, grid, st);
-    return launch_t<N, 32>(dm, B, tok, sin, sout, lg, ex, bad, stats, grid, st);
+    if (dm.R <= 8) return launch_t<N, 8, TPR>(dm, B, tok, sin, sout, lg, ex, bad, stats, grid, st);
+    if (dm.R <= 16) return launch_t<N, 16, TPR>(dm, B, tok, sin, sout, lg, ex, bad, stats, grid, st);
+    return launch_t<N, 32, TPR>(dm, B, tok, sin, sout, lg, ex, bad, stats, grid, st);
+}
+
+// TPR = 4 threads per coordinate for a batch of at most two streams per SM (each stream's loads spread over 4x the
+// threads: its step is a chain of dependent loads), 1 above (more streams per SM, fewer reductions)
+template <int N>
+cudaError_t launch_tpr(const FModel &dm, int B, const int32_t *tok, const float *sin, float *sout, float *lg,
+                       int32_t *ex, int *bad, unsigned *stats, int sm_count, cudaStream_t st) {
+    if (B <= 2 * sm_count) return launch_n<N, 4>(dm, B, tok, sin, sout, lg, ex, bad, stats, B, st);
+    const int grid = B < 32 * sm_count ? B : 32 * sm_count;
+    return launch_n<N, 1>(dm, B, tok, sin, sout, lg, ex, bad, stats, grid, st);
 }
 
 }  // namespace
@@ -408,15 +451,15 @@ int ygg_fstep_stats(const ygg_fmodel *m, int batch, const int32_t *d_tokens, con
     cudaGetDevice(&prev);
     if (prev != m->device && cudaSetDevice(m->device) != cudaSuccess) return YGG_E_CUDA;
     const FModel &dm = m->dm;
-    // a block per stream; up to 32 blocks of 64-256 threads an SM, streams beyond that in a grid-stride loop
-    const int grid = batch < 32 * m->sm_count ? batch : 32 * m->sm_count;
+    // a block per stream, streams beyond the grid in a grid-stride loop (launch_tpr picks the block shape)
     const cudaStream_t st = (cudaStream_t)stream;
     unsigned *stats = (unsigned *)d_stats;
+    const int sm = m->sm_count;
     cudaError_t e;
     switch (dm.n) {
-        case 64: e = launch_n<64>(dm, batch, d_tokens, d_state_in, d_state_out, d_logits, d_experts, m->d_bad, stats, grid, st); break;
-        case 128: e = launch_n<128>(dm, batch, d_tokens, d_state_in, d_state_out, d_logits, d_experts, m->d_bad, stats, grid, st); break;
-        default: e = launch_n<256>(dm, batch, d_tokens, d_state_in, d_state_out, d_logits, d_experts, m->d_bad, stats, grid, st); break;
+        case 64: e = launch_tpr<64>(dm, batch, d_tokens, d_state_in, d_state_out, d_logits, d_experts, m->d_bad, stats, sm, st); break;
+        case 128: e = launch_tpr<128>(dm, batch, d_tokens, d_state_in, d_state_out, d_logits, d_experts, m->d_bad, stats, sm, st); break;
+        default: e = launch_tpr<256>(dm, batch, d_tokens, d_state_in, d_state_out, d_logits, d_experts, m->d_bad, stats, sm, st); break;
     }
     if (prev >= 0 && prev != m->device) cudaSetDevice(prev);
     return e == cudaSuccess ? YGG_OK : YGG_E_CUDA;

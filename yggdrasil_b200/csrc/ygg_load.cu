@@ -22,6 +22,9 @@ namespace ygg {
 cudaError_t launch_step(int n, int blk, int r, int r2p, const DevModel &dm, int B, const int32_t *tok, const int8_t *sin,
                         int8_t *sout, float *lg, int32_t *routes, int32_t *acc, uint32_t rec_max, int warps,
                         int slots, int grid_cap, cudaStream_t st);
+cudaError_t launch_phased(int n, int blk, int r, int r2p, const DevModel &dm, int B, const int32_t *tok,
+                          const int8_t *sin, int8_t *sout, float *lg, int32_t *routes, int32_t *acc, int8_t *zq, int warps,
+                          int grid_cap, cudaStream_t st);
 cudaError_t launch_score(int n, int blk, int r, int r2p, const DevModel &dm, int B, int T, const int32_t *tok, int8_t *state,
                          double *bits, uint32_t rec_max, int warps, int slots, int grid_cap, cudaStream_t st);
 size_t block_smem_bytes(uint32_t rec_max, int n, int slots, int warps, int state_bytes);
@@ -46,6 +49,7 @@ struct LaunchCfg {
     DevModel dm;
     int slots_step, slots_score;
     bool coop;           // the step / score runs the latency kernels (ygg_coop.cu): 4 warps per stream
+    bool phased;         // the step runs layer by layer, one launch per layer (phase_kernel in ygg_step.cu)
     bool pipe;           // the score runs the layer wavefront (ygg_coop.cu): L + 1 groups of 4 warps per row
 };
 
@@ -65,6 +69,8 @@ struct ygg_model {
     uint8_t *d_blob;          // every device array
     size_t d_bytes;
     int *d_status;
+    int8_t *d_zq;             // the layer-phased step's readout codes between its launches: [phase_cap][L][32]
+    int phase_min, phase_cap; // the step runs layer-phased for phase_min <= B <= phase_cap (direct record reads)
     uint32_t rec_max;
     int warps, grid_cap;
     int sm_count;
@@ -396,7 +402,11 @@ int ygg_load(const void *file_bytes, size_t nbytes, int device, ygg_model **out)
     m->device = device;
     m->sm_count = prop.multiProcessorCount;
     const size_t status_off = blob.size;
-    m->d_bytes = status_off + 256;
+    // the layer-phased step keeps each stream's readout codes (32 bytes a layer) between its launches, in the model's
+    // own allocation: up to phase_cap streams a launch
+    m->phase_cap = 1 << 18;
+    const size_t zq_off = status_off + 256;
+    m->d_bytes = zq_off + (size_t)m->phase_cap * L * 32;
     int rc = YGG_OK;
     if (cudaMalloc((void **)&m->d_blob, m->d_bytes) != cudaSuccess) {
         rc = YGG_E_OOM;
@@ -424,6 +434,7 @@ int ygg_load(const void *file_bytes, size_t nbytes, int device, ygg_model **out)
     dm.head_b = (const float *)d;
     dm.status = (int *)(d + status_off);
     m->d_status = dm.status;
+    m->d_zq = (int8_t *)(d + zq_off);
     uint32_t rec_max = 0;
     for (int l = 0; l < L; l++) {
         const LayerPlan &P = plan[l];
@@ -497,6 +508,8 @@ int ygg_load(const void *file_bytes, size_t nbytes, int device, ygg_model **out)
     m->force_direct = -1;
     if (const char *e = getenv("YGG_SMALL_BATCH")) m->small_max = atoi(e);
     if (const char *e = getenv("YGG_COOP")) m->coop_max = n == 128 ? atoi(e) : 0;
+    m->phase_min = 1 << 30;
+    if (const char *e = getenv("YGG_PHASED")) m->phase_min = atoi(e) > 0 ? atoi(e) : 1 << 30;
     if (const char *e = getenv("YGG_PIPE")) m->pipe_max = n == 128 && L <= 7 ? atoi(e) : 0;
     m->pipe_split = true;
     if (const char *e = getenv("YGG_PIPE_SPLIT")) m->pipe_split = atoi(e) != 0;
@@ -525,6 +538,7 @@ static LaunchCfg choose(const ygg_model *m, int batch) {
     c.dm.direct = m->force_direct >= 0 ? m->force_direct : (batch > m->small_max ? 1 : 0);
     c.coop = !half && m->force_lanes == 0 && m->force_direct < 0 && batch <= m->coop_max;
     c.pipe = !half && m->force_lanes == 0 && m->force_direct < 0 && batch <= m->pipe_max;
+    c.phased = c.dm.direct && !c.coop && batch >= m->phase_min && batch <= m->phase_cap;
     return c;
 }
 
@@ -550,8 +564,10 @@ int ygg_step_debug(const ygg_model *m, int batch, const int32_t *d_tokens, const
     const cudaError_t e =
         c.coop ? launch_coop_step(dm, batch, d_tokens, d_state_in, d_state_out, d_logits, d_routes, d_acc, m->rec_max,
                                   m->sm_count, (cudaStream_t)stream)
-               : launch_step(dm.n, dm.b, dm.R, dm.R2P, dm, batch, d_tokens, d_state_in, d_state_out, d_logits, d_routes,
-                             d_acc, m->rec_max, m->warps, c.slots_step, m->grid_cap, (cudaStream_t)stream);
+        : c.phased ? launch_phased(dm.n, dm.b, dm.R, dm.R2P, dm, batch, d_tokens, d_state_in, d_state_out, d_logits,
+                                   d_routes, d_acc, m->d_zq, m->warps, m->grid_cap, (cudaStream_t)stream)
+                   : launch_step(dm.n, dm.b, dm.R, dm.R2P, dm, batch, d_tokens, d_state_in, d_state_out, d_logits, d_routes,
+                                 d_acc, m->rec_max, m->warps, c.slots_step, m->grid_cap, (cudaStream_t)stream);
     restore_device(m, prev);
     return e == cudaSuccess ? YGG_OK : YGG_E_CUDA;
 }

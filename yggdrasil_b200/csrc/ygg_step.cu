@@ -153,7 +153,7 @@ __device__ __forceinline__ void finish_state(const DevModel &m, TokenCtx<N / G> 
 // kernel). Returns false if a bounded wait gave up (for every stream of the warp). Always inlined: the warp collectives
 // in it (shuffles, ballots, redux) rely on the caller's converged warp, and both stream groups of a warp run it
 // together.
-template <int N, int BLK, int R, int R2T, int NVT, int G, bool DIRECT, bool QS>
+template <int N, int BLK, int R, int R2T, int NVT, int G, bool DIRECT, bool QS, bool PH = false>
 __device__ __forceinline__ bool layer_step(TokenCtx<N / G> &t, const int l, float (&lg)[kMaxClasses<G>]) {
     constexpr int C = N / G;
     const DevModel &m = t.m;
@@ -264,7 +264,7 @@ __device__ __forceinline__ bool layer_step(TokenCtx<N / G> &t, const int l, floa
     constexpr bool kDefer = defer_head<NVT, G>();
     int8_t *zqs = sc.zq + (kDefer ? l * kZqSlot : 0);
     if (row >= 0 && (G == 32 || R == 16 || (gl & 1) == 0)) zqs[row] = (int8_t)zq;
-    if constexpr (!kDefer) {
+    if constexpr (!kDefer && !PH) {
         __syncwarp();
         head_accumulate<R, NVT, G>(m, y, zqs, lg, lane);
     }
@@ -412,6 +412,77 @@ __global__ void __launch_bounds__(256, blocks_per_sm<N>()) step_kernel(const __g
     }
 }
 
+// Layer l of a layer-phased step: one launch per layer over every stream, so that the records the streams gather
+// at a time are one layer's (c3 / c4: 84 MB, which L2 holds) instead of every layer's (252 MB, which it does not).
+// Between the launches a stream's new state of layer l - 1 waits in state_out (read back here as the state below) and
+// its readout codes in zq_all [B][L][kZqSlot]; the launch of the last layer runs the head of every layer, in layer
+// order (cpu/ygg.cpp:421-434). The arithmetic of each layer is the fused step's (layer_step), so the results are the
+// same bit for bit. Records are read from global memory (no staging slots).
+template <int N, int BLK, int R, int R2T, int LT, int NVT, int G>
+__global__ void __launch_bounds__(256, blocks_per_sm<N>()) phase_kernel(const __grid_constant__ DevModel m, int B, int l,
+                                                    const int32_t *__restrict__ tokens, const int8_t *state_in,
+                                                    int8_t *state_out, float *__restrict__ logits,
+                                                    int32_t *__restrict__ routes, int32_t *__restrict__ acc_out,
+                                                    int8_t *__restrict__ zq_all) {
+    constexpr int P = 32 / G, C = N / G;
+    constexpr bool kDefer = defer_head<NVT, G>();
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = blockDim.x >> 5;
+    const int gh = lane / G, gl = lane & (G - 1);
+    const int sidx = warp * P + gh;
+    Pool pool;
+    Scratch sc;
+    int8_t *unused;
+    block_init(smem, 0, N, 0, P, 0, kMaxLayers * kZqSlot, sidx, pool, sc, unused);
+    const int L = LT > 0 ? LT : m.L, V = m.V, ns = m.ns;
+    const int nv = NVT ? NVT : m.VP / G;
+    for (int base = (blockIdx.x * W + warp) * P; base < B; base += gridDim.x * W * P) {
+        const int s = base + gh;
+        const bool real = s < B;
+        const int se = real ? s : base;
+        const int x = tokens[se];
+        const bool bad = x < 0 || x >= V;   // skipped as in step_kernel: NaN logits, state unchanged
+        const bool live = real && !bad;
+        if (l == 0 && real && bad && gl == 0) atomicOr(m.status, kStatusBadToken);
+        const StepOut o{nullptr, (live && routes) ? routes + (size_t)s * L : nullptr,
+                        (live && acc_out) ? acc_out + (size_t)se * L * ns : nullptr};
+        TokenCtx<C> t{m, pool, sc, 0, warp, lane, bad ? 0 : x, state_in + (size_t)se * L * ns,
+                      state_out + (size_t)se * L * ns, ns, live && C * gl < ns, o, {}};
+        if (l > 0 && t.qlane) t.qbelow = load_q<C>(state_out + ((size_t)se * L + l - 1) * ns + C * gl);
+        float lg[kMaxClasses<G>];
+        layer_step<N, BLK, R, R2T, NVT, G, true, false, true>(t, l, lg);
+        const int8_t *zqs = sc.zq + (kDefer ? l * kZqSlot : 0);
+        __syncwarp();
+        if (live && gl < R) zq_all[((size_t)s * L + l) * kZqSlot + gl] = zqs[gl];
+        if (l == L - 1) {
+            // every layer's codes into the stream's slots, then the head in layer order
+            __syncwarp();
+            if (gl < R)
+                for (int j = 0; j < L; j++) sc.zq[j * kZqSlot + gl] = live ? zq_all[((size_t)s * L + j) * kZqSlot + gl] : 0;
+            __syncwarp();
+            if (live && logits != nullptr) {
+#pragma unroll
+                for (int c = 0; c < kMaxClasses<G>; c++) lg[c] = c < nv ? __ldg(m.head_b + G * c + gl) : 0.0f;
+#pragma unroll 1
+                for (int j = 0; j < L; j++) head_accumulate<R, NVT, G>(m, m.layer[j], sc.zq + j * kZqSlot, lg, lane);
+#pragma unroll
+                for (int c = 0; c < kMaxClasses<G>; c++) {
+                    const int cls = G * c + gl;
+                    if (c < nv && cls < V) logits[(size_t)s * V + cls] = lg[c];
+                }
+            }
+            if (real && bad) {
+                if (logits != nullptr)
+                    for (int c = gl; c < V; c += G) logits[(size_t)s * V + c] = __int_as_float(0x7fc00000);
+                if (routes != nullptr && gl < L) routes[(size_t)s * L + gl] = -1;
+            }
+            __syncwarp();
+        }
+        if (real && bad && state_out != state_in)
+            for (int i = gl; i < ns; i += G) state_out[((size_t)s * L + l) * ns + i] = state_in[((size_t)s * L + l) * ns + i];
+    }
+}
+
 // Rows of `steps` tokens; the state of a row lives in its group's shared memory between tokens, the logits in
 // registers, and the f64 NLL of the next token is summed on chip (cpu/ygg.cpp:513-517). Each warp scores P = 32 / G
 // rows at a time; a row past B, or with a token out of range, runs unseen (token 0, nothing written; the bad row
@@ -522,6 +593,26 @@ static cudaError_t launch_step_t(const DevModel &dm, int B, const int32_t *tok, 
     return cudaGetLastError();
 }
 
+template <int N, int BLK, int R, int R2T, int LT, int NVT, int G, bool D> static SmemLimits &phase_limit() { static SmemLimits l{}; return l; }
+
+// The layer-phased step: one phase_kernel launch per layer (D, the record path, is always direct here).
+template <int N, int BLK, int R, int R2T, int LT, int NVT, int G, bool D>
+static cudaError_t launch_phased_t(const DevModel &dm, int B, const int32_t *tok, const int8_t *sin, int8_t *sout,
+                                   float *lg, int32_t *routes, int32_t *acc, int8_t *zq, int warps, int grid_cap,
+                                   cudaStream_t st) {
+    const size_t smem = block_smem(0, N, 0, warps * (32 / G), 0, kMaxLayers * kZqSlot);
+    cudaError_t e = raise_smem_limit((const void *)phase_kernel<N, BLK, R, R2T, LT, NVT, G>, smem,
+                                     phase_limit<N, BLK, R, R2T, LT, NVT, G, false>());
+    if (e != cudaSuccess) return e;
+    const int L = LT > 0 ? LT : dm.L;
+    for (int l = 0; l < L && e == cudaSuccess; l++) {
+        phase_kernel<N, BLK, R, R2T, LT, NVT, G><<<grid_for<G>(B, warps, grid_cap), 32 * warps, smem, st>>>(
+            dm, B, l, tok, sin, sout, lg, routes, acc, zq);
+        e = cudaGetLastError();
+    }
+    return e;
+}
+
 template <int N, int BLK, int R, int R2T, int LT, int NVT, int G, bool D>
 static cudaError_t launch_score_t(const DevModel &dm, int B, int T, const int32_t *tok, int8_t *state, double *bits,
                                   uint32_t rec_max, int warps, int slots, int grid_cap, cudaStream_t st) {
@@ -587,6 +678,13 @@ cudaError_t launch_step(int n, int blk, int r, int r2p, const DevModel &dm, int 
                         int slots, int grid_cap, cudaStream_t st) {
     const int L = dm.L, VP = dm.VP, lw = dm.lw;
     YGG_DISPATCH(launch_step_t, dm, B, tok, sin, sout, lg, routes, acc, rec_max, warps, slots, grid_cap, st)
+}
+
+cudaError_t launch_phased(int n, int blk, int r, int r2p, const DevModel &dm, int B, const int32_t *tok,
+                          const int8_t *sin, int8_t *sout, float *lg, int32_t *routes, int32_t *acc, int8_t *zq, int warps,
+                          int grid_cap, cudaStream_t st) {
+    const int L = dm.L, VP = dm.VP, lw = dm.lw;
+    YGG_DISPATCH(launch_phased_t, dm, B, tok, sin, sout, lg, routes, acc, zq, warps, grid_cap, st)
 }
 
 cudaError_t launch_score(int n, int blk, int r, int r2p, const DevModel &dm, int B, int T, const int32_t *tok, int8_t *state,

@@ -154,15 +154,15 @@ class B200FloatYggdrasil:
     def step_into(self, tokens, state_in, state_out, logits, experts=None):
         """One step into caller buffers (state_out may be state_in). tokens: an int32 device tensor."""
         torch = _torch()
-        p = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None  # noqa: E731
         stream = torch.cuda.current_stream(self.device).cuda_stream
-        check(lib().ygg_fstep(self._h, tokens.shape[0], p(tokens), p(state_in), p(state_out), p(logits), p(experts),
-                              ctypes.c_void_p(stream)), "ygg_fstep")
+        check(lib().ygg_fstep(self._h, tokens.shape[0], tokens.data_ptr(), state_in.data_ptr(), state_out.data_ptr(),
+                              logits.data_ptr(), experts.data_ptr() if experts is not None else None, stream),
+              "ygg_fstep")
 
     def _step(self, x, h):
         torch = _torch()
         out = torch.empty_like(h)
-        logits = torch.empty(x.shape[0], self.classes, dtype=torch.float32, device=self.device)
+        logits = torch.empty((x.shape[0], self.classes), dtype=torch.float32, device=self.device)
         self.step_into(x, h, out, logits)
         return logits, out
 
@@ -176,6 +176,11 @@ class B200FloatYggdrasil:
     def step(self, tokens, state):
         """One token per stream: tokens (B,) -> logits (B, classes) of the next token, state."""
         torch = _torch()
+        if not self.cuda_graph and type(tokens) is torch.Tensor and tokens.is_cuda and tokens.dtype == torch.int32 \
+                and tokens.device == self.device and tokens.is_contiguous() and type(state) is torch.Tensor \
+                and state.dtype == torch.float32 and state.device == self.device and state.is_contiguous() \
+                and state.shape == (tokens.shape[0], self.layers, self.n):
+            return self._step(tokens, state)   # device tokens and state as they are: no device switch, no copies
         with torch.cuda.device(self.device):
             x = self._tokens(tokens)
             state = self._check_state(state, x.shape[0])

@@ -272,7 +272,10 @@ class B200Yggdrasil:
 
     def generate(self, prompt, n, temperature=1.0, top_k=0, seed=0):
         """Prompt (L,) or (B, L), L >= 1, followed by n sampled tokens. temperature 0: greedy
-        (yggdrasil/inference_triton.py:229-248)."""
+        (yggdrasil/inference_triton.py:229-248). Sampling draws from torch's generator seeded with `seed`, as the
+        reference's Triton backend does; the reference's JAX backend draws from a JAX PRNG key instead
+        (yggdrasil/inference.py:190-202), so for the same seed the sampled tokens differ from that backend's. Greedy
+        decoding (temperature 0) equals the reference's on the same model."""
         torch = _torch()
         prompt = np.asarray(prompt, np.int64)
         x = np.atleast_2d(prompt)
