@@ -34,6 +34,7 @@ constexpr unsigned kFull = 0xFFFFFFFFu;
 constexpr int kMaxLayers = 16;
 constexpr int kLook = 4;                       // router levels per round
 constexpr float kRmsEps = 1e-6f;               // yggdrasil/config.py:8
+constexpr int kBatch = 16;                     // loads a thread issues before it uses them, in the long sums
 
 struct FLayer {
     const float *table;   // token layer [V][n] (T_x[x]); routed [E][V][n]
@@ -144,16 +145,16 @@ __global__ void __launch_bounds__(N * TPR) fstep_kernel(const __grid_constant__ 
                 const int NP = R2 > 0 ? max(1, NT / R2) : 1, span = (N + NP - 1) / NP;
                 if (y.vt != nullptr && t < NP * R2) {
                     const int k = t % R2, i0 = (t / R2) * span, i1 = min(N, i0 + span);
-                    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-                    int i = i0;
-                    for (; i + 3 < i1; i += 4) {
-                        a0 = fmaf(__ldg(y.vt + (size_t)i * R2 + k), below[i], a0);
-                        a1 = fmaf(__ldg(y.vt + (size_t)(i + 1) * R2 + k), below[i + 1], a1);
-                        a2 = fmaf(__ldg(y.vt + (size_t)(i + 2) * R2 + k), below[i + 2], a2);
-                        a3 = fmaf(__ldg(y.vt + (size_t)(i + 3) * R2 + k), below[i + 3], a3);
+                    float acc4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                    for (int c0 = i0; c0 < i1; c0 += kBatch) {   // kBatch independent loads in flight
+                        float w[kBatch];
+#pragma unroll
+                        for (int j = 0; j < kBatch; j++) w[j] = c0 + j < i1 ? __ldg(y.vt + (size_t)(c0 + j) * R2 + k) : 0.0f;
+#pragma unroll
+                        for (int j = 0; j < kBatch; j++)
+                            if (c0 + j < i1) acc4[j & 3] = fmaf(w[j], below[c0 + j], acc4[j & 3]);
                     }
-                    for (; i < i1; i++) a0 = fmaf(__ldg(y.vt + (size_t)i * R2 + k), below[i], a0);
-                    vpart[t] = (a0 + a1) + (a2 + a3);
+                    vpart[t] = (acc4[0] + acc4[1]) + (acc4[2] + acc4[3]);
                 }
                 // router: rounds of kLook levels, node j (0-based heap) right iff f . W_j + b_j > 0; thread t takes the
                 // features t, t + NT, ... of f = [router_embed(x); rms(h_below)]
@@ -209,17 +210,21 @@ __global__ void __launch_bounds__(N * TPR) fstep_kernel(const __grid_constant__ 
             float h = sub == 0 ? __ldg(y.table + (l == 0 ? (size_t)x * N : ((size_t)r * V + x) * N) + row) : 0.0f;
             if (l > 0 && y.ut != nullptr) {
                 const float *u = y.ut + (size_t)r * R2 * N + row;
-                float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-                int k = sub;
-#pragma unroll 2
-                for (; k + 3 * TPR < R2; k += 4 * TPR) {
-                    a0 = fmaf(__ldg(u + (size_t)k * N), vv[k], a0);
-                    a1 = fmaf(__ldg(u + (size_t)(k + TPR) * N), vv[k + TPR], a1);
-                    a2 = fmaf(__ldg(u + (size_t)(k + 2 * TPR) * N), vv[k + 2 * TPR], a2);
-                    a3 = fmaf(__ldg(u + (size_t)(k + 3 * TPR) * N), vv[k + 3 * TPR], a3);
+                float acc4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                for (int k0 = sub; k0 < R2; k0 += kBatch * TPR) {   // kBatch independent loads in flight
+                    float w[kBatch];
+#pragma unroll
+                    for (int j = 0; j < kBatch; j++) {
+                        const int k = k0 + j * TPR;
+                        w[j] = k < R2 ? __ldg(u + (size_t)k * N) : 0.0f;
+                    }
+#pragma unroll
+                    for (int j = 0; j < kBatch; j++) {
+                        const int k = k0 + j * TPR;
+                        if (k < R2) acc4[j & 3] = fmaf(w[j], vv[k], acc4[j & 3]);
+                    }
                 }
-                for (; k < R2; k += TPR) a0 = fmaf(__ldg(u + (size_t)k * N), vv[k], a0);
-                h += (a0 + a1) + (a2 + a3);
+                h += (acc4[0] + acc4[1]) + (acc4[2] + acc4[3]);
             }
             if (y.at != nullptr) {
                 const float *a = y.at + (size_t)r * bsz * N + row;
@@ -259,12 +264,22 @@ __global__ void __launch_bounds__(N * TPR) fstep_kernel(const __grid_constant__ 
             }
             __syncthreads();   // below, zs
         }
-        // logits = output_bias + sum_l z_l Q_l^T, one class per thread
+        // logits = output_bias + sum_l z_l Q_l^T, one class per thread; a layer's R unembedding loads are issued
+        // together (RP is a compile-time bound), so a class costs one load latency per layer
         for (int c = t; c < C; c += NT) {
             float lg = __ldg(m.out_bias + c);
             for (int l = 0; l < L; l++) {
                 const float *q = m.layer[l].qt + c;
-                for (int k = 0; k < R; k++) lg = fmaf(zs[l][k], __ldg(q + (size_t)k * C), lg);
+                float qv[RP];
+#pragma unroll
+                for (int k = 0; k < RP; k++) qv[k] = k < R ? __ldg(q + (size_t)k * C) : 0.0f;
+                float a0 = 0.0f, a1 = 0.0f;
+#pragma unroll
+                for (int k = 0; k < RP; k += 2) {
+                    if (k < R) a0 = fmaf(zs[l][k], qv[k], a0);
+                    if (k + 1 < R) a1 = fmaf(zs[l][k + 1], qv[k + 1], a1);
+                }
+                lg += a0 + a1;
             }
             logits[(size_t)s * C + c] = lg;
         }
