@@ -6,9 +6,10 @@
 // of every layer, for large batches; 4 n threads, 4 per coordinate each taking every fourth term of its sums, for a
 // batch of at most two streams per SM, where a step's time is its chain of dependent loads. Per layer:
 //   1. the router (routed layers): f = [router_embed(x); rms(h_below)], node j goes right iff f . W_j + b_j > 0,
-//      descended kLook = 4 levels per round: the 15 rows of the subtree under the current node are read together,
-//      thread t multiplying coordinate t of each row (and token feature t, t < F), and one block reduction of the 15
-//      partial sums decides the round (inference.py:42-52);
+//      descended kLook = 4 levels per round: the 15 rows of the subtree under the current node are loaded together
+//      (every load issued before any is used, so a round costs one memory latency), thread t multiplying feature t of
+//      each row, and one block reduction of the 15 partial sums (each node's bias added by thread 0) decides the
+//      round (inference.py:42-52);
 //   2. the layer input v = V' rms(h_below) (before the router; the inputs split over the whole block, then the parts
 //      added), an L2 prefetch of the chosen expert's arrays, then h_t = T_r[x][t] + sum_k U'_r[t][k] v_k +
 //      sum_j A_r[t][j] h_prev[block(t) + j] (inference.py:55-63); every expert array is stored transposed so that each
@@ -34,7 +35,6 @@ constexpr unsigned kFull = 0xFFFFFFFFu;
 constexpr int kMaxLayers = 16;
 constexpr int kLook = 4;                       // router levels per round
 constexpr float kRmsEps = 1e-6f;               // yggdrasil/config.py:8
-constexpr int kBatch = 16;                     // loads a thread issues before it uses them, in the long sums
 
 struct FLayer {
     const float *table;   // token layer [V][n] (T_x[x]); routed [E][V][n]
@@ -79,8 +79,9 @@ template <int K> __device__ __forceinline__ float reduce_scatter(float (&v)[K], 
     return r;
 }
 
-// Block sums of K per-thread values into out[0, K) (shared memory); red: NW * K floats of shared scratch. Ends
-// synchronised, so out[] is visible to every thread.
+// Block sums of K per-thread values into out[0, K) (shared memory); red: NW * K floats of shared scratch. Each warp
+// reduce-scatters its K sums into red, then a group of NW lanes per value adds the warps' sums with shuffles. Ends
+// synchronised, so out[] is visible to every thread. Needs K <= 32 (K NW <= the block's threads).
 template <int K, int NW>
 __device__ __forceinline__ void block_sum(float (&v)[K], float *red, float *out, int tid) {
     constexpr int LK = Log2<K>::value;
@@ -88,11 +89,12 @@ __device__ __forceinline__ void block_sum(float (&v)[K], float *red, float *out,
     const float r = reduce_scatter<K>(v, lane);
     if ((lane & ((32 >> LK) - 1)) == 0) red[warp * K + (lane >> (5 - LK))] = r;
     __syncthreads();
-    if (tid < K) {
-        float s = 0.0f;
+    constexpr int kActive = K * NW, kLanes = (kActive + 31) / 32 * 32;   // whole warps take part in the shuffles
+    if (tid < kLanes) {
+        float a = tid < kActive ? red[(tid % NW) * K + tid / NW] : 0.0f;
 #pragma unroll
-        for (int w = 0; w < NW; w++) s += red[w * K + tid];
-        out[tid] = s;
+        for (int off = NW / 2; off > 0; off >>= 1) a += __shfl_xor_sync(kFull, a, off);
+        if (tid < kActive && tid % NW == 0) out[tid / NW] = a;
     }
     __syncthreads();
 }
@@ -112,14 +114,14 @@ __device__ __forceinline__ void max_into(unsigned *p, float v) { atomicMax(p, __
 // per layer [n/16 group maxima of |h|][max |V' rms(h_below)|][R row maxima of |P_r h|] as float bits (the caller
 // zeroes them; an atomicMax per value and warp).
 template <int N, int RP, int TPR>
-__global__ void __launch_bounds__(N * TPR) fstep_kernel(const __grid_constant__ FModel m, int B,
+__global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel(const __grid_constant__ FModel m, int B,
                                                         const int32_t *__restrict__ tokens, const float *state_in,
                                                         float *state_out, float *__restrict__ logits,
                                                         int32_t *__restrict__ experts, int *__restrict__ bad,
                                                         unsigned *__restrict__ stats) {
     constexpr int NT = N * TPR, NW = NT / 32;
     constexpr int GL = 16 * TPR < 32 ? 16 * TPR : 32;   // lanes of one warp that hold one group of 16 coordinates
-    __shared__ float hp[N], below[N], vv[N], vpart[NT], emb[N], red[NW * 32], sums[32];
+    __shared__ float hp[N], below[N], vv[N], vpart[NT], emb[N], red[NW * 32], sums[32], bsh[2][16];
     __shared__ float zs[kMaxLayers][32];
     const int t = threadIdx.x, row = t / TPR, sub = t % TPR;
     const int L = m.L, V = m.V, C = m.C, R = m.R, R2 = m.R2, F = m.F, FIN = m.FIN, bsz = m.b;
@@ -145,16 +147,17 @@ __global__ void __launch_bounds__(N * TPR) fstep_kernel(const __grid_constant__ 
                 const int NP = R2 > 0 ? max(1, NT / R2) : 1, span = (N + NP - 1) / NP;
                 if (y.vt != nullptr && t < NP * R2) {
                     const int k = t % R2, i0 = (t / R2) * span, i1 = min(N, i0 + span);
-                    float acc4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                    for (int c0 = i0; c0 < i1; c0 += kBatch) {   // kBatch independent loads in flight
-                        float w[kBatch];
-#pragma unroll
-                        for (int j = 0; j < kBatch; j++) w[j] = c0 + j < i1 ? __ldg(y.vt + (size_t)(c0 + j) * R2 + k) : 0.0f;
-#pragma unroll
-                        for (int j = 0; j < kBatch; j++)
-                            if (c0 + j < i1) acc4[j & 3] = fmaf(w[j], below[c0 + j], acc4[j & 3]);
+                    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+                    int i = i0;
+#pragma unroll(TPR > 1 ? 4 : 1)
+                    for (; i + 3 < i1; i += 4) {
+                        a0 = fmaf(__ldg(y.vt + (size_t)i * R2 + k), below[i], a0);
+                        a1 = fmaf(__ldg(y.vt + (size_t)(i + 1) * R2 + k), below[i + 1], a1);
+                        a2 = fmaf(__ldg(y.vt + (size_t)(i + 2) * R2 + k), below[i + 2], a2);
+                        a3 = fmaf(__ldg(y.vt + (size_t)(i + 3) * R2 + k), below[i + 3], a3);
                     }
-                    vpart[t] = (acc4[0] + acc4[1]) + (acc4[2] + acc4[3]);
+                    for (; i < i1; i++) a0 = fmaf(__ldg(y.vt + (size_t)i * R2 + k), below[i], a0);
+                    vpart[t] = (a0 + a1) + (a2 + a3);
                 }
                 // router: rounds of kLook levels, node j (0-based heap) right iff f . W_j + b_j > 0; thread t takes the
                 // features t, t + NT, ... of f = [router_embed(x); rms(h_below)]
@@ -165,24 +168,37 @@ __global__ void __launch_bounds__(N * TPR) fstep_kernel(const __grid_constant__ 
                 for (int d0 = 0; d0 < m.D; d0 += kLook) {
                     const int lv = min(kLook, m.D - d0);
                     const int nrows = (1 << lv) - 1;
-                    float part[16];
+                    // the rows' loads first (rows past the round's levels read the current node's row, unused), then
+                    // the products: a load used inside its own branch would stall the warp once per row. Thread k < 15
+                    // loads row k's bias into shared memory meanwhile.
+                    float *bs = bsh[(d0 / kLook) & 1];   // by round parity: the last round's walk may still read the other
+                    if (t < nrows) bs[t] = __ldg(y.bias + node * (1 << (31 - __clz(t + 1))) + t);
+                    float wv[16];
 #pragma unroll
                     for (int k = 0; k < 16; k++) {
-                        part[k] = 0.0f;
-                        if (k < nrows) {
-                            const int lvl = k == 0 ? 0 : k < 3 ? 1 : k < 7 ? 2 : 3;
-                            const float *wr = y.w + (size_t)(node * (1 << lvl) + k) * FIN;
-                            float p = t < FIN ? __ldg(wr + t) * f0 : 0.0f;
-                            if (t + NT < FIN) p = fmaf(__ldg(wr + t + NT), f1, p);
-                            part[k] = p;
+                        const int lvl = k == 0 ? 0 : k < 3 ? 1 : k < 7 ? 2 : 3;
+                        const int nd = k < nrows ? node * (1 << lvl) + k : node;
+                        wv[k] = t < FIN ? __ldg(y.w + (size_t)nd * FIN + t) : 0.0f;
+                    }
+                    float part[16];
+#pragma unroll
+                    for (int k = 0; k < 16; k++) part[k] = k < nrows ? wv[k] * f0 : 0.0f;
+                    if constexpr (TPR == 1) {   // n threads, F + n features: the last F features a second time
+                        if (t + NT < FIN) {
+#pragma unroll
+                            for (int k = 0; k < 16; k++) {
+                                const int lvl = k == 0 ? 0 : k < 3 ? 1 : k < 7 ? 2 : 3;
+                                const int nd = k < nrows ? node * (1 << lvl) + k : node;
+                                wv[k] = __ldg(y.w + (size_t)nd * FIN + t + NT);
+                            }
+#pragma unroll
+                            for (int k = 0; k < 16; k++)
+                                if (k < nrows) part[k] = fmaf(wv[k], f1, part[k]);
                         }
                     }
                     block_sum<16, NW>(part, red, sums, t);
                     int rr = 0;
-                    for (int j = 0; j < lv; j++) {
-                        const bool right = sums[rr] + __ldg(y.bias + node * (1 << j) + rr) > 0.0f;
-                        rr = 2 * rr + 1 + (right ? 1 : 0);
-                    }
+                    for (int j = 0; j < lv; j++) rr = 2 * rr + 1 + (sums[rr] + bs[rr] > 0.0f ? 1 : 0);
                     node = node * (1 << lv) + rr;
                 }
                 r = node - ((1 << m.D) - 1);
@@ -206,34 +222,59 @@ __global__ void __launch_bounds__(N * TPR) fstep_kernel(const __grid_constant__ 
             } else {
                 __syncthreads();   // hp
             }
+            // this thread's readout rows of P_r (k = sub mod TPR), loaded with the expert's other arrays when a
+            // thread holds few of them (TPR > 1); with one thread per coordinate they are loaded at the readout, as
+            // 32 more live registers would cost the large batches their occupancy
+            constexpr int kPV = TPR > 1 ? RP / TPR : 1;
+            float pv[kPV > 0 ? kPV : 1];
+            const float *p = y.pt + (size_t)r * R * N + row;
+            if constexpr (TPR > 1) {
+#pragma unroll
+                for (int j = 0; j < RP / TPR; j++) {
+                    const int k = j * TPR + sub;
+                    pv[j] = k < R ? __ldg(p + (size_t)k * N) : 0.0f;
+                }
+            }
             // h = T_r[x] + U'_r v + A_r h_prev: each of the TPR threads of a coordinate sums every TPR-th term
             float h = sub == 0 ? __ldg(y.table + (l == 0 ? (size_t)x * N : ((size_t)r * V + x) * N) + row) : 0.0f;
             if (l > 0 && y.ut != nullptr) {
                 const float *u = y.ut + (size_t)r * R2 * N + row;
-                float acc4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                for (int k0 = sub; k0 < R2; k0 += kBatch * TPR) {   // kBatch independent loads in flight
-                    float w[kBatch];
-#pragma unroll
-                    for (int j = 0; j < kBatch; j++) {
-                        const int k = k0 + j * TPR;
-                        w[j] = k < R2 ? __ldg(u + (size_t)k * N) : 0.0f;
-                    }
-#pragma unroll
-                    for (int j = 0; j < kBatch; j++) {
-                        const int k = k0 + j * TPR;
-                        if (k < R2) acc4[j & 3] = fmaf(w[j], vv[k], acc4[j & 3]);
-                    }
+                float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+                int k = sub;
+#pragma unroll(TPR > 1 ? 4 : 2)
+                for (; k + 3 * TPR < R2; k += 4 * TPR) {
+                    a0 = fmaf(__ldg(u + (size_t)k * N), vv[k], a0);
+                    a1 = fmaf(__ldg(u + (size_t)(k + TPR) * N), vv[k + TPR], a1);
+                    a2 = fmaf(__ldg(u + (size_t)(k + 2 * TPR) * N), vv[k + 2 * TPR], a2);
+                    a3 = fmaf(__ldg(u + (size_t)(k + 3 * TPR) * N), vv[k + 3 * TPR], a3);
                 }
-                h += (acc4[0] + acc4[1]) + (acc4[2] + acc4[3]);
+                for (; k < R2; k += TPR) a0 = fmaf(__ldg(u + (size_t)k * N), vv[k], a0);
+                h += (a0 + a1) + (a2 + a3);
             }
             if (y.at != nullptr) {
                 const float *a = y.at + (size_t)r * bsz * N + row;
                 const int blk0 = (row / bsz) * bsz;
                 float a0 = 0.0f, a1 = 0.0f;
+                if constexpr (TPR > 1) {
+                    constexpr int kA = 32 / TPR;   // block size <= 32: this thread's columns j = sub mod TPR, loaded first
+                    float av[kA];
+#pragma unroll
+                    for (int jj = 0; jj < kA; jj++) {
+                        const int j = jj * TPR + sub;
+                        av[jj] = j < bsz ? __ldg(a + (size_t)j * N) : 0.0f;
+                    }
+#pragma unroll
+                    for (int jj = 0; jj < kA; jj += 2) {
+                        const int j = jj * TPR + sub;
+                        if (j < bsz) a0 = fmaf(av[jj], hp[blk0 + j], a0);
+                        if (jj + 1 < kA && j + TPR < bsz) a1 = fmaf(av[jj + 1], hp[blk0 + j + TPR], a1);
+                    }
+                } else {
 #pragma unroll 4
-                for (int j = sub; j < bsz; j += 2 * TPR) {
-                    a0 = fmaf(__ldg(a + (size_t)j * N), hp[blk0 + j], a0);
-                    if (j + TPR < bsz) a1 = fmaf(__ldg(a + (size_t)(j + TPR) * N), hp[blk0 + j + TPR], a1);
+                    for (int j = 0; j < bsz; j += 2) {
+                        a0 = fmaf(__ldg(a + (size_t)j * N), hp[blk0 + j], a0);
+                        if (j + 1 < bsz) a1 = fmaf(__ldg(a + (size_t)(j + 1) * N), hp[blk0 + j + 1], a1);
+                    }
                 }
                 h += a0 + a1;
             }
@@ -250,9 +291,11 @@ __global__ void __launch_bounds__(N * TPR) fstep_kernel(const __grid_constant__ 
             // readout z = P_r h (thread sub takes the rows k = sub mod TPR), and sum h^2 for rms(h)
             {
                 float part[RP];
-                const float *p = y.pt + (size_t)r * R * N + row;
 #pragma unroll
-                for (int k = 0; k < RP; k++) part[k] = (k < R && k % TPR == sub) ? __ldg(p + (size_t)k * N) * h : 0.0f;
+                for (int k = 0; k < RP; k++) {
+                    if constexpr (TPR > 1) part[k] = (k % TPR == sub) ? pv[k / TPR] * h : 0.0f;
+                    else part[k] = k < R ? __ldg(p + (size_t)k * N) * h : 0.0f;
+                }
                 block_sum<RP, NW>(part, red, sums, t);
                 if (t < R) {
                     zs[l][t] = sums[t];
@@ -264,24 +307,25 @@ __global__ void __launch_bounds__(N * TPR) fstep_kernel(const __grid_constant__ 
             }
             __syncthreads();   // below, zs
         }
-        // logits = output_bias + sum_l z_l Q_l^T, one class per thread; a layer's R unembedding loads are issued
-        // together (RP is a compile-time bound), so a class costs one load latency per layer
-        for (int c = t; c < C; c += NT) {
-            float lg = __ldg(m.out_bias + c);
-            for (int l = 0; l < L; l++) {
-                const float *q = m.layer[l].qt + c;
-                float qv[RP];
+        // logits = output_bias + sum_l z_l Q_l^T: TPR threads per class, thread sub taking the layers l = sub mod TPR
+        // (a layer's R unembedding loads issued together), then added over the TPR threads
+        for (int c0 = 0; c0 < C; c0 += N) {
+            const int c = c0 + row;
+            float lg = 0.0f;
+            if (c < C) {
+                for (int l = sub; l < L; l += TPR) {
+                    const float *q = m.layer[l].qt + c;
+                    float qv[RP];
 #pragma unroll
-                for (int k = 0; k < RP; k++) qv[k] = k < R ? __ldg(q + (size_t)k * C) : 0.0f;
-                float a0 = 0.0f, a1 = 0.0f;
+                    for (int k = 0; k < RP; k++) qv[k] = k < R ? __ldg(q + (size_t)k * C) : 0.0f;
 #pragma unroll
-                for (int k = 0; k < RP; k += 2) {
-                    if (k < R) a0 = fmaf(zs[l][k], qv[k], a0);
-                    if (k + 1 < R) a1 = fmaf(zs[l][k + 1], qv[k + 1], a1);
+                    for (int k = 0; k < RP; k++)
+                        if (k < R) lg = fmaf(zs[l][k], qv[k], lg);
                 }
-                lg += a0 + a1;
             }
-            logits[(size_t)s * C + c] = lg;
+#pragma unroll
+            for (int off = 1; off < TPR; off <<= 1) lg += __shfl_xor_sync(kFull, lg, off);
+            if (c < C && sub == 0) logits[(size_t)s * C + c] = __ldg(m.out_bias + c) + lg;
         }
         __syncthreads();   // zs, hp before the next stream
     }
