@@ -19,6 +19,7 @@
 // The logits are output_bias + sum_l z_l Q_l^T, in layer order, one class per thread. Everything is fp32 with fused
 // multiply-adds; the reference's own fp32 sums run in other orders, so parity is a tolerance (the reference's own:
 // log-probabilities within 1e-4, cpu/tests/test_triton.py:29-30).
+#include <algorithm>
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <stdlib.h>
@@ -104,6 +105,22 @@ __device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
+// L2 prefetch of `count` floats from p (256-byte aligned) in 16 KB pieces, piece i issued by thread i mod nthreads
+// (g: this thread's index among them)
+__device__ __forceinline__ void prefetch_spread(const float *p, size_t count, unsigned g, unsigned nthreads) {
+    constexpr size_t kPiece = 4096;   // floats
+    const size_t pieces = (count + kPiece - 1) / kPiece;
+    for (size_t i = g; i < pieces; i += nthreads) {
+        const size_t n = min(kPiece, count - i * kPiece) & ~size_t(3);
+        if (n) prefetch_l2(p + i * kPiece, (uint32_t)(n * 4));
+    }
+}
+
+// Barrier `id` (not 0, which __syncthreads uses) among the first `count` threads (a multiple of 32) of the block
+__device__ __forceinline__ void named_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // atomicMax of a non-negative float through its bits (the order of non-negative floats is that of their bits)
 __device__ __forceinline__ void max_into(unsigned *p, float v) { atomicMax(p, __float_as_uint(fabsf(v))); }
 
@@ -126,6 +143,22 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
     const int t = threadIdx.x, row = t / TPR, sub = t % TPR;
     const int L = m.L, V = m.V, C = m.C, R = m.R, R2 = m.R2, F = m.F, FIN = m.FIN, bsz = m.b;
     const int SW = N / 16 + 1 + R;
+    if constexpr (TPR > 1) {   // a batch of a few streams, each step a chain of dependent loads: the arrays every
+        // stream reads (the routed layers' router rows, V' and Q) are prefetched into L2 at once, so that the router
+        // rounds and the layer inputs hit L2 rather than wait on DRAM. The pieces are shared out over the helper
+        // blocks past the streams' (an SM's bulk copies run one after another, and a stream's own loads would queue
+        // behind them), or over the whole grid when there are none.
+        const int H = gridDim.x > B ? gridDim.x - B : 0;
+        if (H == 0 || blockIdx.x >= B) {
+            const unsigned g = (H > 0 ? blockIdx.x - B : blockIdx.x) * NT + t, G = (H > 0 ? H : gridDim.x) * NT;
+            for (int l = 1; l < L; l++) {
+                const FLayer &y = m.layer[l];
+                prefetch_spread(y.w, ((size_t(1) << m.D) - 1) * FIN, g, G);
+                if (y.vt != nullptr) prefetch_spread(y.vt, (size_t)N * R2, g, G);
+            }
+            for (int l = 0; l < L; l++) prefetch_spread(m.layer[l].qt, (size_t)R * C, g, G);
+        }
+    }
     for (int s = blockIdx.x; s < B; s += gridDim.x) {
         const int x = tokens[s];
         if (x < 0 || x >= V) {   // the whole stream is skipped: NaN logits, state unchanged
@@ -135,28 +168,51 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
             if (experts != nullptr && t < L) experts[(size_t)s * L + t] = -1;
             continue;
         }
+        // with TPR > 1 and at most n classes, the head is added layer by layer at the readout (thread (row, sub) holding
+        // class row's sum over the rows k = sub mod TPR); otherwise it follows the last layer
+        const bool head_in_layers = TPR > 1 && C <= N;
+        float lgp = 0.0f;
         for (int l = 0; l < L; l++) {
             const FLayer &y = m.layer[l];
             if (sub == 0) hp[row] = state_in[((size_t)s * L + l) * N + row];
             int r = x;
             if (l > 0) {
                 if (t < F) emb[t] = __ldg(y.embed + (size_t)x * F + t);
-                __syncthreads();   // hp, emb; below was written before the last barrier of the layer below
                 // layer input v = V' rms(h_below): the n inputs split into NP parts, thread (part, k) sums its part of
-                // row k, then thread k adds the parts
+                // row k, then thread k adds the parts. With TPR > 1 a part has at most kVW inputs, and its V' values
+                // are loaded before the barrier that publishes rms(h_below), with the state and embedding loads.
                 const int NP = R2 > 0 ? max(1, NT / R2) : 1, span = (N + NP - 1) / NP;
-                if (y.vt != nullptr && t < NP * R2) {
-                    const int k = t % R2, i0 = (t / R2) * span, i1 = min(N, i0 + span);
+                const bool vpart_on = y.vt != nullptr && t < NP * R2;
+                const int k = R2 > 0 ? t % R2 : 0, i0 = (t / max(R2, 1)) * span, i1 = min(N, i0 + span);
+                constexpr int kVW = TPR > 1 ? 16 : 1;
+                float vw[kVW];
+                if constexpr (TPR > 1) {
+#pragma unroll
+                    for (int j = 0; j < kVW; j++)
+                        vw[j] = vpart_on && span <= kVW && i0 + j < i1 ? __ldg(y.vt + (size_t)(i0 + j) * R2 + k) : 0.0f;
+                }
+                __syncthreads();   // hp, emb; below was written before the last barrier of the layer below
+                if (vpart_on) {
                     float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-                    int i = i0;
+                    if (TPR > 1 && span <= kVW) {
+#pragma unroll
+                        for (int j = 0; j < kVW; j += 4) {
+                            if (i0 + j < i1) a0 = fmaf(vw[j], below[i0 + j], a0);
+                            if (i0 + j + 1 < i1) a1 = fmaf(vw[j + 1], below[i0 + j + 1], a1);
+                            if (i0 + j + 2 < i1) a2 = fmaf(vw[j + 2], below[i0 + j + 2], a2);
+                            if (i0 + j + 3 < i1) a3 = fmaf(vw[j + 3], below[i0 + j + 3], a3);
+                        }
+                    } else {
+                        int i = i0;
 #pragma unroll(TPR > 1 ? 4 : 1)
-                    for (; i + 3 < i1; i += 4) {
-                        a0 = fmaf(__ldg(y.vt + (size_t)i * R2 + k), below[i], a0);
-                        a1 = fmaf(__ldg(y.vt + (size_t)(i + 1) * R2 + k), below[i + 1], a1);
-                        a2 = fmaf(__ldg(y.vt + (size_t)(i + 2) * R2 + k), below[i + 2], a2);
-                        a3 = fmaf(__ldg(y.vt + (size_t)(i + 3) * R2 + k), below[i + 3], a3);
+                        for (; i + 3 < i1; i += 4) {
+                            a0 = fmaf(__ldg(y.vt + (size_t)i * R2 + k), below[i], a0);
+                            a1 = fmaf(__ldg(y.vt + (size_t)(i + 1) * R2 + k), below[i + 1], a1);
+                            a2 = fmaf(__ldg(y.vt + (size_t)(i + 2) * R2 + k), below[i + 2], a2);
+                            a3 = fmaf(__ldg(y.vt + (size_t)(i + 3) * R2 + k), below[i + 3], a3);
+                        }
+                        for (; i < i1; i++) a0 = fmaf(__ldg(y.vt + (size_t)i * R2 + k), below[i], a0);
                     }
-                    for (; i < i1; i++) a0 = fmaf(__ldg(y.vt + (size_t)i * R2 + k), below[i], a0);
                     vpart[t] = (a0 + a1) + (a2 + a3);
                 }
                 // router: rounds of kLook levels, node j (0-based heap) right iff f . W_j + b_j > 0; thread t takes the
@@ -165,6 +221,46 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
                 if (t < FIN) f0 = t < F ? emb[t] : below[t - F];
                 if (t + NT < FIN) f1 = t + NT < F ? emb[t + NT] : below[t + NT - F];
                 int node = 0;
+                if constexpr (TPR > 1) {
+                    // a batch of a few streams: only the RW warps that hold a feature route (thread t < F + n, one
+                    // feature each), with named barriers among themselves, so that the rounds cost them their loads
+                    // and two short barriers, not the block's 32 warps' issue; the other warps wait for the node
+                    const int RW = (FIN + 31) / 32, lane = t & 31;
+                    if (t < RW * 32) {
+                        for (int d0 = 0; d0 < m.D; d0 += kLook) {
+                            const int lv = min(kLook, m.D - d0);
+                            const int nrows = (1 << lv) - 1;
+                            if (t < nrows) bsh[0][t] = __ldg(y.bias + node * (1 << (31 - __clz(t + 1))) + t);
+                            float wv[16];
+#pragma unroll
+                            for (int k = 0; k < 16; k++) {
+                                const int lvl = k == 0 ? 0 : k < 3 ? 1 : k < 7 ? 2 : 3;
+                                const int nd = k < nrows ? node * (1 << lvl) + k : node;
+                                wv[k] = t < FIN ? __ldg(y.w + (size_t)nd * FIN + t) : 0.0f;
+                            }
+                            float part[16];
+#pragma unroll
+                            for (int k = 0; k < 16; k++) part[k] = k < nrows ? wv[k] * f0 : 0.0f;
+                            const float rs = reduce_scatter<16>(part, lane);   // lanes 2k, 2k + 1: this warp's row k
+                            if ((lane & 1) == 0) red[(t >> 5) * 16 + (lane >> 1)] = rs;
+                            named_sync(1, RW * 32);
+                            if (t < 32) {   // warp 0: lane k < 15 adds row k over the warps and its bias, then the walk
+                                float a = 0.0f;
+                                if (lane < nrows) {
+                                    for (int w = 0; w < RW; w++) a += red[w * 16 + lane];
+                                    a += bsh[0][lane];
+                                }
+                                int rr = 0;
+                                for (int j = 0; j < lv; j++) rr = 2 * rr + 1 + (__shfl_sync(kFull, a, rr) > 0.0f ? 1 : 0);
+                                if (lane == 0) bsh[1][0] = __int_as_float(node * (1 << lv) + rr);
+                            }
+                            named_sync(1, RW * 32);
+                            node = __float_as_int(bsh[1][0]);
+                        }
+                    }
+                    __syncthreads();   // the node; vpart
+                    node = __float_as_int(bsh[1][0]);
+                } else {
                 for (int d0 = 0; d0 < m.D; d0 += kLook) {
                     const int lv = min(kLook, m.D - d0);
                     const int nrows = (1 << lv) - 1;
@@ -201,6 +297,7 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
                     for (int j = 0; j < lv; j++) rr = 2 * rr + 1 + (sums[rr] + bs[rr] > 0.0f ? 1 : 0);
                     node = node * (1 << lv) + rr;
                 }
+                }
                 r = node - ((1 << m.D) - 1);
                 // the chosen expert's arrays towards L2 while the layer input is finished (one thread each)
                 if (t == 0) prefetch_l2(y.table + ((size_t)r * V + x) * N, N * 4u);
@@ -228,11 +325,13 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
             constexpr int kPV = TPR > 1 ? RP / TPR : 1;
             float pv[kPV > 0 ? kPV : 1];
             const float *p = y.pt + (size_t)r * R * N + row;
+            float qv[kPV > 0 ? kPV : 1];   // Q_l[k][class row], k = sub mod TPR, when the head is added here
             if constexpr (TPR > 1) {
 #pragma unroll
                 for (int j = 0; j < RP / TPR; j++) {
                     const int k = j * TPR + sub;
                     pv[j] = k < R ? __ldg(p + (size_t)k * N) : 0.0f;
+                    qv[j] = head_in_layers && k < R && row < C ? __ldg(y.qt + (size_t)k * C + row) : 0.0f;
                 }
             }
             // h = T_r[x] + U'_r v + A_r h_prev: each of the TPR threads of a coordinate sums every TPR-th term
@@ -301,15 +400,27 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
                     zs[l][t] = sums[t];
                     if (stats != nullptr) max_into(stats + (size_t)l * SW + N / 16 + 1 + t, sums[t]);
                 }
+                if constexpr (TPR > 1) {
+                    if (head_in_layers) {
+#pragma unroll
+                        for (int j = 0; j < RP / TPR; j++)
+                            if (j * TPR + sub < R) lgp = fmaf(sums[j * TPR + sub], qv[j], lgp);
+                    }
+                }
                 float sq[1] = {sub == 0 ? h * h : 0.0f};
                 block_sum<1, NW>(sq, red, sums, t);
                 if (sub == 0) below[row] = h * rsqrtf(sums[0] / (float)N + kRmsEps);
             }
             __syncthreads();   // below, zs
         }
+        if (head_in_layers) {   // logits = output_bias + the TPR threads' sums of class row
+#pragma unroll
+            for (int off = 1; off < TPR; off <<= 1) lgp += __shfl_xor_sync(kFull, lgp, off);
+            if (row < C && sub == 0) logits[(size_t)s * C + row] = __ldg(m.out_bias + row) + lgp;
+        }
         // logits = output_bias + sum_l z_l Q_l^T: TPR threads per class, thread sub taking the layers l = sub mod TPR
         // (a layer's R unembedding loads issued together), then added over the TPR threads
-        for (int c0 = 0; c0 < C; c0 += N) {
+        for (int c0 = 0; c0 < (head_in_layers ? 0 : C); c0 += N) {
             const int c = c0 + row;
             float lg = 0.0f;
             if (c < C) {
@@ -369,7 +480,9 @@ cudaError_t launch_n(const FModel &dm, int B, const int32_t *tok, const float *s
 template <int N>
 cudaError_t launch_tpr(const FModel &dm, int B, const int32_t *tok, const float *sin, float *sout, float *lg,
                        int32_t *ex, int *bad, unsigned *stats, int sm_count, cudaStream_t st) {
-    if (B <= 2 * sm_count) return launch_n<N, 4>(dm, B, tok, sin, sout, lg, ex, bad, stats, B, st);
+    // up to 32 helper blocks that only prefetch, while SMs are left over
+    if (B <= 2 * sm_count)
+        return launch_n<N, 4>(dm, B, tok, sin, sout, lg, ex, bad, stats, B + std::max(0, std::min(32, sm_count - B)), st);
     const int grid = B < 32 * sm_count ? B : 32 * sm_count;
     return launch_n<N, 1>(dm, B, tok, sin, sout, lg, ex, bad, stats, grid, st);
 }
