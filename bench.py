@@ -392,8 +392,9 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=100, help="timed segments per core of the CPU baseline")
     ap.add_argument("--batch1-steps", type=int, default=512)
     ap.add_argument("--prime", type=int, default=64, help="untimed steps that give every stream a history first")
-    ap.add_argument("--mode", default="step", choices=["step", "score"],
-                    help="step: the decode step (the headline metric); score: whole rows scored on the GPU")
+    ap.add_argument("--mode", default="step", choices=["step", "score", "float"],
+                    help="step: the decode step (the headline metric); score: whole rows scored on the GPU; float: "
+                    "only the fp32 float step's measurement (one GPU)")
     ap.add_argument("--score-steps", type=int, default=0, help="tokens per row in score mode (default: the workload's)")
     ap.add_argument("--grouped", action="store_true", help="score mode: also time the leaf-grouped tensor-core path")
     ap.add_argument("--min-group", type=int, default=64, help="streams a leaf needs for the tensor-core path")
@@ -411,6 +412,11 @@ def main():
         return run_reference(args)
 
     import torch
+    if args.mode == "float":
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        print(json.dumps({"mode": "float", **run_float(dev, torch.cuda.current_stream(dev), args.warmup)}))
+        return 0
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

@@ -178,8 +178,9 @@ YGG_API int ygg_fstep(const ygg_fmodel *m, int batch, const int32_t *d_tokens, c
 YGG_API int ygg_fstep_stats(const ygg_fmodel *m, int batch, const int32_t *d_tokens, const float *d_state_in,
                             float *d_state_out, float *d_logits, int32_t *d_experts, float *d_stats, void *stream);
 
-/* YGG_E_TOKEN if a step since the last call met a device token out of range (then cleared), else YGG_OK.
- * Synchronises `stream`. */
+/* YGG_E_TOKEN if a step since the last call met a device token out of range, YGG_E_TIMEOUT if a step's bounded wait
+ * for an asynchronous copy gave up (its results stay exact: the step then read the data from global memory), else
+ * YGG_OK; the record is then cleared. Synchronises `stream`. */
 YGG_API int ygg_fstatus(const ygg_fmodel *m, void *stream, int *status_out);
 
 /* Free a float model; NULL is a no-op. */

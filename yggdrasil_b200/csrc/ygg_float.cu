@@ -8,17 +8,22 @@
 //   1. the router (routed layers): f = [router_embed(x); rms(h_below)], node j goes right iff f . W_j + b_j > 0,
 //      descended kLook = 4 levels per round: the 15 rows of the subtree under the current node are loaded together
 //      (every load issued before any is used, so a round costs one memory latency), thread t multiplying feature t of
-//      each row, and one block reduction of the 15 partial sums (each node's bias added by thread 0) decides the
-//      round (inference.py:42-52);
-//   2. the layer input v = V' rms(h_below) (before the router; the inputs split over the whole block, then the parts
-//      added), an L2 prefetch of the chosen expert's arrays, then h_t = T_r[x][t] + sum_k U'_r[t][k] v_k +
-//      sum_j A_r[t][j] h_prev[block(t) + j] (inference.py:55-63); every expert array is stored transposed so that each
-//      of these loads is coalesced over the block's threads;
+//      each row, and one reduction of the 15 partial sums decides the round (inference.py:42-52). At small batches
+//      only the warps that hold a feature route, reading a copy of the rows blocked by round (a thread's weights
+//      are four 16-byte loads), with one named barrier per round;
+//   2. the layer input v = V' rms(h_below) (the inputs split over the threads, then the parts added; at small batches
+//      V' is copied into shared memory while the layer below finishes and summed by the warps that do not route,
+//      while the others route), an L2 prefetch of the chosen expert's arrays, then h_t = T_r[x][t] + sum_k U'_r[t][k]
+//      v_k + sum_j A_r[t][j] h_prev[block(t) + j] (inference.py:55-63); every expert array is stored transposed so
+//      that each of these loads is coalesced over the block's threads;
 //   3. the readout z = P_r h (one block reduction of the R partial products, a reduce-scatter within each warp) and
 //      rms(h) for the layer above.
-// The logits are output_bias + sum_l z_l Q_l^T, in layer order, one class per thread. Everything is fp32 with fused
-// multiply-adds; the reference's own fp32 sums run in other orders, so parity is a tolerance (the reference's own:
-// log-probabilities within 1e-4, cpu/tests/test_triton.py:29-30).
+// At small batches, helper blocks past the streams' prefetch the arrays every stream reads (router rows, V', Q) into
+// L2 at the start of the launch, and a stream's state of every layer is read at once.
+// The logits are output_bias + sum_l z_l Q_l^T: at small batches added at each layer's readout, else after the last
+// layer, one class per thread. Everything is fp32 with fused multiply-adds; the reference's own fp32 sums run in
+// other orders, so parity is a tolerance (the reference's own: log-probabilities within 1e-4,
+// cpu/tests/test_triton.py:29-30).
 #include <algorithm>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -35,6 +40,7 @@ namespace fstep {
 constexpr unsigned kFull = 0xFFFFFFFFu;
 constexpr int kMaxLayers = 16;
 constexpr int kLook = 4;                       // router levels per round
+constexpr int kVtSmem = 16384;                 // floats: V' (n x R2) is staged in shared memory up to this size
 constexpr float kRmsEps = 1e-6f;               // yggdrasil/config.py:8
 
 struct FLayer {
@@ -45,6 +51,12 @@ struct FLayer {
     const float *embed;   // router_embed [V][F] (routed layers)
     const float *w;       // router rows [E - 1][FIN], heap order from node 0
     const float *bias;    // [E - 1]
+    const float *wb;      // the router rows again, blocked by round for the small-batch step: for each round (kLook
+                          // levels from depth d0 = kLook i), for each node m of depth d0 in order, a block of the
+                          // P - 1 rows of the subtree under m (P = 2^levels of the round) in local heap order (row k =
+                          // 0 the node itself), stored [P/4][FIN][4]: element (k, f) at ((k/4) FIN + f) 4 + k mod 4,
+                          // so that feature f's four rows 4q..4q+3 are one 16-byte load and a warp's loads coalesce
+                          // ([FIN][2] for P = 2); row P - 1 is zero
     const float *vt;      // layer-input down projection, transposed [n][R2]; null: no layer input
     const float *ut;      // layer-input projection [E][R2][n]
 };
@@ -121,6 +133,26 @@ __device__ __forceinline__ void named_sync(int id, int count) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// One-thread bulk copy of `bytes` (16-byte aligned, a multiple of 16) global -> this block's shared memory, completing
+// on the mbarrier at `bar` (which expects the bytes); and a bounded wait for a phase of that mbarrier (false: the
+// copy did not land within the limit)
+__device__ __forceinline__ void bulk_to_shared(float *dst, const float *src, uint32_t bytes, uint64_t *bar) {
+    const unsigned b = (unsigned)__cvta_generic_to_shared(bar);
+    asm volatile("mbarrier.arrive.expect_tx.shared.b64 _, [%0], %1;" ::"r"(b), "r"(bytes) : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"((unsigned)__cvta_generic_to_shared(dst)), "l"(src), "r"(bytes), "r"(b) : "memory");
+}
+__device__ __forceinline__ bool wait_phase(uint64_t *bar, unsigned parity) {
+    const unsigned b = (unsigned)__cvta_generic_to_shared(bar);
+    for (int i = 0; i < (1 << 22); i++) {   // each try may suspend the thread for a while: seconds in all
+        unsigned ok;
+        asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                     : "=r"(ok) : "r"(b), "r"(parity) : "memory");
+        if (ok) return true;
+    }
+    return false;
+}
+
 // atomicMax of a non-negative float through its bits (the order of non-negative floats is that of their bits)
 __device__ __forceinline__ void max_into(unsigned *p, float v) { atomicMax(p, __float_as_uint(fabsf(v))); }
 
@@ -138,8 +170,12 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
                                                         unsigned *__restrict__ stats) {
     constexpr int NT = N * TPR, NW = NT / 32;
     constexpr int GL = 16 * TPR < 32 ? 16 * TPR : 32;   // lanes of one warp that hold one group of 16 coordinates
-    __shared__ float hp[N], below[N], vv[N], vpart[NT], emb[N], red[NW * 32], sums[32], bsh[2][16];
+    __shared__ float hp[TPR == 1 ? N : 1], below[N], vv[N], vpart[NT], emb[N], red[NW * 32], sums[32], bsh[2][16];
     __shared__ float zs[kMaxLayers][32];
+    __shared__ int nodesh;
+    __shared__ float hs[TPR > 1 ? kMaxLayers * N : 1];   // small batches: the stream's state of every layer, read at once
+    extern __shared__ __align__(16) float vts[];          // V' of the next routed layer, when staged (vsm)
+    __shared__ __align__(8) uint64_t vbar;                 // its copy's mbarrier
     const int t = threadIdx.x, row = t / TPR, sub = t % TPR;
     const int L = m.L, V = m.V, C = m.C, R = m.R, R2 = m.R2, F = m.F, FIN = m.FIN, bsz = m.b;
     const int SW = N / 16 + 1 + R;
@@ -159,6 +195,21 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
             for (int l = 0; l < L; l++) prefetch_spread(m.layer[l].qt, (size_t)R * C, g, G);
         }
     }
+    // a batch of a few streams: V' of each routed layer is copied into shared memory (the launch gives the dynamic
+    // shared memory) while the layer below finishes, by one bulk copy that thread 0 issues; every thread waits for its
+    // phase, with a limit after which the launch reports YGG_E_TIMEOUT and the block reads V' from global memory
+    bool vsm = TPR > 1 && R2 > 0 && N * R2 <= kVtSmem;
+    unsigned vphase = 0;
+    if (vsm) {
+        if (t == 0) {
+            asm volatile("mbarrier.init.shared.b64 [%0], 1;" ::"r"((unsigned)__cvta_generic_to_shared(&vbar)));
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        }
+        __syncthreads();
+    }
+    auto stage_vt = [&](const float *vt) {
+        if (t == 0) bulk_to_shared(vts, vt, (uint32_t)(N * R2 * sizeof(float)), &vbar);
+    };
     for (int s = blockIdx.x; s < B; s += gridDim.x) {
         const int x = tokens[s];
         if (x < 0 || x >= V) {   // the whole stream is skipped: NaN logits, state unchanged
@@ -172,29 +223,59 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
         // class row's sum over the rows k = sub mod TPR); otherwise it follows the last layer
         const bool head_in_layers = TPR > 1 && C <= N;
         float lgp = 0.0f;
+        if constexpr (TPR > 1) {   // the stream's state in, every layer's at once (published by layer 0's barrier)
+            for (int i = t; i < L * N; i += NT) hs[i] = state_in[(size_t)s * L * N + i];
+        }
         for (int l = 0; l < L; l++) {
             const FLayer &y = m.layer[l];
-            if (sub == 0) hp[row] = state_in[((size_t)s * L + l) * N + row];
+            if constexpr (TPR == 1) hp[row] = state_in[((size_t)s * L + l) * N + row];
+            const float *hpl = TPR > 1 ? hs + l * N : hp;   // h of this layer before the step
             int r = x;
             if (l > 0) {
                 if (t < F) emb[t] = __ldg(y.embed + (size_t)x * F + t);
                 // layer input v = V' rms(h_below): the n inputs split into NP parts, thread (part, k) sums its part of
-                // row k, then thread k adds the parts. With TPR > 1 a part has at most kVW inputs, and its V' values
-                // are loaded before the barrier that publishes rms(h_below), with the state and embedding loads.
-                const int NP = R2 > 0 ? max(1, NT / R2) : 1, span = (N + NP - 1) / NP;
-                const bool vpart_on = y.vt != nullptr && t < NP * R2;
-                const int k = R2 > 0 ? t % R2 : 0, i0 = (t / max(R2, 1)) * span, i1 = min(N, i0 + span);
+                // row k, then thread k adds the parts. With TPR > 1 and V' in shared memory, the threads past the
+                // routing warps' do it while those route (vsplit); otherwise every thread, before the router, a part
+                // of at most kVW inputs having its V' values loaded before the barrier that publishes rms(h_below).
+                if constexpr (TPR > 1) {
+                    if (vsm) {
+                        if (!wait_phase(&vbar, vphase)) {   // V' did not land: report, and read it from global memory
+                            atomicOr(bad, 2);
+                            vsm = false;
+                        }
+                        vphase ^= 1;
+                    }
+                }
+                const int RWT = TPR > 1 ? (FIN + 31) / 32 * 32 : 0;   // the routing threads
+                const bool vsplit = vsm && R2 <= NT - RWT;
+                const int vb = vsplit ? RWT : 0, vi = t - vb;
+                const int NP = R2 > 0 ? max(1, (NT - vb) / R2) : 1, span = (N + NP - 1) / NP;
+                const bool vpart_on = y.vt != nullptr && vi >= 0 && vi < NP * R2;
+                const int k = R2 > 0 && vi >= 0 ? vi % R2 : 0, i0 = (vi >= 0 ? vi / max(R2, 1) : 0) * span,
+                          i1 = min(N, i0 + span);
                 constexpr int kVW = TPR > 1 ? 16 : 1;
                 float vw[kVW];
                 if constexpr (TPR > 1) {
+                    if (!vsm) {
 #pragma unroll
-                    for (int j = 0; j < kVW; j++)
-                        vw[j] = vpart_on && span <= kVW && i0 + j < i1 ? __ldg(y.vt + (size_t)(i0 + j) * R2 + k) : 0.0f;
+                        for (int j = 0; j < kVW; j++)
+                            vw[j] = vpart_on && span <= kVW && i0 + j < i1 ? __ldg(y.vt + (size_t)(i0 + j) * R2 + k) : 0.0f;
+                    }
                 }
-                __syncthreads();   // hp, emb; below was written before the last barrier of the layer below
-                if (vpart_on) {
+                __syncthreads();   // hs, emb, V'; below was written before the last barrier of the layer below
+                auto layer_input_part = [&]() {
                     float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
-                    if (TPR > 1 && span <= kVW) {
+                    if (vsm) {
+                        int i = i0;
+#pragma unroll 4
+                        for (; i + 3 < i1; i += 4) {
+                            a0 = fmaf(vts[i * R2 + k], below[i], a0);
+                            a1 = fmaf(vts[(i + 1) * R2 + k], below[i + 1], a1);
+                            a2 = fmaf(vts[(i + 2) * R2 + k], below[i + 2], a2);
+                            a3 = fmaf(vts[(i + 3) * R2 + k], below[i + 3], a3);
+                        }
+                        for (; i < i1; i++) a0 = fmaf(vts[i * R2 + k], below[i], a0);
+                    } else if (TPR > 1 && span <= kVW) {
 #pragma unroll
                         for (int j = 0; j < kVW; j += 4) {
                             if (i0 + j < i1) a0 = fmaf(vw[j], below[i0 + j], a0);
@@ -213,8 +294,9 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
                         }
                         for (; i < i1; i++) a0 = fmaf(__ldg(y.vt + (size_t)i * R2 + k), below[i], a0);
                     }
-                    vpart[t] = (a0 + a1) + (a2 + a3);
-                }
+                    vpart[vi] = (a0 + a1) + (a2 + a3);
+                };
+                if (vpart_on && !vsplit) layer_input_part();
                 // router: rounds of kLook levels, node j (0-based heap) right iff f . W_j + b_j > 0; thread t takes the
                 // features t, t + NT, ... of f = [router_embed(x); rms(h_below)]
                 float f0 = 0.0f, f1 = 0.0f;
@@ -223,43 +305,54 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
                 int node = 0;
                 if constexpr (TPR > 1) {
                     // a batch of a few streams: only the RW warps that hold a feature route (thread t < F + n, one
-                    // feature each), with named barriers among themselves, so that the rounds cost them their loads
-                    // and two short barriers, not the block's 32 warps' issue; the other warps wait for the node
+                    // feature each), so that a round costs them their loads and one short barrier rather than the
+                    // block's 32 warps' issue. Thread t reads its feature's weights of the round's rows from the
+                    // round-blocked copy (16-byte loads that coalesce over the warp), each warp reduce-scatters its 15
+                    // partial sums into red, and after a named barrier every routing warp adds the warps' sums and
+                    // walks the round itself (same order, same node). red and the biases alternate by round parity,
+                    // so the next round's writes never meet this round's reads. The other warps meanwhile sum the
+                    // layer input (vsplit), then wait for the node.
                     const int RW = (FIN + 31) / 32, lane = t & 31;
                     if (t < RW * 32) {
+                        size_t woff = 0;   // the round's first block in wb
                         for (int d0 = 0; d0 < m.D; d0 += kLook) {
-                            const int lv = min(kLook, m.D - d0);
-                            const int nrows = (1 << lv) - 1;
-                            if (t < nrows) bsh[0][t] = __ldg(y.bias + node * (1 << (31 - __clz(t + 1))) + t);
+                            const int lv = min(kLook, m.D - d0), P = 1 << lv;
+                            const int nrows = P - 1, par = (d0 / kLook) & 1;
+                            if (t < nrows) bsh[par][t] = __ldg(y.bias + node * (1 << (31 - __clz(t + 1))) + t);
+                            const float *blk = y.wb + woff + (size_t)(node - ((1 << d0) - 1)) * FIN * P;
                             float wv[16];
 #pragma unroll
-                            for (int k = 0; k < 16; k++) {
-                                const int lvl = k == 0 ? 0 : k < 3 ? 1 : k < 7 ? 2 : 3;
-                                const int nd = k < nrows ? node * (1 << lvl) + k : node;
-                                wv[k] = t < FIN ? __ldg(y.w + (size_t)nd * FIN + t) : 0.0f;
+                            for (int q = 0; q < 4; q++) {
+                                float4 v4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                                if (t < FIN && 4 * q < P) {
+                                    if (P >= 4) v4 = __ldg(reinterpret_cast<const float4 *>(blk) + (size_t)q * FIN + t);
+                                    else v4.x = __ldg(blk + 2 * t);   // P = 2: the round's one row
+                                }
+                                wv[4 * q] = v4.x; wv[4 * q + 1] = v4.y; wv[4 * q + 2] = v4.z; wv[4 * q + 3] = v4.w;
                             }
                             float part[16];
 #pragma unroll
                             for (int k = 0; k < 16; k++) part[k] = k < nrows ? wv[k] * f0 : 0.0f;
                             const float rs = reduce_scatter<16>(part, lane);   // lanes 2k, 2k + 1: this warp's row k
-                            if ((lane & 1) == 0) red[(t >> 5) * 16 + (lane >> 1)] = rs;
+                            float *rd = red + par * (NW * 16);
+                            if ((lane & 1) == 0) rd[(t >> 5) * 16 + (lane >> 1)] = rs;
                             named_sync(1, RW * 32);
-                            if (t < 32) {   // warp 0: lane k < 15 adds row k over the warps and its bias, then the walk
-                                float a = 0.0f;
-                                if (lane < nrows) {
-                                    for (int w = 0; w < RW; w++) a += red[w * 16 + lane];
-                                    a += bsh[0][lane];
-                                }
-                                int rr = 0;
-                                for (int j = 0; j < lv; j++) rr = 2 * rr + 1 + (__shfl_sync(kFull, a, rr) > 0.0f ? 1 : 0);
-                                if (lane == 0) bsh[1][0] = __int_as_float(node * (1 << lv) + rr);
+                            float a = 0.0f;   // lane k < nrows: row k over the warps, and its bias
+                            if (lane < nrows) {
+                                for (int w = 0; w < RW; w++) a += rd[w * 16 + lane];
+                                a += bsh[par][lane];
                             }
-                            named_sync(1, RW * 32);
-                            node = __float_as_int(bsh[1][0]);
+                            int rr = 0;
+                            for (int j = 0; j < lv; j++) rr = 2 * rr + 1 + (__shfl_sync(kFull, a, rr) > 0.0f ? 1 : 0);
+                            node = node * (1 << lv) + rr;
+                            woff += ((size_t)FIN << d0) * P;
                         }
+                        if (t == 0) nodesh = node;
+                    } else if (vpart_on && vsplit) {
+                        layer_input_part();
                     }
-                    __syncthreads();   // the node; vpart
-                    node = __float_as_int(bsh[1][0]);
+                    __syncthreads();   // the node; vpart (V' in shared memory is read no more in this layer)
+                    node = nodesh;
                 } else {
                 for (int d0 = 0; d0 < m.D; d0 += kLook) {
                     const int lv = min(kLook, m.D - d0);
@@ -365,14 +458,14 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
 #pragma unroll
                     for (int jj = 0; jj < kA; jj += 2) {
                         const int j = jj * TPR + sub;
-                        if (j < bsz) a0 = fmaf(av[jj], hp[blk0 + j], a0);
-                        if (jj + 1 < kA && j + TPR < bsz) a1 = fmaf(av[jj + 1], hp[blk0 + j + TPR], a1);
+                        if (j < bsz) a0 = fmaf(av[jj], hpl[blk0 + j], a0);
+                        if (jj + 1 < kA && j + TPR < bsz) a1 = fmaf(av[jj + 1], hpl[blk0 + j + TPR], a1);
                     }
                 } else {
 #pragma unroll 4
                     for (int j = 0; j < bsz; j += 2) {
-                        a0 = fmaf(__ldg(a + (size_t)j * N), hp[blk0 + j], a0);
-                        if (j + 1 < bsz) a1 = fmaf(__ldg(a + (size_t)(j + 1) * N), hp[blk0 + j + 1], a1);
+                        a0 = fmaf(__ldg(a + (size_t)j * N), hpl[blk0 + j], a0);
+                        if (j + 1 < bsz) a1 = fmaf(__ldg(a + (size_t)(j + 1) * N), hpl[blk0 + j + 1], a1);
                     }
                 }
                 h += a0 + a1;
@@ -380,6 +473,7 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
 #pragma unroll
             for (int off = 1; off < TPR; off <<= 1) h += __shfl_xor_sync(kFull, h, off);
             if (sub == 0) state_out[((size_t)s * L + l) * N + row] = h;
+            if (vsm && l + 1 < L) stage_vt(m.layer[l + 1].vt);   // the next layer's V', while this one finishes
             if (experts != nullptr && t == 0) experts[(size_t)s * L + l] = r;
             if (stats != nullptr) {   // group maxima of |h|, a warp's share of each group of 16 coordinates at a time
                 float a = fabsf(h);
@@ -463,7 +557,20 @@ size_t align_floats(size_t x) { return (x + 63) / 64 * 64; }   // 256-byte align
 template <int N, int RP, int TPR>
 cudaError_t launch_t(const FModel &dm, int B, const int32_t *tok, const float *sin, float *sout, float *lg, int32_t *ex,
                      int *bad, unsigned *stats, int grid, cudaStream_t st) {
-    fstep_kernel<N, RP, TPR><<<grid, N * TPR, 0, st>>>(dm, B, tok, sin, sout, lg, ex, bad, stats);
+    // the small-batch instances stage V' in dynamic shared memory (the kernel's vsm)
+    const size_t dyn = TPR > 1 && dm.R2 > 0 && N * dm.R2 <= kVtSmem ? (size_t)N * dm.R2 * sizeof(float) : 0;
+    if (dyn > 0) {
+        static bool opted[64] = {};   // per device: the opt-in above the default 48 KB
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (dev < 0 || dev >= 64 || !opted[dev]) {
+            const cudaError_t e = cudaFuncSetAttribute(fstep_kernel<N, RP, TPR>,
+                                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kVtSmem * 4);
+            if (e != cudaSuccess) return e;
+            if (dev >= 0 && dev < 64) opted[dev] = true;
+        }
+    }
+    fstep_kernel<N, RP, TPR><<<grid, N * TPR, dyn, st>>>(dm, B, tok, sin, sout, lg, ex, bad, stats);
     return cudaGetLastError();
 }
 
@@ -518,7 +625,7 @@ int ygg_fload(const ygg_fshape_t *sh, const float *const *arrays, int device, yg
         blob.resize(off + align_floats(count), 0.0f);
         return off;
     };
-    struct Off { size_t table, at, pt, qt, embed, w, bias, vt, ut; bool has_at, has_v; };
+    struct Off { size_t table, at, pt, qt, embed, w, bias, wb, vt, ut; bool has_at, has_v; };
     std::vector<Off> offs(L);
     for (int l = 0; l < L; l++) {
         const float *const *a = arrays + (size_t)l * YGG_F_ARRAYS_PER_LAYER;
@@ -550,6 +657,26 @@ int ygg_fload(const ygg_fshape_t *sh, const float *const *arrays, int device, yg
             memcpy(blob.data() + o.w, a[5], (size_t)(E - 1) * FIN * sizeof(float));
             o.bias = take(E - 1);
             memcpy(blob.data() + o.bias, a[6], (size_t)(E - 1) * sizeof(float));
+            size_t wbn = 0;   // the round-blocked copy of the rows (FLayer::wb)
+            for (int d0 = 0; d0 < D; d0 += kLook) wbn += ((size_t)FIN << d0) << std::min(kLook, D - d0);
+            o.wb = take(wbn);
+            size_t woff = o.wb;
+            for (int d0 = 0; d0 < D; d0 += kLook) {
+                const int lv = std::min(kLook, D - d0), P = 1 << lv;
+                for (size_t mi = 0; mi < ((size_t)1 << d0); mi++) {
+                    const size_t root = ((size_t)1 << d0) - 1 + mi;
+                    for (int k = 0; k < P - 1; k++) {
+                        int lvl = 0;
+                        while ((2 << lvl) - 1 <= k) lvl++;   // the level of local row k: 2^lvl - 1 <= k < 2^(lvl+1) - 1
+                        const size_t nd = (root << lvl) + k;
+                        const size_t blk = woff + (size_t)mi * FIN * P;
+                        for (int f = 0; f < FIN; f++)
+                            blob[P >= 4 ? blk + ((size_t)(k / 4) * FIN + f) * 4 + k % 4 : blk + (size_t)f * 2 + k] =
+                                a[5][nd * FIN + f];
+                    }
+                }
+                woff += ((size_t)FIN << d0) * P;
+            }
             o.has_v = R2 > 0;
             if (o.has_v) {
                 o.vt = take((size_t)n * R2);   // (R2, n) -> (n, R2)
@@ -605,6 +732,7 @@ int ygg_fload(const ygg_fshape_t *sh, const float *const *arrays, int device, yg
             y.embed = d + o.embed;
             y.w = d + o.w;
             y.bias = d + o.bias;
+            y.wb = d + o.wb;
             y.vt = o.has_v ? d + o.vt : nullptr;
             y.ut = o.has_v ? d + o.ut : nullptr;
         }
@@ -654,7 +782,7 @@ int ygg_fstatus(const ygg_fmodel *m, void *stream, int *status_out) {
     if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
     if (prev >= 0 && prev != m->device) cudaSetDevice(prev);
     if (e != cudaSuccess) return YGG_E_CUDA;
-    *status_out = v ? YGG_E_TOKEN : YGG_OK;
+    *status_out = (v & 2) ? YGG_E_TIMEOUT : v ? YGG_E_TOKEN : YGG_OK;
     return YGG_OK;
 }
 

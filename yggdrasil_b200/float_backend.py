@@ -143,13 +143,16 @@ class B200FloatYggdrasil:
         return torch.as_tensor(np.ascontiguousarray(a, np.int32)).to(self.device)
 
     def status(self):
-        """Raise ValueError if a step since the last call met a device token out of range."""
+        """Raise ValueError if a step since the last call met a device token out of range, RuntimeError if one of its
+        bounded waits for an asynchronous copy gave up (its results are still exact)."""
         torch = _torch()
         out = ctypes.c_int(0)
         stream = torch.cuda.current_stream(self.device).cuda_stream
         check(lib().ygg_fstatus(self._h, ctypes.c_void_p(stream), ctypes.byref(out)), "ygg_fstatus")
         if out.value == _native.YGG_E_TOKEN:
             raise ValueError("a device token was out of range (those streams were skipped)")
+        if out.value == _native.YGG_E_TIMEOUT:
+            raise RuntimeError("a step's bounded wait for an asynchronous copy gave up (it read global memory instead)")
 
     def step_into(self, tokens, state_in, state_out, logits, experts=None):
         """One step into caller buffers (state_out may be state_in). tokens: an int32 device tensor."""
