@@ -169,14 +169,17 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
                                                         int32_t *__restrict__ experts, int *__restrict__ bad,
                                                         unsigned *__restrict__ stats) {
     constexpr int NT = N * TPR, NW = NT / 32;
-    constexpr int GL = 16 * TPR < 32 ? 16 * TPR : 32;   // lanes of one warp that hold one group of 16 coordinates
+    static_assert(TPR == 1 || TPR == 4, "the parts of a coordinate's sums are added as four");
     __shared__ float hp[TPR == 1 ? N : 1], below[N], vv[N], vpart[NT], emb[N], red[NW * 32], sums[32], bsh[2][16];
     __shared__ float zs[kMaxLayers][32];
     __shared__ int nodesh;
     __shared__ float hs[TPR > 1 ? kMaxLayers * N : 1];   // small batches: the stream's state of every layer, read at once
     extern __shared__ __align__(16) float vts[];          // V' of the next routed layer, when staged (vsm)
     __shared__ __align__(8) uint64_t vbar;                 // its copy's mbarrier
-    const int t = threadIdx.x, row = t / TPR, sub = t % TPR;
+    // thread t: coordinate row, part sub of its sums; with TPR > 1 the parts are quarters of the block (a warp holds 32
+    // consecutive coordinates of one part, so that its loads of an expert row are one line), added in shared memory
+    const int t = threadIdx.x, row = TPR > 1 ? t % N : t, sub = TPR > 1 ? t / N : 0;
+    __shared__ float xq[TPR > 1 ? TPR * N : 1];   // the TPR parts of a sum per coordinate
     const int L = m.L, V = m.V, C = m.C, R = m.R, R2 = m.R2, F = m.F, FIN = m.FIN, bsz = m.b;
     const int SW = N / 16 + 1 + R;
     if constexpr (TPR > 1) {   // a batch of a few streams, each step a chain of dependent loads: the arrays every
@@ -189,7 +192,9 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
             const unsigned g = (H > 0 ? blockIdx.x - B : blockIdx.x) * NT + t, G = (H > 0 ? H : gridDim.x) * NT;
             for (int l = 1; l < L; l++) {
                 const FLayer &y = m.layer[l];
-                prefetch_spread(y.w, ((size_t(1) << m.D) - 1) * FIN, g, G);
+                size_t wbn = 0;   // the round-blocked router rows, which the small-batch router reads
+                for (int d0 = 0; d0 < m.D; d0 += kLook) wbn += ((size_t)FIN << d0) << min(kLook, m.D - d0);
+                prefetch_spread(y.wb, wbn, g, G);
                 if (y.vt != nullptr) prefetch_spread(y.vt, (size_t)N * R2, g, G);
             }
             for (int l = 0; l < L; l++) prefetch_spread(m.layer[l].qt, (size_t)R * C, g, G);
@@ -339,7 +344,9 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
                             named_sync(1, RW * 32);
                             float a = 0.0f;   // lane k < nrows: row k over the warps, and its bias
                             if (lane < nrows) {
-                                for (int w = 0; w < RW; w++) a += rd[w * 16 + lane];
+#pragma unroll
+                                for (int w = 0; w < 16; w++)   // RW <= 16 (F + n <= 2 n <= 512)
+                                    if (w < RW) a += rd[w * 16 + lane];
                                 a += bsh[par][lane];
                             }
                             int rr = 0;
@@ -470,16 +477,19 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
                 }
                 h += a0 + a1;
             }
-#pragma unroll
-            for (int off = 1; off < TPR; off <<= 1) h += __shfl_xor_sync(kFull, h, off);
+            if constexpr (TPR > 1) {   // the parts of h, in a fixed order (every part's thread gets the same h)
+                xq[sub * N + row] = h;
+                __syncthreads();
+                h = (xq[row] + xq[N + row]) + (xq[2 * N + row] + xq[3 * N + row]);
+            }
             if (sub == 0) state_out[((size_t)s * L + l) * N + row] = h;
             if (vsm && l + 1 < L) stage_vt(m.layer[l + 1].vt);   // the next layer's V', while this one finishes
             if (experts != nullptr && t == 0) experts[(size_t)s * L + l] = r;
             if (stats != nullptr) {   // group maxima of |h|, a warp's share of each group of 16 coordinates at a time
                 float a = fabsf(h);
 #pragma unroll
-                for (int off = TPR; off < GL; off <<= 1) a = fmaxf(a, __shfl_xor_sync(kFull, a, off));
-                if ((t & (GL - 1)) == 0) max_into(stats + (size_t)l * SW + row / 16, a);
+                for (int off = 1; off < 16; off <<= 1) a = fmaxf(a, __shfl_xor_sync(kFull, a, off));
+                if (sub == 0 && (t & 15) == 0) max_into(stats + (size_t)l * SW + row / 16, a);
             }
             // readout z = P_r h (thread sub takes the rows k = sub mod TPR), and sum h^2 for rms(h)
             {
@@ -508,9 +518,11 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
             __syncthreads();   // below, zs
         }
         if (head_in_layers) {   // logits = output_bias + the TPR threads' sums of class row
-#pragma unroll
-            for (int off = 1; off < TPR; off <<= 1) lgp += __shfl_xor_sync(kFull, lgp, off);
-            if (row < C && sub == 0) logits[(size_t)s * C + row] = __ldg(m.out_bias + row) + lgp;
+            xq[sub * N + row] = lgp;   // (the last use of xq, h's parts, was before the readout's barriers)
+            __syncthreads();
+            if (row < C && sub == 0)
+                logits[(size_t)s * C + row] =
+                    __ldg(m.out_bias + row) + ((xq[row] + xq[N + row]) + (xq[2 * N + row] + xq[3 * N + row]));
         }
         // logits = output_bias + sum_l z_l Q_l^T: TPR threads per class, thread sub taking the layers l = sub mod TPR
         // (a layer's R unembedding loads issued together), then added over the TPR threads
@@ -528,9 +540,16 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
                         if (k < R) lg = fmaf(zs[l][k], qv[k], lg);
                 }
             }
-#pragma unroll
-            for (int off = 1; off < TPR; off <<= 1) lg += __shfl_xor_sync(kFull, lg, off);
-            if (c < C && sub == 0) logits[(size_t)s * C + c] = __ldg(m.out_bias + c) + lg;
+            if constexpr (TPR > 1) {
+                xq[sub * N + row] = lg;
+                __syncthreads();
+                if (c < C && sub == 0)
+                    logits[(size_t)s * C + c] =
+                        __ldg(m.out_bias + c) + ((xq[row] + xq[N + row]) + (xq[2 * N + row] + xq[3 * N + row]));
+                __syncthreads();   // xq before the next classes
+            } else {
+                if (c < C) logits[(size_t)s * C + c] = __ldg(m.out_bias + c) + lg;
+            }
         }
         __syncthreads();   // zs, hp before the next stream
     }
