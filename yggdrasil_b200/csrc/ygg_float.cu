@@ -399,11 +399,24 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
                 }
                 }
                 r = node - ((1 << m.D) - 1);
-                // the chosen expert's arrays towards L2 while the layer input is finished (one thread each)
-                if (t == 0) prefetch_l2(y.table + ((size_t)r * V + x) * N, N * 4u);
-                if (t == 32 && y.ut != nullptr) prefetch_l2(y.ut + (size_t)r * R2 * N, (uint32_t)R2 * N * 4u);
-                if (t == 64 % NT && y.at != nullptr) prefetch_l2(y.at + (size_t)r * bsz * N, (uint32_t)bsz * N * 4u);
-                if (t == 96 % NT) prefetch_l2(y.pt + (size_t)r * R * N, (uint32_t)R * N * 4u);
+                // the chosen expert's arrays towards L2 while the layer input is finished: at small batches one
+                // 128-byte line per thread (the requests leave at once, over the whole block), else one bulk
+                // prefetch per array
+                if constexpr (TPR > 1) {
+                    const int lt = N / 32, lu = y.ut != nullptr ? R2 * N / 32 : 0, la = y.at != nullptr ? bsz * N / 32 : 0;
+                    for (int i = t; i < lt + lu + la + R * N / 32; i += NT) {
+                        const float *a = i < lt ? y.table + ((size_t)r * V + x) * N + 32 * i
+                                       : i < lt + lu ? y.ut + (size_t)r * R2 * N + 32 * (i - lt)
+                                       : i < lt + lu + la ? y.at + (size_t)r * bsz * N + 32 * (i - lt - lu)
+                                       : y.pt + (size_t)r * R * N + 32 * (i - lt - lu - la);
+                        asm volatile("prefetch.global.L2 [%0];" ::"l"(a));
+                    }
+                } else {
+                    if (t == 0) prefetch_l2(y.table + ((size_t)r * V + x) * N, N * 4u);
+                    if (t == 32 && y.ut != nullptr) prefetch_l2(y.ut + (size_t)r * R2 * N, (uint32_t)R2 * N * 4u);
+                    if (t == 64 % NT && y.at != nullptr) prefetch_l2(y.at + (size_t)r * bsz * N, (uint32_t)bsz * N * 4u);
+                    if (t == 96 % NT) prefetch_l2(y.pt + (size_t)r * R * N, (uint32_t)R * N * 4u);
+                }
                 if (y.vt != nullptr && t < R2) {
                     float a = 0.0f;
                     for (int q = 0; q < NP; q++) a += vpart[q * R2 + t];
