@@ -33,6 +33,14 @@ def _torch():
     return torch
 
 
+def _raw_stream(index: int) -> int:
+    """The current CUDA stream of device `index` as a raw pointer (torch's own accessor, which step() calls once per
+    token; torch.cuda.current_stream builds a Stream object around the same pointer)."""
+    torch = _torch()
+    get = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    return get(index) if get is not None else torch.cuda.current_stream(index).cuda_stream
+
+
 class Yggdrasil:
     """Backend dispatch of the reference's ``Yggdrasil.load`` (yggdrasil/inference.py:158-169)."""
 
@@ -90,6 +98,7 @@ class B200Yggdrasil:
         self.layers, self.n, self.vocab = info.n_layers, info.d_state, info.vocab
         self.classes, self.depth = info.vocab, info.router_depth
         self.cuda_graph, self._graphs = cuda_graph, {}
+        self._dix, self._state_shape = self.device.index, (self.layers, self.n)
 
     def __del__(self):
         h = getattr(self, "_h", None)
@@ -148,7 +157,7 @@ class B200Yggdrasil:
         """One step into caller buffers (state_out may be state_in: in place). tokens: an int32 device tensor."""
         torch = _torch()
         b = tokens.shape[0]
-        stream = torch.cuda.current_stream(self.device).cuda_stream
+        stream = _raw_stream(self._dix)
         if routes is None and acc is None:
             # pointers as plain ints (the bound argtypes convert them): the per-token path of step()
             code = lib().ygg_step(self._h, b, tokens.data_ptr(), state_in.data_ptr(), state_out.data_ptr(),
@@ -162,17 +171,20 @@ class B200Yggdrasil:
     def _step(self, x, h):
         torch = _torch()
         out = torch.empty_like(h)
-        logits = torch.empty((x.shape[0], self.vocab), dtype=torch.float32, device=self.device)
-        self.step_into(x, h, out, logits)
+        logits = torch.empty((x.shape[0], self.vocab), dtype=torch.float32, device=h.device)
+        code = lib().ygg_step(self._h, x.shape[0], x.data_ptr(), h.data_ptr(), out.data_ptr(), logits.data_ptr(),
+                              _raw_stream(self._dix))
+        if code:
+            check(code, "ygg_step")
         return logits, out
 
     def step(self, tokens, state):
         """One token per stream: tokens (B,) -> logits (B, classes) of the next token, and the new state."""
         torch = _torch()
-        if not self.cuda_graph and type(tokens) is torch.Tensor and tokens.is_cuda and tokens.dtype == torch.int32 \
-                and tokens.device == self.device and tokens.is_contiguous() and type(state) is torch.Tensor \
-                and state.dtype == torch.int8 and state.device == self.device and state.is_contiguous() \
-                and state.shape == (tokens.shape[0], self.layers, self.n):
+        if not self.cuda_graph and type(tokens) is torch.Tensor and type(state) is torch.Tensor \
+                and tokens.dtype is torch.int32 and state.dtype is torch.int8 and tokens.get_device() == self._dix \
+                and state.get_device() == self._dix and tokens.dim() == 1 and tokens.is_contiguous() \
+                and state.is_contiguous() and state.shape[0] == tokens.shape[0] and state.shape[1:] == self._state_shape:
             return self._step(tokens, state)   # device tokens and state as they are: no device switch, no copies
         with torch.cuda.device(self.device):
             x = self._tokens(tokens)
