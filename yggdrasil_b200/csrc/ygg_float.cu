@@ -173,6 +173,7 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
     __shared__ float hp[TPR == 1 ? N : 1], below[N], vv[N], vpart[NT], emb[N], red[NW * 32], sums[32], bsh[2][16];
     __shared__ float zs[kMaxLayers][32];
     __shared__ int nodesh;
+    __shared__ float rmsq;   // small batches: sum of h^2 of the layer
     __shared__ float hs[TPR > 1 ? kMaxLayers * N : 1];   // small batches: the stream's state of every layer, read at once
     extern __shared__ __align__(16) float vts[];          // V' of the next routed layer, when staged (vsm)
     __shared__ __align__(8) uint64_t vbar;                 // its copy's mbarrier
@@ -505,7 +506,49 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
                 if (sub == 0 && (t & 15) == 0) max_into(stats + (size_t)l * SW + row / 16, a);
             }
             // readout z = P_r h (thread sub takes the rows k = sub mod TPR), and sum h^2 for rms(h)
-            {
+            if constexpr (TPR > 1) {
+                // a warp holds one part sub (rows k = 4 j + sub): it reduce-scatters its KQ sums into red, its h^2 too
+                // when sub = 0; after one barrier warp 0 adds the NWS warps of each part and the h^2 sums (fixed
+                // orders), and after a second every thread has z and rms(h)
+                constexpr int KQ = RP / TPR > 1 ? RP / TPR : 2, NWS = N / 32, LKQ = Log2<KQ>::value;
+                const int lane = t & 31, warp = t >> 5;
+                float pq[KQ];
+#pragma unroll
+                for (int j = 0; j < KQ; j++) pq[j] = j < RP / TPR ? pv[j] * h : 0.0f;
+                const float rsum = reduce_scatter<KQ>(pq, lane);   // lane l: this warp's sum of pq[l >> (5 - LKQ)]
+                if ((lane & ((32 >> LKQ) - 1)) == 0) red[warp * KQ + (lane >> (5 - LKQ))] = rsum;
+                if (sub == 0) {
+                    float q = h * h;
+#pragma unroll
+                    for (int off = 16; off > 0; off >>= 1) q += __shfl_xor_sync(kFull, q, off);
+                    if (lane == 0) red[NW * KQ + warp] = q;
+                }
+                __syncthreads();
+                if (t < 32) {
+                    float z = 0.0f;
+                    if (lane < R) {
+                        const int ks = lane % TPR, kj = lane / TPR;
+#pragma unroll
+                        for (int w = 0; w < NWS; w++) z += red[(ks * NWS + w) * KQ + kj];
+                        sums[lane] = z;
+                        zs[l][lane] = z;
+                        if (stats != nullptr) max_into(stats + (size_t)l * SW + N / 16 + 1 + lane, z);
+                    }
+                    if (lane == 0) {
+                        float q = 0.0f;
+#pragma unroll
+                        for (int w = 0; w < NWS; w++) q += red[NW * KQ + w];
+                        rmsq = q;
+                    }
+                }
+                __syncthreads();
+                if (head_in_layers) {
+#pragma unroll
+                    for (int j = 0; j < RP / TPR; j++)
+                        if (j * TPR + sub < R) lgp = fmaf(sums[j * TPR + sub], qv[j], lgp);
+                }
+                if (sub == 0) below[row] = h * rsqrtf(rmsq / (float)N + kRmsEps);
+            } else {
                 float part[RP];
 #pragma unroll
                 for (int k = 0; k < RP; k++) {
@@ -516,13 +559,6 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
                 if (t < R) {
                     zs[l][t] = sums[t];
                     if (stats != nullptr) max_into(stats + (size_t)l * SW + N / 16 + 1 + t, sums[t]);
-                }
-                if constexpr (TPR > 1) {
-                    if (head_in_layers) {
-#pragma unroll
-                        for (int j = 0; j < RP / TPR; j++)
-                            if (j * TPR + sub < R) lgp = fmaf(sums[j * TPR + sub], qv[j], lgp);
-                    }
                 }
                 float sq[1] = {sub == 0 ? h * h : 0.0f};
                 block_sum<1, NW>(sq, red, sums, t);
