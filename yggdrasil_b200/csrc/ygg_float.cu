@@ -241,8 +241,10 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
                 if (t < F) emb[t] = __ldg(y.embed + (size_t)x * F + t);
                 // layer input v = V' rms(h_below): the n inputs split into NP parts, thread (part, k) sums its part of
                 // row k, then thread k adds the parts. With TPR > 1 and V' in shared memory, the threads past the
-                // routing warps' do it while those route (vsplit); otherwise every thread, before the router, a part
-                // of at most kVW inputs having its V' values loaded before the barrier that publishes rms(h_below).
+                // routing warps' do it while those route and add the parts among themselves (vsplit); otherwise every
+                // thread, before the router, a part of at most kVW inputs having its V' values loaded before the
+                // barrier that publishes rms(h_below) (when V' is not staged at all).
+                const bool vstaged = vsm;   // block-uniform: V' was to be in shared memory for this layer
                 if constexpr (TPR > 1) {
                     if (vsm) {
                         if (!wait_phase(&vbar, vphase)) {   // V' did not land: report, and read it from global memory
@@ -253,22 +255,28 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
                     }
                 }
                 const int RWT = TPR > 1 ? (FIN + 31) / 32 * 32 : 0;   // the routing threads
+                constexpr int kVW = TPR > 1 ? 16 : 1;
+                float vw[kVW];
+                int NP = R2 > 0 ? max(1, NT / R2) : 1, span = (N + NP - 1) / NP;   // the unsplit parts
+                if constexpr (TPR > 1) {
+                    if (!vstaged) {
+                        const int k0 = R2 > 0 ? t % R2 : 0, j0 = (t / max(R2, 1)) * span, j1 = min(N, j0 + span);
+                        const bool on = y.vt != nullptr && t < NP * R2 && span <= kVW;
+#pragma unroll
+                        for (int j = 0; j < kVW; j++)
+                            vw[j] = on && j0 + j < j1 ? __ldg(y.vt + (size_t)(j0 + j) * R2 + k0) : 0.0f;
+                    }
+                }
+                // hs, emb, V'; below was written before the last barrier of the layer below. The vote makes the
+                // outcome of the V' wait the block's, so that the split and its barrier below are uniform.
+                if constexpr (TPR > 1) vsm = __syncthreads_and(vsm);
+                else __syncthreads();
                 const bool vsplit = vsm && R2 <= NT - RWT;
                 const int vb = vsplit ? RWT : 0, vi = t - vb;
-                const int NP = R2 > 0 ? max(1, (NT - vb) / R2) : 1, span = (N + NP - 1) / NP;
+                if (vsplit) { NP = max(1, (NT - vb) / R2); span = (N + NP - 1) / NP; }
                 const bool vpart_on = y.vt != nullptr && vi >= 0 && vi < NP * R2;
                 const int k = R2 > 0 && vi >= 0 ? vi % R2 : 0, i0 = (vi >= 0 ? vi / max(R2, 1) : 0) * span,
                           i1 = min(N, i0 + span);
-                constexpr int kVW = TPR > 1 ? 16 : 1;
-                float vw[kVW];
-                if constexpr (TPR > 1) {
-                    if (!vsm) {
-#pragma unroll
-                        for (int j = 0; j < kVW; j++)
-                            vw[j] = vpart_on && span <= kVW && i0 + j < i1 ? __ldg(y.vt + (size_t)(i0 + j) * R2 + k) : 0.0f;
-                    }
-                }
-                __syncthreads();   // hs, emb, V'; below was written before the last barrier of the layer below
                 auto layer_input_part = [&]() {
                     float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
                     if (vsm) {
@@ -281,7 +289,7 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
                             a3 = fmaf(vts[(i + 3) * R2 + k], below[i + 3], a3);
                         }
                         for (; i < i1; i++) a0 = fmaf(vts[i * R2 + k], below[i], a0);
-                    } else if (TPR > 1 && span <= kVW) {
+                    } else if (TPR > 1 && !vstaged && span <= kVW) {
 #pragma unroll
                         for (int j = 0; j < kVW; j += 4) {
                             if (i0 + j < i1) a0 = fmaf(vw[j], below[i0 + j], a0);
@@ -356,10 +364,16 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
                             woff += ((size_t)FIN << d0) * P;
                         }
                         if (t == 0) nodesh = node;
-                    } else if (vpart_on && vsplit) {
-                        layer_input_part();
+                    } else if (vsplit) {   // the other warps: the layer input's parts, then their sum
+                        if (vpart_on) layer_input_part();
+                        named_sync(2, NT - RWT);
+                        if (vi < R2) {
+                            float a = 0.0f;
+                            for (int q = 0; q < NP; q++) a += vpart[q * R2 + vi];
+                            vv[vi] = a;
+                        }
                     }
-                    __syncthreads();   // the node; vpart (V' in shared memory is read no more in this layer)
+                    __syncthreads();   // the node; v (V' in shared memory is read no more in this layer)
                     node = nodesh;
                 } else {
                 for (int d0 = 0; d0 < m.D; d0 += kLook) {
@@ -418,12 +432,14 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
                     if (t == 64 % NT && y.at != nullptr) prefetch_l2(y.at + (size_t)r * bsz * N, (uint32_t)bsz * N * 4u);
                     if (t == 96 % NT) prefetch_l2(y.pt + (size_t)r * R * N, (uint32_t)R * N * 4u);
                 }
-                if (y.vt != nullptr && t < R2) {
-                    float a = 0.0f;
-                    for (int q = 0; q < NP; q++) a += vpart[q * R2 + t];
-                    vv[t] = a;
+                if (!vsplit) {
+                    if (y.vt != nullptr && t < R2) {
+                        float a = 0.0f;
+                        for (int q = 0; q < NP; q++) a += vpart[q * R2 + t];
+                        vv[t] = a;
+                    }
+                    __syncthreads();   // vv
                 }
-                __syncthreads();   // vv
                 if (stats != nullptr && y.vt != nullptr) {
                     float a = t < R2 ? fabsf(vv[t]) : 0.0f;
 #pragma unroll
