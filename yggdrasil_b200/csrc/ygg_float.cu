@@ -175,6 +175,7 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
     __shared__ int nodesh;
     __shared__ float rmsq;   // small batches: sum of h^2 of the layer
     __shared__ float hs[TPR > 1 ? kMaxLayers * N : 1];   // small batches: the stream's state of every layer, read at once
+    __shared__ float es[TPR > 1 ? kMaxLayers * 32 : 1];  // and the token's router embedding of every layer (F <= 32)
     extern __shared__ __align__(16) float vts[];          // V' of the next routed layer, when staged (vsm)
     __shared__ __align__(8) uint64_t vbar;                 // its copy's mbarrier
     // thread t: coordinate row, part sub of its sums; with TPR > 1 the parts are quarters of the block (a warp holds 32
@@ -231,6 +232,9 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
         float lgp = 0.0f;
         if constexpr (TPR > 1) {   // the stream's state in, every layer's at once (published by layer 0's barrier)
             for (int i = t; i < L * N; i += NT) hs[i] = state_in[(size_t)s * L * N + i];
+            if (F <= 32)
+                for (int i = t; i < (L - 1) * 32; i += NT)
+                    if (i % 32 < F) es[i] = __ldg(m.layer[1 + i / 32].embed + (size_t)x * F + i % 32);
         }
         for (int l = 0; l < L; l++) {
             const FLayer &y = m.layer[l];
@@ -238,7 +242,7 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
             const float *hpl = TPR > 1 ? hs + l * N : hp;   // h of this layer before the step
             int r = x;
             if (l > 0) {
-                if (t < F) emb[t] = __ldg(y.embed + (size_t)x * F + t);
+                if (t < F) emb[t] = TPR > 1 && F <= 32 ? es[(l - 1) * 32 + t] : __ldg(y.embed + (size_t)x * F + t);
                 // layer input v = V' rms(h_below): the n inputs split into NP parts, thread (part, k) sums its part of
                 // row k, then thread k adds the parts. With TPR > 1 and V' in shared memory, the threads past the
                 // routing warps' do it while those route and add the parts among themselves (vsplit); otherwise every
@@ -358,8 +362,9 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
                                     if (w < RW) a += rd[w * 16 + lane];
                                 a += bsh[par][lane];
                             }
+                            const unsigned dec = __ballot_sync(kFull, lane < nrows && a > 0.0f);   // bit k: row k right
                             int rr = 0;
-                            for (int j = 0; j < lv; j++) rr = 2 * rr + 1 + (__shfl_sync(kFull, a, rr) > 0.0f ? 1 : 0);
+                            for (int j = 0; j < lv; j++) rr = 2 * rr + 1 + (int)((dec >> rr) & 1u);
                             node = node * (1 << lv) + rr;
                             woff += ((size_t)FIN << d0) * P;
                         }
