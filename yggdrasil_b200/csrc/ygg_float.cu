@@ -3,8 +3,9 @@
 // :187-194), as the backend "b200f".
 //
 // One block serves one stream at a time (grid-stride over the streams): n threads, thread t owning state coordinate t
-// of every layer, for large batches; 4 n threads, 4 per coordinate each taking every fourth term of its sums, for a
-// batch of at most two streams per SM, where a step's time is its chain of dependent loads. Per layer:
+// of every layer, for large batches; 4 n threads for a batch of at most two streams per SM, where a step's time is
+// its chain of dependent loads: four quarter-blocks, quarter s taking the terms s mod 4 of every coordinate's sums
+// (a warp then holds 32 consecutive coordinates, so its expert loads are whole lines). Per layer:
 //   1. the router (routed layers): f = [router_embed(x); rms(h_below)], node j goes right iff f . W_j + b_j > 0,
 //      descended kLook = 4 levels per round: the 15 rows of the subtree under the current node are loaded together
 //      (every load issued before any is used, so a round costs one memory latency), thread t multiplying feature t of
@@ -16,10 +17,10 @@
 //      while the others route), an L2 prefetch of the chosen expert's arrays, then h_t = T_r[x][t] + sum_k U'_r[t][k]
 //      v_k + sum_j A_r[t][j] h_prev[block(t) + j] (inference.py:55-63); every expert array is stored transposed so
 //      that each of these loads is coalesced over the block's threads;
-//   3. the readout z = P_r h (one block reduction of the R partial products, a reduce-scatter within each warp) and
-//      rms(h) for the layer above.
+//   3. the readout z = P_r h (a reduce-scatter within each warp, then the warps' sums added; at small batches per
+//      quarter-block, with the sum of h^2, behind two barriers) and rms(h) for the layer above.
 // At small batches, helper blocks past the streams' prefetch the arrays every stream reads (router rows, V', Q) into
-// L2 at the start of the launch, and a stream's state of every layer is read at once.
+// L2 at the start of the launch, and a stream's state and router embeddings of every layer are read at once.
 // The logits are output_bias + sum_l z_l Q_l^T: at small batches added at each layer's readout, else after the last
 // layer, one class per thread. Everything is fp32 with fused multiply-adds; the reference's own fp32 sums run in
 // other orders, so parity is a tolerance (the reference's own: log-probabilities within 1e-4,
