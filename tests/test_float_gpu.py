@@ -81,6 +81,39 @@ def test_float_step_matches_oracle_on_many_streams(rec, tmp_path, torch):
     np.testing.assert_allclose(model.score(x[:64, :8], state=h), om.score(x[:64, :8], st[:64]), rtol=BITS_RTOL)
 
 
+SMALL_BATCH_SHAPES = [
+    dict(vocab=256, n=256, block=16, depth=3, readout=32, layer_input=128, input_rank=64, router_token=16, routed=2),
+    dict(vocab=200, n=128, block=16, depth=9, readout=16, layer_input=32, input_rank=32, router_token=16, routed=2),
+    dict(vocab=40, n=64, block=8, depth=7, readout=8, layer_input=16, input_rank=16, router_token=8, routed=3),
+]
+
+
+@pytest.mark.parametrize("shape", SMALL_BATCH_SHAPES, ids=["n256-R2128-D3", "n128-V200-D9", "n64-D7"])
+def test_float_small_batch_branches_match_oracle(shape, torch):
+    """The small-batch step (at most two streams per SM, four threads per coordinate) on random float models whose
+    shapes take its other branches: V' too large to stage in shared memory (n 256, R2 128) with the layer input
+    summed before the router, a single router round (depth 3), more classes than coordinates (the head after the last
+    layer), a last round of one level (depth 9) and of three (depth 7). Six streams, 12 steps, each from the oracle's
+    state, against the float64 oracle with the reference's tolerances."""
+    from yggdrasil_b200 import synth
+    from yggdrasil_b200.float_backend import B200FloatYggdrasil
+    layers, ob = synth.random_float_layers(shape, seed=11)
+    model, om = B200FloatYggdrasil(layers, ob), FloatOracle(layers, ob)
+    x = np.random.default_rng(3).integers(0, model.vocab, (6, 12))
+    st = om.init_state(6)
+    off = total = mism = 0
+    for t in range(x.shape[1]):
+        lg, new, ex = model.step_experts(x[:, t], torch.as_tensor(st, dtype=torch.float32, device=model.device))
+        olg, ost, oex = om.step(x[:, t], st)
+        mism += int((ex.cpu().numpy() != oex).sum())
+        d = np.abs(log_softmax(lg.cpu().numpy()) - log_softmax(olg)).max(-1)
+        off, total = off + int((d > ATOL).sum()), total + len(d)
+        np.testing.assert_allclose(new.cpu().numpy(), ost, rtol=1e-4, atol=1e-5 * np.abs(ost).max())
+        st = ost
+    assert off <= FLIPS * total and mism <= FLIPS * total * model.layers, (off, mism, total)
+    model.status()
+
+
 def test_float_cuda_graph_and_in_place(tmp_path, torch):
     """The CUDA-graph step equals the plain step exactly; an in-place step_into equals a step."""
     npz = tmp_path / "ck.npz"
