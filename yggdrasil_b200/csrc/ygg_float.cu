@@ -247,9 +247,7 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
                 // layer input v = V' rms(h_below): the n inputs split into NP parts, thread (part, k) sums its part of
                 // row k, then thread k adds the parts. With TPR > 1 and V' in shared memory, the threads past the
                 // routing warps' do it while those route and add the parts among themselves (vsplit); otherwise every
-                // thread, before the router, a part of at most kVW inputs having its V' values loaded before the
-                // barrier that publishes rms(h_below) (when V' is not staged at all).
-                const bool vstaged = vsm;   // block-uniform: V' was to be in shared memory for this layer
+                // thread does, before the router, reading V' from global memory.
                 if constexpr (TPR > 1) {
                     if (vsm) {
                         if (!wait_phase(&vbar, vphase)) {   // V' did not land: report, and read it from global memory
@@ -260,18 +258,7 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
                     }
                 }
                 const int RWT = TPR > 1 ? (FIN + 31) / 32 * 32 : 0;   // the routing threads
-                constexpr int kVW = TPR > 1 ? 16 : 1;
-                float vw[kVW];
                 int NP = R2 > 0 ? max(1, NT / R2) : 1, span = (N + NP - 1) / NP;   // the unsplit parts
-                if constexpr (TPR > 1) {
-                    if (!vstaged) {
-                        const int k0 = R2 > 0 ? t % R2 : 0, j0 = (t / max(R2, 1)) * span, j1 = min(N, j0 + span);
-                        const bool on = y.vt != nullptr && t < NP * R2 && span <= kVW;
-#pragma unroll
-                        for (int j = 0; j < kVW; j++)
-                            vw[j] = on && j0 + j < j1 ? __ldg(y.vt + (size_t)(j0 + j) * R2 + k0) : 0.0f;
-                    }
-                }
                 // hs, emb, V'; below was written before the last barrier of the layer below. The vote makes the
                 // outcome of the V' wait the block's, so that the split and its barrier below are uniform.
                 if constexpr (TPR > 1) vsm = __syncthreads_and(vsm);
@@ -294,14 +281,6 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
                             a3 = fmaf(vts[(i + 3) * R2 + k], below[i + 3], a3);
                         }
                         for (; i < i1; i++) a0 = fmaf(vts[i * R2 + k], below[i], a0);
-                    } else if (TPR > 1 && !vstaged && span <= kVW) {
-#pragma unroll
-                        for (int j = 0; j < kVW; j += 4) {
-                            if (i0 + j < i1) a0 = fmaf(vw[j], below[i0 + j], a0);
-                            if (i0 + j + 1 < i1) a1 = fmaf(vw[j + 1], below[i0 + j + 1], a1);
-                            if (i0 + j + 2 < i1) a2 = fmaf(vw[j + 2], below[i0 + j + 2], a2);
-                            if (i0 + j + 3 < i1) a3 = fmaf(vw[j + 3], below[i0 + j + 3], a3);
-                        }
                     } else {
                         int i = i0;
 #pragma unroll(TPR > 1 ? 4 : 1)
