@@ -399,9 +399,9 @@ __global__ void __launch_bounds__(N * TPR, TPR == 1 ? 1024 / N : 1) fstep_kernel
                 }
                 }
                 r = node - ((1 << m.D) - 1);
-                // the chosen expert's arrays towards L2 while the layer input is finished: at small batches one
-                // 128-byte line per thread (the requests leave at once, over the whole block), else one bulk
-                // prefetch per array
+                // the chosen expert's arrays towards L2 (without the split, while the layer input's parts are added):
+                // at small batches one 128-byte line per thread (the requests leave at once, over the whole block),
+                // else one bulk prefetch per array
                 if constexpr (TPR > 1) {
                     const int lt = N / 32, lu = y.ut != nullptr ? R2 * N / 32 : 0, la = y.at != nullptr ? bsz * N / 32 : 0;
                     for (int i = t; i < lt + lu + la + R * N / 32; i += NT) {
